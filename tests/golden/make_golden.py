@@ -1,0 +1,549 @@
+"""Generate golden fixtures by running the reference's own Python on CPU.
+
+Run in a container where the reference checkout exists (it is NOT available on
+the GPU box; the fixtures it writes are committed next to this script):
+
+    TORCHDYNAMO_DISABLE=1 TRITON_INTERPRET=1 python tests/golden/make_golden.py \
+        --reference /path/to/VoiceAgent
+
+``TORCHDYNAMO_DISABLE`` turns the reference's ``@torch.compile`` decorators into
+plain eager calls; ``TRITON_INTERPRET`` runs its Triton kernels (the KV store and
+the TTS paged decode) on the CPU interpreter. What each fixture pins:
+
+* ``audio_pack.json``   -- ``audio/tokens.py`` + ``audio/batcher.py`` metadata
+* ``decoder_pack.npz``  -- ``ModelRunner._prepare`` (model_runner.py:183-233)
+* ``decode_bucket.npz`` -- ``GraphRunner.run`` staging (graph_runner.py:149-191)
+* ``block_manager.json``-- ``BlockManager`` allocation traces with prefix caching
+* ``store.npz``         -- ``store_kvcache`` Triton kernel (attention.py:31-67)
+* ``paged_decode.npz``  -- TTS paged decode, its torch reference path
+  (the Triton launcher refuses CPU tensors)
+* ``norm_rope.npz``     -- RMSNorm + RotaryEmbedding as used in qwen3.py:42-48
+* ``elementwise.npz``   -- fused add-RMSNorm and SiluAndMul (layernorm.py, activation.py)
+* ``sampler.npz``       -- greedy ``Sampler`` (sampler.py:16-27)
+* ``model_tiny.npz``    -- upstream HF Qwen3-ASR thinker on a tiny seeded config
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+REPO = HERE.parents[1]
+sys.path.insert(0, str(REPO))
+
+
+def _f32(t):
+    return t.detach().float().cpu().numpy()
+
+
+# ------------------------------------------------------------------- requests
+
+
+def _make_request(prompt_len, audio_offset, audio_length, block_size=256, seed_ids=None):
+    import torch
+    from qwen_asr_vllm.audio.frontend import AudioFeatures
+    from qwen_asr_vllm.engine.request import AsrRequest, SamplingParams
+    from qwen_asr_vllm.prompt import PromptLayout
+
+    suffix = prompt_len - audio_offset - audio_length
+    ids = (list(range(1000, 1000 + audio_offset)) + [151676] * audio_length
+           + list(range(2000, 2000 + suffix)))
+    if seed_ids is not None:
+        ids = list(seed_ids)
+    frames = max(1, audio_length * 100 // 13)
+    return AsrRequest(
+        features=AudioFeatures(mel=torch.zeros(128, frames), mel_frames=frames,
+                               num_audio_tokens=audio_length, audio_seconds=audio_length / 13),
+        layout=PromptLayout(token_ids=ids, audio_offset=audio_offset, audio_length=audio_length),
+        sampling=SamplingParams(),
+        block_size=block_size,
+        stop_token_ids={151643, 151645},
+    )
+
+
+# -------------------------------------------------------------------- fixtures
+
+
+def gen_audio_pack(out: Path):
+    import torch
+    from qwen_asr_vllm.audio.batcher import build_window_boundaries, pack_audio_batch
+    from qwen_asr_vllm.audio.tokens import num_audio_tokens
+
+    rng = np.random.default_rng(0)
+    cases = [[350, 200, 105], [100], [7], [208 * 100 // 13 + 1], [2500], [99, 100, 101, 199, 200, 201]]
+    cases += [list(map(int, rng.integers(1, 6000, size=int(rng.integers(1, 33))))) for _ in range(12)]
+    packs = []
+    for frames in cases:
+        b = pack_audio_batch([torch.zeros(128, f) for f in frames], n_window_infer=800)
+        packs.append({
+            "mel_frames": frames,
+            "chunk_lengths": b.chunk_lengths.tolist(),
+            "chunk_valid_lens": b.chunk_valid_lens.tolist(),
+            "cu_seqlens": b.cu_seqlens.tolist(),
+            "audio_token_lens": list(b.audio_token_lens),
+            "window_tokens": b.window_tokens,
+            "max_seqlen": int(b.max_seqlen),
+        })
+    windows = [{"lens": lens, "window": w, "boundaries": build_window_boundaries(lens, w)}
+               for lens, w in [([46, 26, 95], 104), ([250], 104), ([208], 104), ([1, 103, 104, 105], 104)]]
+    data = {
+        "num_audio_tokens": [num_audio_tokens(f) for f in range(1, 6000)],
+        "packs": packs,
+        "windows": windows,
+    }
+    (out / "audio_pack.json").write_text(json.dumps(data))
+
+
+def _allocate_batch(manager, specs):
+    """specs: list of (prompt_len, audio_offset, audio_len, n_decoded)."""
+    reqs = []
+    for prompt_len, off, alen, n_dec in specs:
+        r = _make_request(prompt_len, off, alen)
+        manager.allocate(r)
+        for step in range(n_dec):
+            r.num_computed_tokens = len(r)
+            r.append_token(3000 + step)
+            manager.may_append(r)
+        reqs.append(r)
+    return reqs
+
+
+def gen_decoder_pack(out: Path):
+    from types import SimpleNamespace
+
+    from qwen_asr_vllm.engine.block_manager import BlockManager
+    from qwen_asr_vllm.engine.model_runner import ModelRunner
+    from qwen_asr_vllm.engine.scheduler import ModelBatch
+
+    rng = np.random.default_rng(1)
+    arrays = {}
+    batches = [
+        # (prefill specs, decode specs)
+        ([(70, 9, 52, 0)], []),
+        ([], [(70, 9, 52, 5)]),
+        ([(300, 9, 270, 0), (40, 9, 13, 0)], [(256, 9, 200, 1), (255, 9, 200, 1), (600, 9, 560, 40)]),
+        ([(700, 609, 46, 0)], [(62, 9, 46, 3)]),
+    ]
+    for _ in range(4):
+        npre = int(rng.integers(0, 4))
+        ndec = int(rng.integers(1 if npre == 0 else 0, 20))
+        pre = [(int(p), 9, int(p) - 18, 0) for p in rng.integers(20, 900, size=npre)]
+        dec = [(int(p), 9, int(p) - 18, int(d)) for p, d in zip(rng.integers(20, 900, size=ndec),
+                                                               rng.integers(1, 300, size=ndec))]
+        batches.append((pre, dec))
+
+    stub = SimpleNamespace(block_size=256, device="cpu", _audio_span=ModelRunner._audio_span)
+    for bi, (pre_specs, dec_specs) in enumerate(batches):
+        manager = BlockManager(num_blocks=4096, block_size=256, enable_prefix_cache=False)
+        # Shuffle physical block order so tables are not trivially contiguous.
+        order = list(rng.permutation(4096))
+        manager.free_block_ids = dict.fromkeys(int(i) for i in order)
+        pre = _allocate_batch(manager, pre_specs)
+        dec = _allocate_batch(manager, dec_specs)
+        for r in dec:  # a decode row has computed everything but its last token
+            r.num_computed_tokens = len(r) - 1
+        batch = ModelBatch(prefill=pre, decode=dec)
+        input_ids, positions, ctx, _ = ModelRunner._prepare(stub, batch)
+        reqs = batch.requests
+        p = f"b{bi}_"
+        arrays[p + "starts"] = np.asarray([r.num_computed_tokens for r in reqs], np.int32)
+        arrays[p + "ends"] = np.asarray([len(r) for r in reqs], np.int32)
+        arrays[p + "table_lens"] = np.asarray([len(r.block_table) for r in reqs], np.int32)
+        arrays[p + "tables_flat"] = np.asarray(sum((list(r.block_table) for r in reqs), []), np.int32)
+        arrays[p + "token_lens"] = np.asarray([len(r.token_ids) for r in reqs], np.int32)
+        arrays[p + "tokens_flat"] = np.asarray(sum((list(r.token_ids) for r in reqs), []), np.int64)
+        arrays[p + "input_ids"] = input_ids.numpy()
+        arrays[p + "positions"] = positions.numpy()
+        arrays[p + "slot_mapping"] = ctx.slot_mapping.numpy()
+        arrays[p + "cu_seqlens_q"] = ctx.cu_seqlens_q.numpy()
+        arrays[p + "cu_seqlens_k"] = ctx.cu_seqlens_k.numpy()
+        arrays[p + "max_seqlen"] = np.asarray([ctx.max_seqlen_q, ctx.max_seqlen_k], np.int32)
+        arrays[p + "block_tables"] = ctx.block_tables.numpy()
+    arrays["num_batches"] = np.asarray(len(batches))
+    np.savez_compressed(out / "decoder_pack.npz", **arrays)
+
+
+def gen_decode_bucket(out: Path):
+    import torch
+    from qwen_asr_vllm.engine.block_manager import BlockManager
+    from qwen_asr_vllm.engine.graph_runner import GraphRunner
+
+    class _Graph:
+        def replay(self):
+            pass
+
+    rng = np.random.default_rng(2)
+    arrays = {}
+    cases = [(1, 1), (3, 4), (17, 24), (32, 32), (5, 8)]
+    for ci, (b, bucket) in enumerate(cases):
+        runner = GraphRunner.__new__(GraphRunner)
+        runner.device = torch.device("cpu")
+        runner.block_size = 256
+        runner.config = type("C", (), {"max_model_len": 4096})()
+        runner.max_blocks = 16
+        runner.buckets = (1, 2, 4, 8, 16, 24, 32, 48, 64)
+        runner.max_batch_size = 64
+        runner._allocate_buffers()
+        runner.graphs = {bucket: _Graph()}
+        runner.outputs = {bucket: torch.zeros(bucket, 4)}
+        manager = BlockManager(num_blocks=4096, block_size=256, enable_prefix_cache=False)
+        manager.free_block_ids = dict.fromkeys(int(i) for i in rng.permutation(4096))
+        specs = [(int(p), 9, int(p) - 18, int(d)) for p, d in zip(rng.integers(20, 1500, size=b),
+                                                                 rng.integers(1, 500, size=b))]
+        reqs = _allocate_batch(manager, specs)
+        runner.run(reqs)
+        p = f"c{ci}_"
+        arrays[p + "bucket"] = np.asarray(bucket)
+        arrays[p + "lens"] = np.asarray([len(r) for r in reqs], np.int32)
+        arrays[p + "last_ids"] = np.asarray([r.last_token_id for r in reqs], np.int64)
+        arrays[p + "table_lens"] = np.asarray([len(r.block_table) for r in reqs], np.int32)
+        arrays[p + "tables_flat"] = np.asarray(sum((list(r.block_table) for r in reqs), []), np.int32)
+        arrays[p + "input_ids"] = runner.input_ids[:bucket].numpy()
+        arrays[p + "positions"] = runner.positions[:bucket].numpy()
+        arrays[p + "slot_mapping"] = runner.slot_mapping[:bucket].numpy()
+        arrays[p + "cu_seqlens_k"] = runner.cu_seqlens_k[: bucket + 1].numpy()
+        arrays[p + "block_tables"] = runner.block_tables[:bucket].numpy()
+    arrays["num_cases"] = np.asarray(len(cases))
+    np.savez_compressed(out / "decode_bucket.npz", **arrays)
+
+
+def gen_block_manager(out: Path):
+    from qwen_asr_vllm.engine.block_manager import BlockManager
+
+    traces = []
+    for prefix_cache in (True, False):
+        manager = BlockManager(num_blocks=24, block_size=256, enable_prefix_cache=prefix_cache)
+        reqs = {}
+        ops = [
+            ("alloc", "a", (700, 609, 46)), ("alloc", "b", (700, 609, 46)),
+            ("alloc", "c", (600, 0, 590)), ("append", "a", 260), ("dealloc", "b", None),
+            ("alloc", "d", (700, 609, 46)), ("alloc", "e", (300, 9, 270)),
+            ("append", "e", 300), ("dealloc", "a", None), ("dealloc", "c", None),
+            ("alloc", "f", (1100, 900, 100)), ("alloc", "g", (1100, 900, 100)),
+        ]
+        log = []
+        for op, name, arg in ops:
+            if op == "alloc":
+                r = _make_request(*arg)
+                reqs[name] = r
+                ok = manager.can_allocate(r)
+                if ok:
+                    manager.allocate(r)
+                log.append({"op": op, "name": name, "arg": list(arg), "ok": ok,
+                            "table": list(r.block_table), "cached": r.num_cached_tokens,
+                            "computed": r.num_computed_tokens, "free": manager.num_free_blocks})
+            elif op == "append":
+                r = reqs[name]
+                tables = []
+                for step in range(arg):
+                    r.append_token(5000 + step)
+                    if manager.can_append(r):
+                        manager.may_append(r)
+                    tables.append(len(r.block_table))
+                log.append({"op": op, "name": name, "arg": arg, "table": list(r.block_table),
+                            "free": manager.num_free_blocks})
+            else:
+                manager.deallocate(reqs[name])
+                log.append({"op": op, "name": name, "free": manager.num_free_blocks,
+                            "free_order": list(manager.free_block_ids)})
+        traces.append({"prefix_cache": prefix_cache, "log": log,
+                       "hash_example": BlockManager.compute_hash(list(range(256)))})
+    (out / "block_manager.json").write_text(json.dumps(traces))
+
+
+def _bf16_bits(t):
+    """bf16 tensor -> its raw uint16 bit patterns (exact and half the size of fp32)."""
+    import torch
+
+    return t.detach().cpu().contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+def gen_store(out: Path):
+    import torch
+    from qwen_asr_vllm.layers.attention import store_kvcache
+
+    g = torch.Generator().manual_seed(3)
+    t, hq, hkv, d, nblocks = 37, 4, 2, 64, 2
+    qkv = torch.randn(t, (hq + 2 * hkv) * d, generator=g).bfloat16()
+    k = qkv[:, hq * d : (hq + hkv) * d].view(t, hkv, d)
+    v = qkv[:, (hq + hkv) * d :].view(t, hkv, d)
+    kc = torch.randn(nblocks, 256, hkv, d, generator=g).bfloat16()
+    vc = torch.randn(nblocks, 256, hkv, d, generator=g).bfloat16()
+    slots = torch.randperm(nblocks * 256, generator=g)[:t].to(torch.int32)
+    slots[[0, 5, 36]] = -1
+    kc0, vc0 = kc.clone(), vc.clone()
+    store_kvcache(k, v, kc, vc, slots)
+    np.savez_compressed(out / "store.npz", qkv=_bf16_bits(qkv), k_cache_before=_bf16_bits(kc0),
+                        v_cache_before=_bf16_bits(vc0), slots=slots.numpy(),
+                        k_cache=_bf16_bits(kc), v_cache=_bf16_bits(vc),
+                        dims=np.asarray([t, hq, hkv, d, nblocks]))
+
+
+def gen_paged_decode(out: Path):
+    """The reference's own paged decode (TTS module) in the TTS pool layout.
+
+    Inputs are drawn in the engine's layout (N, 256, H_kv, D) and permuted to the
+    TTS layout (N, H_kv, 256, D) for the call; the fixture stores the engine
+    layout so consumers need no permutation.
+    """
+    import torch
+    from qwen_asr_vllm.agent.qwen_tts_paged_attention import paged_attention_decode
+
+    g = torch.Generator().manual_seed(4)
+    b, hq, hkv, d, bs, nblocks = 5, 4, 2, 64, 256, 10
+    lens = torch.tensor([1, 64, 255, 257, 520], dtype=torch.long)
+    kc = (torch.randn(nblocks, bs, hkv, d, generator=g) / d**0.5).bfloat16()
+    vc = (torch.randn(nblocks, bs, hkv, d, generator=g) / d**0.5).bfloat16()
+    q = (torch.randn(b, hq, d, generator=g) / d**0.5).bfloat16()
+    perm = torch.randperm(nblocks, generator=g)
+    width = 3
+    tables = torch.zeros(b, width, dtype=torch.long)
+    cursor = 0
+    for row, length in enumerate(lens.tolist()):
+        need = (length + bs - 1) // bs
+        tables[row, :need] = perm[cursor : cursor + need]
+        cursor += need
+    kp, vp = kc.permute(0, 2, 1, 3).contiguous(), vc.permute(0, 2, 1, 3).contiguous()
+    ref = paged_attention_decode(q.float().unsqueeze(2), kp.float(), vp.float(), tables, lens,
+                                 use_triton=False)
+    np.savez_compressed(out / "paged_decode.npz", q=_bf16_bits(q), k_cache=_bf16_bits(kc),
+                        v_cache=_bf16_bits(vc),
+                        lens=lens.numpy().astype(np.int32), tables=tables.numpy().astype(np.int32),
+                        out_reference=_f32(ref.squeeze(2)))
+
+
+def gen_norm_rope(out: Path):
+    import torch
+    from qwen_asr_vllm.layers.layernorm import RMSNorm
+    from qwen_asr_vllm.layers.rotary_embedding import RotaryEmbedding
+
+    g = torch.Generator().manual_seed(5)
+    t, hq, hkv, d = 12, 16, 8, 128
+    qkv = (torch.randn(t, (hq + 2 * hkv) * d, generator=g) * 2).bfloat16()
+    positions = torch.randint(0, 4096, (t,), generator=g)
+    q_norm, k_norm = RMSNorm(d, 1e-6), RMSNorm(d, 1e-6)
+    with torch.no_grad():
+        q_norm.weight.copy_(torch.rand(d, generator=g) + 0.5)
+        k_norm.weight.copy_(torch.rand(d, generator=g) + 0.5)
+    q_norm, k_norm = q_norm.bfloat16(), k_norm.bfloat16()
+    rope = RotaryEmbedding(d, 4096, 1_000_000.0)
+    q, k, v = qkv.split([hq * d, hkv * d, hkv * d], dim=-1)
+    qn = q_norm(q.reshape(-1, hq, d))
+    kn = k_norm(k.reshape(-1, hkv, d))
+    qr, kr = rope(positions, qn, kn)
+    np.savez_compressed(out / "norm_rope.npz", qkv=_bf16_bits(qkv), positions=positions.numpy(),
+                        q_weight=_bf16_bits(q_norm.weight), k_weight=_bf16_bits(k_norm.weight),
+                        cos_sin_cache=_f32(rope.cos_sin_cache.squeeze(1)[positions]),
+                        q_normed=_bf16_bits(qn), k_normed=_bf16_bits(kn), q_out=_bf16_bits(qr),
+                        k_out=_bf16_bits(kr))
+
+
+def gen_elementwise(out: Path):
+    import torch
+    from qwen_asr_vllm.layers.activation import SiluAndMul
+    from qwen_asr_vllm.layers.layernorm import RMSNorm
+
+    g = torch.Generator().manual_seed(6)
+    x = torch.randn(19, 1024, generator=g).bfloat16()
+    res = torch.randn(19, 1024, generator=g).bfloat16()
+    norm = RMSNorm(1024, 1e-6)
+    with torch.no_grad():
+        norm.weight.copy_(torch.rand(1024, generator=g) + 0.5)
+    norm = norm.bfloat16()
+    y_plain = norm(x.clone())
+    y_add, r_add = norm(x.clone(), res.clone())
+    gu = (torch.randn(19, 2 * 3072, generator=g) * 3).bfloat16()
+    act = SiluAndMul()(gu)
+    np.savez_compressed(out / "elementwise.npz", x=_bf16_bits(x), residual=_bf16_bits(res),
+                        weight=_bf16_bits(norm.weight), rms=_bf16_bits(y_plain),
+                        add_rms=_bf16_bits(y_add), add_residual=_bf16_bits(r_add),
+                        gate_up=_bf16_bits(gu), silu_mul=_bf16_bits(act))
+
+
+def gen_sampler(out: Path):
+    import torch
+    from qwen_asr_vllm.layers.sampler import Sampler
+
+    g = torch.Generator().manual_seed(7)
+    logits = torch.randn(5, 151936, generator=g).bfloat16()
+    logits[1, 100] = 30.0
+    logits[1, 90000] = 30.0  # tie: first index wins
+    logits[2, :] = -5.0      # all equal
+    logits[3, 151935] = 1e4  # last index
+    logits[4, 0] = float("inf")
+    logits[4, 7] = float("inf")
+    ids = Sampler()(logits, torch.zeros(5))
+    np.savez_compressed(out / "sampler.npz", logits=_bf16_bits(logits), ids=ids.numpy())
+
+
+# -------------------------------------------------------------------- HF model
+
+
+def tiny_thinker_config():
+    """A small Qwen3-ASR configuration with the real structure (GQA, QK-norm, 3 convs)."""
+    return {
+        "audio": dict(num_mel_bins=128, d_model=64, encoder_layers=2, encoder_attention_heads=4,
+                      encoder_ffn_dim=96, downsample_hidden_size=16, output_dim=96, n_window=50,
+                      n_window_infer=800, conv_chunksize=500, max_source_positions=1500),
+        "text": dict(vocab_size=512, hidden_size=96, intermediate_size=160, num_hidden_layers=2,
+                     num_attention_heads=4, num_key_value_heads=2, head_dim=32, rms_norm_eps=1e-6,
+                     rope_theta=1_000_000.0, max_position_embeddings=4096, tie_word_embeddings=True),
+        "audio_token_id": 500,
+        "audio_start_token_id": 498,
+        "audio_end_token_id": 499,
+    }
+
+
+def _import_hf_with_shims():
+    """Import the upstream modeling file under transformers 5.x.
+
+    Four runtime shims, no file edits (the file targets transformers 4.57):
+    ``check_model_inputs`` callable with no arguments, a ``default`` RoPE init
+    function, the same on the rotary class, and ``pad_token_id = None`` on configs
+    (set in :func:`_build_hf_thinker`).
+    """
+    import functools
+
+    import torch
+    import transformers.utils.generic as generic
+    from transformers import modeling_rope_utils
+
+    original = generic.check_model_inputs
+    if not getattr(original, "_golden_shim", False):
+        def check_model_inputs(func=None, **kwargs):
+            if func is None:
+                return lambda f: original(f, **kwargs) if kwargs else original(f)
+            return original(func, **kwargs) if kwargs else original(func)
+
+        check_model_inputs._golden_shim = True
+        generic.check_model_inputs = check_model_inputs
+
+    def default_rope(config, device=None, *args, **kwargs):
+        base = config.rope_theta
+        dim = getattr(config, "head_dim", None) or config.hidden_size // config.num_attention_heads
+        inv = 1.0 / (base ** (torch.arange(0, dim, 2, dtype=torch.int64).float().to(device) / dim))
+        return inv, 1.0
+
+    modeling_rope_utils.ROPE_INIT_FUNCTIONS.setdefault("default", default_rope)
+    from reference import modeling_qwen3_asr as hf
+
+    hf.Qwen3ASRThinkerTextRotaryEmbedding.compute_default_rope_parameters = staticmethod(
+        functools.partial(default_rope))
+    return hf
+
+
+def _build_hf_thinker(hf, cfg: dict, weights):
+    import torch
+    from reference import configuration_qwen3_asr as hfc
+
+    audio = hfc.Qwen3ASRAudioEncoderConfig(**cfg["audio"])
+    text = hfc.Qwen3ASRTextConfig(**cfg["text"], rope_scaling={"mrope_section": [8, 4, 4],
+                                                               "rope_type": "default"})
+    thinker_cfg = hfc.Qwen3ASRThinkerConfig(audio_config=audio.to_dict(), text_config=text.to_dict(),
+                                            audio_token_id=cfg["audio_token_id"],
+                                            audio_start_token_id=cfg["audio_start_token_id"])
+    thinker_cfg.pad_token_id = None
+    thinker_cfg.text_config.pad_token_id = None
+    thinker_cfg._attn_implementation = "eager"
+    thinker_cfg.audio_config._attn_implementation = "eager"
+    thinker_cfg.text_config._attn_implementation = "eager"
+    model = hf.Qwen3ASRThinkerForConditionalGeneration(thinker_cfg).float().eval()
+    state = {k: v for k, v in weights.items()}
+    missing, unexpected = model.load_state_dict(state, strict=False)
+    missing = [m for m in missing if m != "lm_head.weight"]
+    if missing or unexpected:
+        raise RuntimeError(f"weight mismatch: missing={missing[:5]} unexpected={unexpected[:5]}")
+    with torch.no_grad():
+        model.lm_head.weight.copy_(weights["lm_head.weight"])
+    return model
+
+
+def _hf_greedy(thinker, prompt, mel, frames, steps):
+    """Manual greedy loop over ``forward`` with a DynamicCache (generate() needs
+    ``cache_position`` that transformers 5.x leaves unset)."""
+    import torch
+    from transformers import DynamicCache
+
+    ids = torch.tensor([prompt])
+    cache = DynamicCache()
+    mask = torch.ones_like(ids)
+    out = thinker(input_ids=ids, input_features=mel.unsqueeze(0),
+                  feature_attention_mask=torch.ones(1, frames, dtype=torch.long),
+                  attention_mask=mask, past_key_values=cache, use_cache=True,
+                  cache_position=torch.arange(ids.shape[1]))
+    first_logits = out.logits[0, -1]
+    tokens = [int(first_logits.argmax())]
+    length = ids.shape[1]
+    for _ in range(steps - 1):
+        step_ids = torch.tensor([[tokens[-1]]])
+        mask = torch.ones(1, length + 1, dtype=torch.long)
+        out = thinker(input_ids=step_ids, attention_mask=mask, past_key_values=cache,
+                      use_cache=True, cache_position=torch.tensor([length]),
+                      position_ids=torch.tensor([[length]]))
+        length += 1
+        tokens.append(int(out.logits[0, -1].argmax()))
+    return tokens, first_logits
+
+
+def gen_model_tiny(out: Path):
+    """Upstream HF thinker (reference/modeling_qwen3_asr.py) on a seeded tiny config."""
+    import torch
+    from oracle import model as omodel
+
+    hf = _import_hf_with_shims()
+    cfg = tiny_thinker_config()
+    weights = omodel.init_weights(cfg, seed=11)
+    thinker = _build_hf_thinker(hf, cfg, weights)
+
+    g = torch.Generator().manual_seed(12)
+    frames = 437
+    mel = torch.randn(128, frames, generator=g) * 0.5
+    n_audio = omodel.num_audio_tokens(frames)
+    prompt = ([344, 13, 14, 345, 15, 344, 16, 17, 498]
+              + [500] * n_audio + [499, 345, 15, 344, 18, 19, 20, 21, 22])
+    with torch.no_grad():
+        audio = thinker.get_audio_features(mel.unsqueeze(0),
+                                           feature_attention_mask=torch.ones(1, frames, dtype=torch.long))
+        tokens, logits0 = _hf_greedy(thinker, prompt, mel, frames, steps=12)
+    np.savez_compressed(out / "model_tiny.npz", mel=mel.numpy(), prompt=np.asarray(prompt),
+                        audio_features=_f32(audio), greedy=np.asarray(tokens),
+                        first_logits=_f32(logits0), seed=np.asarray(11))
+
+
+GENERATORS = {
+    "audio_pack": gen_audio_pack,
+    "decoder_pack": gen_decoder_pack,
+    "decode_bucket": gen_decode_bucket,
+    "block_manager": gen_block_manager,
+    "store": gen_store,
+    "paged_decode": gen_paged_decode,
+    "norm_rope": gen_norm_rope,
+    "elementwise": gen_elementwise,
+    "sampler": gen_sampler,
+    "model_tiny": gen_model_tiny,
+}
+
+
+def main():
+    parser = argparse.ArgumentParser()
+    parser.add_argument("--reference", required=True, help="VoiceAgent checkout")
+    parser.add_argument("--only", nargs="*", default=None)
+    args = parser.parse_args()
+    if os.environ.get("TORCHDYNAMO_DISABLE") != "1":
+        raise SystemExit("set TORCHDYNAMO_DISABLE=1 (eager reference semantics)")
+    sys.path.insert(0, args.reference)
+    for name, fn in GENERATORS.items():
+        if args.only and name not in args.only:
+            continue
+        fn(HERE)
+        print("wrote", name)
+
+
+if __name__ == "__main__":
+    main()
