@@ -1,0 +1,218 @@
+/*
+ * b200asr -- B200 (sm_100a) kernels for the ragged continuous-batching path of the
+ * qwen-asr-vllm engine (Qwen3-ASR). C ABI: plain device pointers, sizes and a CUDA
+ * stream; no framework types. Every call is asynchronous on `stream`, launches only
+ * kernels (no allocation, no host synchronisation), and may therefore be captured
+ * in a CUDA graph. All tensors are device memory owned by the caller.
+ *
+ * Types: "bf16" = 16-bit bfloat16 element, passed as void*. Row strides are in
+ * ELEMENTS. Every function returns B200ASR_OK (0) or an error code; the message of
+ * the last failure on the calling thread is available from b200asr_last_error().
+ *
+ * Device-side index checks: where a kernel meets an index outside the caller's
+ * declared bounds (a KV slot or block id outside the pool, a position outside the
+ * RoPE table) it skips that access and ORs a bit into *error_flag (when non-NULL):
+ *   B200ASR_DEVERR_SLOT 1, B200ASR_DEVERR_BLOCK 2, B200ASR_DEVERR_POSITION 4,
+ *   B200ASR_DEVERR_LENGTH 8. The host reads the word after the step.
+ *
+ * Reference locations are paths inside the qwen-asr-vllm project.
+ */
+#ifndef B200ASR_H_
+#define B200ASR_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define B200ASR_API __attribute__((visibility("default")))
+#else
+#define B200ASR_API
+#endif
+
+typedef struct CUstream_st *b200asr_stream_t; /* == cudaStream_t */
+
+enum {
+  B200ASR_OK = 0,
+  B200ASR_ERR_INVALID = 1,     /* bad shape, stride, alignment or null pointer */
+  B200ASR_ERR_CUDA = 2,        /* a CUDA runtime/driver call failed */
+  B200ASR_ERR_UNSUPPORTED = 3, /* configuration outside what the kernels handle */
+  B200ASR_ERR_WORKSPACE = 4    /* caller workspace too small */
+};
+
+enum {
+  B200ASR_DEVERR_SLOT = 1,
+  B200ASR_DEVERR_BLOCK = 2,
+  B200ASR_DEVERR_POSITION = 4,
+  B200ASR_DEVERR_LENGTH = 8
+};
+
+/* Library version (major*10000 + minor*100 + patch) and last error message. */
+B200ASR_API int b200asr_version(void);
+B200ASR_API const char *b200asr_last_error(void);
+
+/* ---------------------------------------------------------------- packers ----
+ * Replaces ModelRunner._prepare (engine/model_runner.py:183-233): builds the ragged
+ * decoder metadata of a mixed prefill/decode batch on the GPU.
+ *   req_start[b]  = num_computed_tokens, req_end[b] = len(request)
+ *   table_off[b], table_len[b] index the concatenated block tables `tables`
+ *   query_tokens  = concatenated token ids of every request's query span
+ * Outputs: input_ids i64[T], positions i64[T], slot_mapping i32[T]
+ * (= table[p / block_size] * block_size + p % block_size), cu_seqlens_q/k i32[B+1],
+ * max_seqlen i32[2] (q, k), block_tables i32[B, width] padded with -1,
+ * last_token_index i64[B] (= cu_seqlens_q[b+1] - 1). T = sum(end - start) must be
+ * passed as total_tokens and width >= max(table_len).                              */
+B200ASR_API int b200asr_pack_decoder(const int32_t *req_start, const int32_t *req_end,
+                         const int32_t *table_off, const int32_t *table_len,
+                         const int32_t *tables, const int32_t *query_tokens,
+                         int32_t batch, int32_t total_tokens, int32_t width,
+                         int32_t block_size, int64_t *input_ids, int64_t *positions,
+                         int32_t *slot_mapping, int32_t *cu_seqlens_q, int32_t *cu_seqlens_k,
+                         int32_t *max_seqlen, int32_t *block_tables,
+                         int64_t *last_token_index, b200asr_stream_t stream);
+
+/* Replaces GraphRunner.run host staging (engine/graph_runner.py:149-191): fills the
+ * static decode buffers of a CUDA-graph bucket. Rows >= batch are padding: slot -1,
+ * key length 1, all-zero block-table row, input id and position 0.
+ *   lens[b] = len(request), last_ids[b] = last token id.
+ * Outputs (sized for `bucket`): input_ids i64, positions i64, slot_mapping i32,
+ * cu_seqlens_k i32[bucket+1], block_tables i32[bucket, max_blocks].              */
+B200ASR_API int b200asr_pack_decode_bucket(const int32_t *lens, const int32_t *last_ids,
+                               const int32_t *table_off, const int32_t *table_len,
+                               const int32_t *tables, int32_t batch, int32_t bucket,
+                               int32_t max_blocks, int32_t block_size, int64_t *input_ids,
+                               int64_t *positions, int32_t *slot_mapping,
+                               int32_t *cu_seqlens_k, int32_t *block_tables,
+                               b200asr_stream_t stream);
+
+/* Replaces the metadata of pack_audio_batch (audio/batcher.py:101-141) and
+ * num_audio_tokens/chunk_lengths_for (audio/tokens.py:30-52).
+ *   mel_frames[b] > 0 for each request.
+ * Outputs: chunk_lengths i64[C], chunk_valid_lens i64[C], chunk_start i32[C]
+ * (first mel frame of each chunk), audio_token_lens i32[B], cu_seqlens i32[W+1]
+ * (attention windows of `window_tokens`), counts i32[3] = {C, W, max_seqlen}.
+ * Capacities max_chunks / max_windows bound the outputs (B200ASR_DEVERR_LENGTH is
+ * raised in *error_flag if exceeded).                                            */
+B200ASR_API int b200asr_pack_audio(const int32_t *mel_frames, int32_t batch, int32_t chunk_frames,
+                       int32_t window_tokens, int32_t max_chunks, int32_t max_windows,
+                       int64_t *chunk_lengths, int64_t *chunk_valid_lens, int32_t *chunk_start,
+                       int32_t *audio_token_lens, int32_t *cu_seqlens, int32_t *counts,
+                       int32_t *error_flag, b200asr_stream_t stream);
+
+/* Replaces AudioEncoder._chunk_and_pad (models/audio_encoder.py:130-143): packed
+ * mel bf16[bins, total_frames] -> padded bf16[num_chunks, bins, chunk_frames] with
+ * zeros past each chunk's length.                                                */
+B200ASR_API int b200asr_audio_chunk_pad(const void *mel, int32_t bins, int32_t total_frames,
+                            const int32_t *chunk_start, const int64_t *chunk_lengths,
+                            int32_t num_chunks, int32_t chunk_frames, void *padded,
+                            b200asr_stream_t stream);
+
+/* ------------------------------------------------------------------ KV store ----
+ * Replaces store_kvcache / _store_kvcache_kernel (layers/attention.py:31-67).
+ * key/value: bf16 [T, num_kv_heads, head_dim] with row strides (elements) and a
+ * contiguous [num_kv_heads * head_dim] row; caches: bf16 [num_slots, num_kv_heads *
+ * head_dim]. slot_mapping[t] == -1 skips token t.                                 */
+B200ASR_API int b200asr_store_kvcache(const void *key, int64_t key_row_stride, const void *value,
+                          int64_t value_row_stride, void *k_cache, void *v_cache,
+                          const int32_t *slot_mapping, int32_t num_tokens,
+                          int32_t num_kv_heads, int32_t head_dim, int64_t num_slots,
+                          int32_t *error_flag, b200asr_stream_t stream);
+
+/* --------------------------------------------------------- norm + rope + store ----
+ * Replaces Qwen3Attention.forward lines 43-48 (models/qwen3.py) plus the KV store:
+ * from the fused qkv row [q | k | v] (bf16, row stride qkv_row_stride) computes
+ * per-head RMSNorm of q and k (layers/layernorm.py:19-25, eps, bf16 weights), then
+ * half-split RoPE (layers/rotary_embedding.py:9-32) at positions[t] using
+ * cos_sin_cache fp32 [max_position, head_dim] = [cos | sin], writes q to q_out
+ * (bf16 [T, num_heads, head_dim], row stride q_out_row_stride) and k, v into the
+ * paged caches at slot_mapping[t] (-1 skips). If k_out is non-NULL the rotated k is
+ * also written there (bf16 [T, num_kv_heads, head_dim], contiguous).               */
+B200ASR_API int b200asr_qk_norm_rope_store(const void *qkv, int64_t qkv_row_stride,
+                               const int64_t *positions, int32_t num_tokens,
+                               int32_t num_heads, int32_t num_kv_heads, int32_t head_dim,
+                               const void *q_norm_weight, const void *k_norm_weight,
+                               float eps, const float *cos_sin_cache, int32_t max_position,
+                               void *q_out, int64_t q_out_row_stride, void *k_out,
+                               void *k_cache, void *v_cache, const int32_t *slot_mapping,
+                               int64_t num_slots, int32_t *error_flag,
+                               b200asr_stream_t stream);
+
+/* Replaces RMSNorm._norm / RMSNorm._add_norm (layers/layernorm.py:19-36).
+ * x bf16 [rows, hidden]. With residual == NULL: out = norm(x) * w. Otherwise
+ * s = x + residual (fp32); residual <- bf16(s) (in place); out = norm(s) * w.     */
+B200ASR_API int b200asr_rmsnorm(const void *x, void *residual, const void *weight, float eps,
+                    int32_t rows, int32_t hidden, void *out, b200asr_stream_t stream);
+
+/* Replaces SiluAndMul (layers/activation.py:8-14): x bf16 [rows, 2*inner] ->
+ * out bf16 [rows, inner] = silu(x[:, :inner]) * x[:, inner:].                    */
+B200ASR_API int b200asr_silu_mul(const void *x, int32_t rows, int32_t inner, void *out,
+                     b200asr_stream_t stream);
+
+/* ---------------------------------------------------------------- attention ----
+ * Split-K paged decode. Replaces the decode use of flash_attn_varlen_func with a
+ * block table inside the CUDA-graph decode (layers/attention.py:96-107 with
+ * max_seqlen_q = 1, engine/graph_runner.py:81-94). One query token per sequence:
+ * q bf16 [batch, num_heads, head_dim] (row stride q_row_stride), context length of
+ * sequence b = cu_seqlens_k[b+1] - cu_seqlens_k[b]; keys/values from the paged
+ * caches bf16 [num_blocks, block_size, num_kv_heads, head_dim] through
+ * block_tables i32 [batch, bt_stride]. out bf16 [batch, num_heads, head_dim].
+ * Supported: head_dim 128, block_size 256, num_heads / num_kv_heads in {1,2,4,8},
+ * num_kv_heads <= 8. workspace: device scratch of at least
+ * b200asr_paged_decode_workspace_size(batch, max_seqlen_k, num_heads, head_dim)
+ * bytes; its contents need no initialisation.                                     */
+B200ASR_API size_t b200asr_paged_decode_workspace_size(int32_t batch, int32_t max_seqlen_k,
+                                           int32_t num_heads, int32_t head_dim);
+B200ASR_API int b200asr_paged_decode(const void *q, int64_t q_row_stride, const void *k_cache,
+                         const void *v_cache, int32_t num_blocks, int32_t block_size,
+                         int32_t num_heads, int32_t num_kv_heads, int32_t head_dim,
+                         const int32_t *cu_seqlens_k, const int32_t *block_tables,
+                         int32_t bt_stride, int32_t batch, int32_t max_seqlen_k, float scale,
+                         void *out, int64_t out_row_stride, void *workspace,
+                         size_t workspace_bytes, int32_t *error_flag, b200asr_stream_t stream);
+
+/* Varlen causal GQA attention over the paged KV cache on tcgen05 tensor cores.
+ * Replaces PagedAttention.forward (layers/attention.py:87-107) for prefill and mixed
+ * batches: flash_attn_varlen_func(q, k_cache, v_cache, cu_seqlens_q, cu_seqlens_k,
+ * max_seqlen_q, max_seqlen_k, softmax_scale, causal=True, block_table) with the
+ * causal mask aligned bottom-right (query i of a row with Lq queries and Lk keys
+ * sees keys 0 .. Lk - Lq + i). Rows with one query are decode rows.
+ * q bf16 [total_q, num_heads, head_dim]; out likewise. Supported: head_dim 128,
+ * block_size a multiple of 64, num_heads == 2 * num_kv_heads.                     */
+B200ASR_API int b200asr_paged_prefill(const void *q, int64_t q_row_stride, const void *k_cache,
+                          const void *v_cache, int32_t num_blocks, int32_t block_size,
+                          int32_t num_heads, int32_t num_kv_heads, int32_t head_dim,
+                          const int32_t *cu_seqlens_q, const int32_t *cu_seqlens_k,
+                          const int32_t *block_tables, int32_t bt_stride, int32_t batch,
+                          int32_t total_q, int32_t max_seqlen_q, float scale, void *out,
+                          int64_t out_row_stride, int32_t *error_flag,
+                          b200asr_stream_t stream);
+
+/* Bidirectional varlen attention inside segments on tcgen05 tensor cores. Replaces
+ * VarlenSelfAttention.forward (layers/attention.py:121-139, called from
+ * models/audio_encoder.py:58-67): flash_attn_varlen_func(q, k, v, cu_seqlens,
+ * cu_seqlens, max_seqlen, max_seqlen, scale, causal=False).
+ * q/k/v bf16 [total_tokens, num_heads, head_dim] with row strides (elements);
+ * out bf16 likewise. Supported: head_dim 64, segments of at most 128 tokens
+ * (the encoder's windows are 104).                                                */
+B200ASR_API int b200asr_varlen_attention(const void *q, int64_t q_row_stride, const void *k,
+                             int64_t k_row_stride, const void *v, int64_t v_row_stride,
+                             const int32_t *cu_seqlens, int32_t num_segments,
+                             int32_t total_tokens, int32_t max_seqlen, int32_t num_heads,
+                             int32_t head_dim, float scale, void *out, int64_t out_row_stride,
+                             int32_t *error_flag, b200asr_stream_t stream);
+
+/* ------------------------------------------------------------------ sampler ----
+ * Replaces the greedy branch of Sampler.forward (layers/sampler.py:16-20):
+ * out_ids[b] = argmax over logits[b, :vocab] (bf16, row stride in elements) in
+ * fp32, first index on ties, NaN counted as the maximum.                          */
+B200ASR_API int b200asr_greedy_argmax(const void *logits, int64_t row_stride, int32_t batch,
+                          int32_t vocab, int64_t *out_ids, b200asr_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B200ASR_H_ */

@@ -1,0 +1,8 @@
+"""B200-native ragged continuous-batching path of the qwen-asr-vllm engine.
+
+The CUDA kernels live in ``libb200asr.so`` (C ABI in ``include/b200asr.h``), built
+in-tree by ``python -m voiceagent_b200.build``; ``voiceagent_b200.kernels`` wraps them
+for torch tensors. Importing the package does not require a GPU.
+"""
+
+__version__ = "0.1.0"

@@ -1,0 +1,581 @@
+// Tensor-core (tcgen05 / TMEM / TMA) attention kernels for sm_100a.
+//
+// paged_prefill    <- PagedAttention.forward prefill/mixed rows (layers/attention.py:87-107):
+//                     flash_attn_varlen_func(..., causal=True, block_table=...) over the
+//                     paged cache, causal mask aligned bottom-right.
+// varlen_attention <- VarlenSelfAttention.forward (layers/attention.py:121-139) for the
+//                     audio encoder's 104-token windows, causal=False.
+//
+// Common structure (one CTA = 6 warps):
+//   warps 0-3  softmax / correction / epilogue; thread i owns accumulator row i (TMEM
+//              lane i), so row max and row sum need no shuffles;
+//   warp 4     TMA producer (one elected lane);
+//   warp 5     TMEM allocator and tcgen05.mma issuer (one elected lane).
+// Operands live in shared memory in the 128-byte-swizzled layout TMA writes and the
+// UMMA descriptors read (8-row x 128-byte atoms, 1024-byte aligned). Q and K are
+// K-major; V is read as an MN-major B operand straight from its [key][dim] tile; P is
+// written by the softmax threads in the same swizzled K-major layout.
+#include "common.cuh"
+
+namespace b200asr {
+
+constexpr int kTcThreads = 192;
+constexpr float kTcLog2e = 1.4426950408889634f;
+
+__device__ __forceinline__ int named_bar_softmax() { return 128; }
+__device__ __forceinline__ void softmax_bar() {
+  asm volatile("bar.sync 1, 128;" ::: "memory");
+}
+
+// Store one 64-column bf16 row (from fp32 `p`) into a K-major SW128 tile at row r.
+__device__ __forceinline__ void store_p_row64(uint8_t *tile, int r, const float *p) {
+  uint8_t *row = tile + (r >> 3) * 1024 + (r & 7) * 128;
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    uint4 v;
+    v.x = pack2(p[8 * c + 0], p[8 * c + 1]);
+    v.y = pack2(p[8 * c + 2], p[8 * c + 3]);
+    v.z = pack2(p[8 * c + 4], p[8 * c + 5]);
+    v.w = pack2(p[8 * c + 6], p[8 * c + 7]);
+    *reinterpret_cast<uint4 *>(row + ((c ^ (r & 7)) << 4)) = v;
+  }
+}
+
+// =============================================================================
+// Paged causal GQA prefill, head_dim 128, query heads = 2 x KV heads.
+// CTA = (64 query tokens of one sequence) x (one KV head g): M rows 0-63 are query
+// head 2g, rows 64-127 query head 2g+1, tokens t = row & 63.
+// =============================================================================
+
+constexpr int kPfBN = 64;                      // keys per KV tile
+constexpr int kPfQBytes = 128 * 128 * 2;       // 32 KiB: 2 d-halves x [128 rows x 128 B]
+constexpr int kPfKVBytes = kPfBN * 128 * 2;    // 16 KiB: 2 d-halves x [64 rows x 128 B]
+constexpr int kPfPBytes = 128 * kPfBN * 2;     // 16 KiB: [128 rows x 128 B]
+constexpr int kPfStages = 2;
+constexpr int kPfSmem = 1024 /*align slack*/ + kPfQBytes + 2 * kPfStages * kPfKVBytes + kPfPBytes + 256;
+
+struct PrefillArgs {
+  const int32_t *cu_seqlens_q;
+  const int32_t *cu_seqlens_k;
+  const int32_t *block_tables;
+  int bt_stride;
+  int batch;
+  int num_blocks;
+  int block_size;
+  int num_kv_heads;
+  float scale_log2;
+  __nv_bfloat16 *out;
+  int64_t out_stride;
+  int32_t *error_flag;
+};
+
+__global__ void __launch_bounds__(kTcThreads, 1)
+    paged_prefill_kernel(const __grid_constant__ CUtensorMap tm_q,
+                         const __grid_constant__ CUtensorMap tm_k,
+                         const __grid_constant__ CUtensorMap tm_v, const PrefillArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                              ~uintptr_t(1023));
+  uint8_t *sQ = smem;
+  uint8_t *sK = sQ + kPfQBytes;                  // [stage] 16 KiB each
+  uint8_t *sV = sK + kPfStages * kPfKVBytes;     // [stage] 16 KiB each
+  uint8_t *sP = sV + kPfStages * kPfKVBytes;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(sP + kPfPBytes);
+  uint64_t *q_full = bars + 0;
+  uint64_t *kv_full = bars + 1;   // [2]
+  uint64_t *kv_empty = bars + 3;  // [2]
+  uint64_t *s_full = bars + 5;    // [2]
+  uint64_t *s_free = bars + 7;    // [2]
+  uint64_t *p_full = bars + 9;
+  uint64_t *o_done = bars + 10;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 11);
+  __shared__ int abort_flag;
+  __shared__ int s_tile_info[4];
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = blockIdx.y;
+
+  // ---- locate (sequence, query tile) of this CTA
+  if (warp == 0) {
+    int carry = 0, found = -1, found_tile = 0;
+    for (int b0 = 0; b0 < a.batch && found < 0; b0 += 32) {
+      const int b = b0 + lane;
+      int n = 0;
+      if (b < a.batch) n = (a.cu_seqlens_q[b + 1] - a.cu_seqlens_q[b] + 63) / 64;
+      int incl = n;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+      }
+      const int excl = carry + incl - n;
+      const bool mine = b < a.batch && (int)blockIdx.x >= excl && (int)blockIdx.x < excl + n;
+      const unsigned ball = __ballot_sync(0xffffffffu, mine);
+      if (ball) {
+        const int src = __ffs(ball) - 1;
+        found = b0 + src;
+        found_tile = static_cast<int>(blockIdx.x) - __shfl_sync(0xffffffffu, excl, src);
+      }
+      carry += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    if (lane == 0) {
+      s_tile_info[0] = found;
+      s_tile_info[1] = found_tile;
+    }
+  }
+  __syncthreads();
+  const int b = s_tile_info[0];
+  if (b < 0) return;  // grid upper bound overshoot: no work, nothing allocated
+  const int qtile = s_tile_info[1];
+  const int q_len = a.cu_seqlens_q[b + 1] - a.cu_seqlens_q[b];
+  const int k_len = a.cu_seqlens_k[b + 1] - a.cu_seqlens_k[b];
+  const int q0 = a.cu_seqlens_q[b] + qtile * 64;
+  const int nq = min(64, q_len - qtile * 64);
+  const int offset = k_len - q_len;                 // bottom-right alignment
+  const int p_first = offset + qtile * 64;          // absolute position of token 0
+  const int n_kv = min(k_len, p_first + nq);        // keys any row of this tile may see
+  const int n_tiles = n_kv > 0 ? (n_kv + kPfBN - 1) / kPfBN : 0;
+
+  if (tid == 0) {
+    abort_flag = 0;
+    mbar_init(q_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+      mbar_init(&s_full[s], 1);
+      mbar_init(&s_free[s], 128);
+    }
+    mbar_init(p_full, 128);
+    mbar_init(o_done, 1);
+    fence_barrier_init();
+  }
+  if (warp == 5) {
+    tmem_alloc(tmem_slot, 256);
+    tmem_relinquish();
+  }
+  if (warp == 4 && lane == 0) {
+    prefetch_tmap(&tm_q);
+    prefetch_tmap(&tm_k);
+    prefetch_tmap(&tm_v);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (n_tiles == 0 || offset < 0) {
+    if (tid == 0 && offset < 0) raise_flag(a.error_flag, B200ASR_DEVERR_LENGTH);
+  } else if (warp == 4) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      mbar_arrive_expect_tx(q_full, kPfQBytes);
+      for (int hh = 0; hh < 2; ++hh)
+        for (int dh = 0; dh < 2; ++dh)
+          tma_load_3d(sQ + dh * 16384 + hh * 8192, &tm_q, dh * 64, 2 * g + hh, q0, q_full);
+      for (int j = 0; j < n_tiles; ++j) {
+        const int st = j & 1;
+        if (!mbar_wait(&kv_empty[st], ((j >> 1) & 1) ^ 1, a.error_flag, &abort_flag)) break;
+        const int key0 = j * kPfBN;
+        int block = a.block_tables[static_cast<int64_t>(b) * a.bt_stride + key0 / a.block_size];
+        if (block < 0 || block >= a.num_blocks) {
+          raise_flag(a.error_flag, B200ASR_DEVERR_BLOCK);
+          block = 0;
+        }
+        const int slot = block * a.block_size + (key0 % a.block_size);
+        mbar_arrive_expect_tx(&kv_full[st], 2 * kPfKVBytes);
+        uint8_t *k_dst = sK + st * kPfKVBytes;
+        uint8_t *v_dst = sV + st * kPfKVBytes;
+        for (int dh = 0; dh < 2; ++dh) {
+          tma_load_3d(k_dst + dh * 8192, &tm_k, dh * 64, g, slot, &kv_full[st]);
+          tma_load_3d(v_dst + dh * 8192, &tm_v, dh * 64, g, slot, &kv_full[st]);
+        }
+      }
+    }
+  } else if (warp == 5) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = idesc_bf16_f32(128, kPfBN, false, false);
+      constexpr uint32_t idesc_o = idesc_bf16_f32(128, 128, false, true);
+      const uint32_t q_base = smem_addr(sQ), k_base = smem_addr(sK), v_base = smem_addr(sV),
+                     p_base = smem_addr(sP);
+      bool ok = mbar_wait(q_full, 0, a.error_flag, &abort_flag);
+      auto issue_pv = [&](int jj) {
+        const uint32_t vb = v_base + (jj & 1) * kPfKVBytes;
+#pragma unroll
+        for (int k = 0; k < kPfBN / 16; ++k) {
+          const uint64_t ad = smem_desc_sw128(p_base + k * 32, 16, 1024);
+          const uint64_t bd = smem_desc_sw128(vb + k * 2048, 8192, 1024);
+          umma_f16_ss(tmem + 128, ad, bd, idesc_o, (jj > 0 || k > 0) ? 1u : 0u);
+        }
+        umma_commit(&kv_empty[jj & 1]);
+        umma_commit(o_done);
+      };
+      for (int j = 0; ok && j < n_tiles; ++j) {
+        const int st = j & 1;
+        if (!mbar_wait(&kv_full[st], (j >> 1) & 1, a.error_flag, &abort_flag)) break;
+        if (j >= 2 && !mbar_wait(&s_free[j & 1], ((j - 2) >> 1) & 1, a.error_flag, &abort_flag))
+          break;
+        tc_fence_after();
+        const uint32_t kb = k_base + st * kPfKVBytes;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const uint32_t off = (k >> 2) * 16384 + (k & 3) * 32;
+          const uint32_t koff = (k >> 2) * 8192 + (k & 3) * 32;
+          const uint64_t ad = smem_desc_sw128(q_base + off, 16, 1024);
+          const uint64_t bd = smem_desc_sw128(kb + koff, 16, 1024);
+          umma_f16_ss(tmem + (j & 1) * kPfBN, ad, bd, idesc_s, k > 0 ? 1u : 0u);
+        }
+        umma_commit(&s_full[j & 1]);
+        if (j >= 1) {
+          if (!mbar_wait(p_full, (j - 1) & 1, a.error_flag, &abort_flag)) break;
+          tc_fence_after();
+          issue_pv(j - 1);
+        }
+      }
+      if (!abort_flag && mbar_wait(p_full, (n_tiles - 1) & 1, a.error_flag, &abort_flag)) {
+        tc_fence_after();
+        issue_pv(n_tiles - 1);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ softmax (warps 0-3)
+    const int r = tid;                   // accumulator row == TMEM lane
+    const int t = r & 63;
+    const int head = 2 * g + (r >> 6);
+    const int p_row = p_first + t;       // last key this row may attend
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_tiles; ++j) {
+      if (!mbar_wait(&s_full[j & 1], (j >> 1) & 1, a.error_flag, &abort_flag)) { ok = false; break; }
+      tc_fence_after();
+      float s[kPfBN];
+      tmem_ld32(lane_base + (j & 1) * kPfBN, s);
+      tmem_ld32(lane_base + (j & 1) * kPfBN + 32, s + 32);
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(&s_free[j & 1]);
+      const int key0 = j * kPfBN;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < kPfBN; ++c) {
+        s[c] = (key0 + c <= p_row) ? s[c] * a.scale_log2 : -INFINITY;
+        mx = fmaxf(mx, s[c]);
+      }
+      const float m_new = fmaxf(m, mx);
+      const float alpha = exp2f(m - m_new);  // m = -inf on the first tile -> 0
+      float sum = 0.f;
+#pragma unroll
+      for (int c = 0; c < kPfBN; ++c) {
+        s[c] = exp2f(s[c] - m_new);
+        sum += s[c];
+      }
+      l = l * alpha + sum;
+      m = m_new;
+      if (j > 0) {
+        if (!mbar_wait(o_done, (j - 1) & 1, a.error_flag, &abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, alpha < 1.f)) {
+#pragma unroll
+          for (int cc = 0; cc < 4; ++cc) {
+            float o[32];
+            tmem_ld32(lane_base + 128 + cc * 32, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] *= alpha;
+            tmem_st32(lane_base + 128 + cc * 32, o);
+          }
+          tmem_wait_st();
+        }
+      }
+      store_p_row64(sP, r, s);
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(p_full);
+    }
+    if (ok && mbar_wait(o_done, (n_tiles - 1) & 1, a.error_flag, &abort_flag)) {
+      tc_fence_after();
+      const float inv = 1.f / l;
+      __nv_bfloat16 *dst = a.out + static_cast<int64_t>(q0 + t) * a.out_stride + head * 128;
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) {
+        float o[32];
+        tmem_ld32(lane_base + 128 + cc * 32, o);
+        tmem_wait_ld();
+        if (t < nq) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            uint4 v;
+            v.x = pack2(o[8 * i + 0] * inv, o[8 * i + 1] * inv);
+            v.y = pack2(o[8 * i + 2] * inv, o[8 * i + 3] * inv);
+            v.z = pack2(o[8 * i + 4] * inv, o[8 * i + 5] * inv);
+            v.w = pack2(o[8 * i + 6] * inv, o[8 * i + 7] * inv);
+            *reinterpret_cast<uint4 *>(dst + cc * 32 + i * 8) = v;
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+}
+
+// =============================================================================
+// Windowed bidirectional attention, head_dim 64, segments of at most 128 tokens.
+// CTA = (segment, head). S = Q K^T (128x128, K=64), softmax over the whole row
+// (no online rescaling needed), O = P V (128x64, K=128).
+// =============================================================================
+
+constexpr int kWinTile = 16384;  // [128 rows x 128 B]
+constexpr int kWinSmem = 1024 + 3 * kWinTile + 2 * kWinTile + 128;
+
+struct WindowArgs {
+  const int32_t *cu_seqlens;
+  int num_segments;
+  float scale_log2;
+  __nv_bfloat16 *out;
+  int64_t out_stride;
+  int32_t *error_flag;
+};
+
+__global__ void __launch_bounds__(kTcThreads, 2)
+    varlen_window_kernel(const __grid_constant__ CUtensorMap tm_q,
+                         const __grid_constant__ CUtensorMap tm_k,
+                         const __grid_constant__ CUtensorMap tm_v, const WindowArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                              ~uintptr_t(1023));
+  uint8_t *sQ = smem, *sK = smem + kWinTile, *sV = smem + 2 * kWinTile, *sP = smem + 3 * kWinTile;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + 5 * kWinTile);
+  uint64_t *ld_full = bars, *s_full = bars + 1, *p_full = bars + 2, *o_full = bars + 3;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 4);
+  __shared__ int abort_flag;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int seg = blockIdx.x, h = blockIdx.y;
+  const int row0 = a.cu_seqlens[seg];
+  const int len = a.cu_seqlens[seg + 1] - row0;
+  if (len <= 0) return;
+  if (len > 128) {
+    if (tid == 0) raise_flag(a.error_flag, B200ASR_DEVERR_LENGTH);
+    return;
+  }
+  if (tid == 0) {
+    abort_flag = 0;
+    mbar_init(ld_full, 1);
+    mbar_init(s_full, 1);
+    mbar_init(p_full, 128);
+    mbar_init(o_full, 1);
+    fence_barrier_init();
+  }
+  if (warp == 5) {
+    tmem_alloc(tmem_slot, 256);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 4) {
+    if (lane == 0) {
+      mbar_arrive_expect_tx(ld_full, 3 * kWinTile);
+      tma_load_3d(sQ, &tm_q, 0, h, row0, ld_full);
+      tma_load_3d(sK, &tm_k, 0, h, row0, ld_full);
+      tma_load_3d(sV, &tm_v, 0, h, row0, ld_full);
+    }
+  } else if (warp == 5) {
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = idesc_bf16_f32(128, 128, false, false);
+      constexpr uint32_t idesc_o = idesc_bf16_f32(128, 64, false, true);
+      const uint32_t qb = smem_addr(sQ), kb = smem_addr(sK), vb = smem_addr(sV), pb = smem_addr(sP);
+      if (mbar_wait(ld_full, 0, a.error_flag, &abort_flag)) {
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          umma_f16_ss(tmem, smem_desc_sw128(qb + k * 32, 16, 1024),
+                      smem_desc_sw128(kb + k * 32, 16, 1024), idesc_s, k > 0 ? 1u : 0u);
+        umma_commit(s_full);
+        if (mbar_wait(p_full, 0, a.error_flag, &abort_flag)) {
+          tc_fence_after();
+#pragma unroll
+          for (int k = 0; k < 8; ++k)
+            umma_f16_ss(tmem + 128,
+                        smem_desc_sw128(pb + (k >> 2) * kWinTile + (k & 3) * 32, 16, 1024),
+                        smem_desc_sw128(vb + k * 2048, kWinTile, 1024), idesc_o, k > 0 ? 1u : 0u);
+          umma_commit(o_full);
+        }
+      }
+    }
+  } else {
+    const int r = tid;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    if (mbar_wait(s_full, 0, a.error_flag, &abort_flag)) {
+      tc_fence_after();
+      float s[128];
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) tmem_ld32(lane_base + cc * 32, s + cc * 32);
+      tmem_wait_ld();
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 128; ++c) {
+        s[c] = c < len ? s[c] * a.scale_log2 : -INFINITY;
+        mx = fmaxf(mx, s[c]);
+      }
+      float sum = 0.f;
+#pragma unroll
+      for (int c = 0; c < 128; ++c) {
+        s[c] = exp2f(s[c] - mx);
+        sum += s[c];
+      }
+      store_p_row64(sP, r, s);
+      store_p_row64(sP + kWinTile, r, s + 64);
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(p_full);
+      if (mbar_wait(o_full, 0, a.error_flag, &abort_flag)) {
+        tc_fence_after();
+        const float inv = 1.f / sum;
+        __nv_bfloat16 *dst = a.out + static_cast<int64_t>(row0 + r) * a.out_stride + h * 64;
+#pragma unroll
+        for (int cc = 0; cc < 2; ++cc) {
+          float o[32];
+          tmem_ld32(lane_base + 128 + cc * 32, o);
+          tmem_wait_ld();
+          if (r < len) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              uint4 v;
+              v.x = pack2(o[8 * i + 0] * inv, o[8 * i + 1] * inv);
+              v.y = pack2(o[8 * i + 2] * inv, o[8 * i + 3] * inv);
+              v.z = pack2(o[8 * i + 4] * inv, o[8 * i + 5] * inv);
+              v.w = pack2(o[8 * i + 6] * inv, o[8 * i + 7] * inv);
+              *reinterpret_cast<uint4 *>(dst + cc * 32 + i * 8) = v;
+            }
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+}
+
+int set_smem_attr(const void *fn, int bytes, const char *what) {
+  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) {
+    set_error("%s: cannot reserve %d bytes of shared memory: %s", what, bytes, cudaGetErrorString(e));
+    return B200ASR_ERR_CUDA;
+  }
+  return B200ASR_OK;
+}
+
+}  // namespace b200asr
+
+using namespace b200asr;
+
+extern "C" int b200asr_paged_prefill(const void *q, int64_t q_row_stride, const void *k_cache,
+                                     const void *v_cache, int32_t num_blocks, int32_t block_size,
+                                     int32_t num_heads, int32_t num_kv_heads, int32_t head_dim,
+                                     const int32_t *cu_seqlens_q, const int32_t *cu_seqlens_k,
+                                     const int32_t *block_tables, int32_t bt_stride, int32_t batch,
+                                     int32_t total_q, int32_t max_seqlen_q, float scale, void *out,
+                                     int64_t out_row_stride, int32_t *error_flag,
+                                     b200asr_stream_t stream) {
+  B200_REQUIRE(head_dim == 128, "paged_prefill: head_dim %d unsupported (needs 128)", head_dim);
+  B200_REQUIRE(num_kv_heads >= 1 && num_heads == 2 * num_kv_heads,
+               "paged_prefill: needs num_heads == 2 * num_kv_heads (got %d / %d)", num_heads,
+               num_kv_heads);
+  B200_REQUIRE(batch >= 0 && total_q >= 0, "paged_prefill: bad sizes");
+  if (batch == 0 || total_q == 0) return B200ASR_OK;
+  B200_REQUIRE(block_size >= 64 && block_size % 64 == 0,
+               "paged_prefill: block_size %d must be a multiple of 64", block_size);
+  B200_REQUIRE(q && k_cache && v_cache && cu_seqlens_q && cu_seqlens_k && block_tables && out,
+               "paged_prefill: null pointer");
+  B200_REQUIRE(aligned16(q) && aligned16(k_cache) && aligned16(v_cache) && aligned16(out) &&
+                   q_row_stride % 8 == 0 && out_row_stride % 8 == 0,
+               "paged_prefill: tensors and row strides must be 16-byte aligned");
+  CUtensorMap tq, tk, tv;
+  const uint64_t slots = static_cast<uint64_t>(num_blocks) * block_size;
+  if (!make_tmap_3d_bf16(&tq, q, 128, num_heads, total_q, 256, q_row_stride * 2, 64, 1, 64) ||
+      !make_tmap_3d_bf16(&tk, k_cache, 128, num_kv_heads, slots, 256, num_kv_heads * 256ull, 64, 1, 64) ||
+      !make_tmap_3d_bf16(&tv, v_cache, 128, num_kv_heads, slots, 256, num_kv_heads * 256ull, 64, 1, 64))
+    return B200ASR_ERR_CUDA;
+  static bool configured = false;
+  if (!configured) {
+    int rc = set_smem_attr(reinterpret_cast<const void *>(paged_prefill_kernel), kPfSmem,
+                           "paged_prefill");
+    if (rc) return rc;
+    configured = true;
+  }
+  PrefillArgs a;
+  a.cu_seqlens_q = cu_seqlens_q;
+  a.cu_seqlens_k = cu_seqlens_k;
+  a.block_tables = block_tables;
+  a.bt_stride = bt_stride;
+  a.batch = batch;
+  a.num_blocks = num_blocks;
+  a.block_size = block_size;
+  a.num_kv_heads = num_kv_heads;
+  a.scale_log2 = scale * kTcLog2e;
+  a.out = static_cast<__nv_bfloat16 *>(out);
+  a.out_stride = out_row_stride;
+  a.error_flag = error_flag;
+  (void)max_seqlen_q;
+  const int tiles = total_q / 64 + batch;  // >= sum over rows of ceil(q_len / 64)
+  dim3 grid(tiles, num_kv_heads);
+  paged_prefill_kernel<<<grid, kTcThreads, kPfSmem, stream>>>(tq, tk, tv, a);
+  B200_CUDA_LAUNCH_CHECK("paged_prefill");
+  return B200ASR_OK;
+}
+
+extern "C" int b200asr_varlen_attention(const void *q, int64_t q_row_stride, const void *k,
+                                        int64_t k_row_stride, const void *v, int64_t v_row_stride,
+                                        const int32_t *cu_seqlens, int32_t num_segments,
+                                        int32_t total_tokens, int32_t max_seqlen, int32_t num_heads,
+                                        int32_t head_dim, float scale, void *out,
+                                        int64_t out_row_stride, int32_t *error_flag,
+                                        b200asr_stream_t stream) {
+  B200_REQUIRE(head_dim == 64, "varlen_attention: head_dim %d unsupported (needs 64)", head_dim);
+  B200_REQUIRE(max_seqlen <= 128, "varlen_attention: segments up to 128 tokens (got %d)", max_seqlen);
+  B200_REQUIRE(num_segments >= 0 && total_tokens >= 0 && num_heads >= 1, "varlen_attention: bad sizes");
+  if (num_segments == 0 || total_tokens == 0) return B200ASR_OK;
+  B200_REQUIRE(q && k && v && cu_seqlens && out, "varlen_attention: null pointer");
+  B200_REQUIRE(aligned16(q) && aligned16(k) && aligned16(v) && aligned16(out) &&
+                   q_row_stride % 8 == 0 && k_row_stride % 8 == 0 && v_row_stride % 8 == 0 &&
+                   out_row_stride % 8 == 0,
+               "varlen_attention: tensors and row strides must be 16-byte aligned");
+  B200_REQUIRE(num_segments <= 0x7fffffff && num_heads <= 65535, "varlen_attention: grid too large");
+  CUtensorMap tq, tk, tv;
+  if (!make_tmap_3d_bf16(&tq, q, 64, num_heads, total_tokens, 128, q_row_stride * 2, 64, 1, 128) ||
+      !make_tmap_3d_bf16(&tk, k, 64, num_heads, total_tokens, 128, k_row_stride * 2, 64, 1, 128) ||
+      !make_tmap_3d_bf16(&tv, v, 64, num_heads, total_tokens, 128, v_row_stride * 2, 64, 1, 128))
+    return B200ASR_ERR_CUDA;
+  static bool configured = false;
+  if (!configured) {
+    int rc = set_smem_attr(reinterpret_cast<const void *>(varlen_window_kernel), kWinSmem,
+                           "varlen_attention");
+    if (rc) return rc;
+    configured = true;
+  }
+  WindowArgs a;
+  a.cu_seqlens = cu_seqlens;
+  a.num_segments = num_segments;
+  a.scale_log2 = scale * kTcLog2e;
+  a.out = static_cast<__nv_bfloat16 *>(out);
+  a.out_stride = out_row_stride;
+  a.error_flag = error_flag;
+  dim3 grid(num_segments, num_heads);
+  varlen_window_kernel<<<grid, kTcThreads, kWinSmem, stream>>>(tq, tk, tv, a);
+  B200_CUDA_LAUNCH_CHECK("varlen_attention");
+  return B200ASR_OK;
+}

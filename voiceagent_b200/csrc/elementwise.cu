@@ -1,0 +1,306 @@
+// Memory-bound per-token kernels of the decoder layer.
+//
+// store_kvcache        <- _store_kvcache_kernel / store_kvcache (layers/attention.py:31-67)
+// qk_norm_rope_store   <- Qwen3Attention.forward q/k norm + RoPE (models/qwen3.py:43-48),
+//                         RMSNorm._norm (layers/layernorm.py:19-25),
+//                         RotaryEmbedding.forward (layers/rotary_embedding.py:9-32),
+//                         fused with the KV store of PagedAttention.forward (attention.py:90)
+// rmsnorm / add        <- RMSNorm._norm / RMSNorm._add_norm (layers/layernorm.py:19-36)
+// silu_mul             <- SiluAndMul.forward (layers/activation.py:11-14)
+//
+// Rounding follows the reference's eager semantics: fp32 math, a bf16 rounding after
+// the normalisation, another after the weight multiply, one after the rotation.
+#include "common.cuh"
+
+namespace b200asr {
+
+// ------------------------------------------------------------------ KV store
+// One warp copies one (token, K|V) row of `hidden` bf16 with 16-byte accesses.
+__global__ void store_kvcache_kernel(const __nv_bfloat16 *__restrict__ key, int64_t key_stride,
+                                     const __nv_bfloat16 *__restrict__ value,
+                                     int64_t value_stride, __nv_bfloat16 *__restrict__ k_cache,
+                                     __nv_bfloat16 *__restrict__ v_cache,
+                                     const int32_t *__restrict__ slot_mapping, int num_tokens,
+                                     int hidden, int64_t num_slots, int32_t *error_flag) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= 2 * num_tokens) return;
+  const int t = warp >> 1;
+  const bool is_v = warp & 1;
+  const int64_t slot = slot_mapping[t];
+  if (slot == -1) return;
+  if (slot < 0 || slot >= num_slots) {
+    if (lane == 0) raise_flag(error_flag, B200ASR_DEVERR_SLOT);
+    return;
+  }
+  const uint4 *src = reinterpret_cast<const uint4 *>(is_v ? value + t * value_stride
+                                                          : key + t * key_stride);
+  uint4 *dst = reinterpret_cast<uint4 *>((is_v ? v_cache : k_cache) + slot * hidden);
+  const int n16 = hidden >> 3;
+  for (int i = lane; i < n16; i += 32) dst[i] = __ldg(src + i);
+}
+
+// ------------------------------------------------------ QK norm + RoPE + store
+// One warp per (token, head-vector). Tasks 0..H-1: query heads; H..H+Hkv-1: key
+// heads; H+Hkv..H+2Hkv-1: value heads (plain copy into the cache).
+// Lane l holds EPL = head_dim/32 consecutive elements starting at l*EPL; the RoPE
+// partner of element d (< D/2) is d + D/2, which lives in lane l ^ 16.
+template <int EPL>
+__global__ void qk_norm_rope_store_kernel(
+    const __nv_bfloat16 *__restrict__ qkv, int64_t qkv_stride, const int64_t *__restrict__ positions,
+    int num_tokens, int num_heads, int num_kv_heads, const __nv_bfloat16 *__restrict__ qw,
+    const __nv_bfloat16 *__restrict__ kw, float eps, const float *__restrict__ cos_sin,
+    int max_position, __nv_bfloat16 *__restrict__ q_out, int64_t q_out_stride,
+    __nv_bfloat16 *__restrict__ k_out, __nv_bfloat16 *__restrict__ k_cache,
+    __nv_bfloat16 *__restrict__ v_cache, const int32_t *__restrict__ slot_mapping,
+    int64_t num_slots, int32_t *error_flag) {
+  constexpr int D = EPL * 32;
+  const int tasks_per_token = num_heads + 2 * num_kv_heads;
+  const int64_t task = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (task >= static_cast<int64_t>(num_tokens) * tasks_per_token) return;
+  const int t = static_cast<int>(task / tasks_per_token);
+  const int j = static_cast<int>(task - static_cast<int64_t>(t) * tasks_per_token);
+  const int kv_hidden = num_kv_heads * D;
+  const __nv_bfloat16 *row = qkv + t * qkv_stride;
+
+  float x[EPL];
+  const __nv_bfloat16 *src = row + static_cast<int64_t>(j) * D + lane * EPL;
+  if constexpr (EPL == 4) {
+    const uint2 u = *reinterpret_cast<const uint2 *>(src);
+    x[0] = __uint_as_float(u.x << 16);
+    x[1] = __uint_as_float(u.x & 0xffff0000u);
+    x[2] = __uint_as_float(u.y << 16);
+    x[3] = __uint_as_float(u.y & 0xffff0000u);
+  } else {
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) x[e] = bf2f(src[e]);
+  }
+
+  if (j >= num_heads + num_kv_heads) {  // value head: copy into the cache
+    const int64_t slot = slot_mapping ? slot_mapping[t] : -1;
+    if (slot == -1) return;
+    if (slot < 0 || slot >= num_slots) {
+      if (lane == 0) raise_flag(error_flag, B200ASR_DEVERR_SLOT);
+      return;
+    }
+    const int h = j - num_heads - num_kv_heads;
+    __nv_bfloat16 *dst = v_cache + slot * kv_hidden + h * D + lane * EPL;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) dst[e] = src[e];
+    return;
+  }
+
+  const bool is_q = j < num_heads;
+  const __nv_bfloat16 *w = is_q ? qw : kw;
+  float ss = 0.f;
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) ss += x[e] * x[e];
+  ss = warp_sum(ss);
+  const float r = rsqrtf(ss / static_cast<float>(D) + eps);
+  float y[EPL];
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) {
+    const float n = bf2f(f2bf(x[e] * r));                      // x.to(bf16)
+    y[e] = bf2f(f2bf(n * bf2f(w[lane * EPL + e])));             // .mul_(weight)
+  }
+  int64_t pos = positions[t];
+  if (pos < 0 || pos >= max_position) {
+    if (lane == 0) raise_flag(error_flag, B200ASR_DEVERR_POSITION);
+    pos = 0;
+  }
+  const float *cs = cos_sin + pos * D;
+  const bool first_half = lane < 16;
+  float o[EPL];
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) {
+    const float partner = __shfl_xor_sync(0xffffffffu, y[e], 16);
+    const int dd = (lane & 15) * EPL + e;  // index within the half
+    const float c = cs[dd], s = cs[D / 2 + dd];
+    // first*cos - second*sin | second*cos + first*sin, each product rounded (no FMA)
+    o[e] = first_half ? __fsub_rn(__fmul_rn(y[e], c), __fmul_rn(partner, s))
+                      : __fadd_rn(__fmul_rn(y[e], c), __fmul_rn(partner, s));
+  }
+
+  __nv_bfloat16 *dst;
+  if (is_q) {
+    dst = q_out + t * q_out_stride + static_cast<int64_t>(j) * D + lane * EPL;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) dst[e] = f2bf(o[e]);
+    return;
+  }
+  const int h = j - num_heads;
+  if (k_out != nullptr) {
+    dst = k_out + static_cast<int64_t>(t) * kv_hidden + h * D + lane * EPL;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) dst[e] = f2bf(o[e]);
+  }
+  const int64_t slot = slot_mapping ? slot_mapping[t] : -1;
+  if (slot == -1) return;
+  if (slot < 0 || slot >= num_slots) {
+    if (lane == 0) raise_flag(error_flag, B200ASR_DEVERR_SLOT);
+    return;
+  }
+  dst = k_cache + slot * kv_hidden + h * D + lane * EPL;
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) dst[e] = f2bf(o[e]);
+}
+
+// ------------------------------------------------------------------- RMSNorm
+// One CTA per row; each thread owns 8 consecutive elements (hidden % 8 == 0).
+__global__ void rmsnorm_kernel(const __nv_bfloat16 *__restrict__ x, __nv_bfloat16 *residual,
+                               const __nv_bfloat16 *__restrict__ weight, float eps, int hidden,
+                               __nv_bfloat16 *__restrict__ out) {
+  __shared__ float red[32];
+  const int64_t row = blockIdx.x;
+  const int i8 = threadIdx.x;
+  const bool active = i8 * 8 < hidden;
+  float v[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  if (active) {
+    unpack8(*reinterpret_cast<const uint4 *>(x + row * hidden + i8 * 8), v);
+    if (residual != nullptr) {
+      float r[8];
+      uint4 *rp = reinterpret_cast<uint4 *>(residual + row * hidden + i8 * 8);
+      unpack8(*rp, r);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[e] += r[e];
+      *rp = make_uint4(pack2(v[0], v[1]), pack2(v[2], v[3]), pack2(v[4], v[5]), pack2(v[6], v[7]));
+    }
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) ss += v[e] * v[e];
+  ss = warp_sum(ss);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) red[warp] = ss;
+  __syncthreads();
+  if (warp == 0) {
+    float t = lane < (blockDim.x + 31) / 32 ? red[lane] : 0.f;
+    t = warp_sum(t);
+    if (lane == 0) red[0] = t;
+  }
+  __syncthreads();
+  const float r = rsqrtf(red[0] / static_cast<float>(hidden) + eps);
+  if (!active) return;
+  float w[8];
+  unpack8(*reinterpret_cast<const uint4 *>(weight + i8 * 8), w);
+  float y[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) y[e] = bf2f(f2bf(bf2f(f2bf(v[e] * r)) * w[e]));
+  *reinterpret_cast<uint4 *>(out + row * hidden + i8 * 8) =
+      make_uint4(pack2(y[0], y[1]), pack2(y[2], y[3]), pack2(y[4], y[5]), pack2(y[6], y[7]));
+}
+
+// ------------------------------------------------------------------- SiLU*mul
+__global__ void silu_mul_kernel(const __nv_bfloat16 *__restrict__ x, int64_t rows, int inner,
+                                __nv_bfloat16 *__restrict__ out) {
+  const int64_t n8 = rows * (inner / 8);
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n8;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t row = i / (inner / 8);
+    const int c = static_cast<int>(i - row * (inner / 8)) * 8;
+    float g[8], u[8], y[8];
+    unpack8(*reinterpret_cast<const uint4 *>(x + row * 2 * inner + c), g);
+    unpack8(*reinterpret_cast<const uint4 *>(x + row * 2 * inner + inner + c), u);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float s = bf2f(f2bf(g[e] / (1.0f + expf(-g[e]))));  // F.silu -> bf16
+      y[e] = s * u[e];
+    }
+    *reinterpret_cast<uint4 *>(out + row * inner + c) =
+        make_uint4(pack2(y[0], y[1]), pack2(y[2], y[3]), pack2(y[4], y[5]), pack2(y[6], y[7]));
+  }
+}
+
+}  // namespace b200asr
+
+using namespace b200asr;
+
+extern "C" int b200asr_store_kvcache(const void *key, int64_t key_row_stride, const void *value,
+                                     int64_t value_row_stride, void *k_cache, void *v_cache,
+                                     const int32_t *slot_mapping, int32_t num_tokens,
+                                     int32_t num_kv_heads, int32_t head_dim, int64_t num_slots,
+                                     int32_t *error_flag, b200asr_stream_t stream) {
+  const int hidden = num_kv_heads * head_dim;
+  B200_REQUIRE(num_tokens >= 0 && num_kv_heads >= 1 && head_dim >= 1 && num_slots >= 1,
+               "store_kvcache: bad sizes");
+  if (num_tokens == 0) return B200ASR_OK;
+  B200_REQUIRE(key && value && k_cache && v_cache && slot_mapping, "store_kvcache: null pointer");
+  B200_REQUIRE(hidden % 8 == 0 && key_row_stride % 8 == 0 && value_row_stride % 8 == 0 &&
+                   aligned16(key) && aligned16(value) && aligned16(k_cache) && aligned16(v_cache),
+               "store_kvcache: rows must be 16-byte aligned (hidden %d, strides %lld/%lld)",
+               hidden, (long long)key_row_stride, (long long)value_row_stride);
+  const int64_t threads = 2LL * num_tokens * 32;
+  const int block = 256;
+  store_kvcache_kernel<<<static_cast<unsigned>((threads + block - 1) / block), block, 0, stream>>>(
+      static_cast<const __nv_bfloat16 *>(key), key_row_stride,
+      static_cast<const __nv_bfloat16 *>(value), value_row_stride,
+      static_cast<__nv_bfloat16 *>(k_cache), static_cast<__nv_bfloat16 *>(v_cache), slot_mapping,
+      num_tokens, hidden, num_slots, error_flag);
+  B200_CUDA_LAUNCH_CHECK("store_kvcache");
+  return B200ASR_OK;
+}
+
+extern "C" int b200asr_qk_norm_rope_store(
+    const void *qkv, int64_t qkv_row_stride, const int64_t *positions, int32_t num_tokens,
+    int32_t num_heads, int32_t num_kv_heads, int32_t head_dim, const void *q_norm_weight,
+    const void *k_norm_weight, float eps, const float *cos_sin_cache, int32_t max_position,
+    void *q_out, int64_t q_out_row_stride, void *k_out, void *k_cache, void *v_cache,
+    const int32_t *slot_mapping, int64_t num_slots, int32_t *error_flag,
+    b200asr_stream_t stream) {
+  B200_REQUIRE(num_tokens >= 0 && num_heads >= 1 && num_kv_heads >= 1 && max_position >= 1,
+               "qk_norm_rope_store: bad sizes");
+  B200_REQUIRE(head_dim == 64 || head_dim == 128, "qk_norm_rope_store: head_dim %d unsupported",
+               head_dim);
+  if (num_tokens == 0) return B200ASR_OK;
+  B200_REQUIRE(qkv && positions && q_norm_weight && k_norm_weight && cos_sin_cache && q_out,
+               "qk_norm_rope_store: null pointer");
+  B200_REQUIRE(slot_mapping == nullptr || (k_cache && v_cache && num_slots >= 1),
+               "qk_norm_rope_store: slot_mapping given without caches");
+  B200_REQUIRE(qkv_row_stride % 4 == 0 && (reinterpret_cast<uintptr_t>(qkv) & 7) == 0,
+               "qk_norm_rope_store: qkv rows must be 8-byte aligned");
+  const int64_t warps = static_cast<int64_t>(num_tokens) * (num_heads + 2 * num_kv_heads);
+  const int block = 256;
+  const unsigned grid = static_cast<unsigned>((warps * 32 + block - 1) / block);
+  auto kfn = head_dim == 128 ? qk_norm_rope_store_kernel<4> : qk_norm_rope_store_kernel<2>;
+  kfn<<<grid, block, 0, stream>>>(
+      static_cast<const __nv_bfloat16 *>(qkv), qkv_row_stride, positions, num_tokens, num_heads,
+      num_kv_heads, static_cast<const __nv_bfloat16 *>(q_norm_weight),
+      static_cast<const __nv_bfloat16 *>(k_norm_weight), eps, cos_sin_cache, max_position,
+      static_cast<__nv_bfloat16 *>(q_out), q_out_row_stride, static_cast<__nv_bfloat16 *>(k_out),
+      static_cast<__nv_bfloat16 *>(k_cache), static_cast<__nv_bfloat16 *>(v_cache), slot_mapping,
+      num_slots, error_flag);
+  B200_CUDA_LAUNCH_CHECK("qk_norm_rope_store");
+  return B200ASR_OK;
+}
+
+extern "C" int b200asr_rmsnorm(const void *x, void *residual, const void *weight, float eps,
+                               int32_t rows, int32_t hidden, void *out, b200asr_stream_t stream) {
+  B200_REQUIRE(rows >= 0 && hidden >= 8 && hidden % 8 == 0 && hidden <= 8 * 1024,
+               "rmsnorm: hidden %d must be a multiple of 8 in [8, 8192]", hidden);
+  if (rows == 0) return B200ASR_OK;
+  B200_REQUIRE(x && weight && out, "rmsnorm: null pointer");
+  B200_REQUIRE(aligned16(x) && aligned16(weight) && aligned16(out) &&
+                   (residual == nullptr || aligned16(residual)),
+               "rmsnorm: tensors must be 16-byte aligned");
+  const int threads = ((hidden / 8) + 31) / 32 * 32;
+  rmsnorm_kernel<<<rows, threads, 0, stream>>>(
+      static_cast<const __nv_bfloat16 *>(x), static_cast<__nv_bfloat16 *>(residual),
+      static_cast<const __nv_bfloat16 *>(weight), eps, hidden, static_cast<__nv_bfloat16 *>(out));
+  B200_CUDA_LAUNCH_CHECK("rmsnorm");
+  return B200ASR_OK;
+}
+
+extern "C" int b200asr_silu_mul(const void *x, int32_t rows, int32_t inner, void *out,
+                                b200asr_stream_t stream) {
+  B200_REQUIRE(rows >= 0 && inner >= 8 && inner % 8 == 0, "silu_mul: inner %d must be a multiple of 8",
+               inner);
+  if (rows == 0) return B200ASR_OK;
+  B200_REQUIRE(x && out && aligned16(x) && aligned16(out), "silu_mul: null or unaligned pointer");
+  const int64_t n8 = static_cast<int64_t>(rows) * (inner / 8);
+  const unsigned grid = static_cast<unsigned>(std::min<int64_t>((n8 + 255) / 256, 148 * 32));
+  silu_mul_kernel<<<grid, 256, 0, stream>>>(static_cast<const __nv_bfloat16 *>(x), rows, inner,
+                                            static_cast<__nv_bfloat16 *>(out));
+  B200_CUDA_LAUNCH_CHECK("silu_mul");
+  return B200ASR_OK;
+}

@@ -1,0 +1,227 @@
+"""Torch-facing wrappers over the b200asr C ABI.
+
+Each wrapper checks dtypes, devices, shapes and strides on the host (the way the
+reference's asserts do, e.g. layers/attention.py:59-64), then launches on the current
+CUDA stream. Nothing here allocates inside a captured region when the caller passes
+``out=`` / workspace tensors, so the calls are CUDA-graph capturable.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from voiceagent_b200._lib import check, lib
+
+BF16 = torch.bfloat16
+
+
+def _p(t: torch.Tensor | None):
+    return None if t is None else t.data_ptr()
+
+
+def _stream():
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _need(cond: bool, msg: str) -> None:
+    if not cond:
+        raise ValueError(msg)
+
+
+def _cuda(*tensors: torch.Tensor | None) -> None:
+    for t in tensors:
+        if t is not None:
+            _need(t.is_cuda, "b200asr kernels need CUDA tensors")
+
+
+# --------------------------------------------------------------------- packers
+
+
+def pack_decoder(req_start, req_end, table_off, table_len, tables, query_tokens, *,
+                 total_tokens: int, width: int, block_size: int, out: dict) -> None:
+    """``ModelRunner._prepare`` (engine/model_runner.py:183-233) on the GPU.
+
+    Inputs are int32 device tensors; ``out`` holds preallocated device tensors
+    ``input_ids``/``positions`` (i64), ``slot_mapping`` (i32), ``cu_seqlens_q``/
+    ``cu_seqlens_k`` (i32), ``max_seqlen`` (i32[2]), ``block_tables`` (i32 [B, width])
+    and ``last_token_index`` (i64).
+    """
+    batch = req_start.numel()
+    _cuda(req_start, req_end, table_off, table_len, tables, query_tokens)
+    for t in (req_start, req_end, table_off, table_len, tables, query_tokens):
+        _need(t.dtype == torch.int32, "pack_decoder inputs are int32")
+    check(lib.b200asr_pack_decoder(
+        _p(req_start), _p(req_end), _p(table_off), _p(table_len), _p(tables), _p(query_tokens),
+        batch, total_tokens, width, block_size, _p(out["input_ids"]), _p(out["positions"]),
+        _p(out["slot_mapping"]), _p(out["cu_seqlens_q"]), _p(out["cu_seqlens_k"]),
+        _p(out["max_seqlen"]), _p(out["block_tables"]), _p(out["last_token_index"]), _stream()),
+        "pack_decoder")
+
+
+def pack_decode_bucket(lens, last_ids, table_off, table_len, tables, *, batch: int, bucket: int,
+                       max_blocks: int, block_size: int, input_ids, positions, slot_mapping,
+                       cu_seqlens_k, block_tables) -> None:
+    """``GraphRunner.run`` staging (engine/graph_runner.py:149-191) on the GPU."""
+    check(lib.b200asr_pack_decode_bucket(
+        _p(lens), _p(last_ids), _p(table_off), _p(table_len), _p(tables), batch, bucket,
+        max_blocks, block_size, _p(input_ids), _p(positions), _p(slot_mapping), _p(cu_seqlens_k),
+        _p(block_tables), _stream()), "pack_decode_bucket")
+
+
+def pack_audio(mel_frames, *, chunk_frames: int, window_tokens: int, max_chunks: int,
+               max_windows: int, out: dict, error_flag=None) -> None:
+    """Metadata of ``pack_audio_batch`` (audio/batcher.py:101-141) on the GPU."""
+    _need(mel_frames.dtype == torch.int32, "mel_frames is int32")
+    check(lib.b200asr_pack_audio(
+        _p(mel_frames), mel_frames.numel(), chunk_frames, window_tokens, max_chunks, max_windows,
+        _p(out["chunk_lengths"]), _p(out["chunk_valid_lens"]), _p(out["chunk_start"]),
+        _p(out["audio_token_lens"]), _p(out["cu_seqlens"]), _p(out["counts"]), _p(error_flag),
+        _stream()), "pack_audio")
+
+
+def audio_chunk_pad(mel, chunk_start, chunk_lengths, num_chunks: int, chunk_frames: int,
+                    out: torch.Tensor) -> torch.Tensor:
+    """``AudioEncoder._chunk_and_pad`` (models/audio_encoder.py:130-143): mel [bins, F]
+    -> out [num_chunks, bins, chunk_frames] bf16, zero past each chunk's length."""
+    _need(mel.dtype == BF16 and mel.is_contiguous() and out.dtype == BF16, "bf16 contiguous mel")
+    check(lib.b200asr_audio_chunk_pad(
+        _p(mel), mel.shape[0], mel.shape[1], _p(chunk_start), _p(chunk_lengths), num_chunks,
+        chunk_frames, _p(out), _stream()), "audio_chunk_pad")
+    return out
+
+
+# -------------------------------------------------------------------- KV store
+
+
+def store_kvcache(key, value, k_cache, v_cache, slot_mapping, error_flag=None) -> None:
+    """``store_kvcache`` (layers/attention.py:52-67): same arguments and checks."""
+    num_tokens, num_heads, head_dim = key.shape
+    hidden = num_heads * head_dim
+    _cuda(key, value, k_cache, v_cache, slot_mapping)
+    _need(key.dtype == BF16 and value.dtype == BF16 and k_cache.dtype == BF16, "bf16 K/V")
+    _need(key.stride(-1) == 1 and value.stride(-1) == 1, "key/value rows must be contiguous")
+    _need(key.stride(1) == head_dim and value.stride(1) == head_dim, "head stride == head_dim")
+    _need(k_cache.stride(1) == hidden and v_cache.stride(1) == hidden, "cache slot stride")
+    _need(slot_mapping.numel() == num_tokens and slot_mapping.dtype == torch.int32, "slots")
+    num_slots = k_cache.numel() // hidden
+    check(lib.b200asr_store_kvcache(
+        _p(key), key.stride(0), _p(value), value.stride(0), _p(k_cache), _p(v_cache),
+        _p(slot_mapping), num_tokens, num_heads, head_dim, num_slots, _p(error_flag), _stream()),
+        "store_kvcache")
+
+
+# ------------------------------------------------------- norms, rope, activation
+
+
+def qk_norm_rope_store(qkv, positions, *, num_heads: int, num_kv_heads: int, head_dim: int,
+                       q_weight, k_weight, eps: float, cos_sin_cache, q_out, k_cache=None,
+                       v_cache=None, slot_mapping=None, k_out=None, error_flag=None) -> torch.Tensor:
+    """Qwen3Attention q/k RMSNorm + RoPE (models/qwen3.py:43-48) fused with the KV store.
+
+    ``cos_sin_cache`` is fp32 [max_position, head_dim]; returns ``q_out``.
+    """
+    _cuda(qkv, positions, q_weight, k_weight, cos_sin_cache, q_out)
+    _need(qkv.dtype == BF16 and qkv.stride(-1) == 1, "qkv bf16 with contiguous rows")
+    _need(positions.dtype == torch.int64, "positions int64")
+    _need(cos_sin_cache.dtype == torch.float32 and cos_sin_cache.is_contiguous(), "fp32 rope table")
+    num_slots = 0
+    if slot_mapping is not None:
+        _need(slot_mapping.dtype == torch.int32, "slot_mapping int32")
+        num_slots = k_cache.numel() // (num_kv_heads * head_dim)
+    check(lib.b200asr_qk_norm_rope_store(
+        _p(qkv), qkv.stride(0), _p(positions), qkv.shape[0], num_heads, num_kv_heads, head_dim,
+        _p(q_weight), _p(k_weight), float(eps), _p(cos_sin_cache), cos_sin_cache.shape[0],
+        _p(q_out), q_out.stride(0), _p(k_out), _p(k_cache), _p(v_cache), _p(slot_mapping),
+        num_slots, _p(error_flag), _stream()), "qk_norm_rope_store")
+    return q_out
+
+
+def rmsnorm(x, weight, eps: float, residual=None, out=None) -> torch.Tensor:
+    """``RMSNorm`` (layers/layernorm.py:19-36). With ``residual`` it is updated in place
+    to ``x + residual`` (bf16) and the norm is taken of that sum."""
+    _need(x.dtype == BF16 and x.is_contiguous(), "x bf16 contiguous")
+    rows, hidden = x.numel() // x.shape[-1], x.shape[-1]
+    out = torch.empty_like(x) if out is None else out
+    check(lib.b200asr_rmsnorm(_p(x), _p(residual), _p(weight), float(eps), rows, hidden, _p(out),
+                              _stream()), "rmsnorm")
+    return out
+
+
+def silu_mul(x, out=None) -> torch.Tensor:
+    """``SiluAndMul`` (layers/activation.py:11-14)."""
+    _need(x.dtype == BF16 and x.is_contiguous(), "x bf16 contiguous")
+    inner = x.shape[-1] // 2
+    rows = x.numel() // x.shape[-1]
+    if out is None:
+        out = torch.empty(*x.shape[:-1], inner, dtype=x.dtype, device=x.device)
+    check(lib.b200asr_silu_mul(_p(x), rows, inner, _p(out), _stream()), "silu_mul")
+    return out
+
+
+# ------------------------------------------------------------------- attention
+
+
+def paged_decode_workspace_size(batch: int, max_seqlen_k: int, num_heads: int,
+                                head_dim: int = 128) -> int:
+    return int(lib.b200asr_paged_decode_workspace_size(batch, max_seqlen_k, num_heads, head_dim))
+
+
+def paged_decode(q, k_cache, v_cache, cu_seqlens_k, block_tables, *, max_seqlen_k: int,
+                 scale: float, out, workspace, error_flag=None) -> torch.Tensor:
+    """One-token paged decode (split-K). q/out: [B, H, D]; caches [N, bs, Hkv, D]."""
+    _cuda(q, k_cache, v_cache, cu_seqlens_k, block_tables, out, workspace)
+    batch, num_heads, head_dim = q.shape
+    num_blocks, block_size, num_kv_heads, _ = k_cache.shape
+    _need(block_tables.dtype == torch.int32 and cu_seqlens_k.dtype == torch.int32, "int32 metadata")
+    check(lib.b200asr_paged_decode(
+        _p(q), q.stride(0), _p(k_cache), _p(v_cache), num_blocks, block_size, num_heads,
+        num_kv_heads, head_dim, _p(cu_seqlens_k), _p(block_tables), block_tables.stride(0), batch,
+        max_seqlen_k, float(scale), _p(out), out.stride(0), _p(workspace),
+        workspace.numel() * workspace.element_size(), _p(error_flag), _stream()), "paged_decode")
+    return out
+
+
+def paged_prefill(q, k_cache, v_cache, cu_seqlens_q, cu_seqlens_k, block_tables, *,
+                  max_seqlen_q: int, scale: float, out, error_flag=None) -> torch.Tensor:
+    """Varlen causal GQA over the paged cache on tcgen05 (layers/attention.py:96-107)."""
+    _cuda(q, k_cache, v_cache, cu_seqlens_q, cu_seqlens_k, block_tables, out)
+    total_q, num_heads, head_dim = q.shape
+    num_blocks, block_size, num_kv_heads, _ = k_cache.shape
+    batch = cu_seqlens_q.numel() - 1
+    check(lib.b200asr_paged_prefill(
+        _p(q), q.stride(0), _p(k_cache), _p(v_cache), num_blocks, block_size, num_heads,
+        num_kv_heads, head_dim, _p(cu_seqlens_q), _p(cu_seqlens_k), _p(block_tables),
+        block_tables.stride(0), batch, total_q, max_seqlen_q, float(scale), _p(out), out.stride(0),
+        _p(error_flag), _stream()), "paged_prefill")
+    return out
+
+
+def varlen_attention(q, k, v, cu_seqlens, max_seqlen: int, scale: float, out=None,
+                     error_flag=None) -> torch.Tensor:
+    """``VarlenSelfAttention.forward`` (layers/attention.py:121-139), causal=False."""
+    _cuda(q, k, v, cu_seqlens)
+    total, num_heads, head_dim = q.shape
+    for t in (q, k, v):
+        _need(t.dtype == BF16 and t.stride(-1) == 1 and t.stride(1) == head_dim, "q/k/v layout")
+    if out is None:
+        out = torch.empty(total, num_heads, head_dim, dtype=q.dtype, device=q.device)
+    check(lib.b200asr_varlen_attention(
+        _p(q), q.stride(0), _p(k), k.stride(0), _p(v), v.stride(0), _p(cu_seqlens),
+        cu_seqlens.numel() - 1, total, int(max_seqlen), num_heads, head_dim, float(scale), _p(out),
+        out.stride(0), _p(error_flag), _stream()), "varlen_attention")
+    return out
+
+
+# --------------------------------------------------------------------- sampler
+
+
+def greedy_argmax(logits, out=None) -> torch.Tensor:
+    """Greedy branch of ``Sampler`` (layers/sampler.py:16-20): first-max index per row."""
+    _cuda(logits)
+    _need(logits.dtype == BF16 and logits.stride(-1) == 1, "bf16 logits with contiguous rows")
+    batch, vocab = logits.shape
+    if out is None:
+        out = torch.empty(batch, dtype=torch.int64, device=logits.device)
+    check(lib.b200asr_greedy_argmax(_p(logits), logits.stride(0), batch, vocab, _p(out),
+                                    _stream()), "greedy_argmax")
+    return out

@@ -1,0 +1,114 @@
+"""Qwen3 text decoder (models/qwen3.py of the reference).
+
+Dense projections stay on torch matmul (cuBLAS). Per layer the b200asr kernels do:
+input / post-attention RMSNorm (the latter fused with the residual add), per-head
+q/k RMSNorm + RoPE fused with the KV-cache store, paged attention and SiLU*mul.
+"""
+
+from __future__ import annotations
+
+import torch
+from torch import nn
+
+from voiceagent_b200 import kernels as kx
+from voiceagent_b200.config import TextConfig
+from voiceagent_b200.layers.attention import PagedAttention
+from voiceagent_b200.layers.context import get_attention_context
+from voiceagent_b200.layers.norm import RMSNorm, SiluAndMul
+
+
+class Qwen3Attention(nn.Module):
+    def __init__(self, config: TextConfig, rope: "RopeHolder"):
+        super().__init__()
+        self.num_heads = config.num_attention_heads
+        self.num_kv_heads = config.num_key_value_heads
+        self.head_dim = config.head_dim or config.hidden_size // config.num_attention_heads
+        self.q_size = self.num_heads * self.head_dim
+        self.kv_size = self.num_kv_heads * self.head_dim
+        self.eps = config.rms_norm_eps
+        self.qkv_proj = nn.Linear(config.hidden_size, self.q_size + 2 * self.kv_size,
+                                  bias=config.attention_bias)
+        self.o_proj = nn.Linear(self.q_size, config.hidden_size, bias=False)
+        self.q_norm = RMSNorm(self.head_dim, eps=config.rms_norm_eps)
+        self.k_norm = RMSNorm(self.head_dim, eps=config.rms_norm_eps)
+        self.rope = rope
+        self.attn = PagedAttention(self.num_heads, self.head_dim, self.head_dim ** -0.5,
+                                   self.num_kv_heads)
+
+    def forward(self, positions: torch.Tensor, hidden_states: torch.Tensor) -> torch.Tensor:
+        ctx = get_attention_context()
+        qkv = self.qkv_proj(hidden_states)
+        t = qkv.shape[0]
+        q = torch.empty(t, self.num_heads, self.head_dim, dtype=qkv.dtype, device=qkv.device)
+        # q/k RMSNorm + RoPE; K and V go straight into the paged cache.
+        kx.qk_norm_rope_store(
+            qkv, positions, num_heads=self.num_heads, num_kv_heads=self.num_kv_heads,
+            head_dim=self.head_dim, q_weight=self.q_norm.weight, k_weight=self.k_norm.weight,
+            eps=self.eps, cos_sin_cache=self.rope.table, q_out=q, k_cache=self.attn.k_cache,
+            v_cache=self.attn.v_cache, slot_mapping=ctx.slot_mapping, error_flag=ctx.error_flag)
+        attn_out = self.attn(q)
+        return self.o_proj(attn_out.view(t, self.q_size))
+
+
+class Qwen3MLP(nn.Module):
+    def __init__(self, config: TextConfig):
+        super().__init__()
+        if config.hidden_act != "silu":
+            raise ValueError(f"unsupported activation: {config.hidden_act}")
+        self.gate_up_proj = nn.Linear(config.hidden_size, 2 * config.intermediate_size, bias=False)
+        self.down_proj = nn.Linear(config.intermediate_size, config.hidden_size, bias=False)
+        self.act_fn = SiluAndMul()
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        return self.down_proj(self.act_fn(self.gate_up_proj(x)))
+
+
+class Qwen3DecoderLayer(nn.Module):
+    def __init__(self, config: TextConfig, rope: "RopeHolder"):
+        super().__init__()
+        self.self_attn = Qwen3Attention(config, rope)
+        self.mlp = Qwen3MLP(config)
+        self.input_layernorm = RMSNorm(config.hidden_size, eps=config.rms_norm_eps)
+        self.post_attention_layernorm = RMSNorm(config.hidden_size, eps=config.rms_norm_eps)
+
+    def forward(self, positions, hidden_states, residual):
+        if residual is None:
+            residual = hidden_states
+            hidden_states = self.input_layernorm(hidden_states)
+        else:
+            hidden_states, residual = self.input_layernorm(hidden_states, residual)
+        hidden_states = self.self_attn(positions, hidden_states)
+        hidden_states, residual = self.post_attention_layernorm(hidden_states, residual)
+        return self.mlp(hidden_states), residual
+
+
+class RopeHolder(nn.Module):
+    """Owns the fp32 RoPE table shared by every layer (a buffer, not a parameter)."""
+
+    def __init__(self, head_dim: int, max_position: int, base: float):
+        super().__init__()
+        from voiceagent_b200.layers.norm import rope_table
+
+        self.register_buffer("table", rope_table(head_dim, max_position, base, None),
+                             persistent=False)
+
+
+class Qwen3Model(nn.Module):
+    def __init__(self, config: TextConfig, max_position: int):
+        super().__init__()
+        head_dim = config.head_dim or config.hidden_size // config.num_attention_heads
+        self.rope = RopeHolder(head_dim, max_position, config.rope_theta)
+        self.embed_tokens = nn.Embedding(config.vocab_size, config.hidden_size)
+        self.layers = nn.ModuleList(
+            [Qwen3DecoderLayer(config, self.rope) for _ in range(config.num_hidden_layers)])
+        self.norm = RMSNorm(config.hidden_size, eps=config.rms_norm_eps)
+
+    def forward(self, input_ids, positions, inputs_embeds=None) -> torch.Tensor:
+        if (input_ids is None) == (inputs_embeds is None):
+            raise ValueError("pass exactly one of input_ids or inputs_embeds")
+        hidden = self.embed_tokens(input_ids) if inputs_embeds is None else inputs_embeds
+        residual = None
+        for layer in self.layers:
+            hidden, residual = layer(positions, hidden, residual)
+        hidden, _ = self.norm(hidden, residual)
+        return hidden
