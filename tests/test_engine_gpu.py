@@ -1,0 +1,145 @@
+"""End-to-end AsrEngine on the GPU.
+
+Gates (north star): greedy token ids match the reference's own forward path (bf16,
+flash_attn_varlen_func, same weights, teacher forced) on >= 99 % of positions;
+graph decode equals eager decode token for token (the reference's
+test_cuda_graph.py gate), including padded buckets and contexts longer than one KV
+block. The fp32 CPU oracle is reported with a looser bound (bf16 vs fp32 on a
+random-init model flips near-tied argmaxes).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+DURATIONS = [0.9, 2.5, 4.0, 7.3, 12.0, 31.0]
+
+
+@pytest.fixture(scope="module")
+def tiny_dir(tmp_path_factory):
+    from voiceagent_b200.checkpoint import write_checkpoint
+
+    return str(write_checkpoint(tmp_path_factory.mktemp("tiny"), "tiny", weights=False))
+
+
+@pytest.fixture(scope="module")
+def clips():
+    from voiceagent_b200.workload import synthetic_waveform
+
+    rng = np.random.default_rng(11)
+    return [synthetic_waveform(d, rng) for d in DURATIONS]
+
+
+def _engine(path, **kw):
+    from voiceagent_b200.engine.engine import AsrEngine
+
+    settings = dict(max_num_seqs=4, max_model_len=2048, max_num_batched_tokens=4096,
+                    num_kvcache_blocks=64)
+    settings.update(kw)
+    return AsrEngine(path, weights="random", seed=0, **settings)
+
+
+def _run(engine, clips, n_tokens=24):
+    from voiceagent_b200.engine.request import SamplingParams
+
+    return engine.transcribe(clips, language="en",
+                             sampling=SamplingParams(max_new_tokens=n_tokens, ignore_eos=True))
+
+
+def _agreement_with_reference(engine, clips, outputs):
+    from tests import reference_path as ref
+
+    agree = total = 0
+    for clip, out in zip(clips, outputs):
+        feats = engine.frontend(clip)
+        layout = engine.prompt_builder.build(feats.num_audio_tokens, language="English")
+        audio = ref.encode_audio(engine.model, feats.mel)
+        seq = layout.token_ids + out.output_token_ids[:-1]
+        pred = ref.greedy_predictions(engine.model, seq, audio, layout.audio_offset)
+        expect = pred[len(layout.token_ids) - 1:].cpu().tolist()
+        agree += sum(int(a == b) for a, b in zip(expect, out.output_token_ids))
+        total += len(out.output_token_ids)
+    return agree / total
+
+
+def test_tiny_engine_matches_reference_path(tiny_dir, clips):
+    engine = _engine(tiny_dir)
+    outputs = _run(engine, clips)
+    assert [o.num_output_tokens for o in outputs] == [24] * len(clips)
+    assert all(o.finish_reason == "length" for o in outputs)
+    rate = _agreement_with_reference(engine, clips, outputs)
+    assert rate >= 0.99, f"greedy agreement with the reference path {rate:.4f}"
+
+
+def test_encoder_matches_reference_path(tiny_dir, clips):
+    from tests import reference_path as ref
+    from voiceagent_b200.audio.batcher import pack_audio_batch
+
+    engine = _engine(tiny_dir)
+    feats = [engine.frontend(c) for c in clips]
+    batch = pack_audio_batch([f.mel for f in feats], 800, "cuda")
+    packed = engine.model.encode_audio(batch)
+    for f, got in zip(feats, packed):
+        want = ref.encode_audio(engine.model, f.mel)
+        err = (got.float() - want.float()).abs()
+        scale = want.float().abs().max().item()
+        assert err.max().item() <= 2e-2 * max(1.0, scale), err.max().item()
+
+
+def test_graph_decode_equals_eager(tiny_dir, clips):
+    eager = _run(_engine(tiny_dir, enforce_eager=True), clips)
+    graphed_engine = _engine(tiny_dir)
+    assert graphed_engine.model_runner.graph_runner is not None
+    graphed = _run(graphed_engine, clips)
+    assert [o.output_token_ids for o in graphed] == [o.output_token_ids for o in eager]
+
+
+def test_padded_bucket_does_not_leak(tiny_dir, clips):
+    subset = clips[:3]  # three requests replay the bucket of four
+    eager = _run(_engine(tiny_dir, enforce_eager=True), subset)
+    graphed = _run(_engine(tiny_dir), subset)
+    assert [o.output_token_ids for o in graphed] == [o.output_token_ids for o in eager]
+
+
+def test_long_context_crosses_blocks(tiny_dir, clips):
+    from voiceagent_b200.engine.request import SamplingParams
+
+    long_clip = [clips[-1]]  # 31 s -> 403 audio tokens, prompt > 256
+    engine = _engine(tiny_dir, max_num_seqs=1)
+    out = engine.transcribe(long_clip, language="en",
+                            sampling=SamplingParams(max_new_tokens=140, ignore_eos=True))[0]
+    assert out.num_prompt_tokens > 256 and out.num_prompt_tokens + 140 > 512
+    eager = _engine(tiny_dir, max_num_seqs=1, enforce_eager=True).transcribe(
+        long_clip, language="en", sampling=SamplingParams(max_new_tokens=140, ignore_eos=True))[0]
+    assert out.output_token_ids == eager.output_token_ids
+    assert _agreement_with_reference(engine, long_clip, [out]) >= 0.99
+
+
+def test_config0_full_size_against_reference_and_oracle(tmp_path):
+    """Config 0 workload on the 0.6B architecture (random init, seed 0)."""
+    from oracle import model as M
+    from voiceagent_b200.checkpoint import PRESETS, write_checkpoint
+    from voiceagent_b200.engine.request import SamplingParams
+    from voiceagent_b200.workload import config0_clip
+
+    path = str(write_checkpoint(tmp_path / "c06", "0.6b", weights=False))
+    engine = _engine(path, max_num_seqs=1, max_model_len=1024, num_kvcache_blocks=8)
+    clip = config0_clip(0)
+    out = engine.transcribe([clip], language="en",
+                            sampling=SamplingParams(max_new_tokens=48, ignore_eos=True))[0]
+    assert out.num_audio_tokens == 52 and out.num_output_tokens == 48
+    rate = _agreement_with_reference(engine, [clip], [out])
+    assert rate >= 0.99, f"agreement with the bf16 reference path {rate:.4f}"
+
+    oracle = M.OracleThinker(PRESETS["0.6b"], M.init_weights(PRESETS["0.6b"], seed=0))
+    feats = engine.frontend(clip)
+    layout = engine.prompt_builder.build(feats.num_audio_tokens, language="English")
+    audio = oracle.encode_audio(feats.mel.float())
+    _, argmaxes = oracle.greedy(layout.token_ids, audio, 48, forced=out.output_token_ids)
+    fp32_rate = np.mean(np.asarray(argmaxes) == np.asarray(out.output_token_ids))
+    print(f"config0: reference-path agreement {rate:.4f}, fp32 oracle agreement {fp32_rate:.4f}")
+    assert fp32_rate >= 0.8

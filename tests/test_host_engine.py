@@ -1,0 +1,341 @@
+"""Host-side engine logic on CPU: block manager (against the reference's own
+allocation traces), scheduler pressure paths, request lifecycle, prompt layout,
+checkpoint writer / loader, and bucket selection. No GPU needed."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from tests.conftest import load_json
+from voiceagent_b200.audio.frontend import AudioFeatures
+from voiceagent_b200.config import EngineConfig
+from voiceagent_b200.engine.block_manager import BlockManager
+from voiceagent_b200.engine.request import AsrRequest, RequestStage, SamplingParams
+from voiceagent_b200.engine.scheduler import ModelBatch, Scheduler
+from voiceagent_b200.prompt import PromptBuilder, PromptLayout, normalize_language
+
+BS = 256
+AUDIO = 151676
+
+
+def make_request(prompt_len, audio_offset=8, audio_length=13, max_new_tokens=440):
+    suffix = prompt_len - audio_offset - audio_length
+    ids = (list(range(1000, 1000 + audio_offset)) + [AUDIO] * audio_length
+           + list(range(2000, 2000 + suffix)))
+    frames = max(1, audio_length * 100 // 13)
+    return AsrRequest(
+        features=AudioFeatures(mel=torch.zeros(128, frames), mel_frames=frames,
+                               num_audio_tokens=audio_length, audio_seconds=audio_length / 13),
+        layout=PromptLayout(token_ids=ids, audio_offset=audio_offset, audio_length=audio_length),
+        sampling=SamplingParams(max_new_tokens=max_new_tokens), block_size=BS,
+        stop_token_ids={151643, 151645})
+
+
+@pytest.fixture
+def config(tmp_path):
+    from voiceagent_b200.checkpoint import write_checkpoint
+
+    path = write_checkpoint(tmp_path / "ckpt", "tiny", weights=False)
+
+    def build(**kw):
+        settings = dict(model=str(path), max_num_seqs=8, max_model_len=4096,
+                        max_num_batched_tokens=4096)
+        settings.update(kw)
+        return EngineConfig(**settings)
+
+    return build
+
+
+def admit_for_prefill(scheduler, request):
+    request.audio_embeds = torch.zeros(request.layout.audio_length, 4)
+    request.stage = RequestStage.WAITING_PREFILL
+    scheduler.admit_prefill([request])
+    return request
+
+
+def start_decoding(scheduler, manager, request):
+    admit_for_prefill(scheduler, request)
+    manager.allocate(request)
+    request.num_computed_tokens = len(request)
+    request.stage = RequestStage.RUNNING_DECODE
+    scheduler.waiting_prefill.remove(request)
+    scheduler.running.append(request)
+    return request
+
+
+# ------------------------------------------------------------- block manager
+
+
+@pytest.mark.parametrize("trace_index", [0, 1])
+def test_block_manager_reproduces_reference_traces(trace_index):
+    trace = load_json("block_manager.json")[trace_index]
+    manager = BlockManager(num_blocks=24, block_size=BS, enable_prefix_cache=trace["prefix_cache"])
+    reqs = {}
+    for entry in trace["log"]:
+        if entry["op"] == "alloc":
+            r = make_request(*entry["arg"])
+            reqs[entry["name"]] = r
+            ok = manager.can_allocate(r)
+            assert ok == entry["ok"]
+            if ok:
+                manager.allocate(r)
+            assert r.block_table == entry["table"]
+            assert (r.num_cached_tokens, r.num_computed_tokens) == (entry["cached"], entry["computed"])
+        elif entry["op"] == "append":
+            r = reqs[entry["name"]]
+            for step in range(entry["arg"]):
+                r.append_token(5000 + step)
+                if manager.can_append(r):
+                    manager.may_append(r)
+            assert r.block_table == entry["table"]
+        else:
+            manager.deallocate(reqs[entry["name"]])
+            assert list(manager.free_block_ids) == entry["free_order"]
+        assert manager.num_free_blocks == entry["free"]
+    assert BlockManager.compute_hash(list(range(256))) == trace["hash_example"]
+
+
+def test_prefix_reuse_and_audio_isolation():
+    manager = BlockManager(num_blocks=32, block_size=BS)
+    first = make_request(700, 609, 46)
+    second = make_request(700, 609, 46)
+    manager.allocate(first)
+    manager.allocate(second)
+    assert second.num_cached_tokens == 2 * BS
+    assert second.block_table[:2] == first.block_table[:2]
+    assert second.block_table[2] != first.block_table[2]
+    a, b = make_request(600, 0, 590), make_request(600, 0, 590)
+    manager.allocate(a)
+    manager.allocate(b)
+    assert b.num_cached_tokens == 0 and set(a.block_table).isdisjoint(b.block_table)
+
+
+def test_append_allocates_only_on_block_boundary():
+    manager = BlockManager(num_blocks=8, block_size=BS)
+    r = make_request(BS, 9, 46)
+    manager.allocate(r)
+    r.append_token(42)
+    assert manager.can_append(r)
+    manager.may_append(r)
+    assert len(r.block_table) == 2
+    r.append_token(43)
+    manager.may_append(r)
+    assert len(r.block_table) == 2
+
+
+# ----------------------------------------------------------------- scheduler
+
+
+def test_preempts_newest_to_keep_oldest(config):
+    manager = BlockManager(2, BS)
+    s = Scheduler(config(), manager)
+    first = start_decoding(s, manager, make_request(BS))
+    second = start_decoding(s, manager, make_request(BS))
+    first.append_token(7)
+    second.append_token(7)
+    batch = s.schedule_model()
+    assert batch.decode == [first]
+    assert s.stats.num_preemptions == 1
+    assert second.stage is RequestStage.WAITING_PREFILL and second.block_table == []
+    assert second.audio_embeds is not None and second.num_computed_tokens == 0
+
+
+def test_lone_request_that_cannot_grow_is_aborted(config):
+    manager = BlockManager(1, BS)
+    s = Scheduler(config(), manager)
+    only = start_decoding(s, manager, make_request(BS))
+    only.append_token(7)
+    assert not s.schedule_model()
+    assert s.drain_aborted() == [only]
+    assert only.finish_reason == "aborted:out_of_kv_blocks" and not s.has_work
+
+
+def test_unplaceable_request_is_aborted_not_stalled(config):
+    s = Scheduler(config(), BlockManager(2, BS))
+    r = admit_for_prefill(s, make_request(3 * BS))
+    assert not s.schedule_model()
+    assert s.drain_aborted() == [r] and r.finish_reason == "aborted:kv_cache_too_small"
+
+
+def test_transient_pressure_waits(config):
+    manager = BlockManager(2, BS)
+    s = Scheduler(config(), manager)
+    start_decoding(s, manager, make_request(BS))
+    blocked = admit_for_prefill(s, make_request(2 * BS))
+    s.schedule_model()
+    assert not s.aborted and list(s.waiting_prefill) == [blocked]
+
+
+def test_model_oom_rollback_and_cap(config):
+    manager = BlockManager(32, BS)
+    s = Scheduler(config(max_num_seqs=8), manager)
+    reqs = [admit_for_prefill(s, make_request(BS)) for _ in range(8)]
+    batch = s.schedule_model()
+    assert len(batch.prefill) == 8
+    s.on_model_oom(batch)
+    assert list(s.waiting_prefill) == reqs
+    assert all(r.block_table == [] and r.num_computed_tokens == 0 for r in reqs)
+    assert s.model_batch_limit == 4
+    assert len(s.schedule_model().requests) == 4
+    s.relax_limits()
+    assert s.model_batch_limit == 8
+
+
+def test_single_request_oom_gives_up(config):
+    manager = BlockManager(16, BS)
+    s = Scheduler(config(), manager)
+    r = start_decoding(s, manager, make_request(BS // 2))
+    s.on_model_oom(s.schedule_model())
+    assert s.drain_aborted() == [r] and r.finish_reason == "aborted:out_of_memory"
+
+
+def test_audio_oom_requeues_in_order(config):
+    s = Scheduler(config(max_audio_batch_frames=10_000), BlockManager(16, BS))
+    reqs = [make_request(BS) for _ in range(3)]
+    for r in reqs:
+        s.add(r)
+    picked = s.schedule_audio()
+    assert picked == reqs
+    s.on_audio_oom(picked)
+    assert list(s.waiting_encode) == reqs and s.audio_frame_limit < 10_000
+
+
+def test_postprocess_finishes_and_frees(config):
+    manager = BlockManager(8, BS)
+    s = Scheduler(config(), manager)
+    r = make_request(60, 9, 46, max_new_tokens=2)
+    admit_for_prefill(s, r)
+    batch = s.schedule_model()
+    assert batch.prefill == [r] and r.num_tokens_to_compute == 60
+    assert s.postprocess(batch, [11]) == []
+    assert r.stage is RequestStage.RUNNING_DECODE and r.num_tokens_to_compute == 1
+    batch = s.schedule_model()
+    assert batch.decode == [r]
+    assert s.postprocess(batch, [12]) == [r]
+    assert r.finish_reason == "length" and manager.num_free_blocks == 8
+
+
+def test_cancel_waiting_request(config):
+    s = Scheduler(config(), BlockManager(8, BS))
+    r = make_request(60, 9, 46)
+    s.add(r)
+    assert s.cancel(r.request_id)
+    assert s.drain_aborted() == [r] and r.finish_reason == "cancelled"
+    assert not s.cancel(12345678)
+
+
+def test_empty_batch_rollback_is_noop(config):
+    s = Scheduler(config(), BlockManager(16, BS))
+    s.on_model_oom(ModelBatch())
+    assert not s.aborted and not s.has_work
+
+
+# ---------------------------------------------------------- request / prompt
+
+
+def test_request_lifecycle():
+    r = make_request(62, 9, 46)
+    assert r.num_tokens_to_compute == 62
+    r.num_computed_tokens = 62
+    r.append_token(7)
+    assert r.num_tokens_to_compute == 1
+    r.append_token(151645)
+    assert r.check_finished() and r.finish_reason == "stop"
+
+
+def test_sampling_for_audio():
+    assert SamplingParams().max_new_tokens == 440
+    assert SamplingParams.for_audio(5.0).max_new_tokens == 440
+    assert SamplingParams.for_audio(1299.0).max_new_tokens > 4849
+    assert SamplingParams.for_audio(1200.0, max_new_tokens=99).max_new_tokens == 99
+
+
+def test_prompt_template_ids():
+    # pinned by the reference's tests/test_prompt.py:24-47
+    layout = PromptBuilder().build(1)
+    assert layout.token_ids == [151644, 8948, 198, 151645, 198, 151644, 872, 198, 151669, 151676,
+                                151670, 151645, 198, 151644, 77091, 198]
+    assert layout.audio_offset == 9
+    forced = PromptBuilder().build(46, language="English")
+    assert forced.token_ids[-1] == 151704 and len(forced) == 46 + 18
+    assert forced.token_ids[9:55] == [151676] * 46
+    with pytest.raises(ValueError):
+        PromptBuilder().build(0)
+    assert normalize_language("EN") == "English" and normalize_language("") is None
+
+
+# ------------------------------------------------------ checkpoint / loader
+
+
+def test_engine_and_oracle_random_init_agree():
+    from oracle import model as M
+    from voiceagent_b200.checkpoint import PRESETS, random_state_dict
+
+    cfg = PRESETS["tiny"]
+    ours = random_state_dict(cfg, seed=3, dtype=torch.float32)
+    theirs = M.init_weights(cfg, seed=3)
+    assert set(ours) == set(theirs) - ({"lm_head.weight"} if "lm_head.weight" not in ours else set())
+    for name, t in ours.items():
+        assert torch.equal(t, theirs[name]), name
+
+
+def test_checkpoint_roundtrip_into_fused_model(tmp_path):
+    from voiceagent_b200.checkpoint import random_state_dict, write_checkpoint
+    from voiceagent_b200.config import Qwen3ASRConfig
+    from voiceagent_b200.loader import load_weights
+    from voiceagent_b200.qwen3_asr.model import Qwen3ASRForConditionalGeneration
+
+    path = write_checkpoint(tmp_path / "c", "tiny", seed=5)
+    cfg = Qwen3ASRConfig.from_pretrained(str(path))
+    assert cfg.stop_token_ids == [151643, 151645] and cfg.text.hidden_size == 256
+    torch.set_default_dtype(torch.bfloat16)
+    try:
+        model = Qwen3ASRForConditionalGeneration(cfg, 4096)
+    finally:
+        torch.set_default_dtype(torch.float32)
+    load_weights(model, str(path))
+    ref = random_state_dict("tiny", seed=5)
+    qkv = model.model.layers[1].self_attn.qkv_proj.weight
+    assert torch.equal(qkv[:512], ref["model.layers.1.self_attn.q_proj.weight"])
+    assert torch.equal(qkv[512:768], ref["model.layers.1.self_attn.k_proj.weight"])
+    enc = model.audio_tower.layers[0].self_attn.qkv_proj.bias
+    assert torch.equal(enc[128:256], ref["audio_tower.layers.0.self_attn.k_proj.bias"])
+    assert model.lm_head.weight is model.model.embed_tokens.weight
+
+
+def test_loader_rejects_orphans(tmp_path):
+    from safetensors.torch import save_file
+
+    from voiceagent_b200.checkpoint import random_state_dict, write_checkpoint
+    from voiceagent_b200.config import Qwen3ASRConfig
+    from voiceagent_b200.loader import load_weights
+    from voiceagent_b200.qwen3_asr.model import Qwen3ASRForConditionalGeneration
+
+    path = write_checkpoint(tmp_path / "c", "tiny", weights=False)
+    tensors = {"thinker." + k: v for k, v in random_state_dict("tiny").items()}
+    tensors["thinker.bogus.weight"] = torch.zeros(1)
+    save_file(tensors, str(path / "model.safetensors"))
+    model = Qwen3ASRForConditionalGeneration(Qwen3ASRConfig.from_pretrained(str(path)), 4096)
+    with pytest.raises(RuntimeError, match="no destination"):
+        load_weights(model, str(path))
+
+
+def test_bucket_selection():
+    from voiceagent_b200.engine.graph_runner import DEFAULT_BUCKETS, GraphRunner
+
+    runner = GraphRunner.__new__(GraphRunner)
+    runner.buckets = DEFAULT_BUCKETS
+    assert [runner.bucket_for(n) for n in (1, 3, 16, 17, 64)] == [1, 4, 16, 24, 64]
+    assert runner.bucket_for(65) is None
+
+
+def test_audio_token_accounting_matches_oracle():
+    from oracle import kernels as K
+    from voiceagent_b200.audio import tokens as T
+
+    for f in range(1, 3000):
+        assert T.num_audio_tokens(f) == K.num_audio_tokens(f)
+        assert T.chunk_lengths_for(f) == K.chunk_lengths_for(f)
+    assert T.attention_window_tokens(800) == 104

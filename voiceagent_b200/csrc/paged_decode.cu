@@ -349,9 +349,16 @@ template <int H>
 __global__ void decode_combine_kernel(const DecodeArgs a) {
   const int b = blockIdx.x;
   const int h = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // Items before this sequence: warp-parallel sum over the preceding lengths.
   int first = 0;
-  for (int i = 0; i < b; ++i)
-    first += (a.cu_seqlens_k[i + 1] - a.cu_seqlens_k[i] + kDecChunk - 1) / kDecChunk;
+  for (int i0 = 0; i0 < b; i0 += 32) {
+    const int i = i0 + lane;
+    int n_i = 0;
+    if (i < b) n_i = (a.cu_seqlens_k[i + 1] - a.cu_seqlens_k[i] + kDecChunk - 1) / kDecChunk;
+    first += n_i;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) first += __shfl_xor_sync(0xffffffffu, first, o);
   const int len = a.cu_seqlens_k[b + 1] - a.cu_seqlens_k[b];
   const int n = (len + kDecChunk - 1) / kDecChunk;
   __nv_bfloat16 *dst = a.out + b * a.out_stride + h * kDecD + lane * 4;
@@ -361,8 +368,10 @@ __global__ void decode_combine_kernel(const DecodeArgs a) {
     return;
   }
   float mm = -INFINITY;
+#pragma unroll 8
   for (int i = 0; i < n; ++i) mm = fmaxf(mm, a.ws_ml[(static_cast<int64_t>(first + i) * H + h) * 2]);
   float lt = 0.f, o[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 8
   for (int i = 0; i < n; ++i) {
     const int64_t base = static_cast<int64_t>(first + i) * H + h;
     const float mi = a.ws_ml[base * 2];

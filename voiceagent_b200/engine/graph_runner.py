@@ -1,0 +1,148 @@
+"""CUDA-graph decode (engine/graph_runner.py of the reference, B200 version).
+
+One graph per batch bucket. Each graph holds the WHOLE decode step: the
+``pack_decode_bucket`` kernel (building input ids, positions, slot mapping,
+cu_seqlens_k and block tables from a static device descriptor), the 28-layer
+decoder with the split-K paged decode attention, the final norm, the lm_head GEMM
+and the greedy argmax. Per step the host fills a pinned descriptor, issues one
+host-to-device copy, replays, and reads back the bucket's token ids.
+
+Padding rows are encoded in the descriptor as (length 1, empty block table), which
+the packer turns into the reference's padding: slot -1, key length 1, an all-zero
+block-table row.
+"""
+
+from __future__ import annotations
+
+import logging
+
+import torch
+
+from voiceagent_b200 import kernels as kx
+from voiceagent_b200.config import EngineConfig
+from voiceagent_b200.layers.context import AttentionContext, attention_context
+
+logger = logging.getLogger(__name__)
+
+DEFAULT_BUCKETS = (1, 2, 4, 8, 16, 24, 32, 48, 64)
+
+
+class GraphRunner:
+    def __init__(self, model, config: EngineConfig, error_flag: torch.Tensor | None = None,
+                 buckets: tuple[int, ...] = DEFAULT_BUCKETS):
+        self.model = model
+        self.config = config
+        self.device = torch.device(config.device)
+        self.block_size = config.kvcache_block_size
+        self.max_blocks = -(-config.max_model_len // self.block_size)
+        self.buckets = tuple(b for b in buckets if b <= config.max_num_seqs) or (config.max_num_seqs,)
+        self.max_batch = self.buckets[-1]
+        self.error_flag = error_flag
+        self.graphs: dict[int, torch.cuda.CUDAGraph] = {}
+        self.pool = None
+        self._allocate()
+
+    def _allocate(self) -> None:
+        m, dev = self.max_batch, self.device
+        self.desc_len = 4 * m + m * self.max_blocks
+        self.desc = torch.zeros(self.desc_len, dtype=torch.int32, device=dev)
+        self.host_desc = torch.zeros(self.desc_len, dtype=torch.int32, pin_memory=True)
+        self._host_np = self.host_desc.numpy()
+        self.input_ids = torch.zeros(m, dtype=torch.int64, device=dev)
+        self.positions = torch.zeros(m, dtype=torch.int64, device=dev)
+        self.slot_mapping = torch.full((m,), -1, dtype=torch.int32, device=dev)
+        self.cu_seqlens_q = torch.arange(m + 1, dtype=torch.int32, device=dev)
+        self.cu_seqlens_k = torch.zeros(m + 1, dtype=torch.int32, device=dev)
+        self.block_tables = torch.zeros(m, self.max_blocks, dtype=torch.int32, device=dev)
+        self.token_ids = torch.zeros(m, dtype=torch.int64, device=dev)
+        self.host_tokens = torch.zeros(m, dtype=torch.int64, pin_memory=True)
+        self.hidden: dict[int, torch.Tensor] = {}
+        ws_bytes = kx.paged_decode_workspace_size(m, self.config.max_model_len,
+                                                  self.config.model_config.text.num_attention_heads)
+        self.workspace = torch.empty(ws_bytes // 4 + 64, dtype=torch.float32, device=dev)
+
+    def _desc_views(self, bucket: int):
+        m = self.max_batch
+        d = self.desc
+        return (d[0:bucket], d[m:m + bucket], d[2 * m:2 * m + bucket], d[3 * m:3 * m + bucket],
+                d[4 * m:])
+
+    def _context(self, bucket: int) -> AttentionContext:
+        return AttentionContext(
+            cu_seqlens_q=self.cu_seqlens_q[:bucket + 1], cu_seqlens_k=self.cu_seqlens_k[:bucket + 1],
+            max_seqlen_q=1, max_seqlen_k=self.config.max_model_len,
+            slot_mapping=self.slot_mapping[:bucket], block_tables=self.block_tables[:bucket],
+            decode_only=True, decode_workspace=self.workspace, error_flag=self.error_flag)
+
+    def _step(self, bucket: int) -> torch.Tensor:
+        lens, last_ids, toff, tlen, tables = self._desc_views(bucket)
+        kx.pack_decode_bucket(lens, last_ids, toff, tlen, tables, batch=bucket, bucket=bucket,
+                              max_blocks=self.max_blocks, block_size=self.block_size,
+                              input_ids=self.input_ids, positions=self.positions,
+                              slot_mapping=self.slot_mapping, cu_seqlens_k=self.cu_seqlens_k,
+                              block_tables=self.block_tables)
+        hidden = self.model(self.input_ids[:bucket], self.positions[:bucket])
+        logits = self.model.compute_logits(hidden)
+        kx.greedy_argmax(logits, out=self.token_ids[:bucket])
+        return hidden
+
+    def _fill_padding(self, start: int) -> None:
+        m = self.max_batch
+        h = self._host_np
+        h[start:m] = 1            # lens
+        h[m + start:2 * m] = 0    # last ids
+        h[2 * m + start:3 * m] = 0
+        h[3 * m + start:4 * m] = 0  # empty tables
+
+    @torch.inference_mode()
+    def capture(self) -> None:
+        self._fill_padding(0)
+        self.desc.copy_(self.host_desc)
+        for bucket in reversed(self.buckets):
+            with attention_context(self._context(bucket)):
+                for _ in range(2):
+                    self._step(bucket)
+                torch.cuda.synchronize()
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph, self.pool):
+                    self.hidden[bucket] = self._step(bucket)
+            self.pool = self.pool or graph.pool()
+            self.graphs[bucket] = graph
+        torch.cuda.synchronize()
+        logger.info("captured decode graphs for buckets %s", sorted(self.graphs))
+
+    def bucket_for(self, batch_size: int) -> int | None:
+        for b in self.buckets:
+            if b >= batch_size:
+                return b
+        return None
+
+    @torch.inference_mode()
+    def run(self, requests) -> list[int]:
+        """Replay one decode step for `requests`; returns their sampled token ids."""
+        n = len(requests)
+        bucket = self.bucket_for(n)
+        if bucket is None:
+            raise ValueError(f"no captured graph for a batch of {n}")
+        m, h = self.max_batch, self._host_np
+        cursor = 4 * m
+        for i, r in enumerate(requests):
+            table = r.block_table
+            h[i] = len(r)
+            h[m + i] = r.token_ids[-1]
+            h[2 * m + i] = cursor - 4 * m
+            h[3 * m + i] = len(table)
+            h[cursor:cursor + len(table)] = table
+            cursor += len(table)
+        self._fill_padding(n)
+        self.desc[:cursor].copy_(self.host_desc[:cursor], non_blocking=True)
+        self.graphs[bucket].replay()
+        self.host_tokens[:n].copy_(self.token_ids[:n], non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        return self.host_tokens[:n].tolist()
+
+    def release(self) -> None:
+        self.graphs.clear()
+        self.hidden.clear()
+        self.pool = None
+
