@@ -16,6 +16,7 @@ import numpy as np
 import torch
 
 from voiceagent_b200 import kernels as kx
+from voiceagent_b200.profiling import TRANSFERS
 from voiceagent_b200.audio.tokens import (CHUNK_FRAMES, TOKENS_PER_FULL_CHUNK, after_cnn_len,
                                           attention_window_tokens, num_audio_tokens, num_chunks,
                                           num_windows)
@@ -68,6 +69,8 @@ def pack_audio_batch(mels: list[torch.Tensor], n_window_infer: int, device,
     offs = np.arange(base.size, dtype=np.int64) - np.repeat(np.cumsum(valid_np) - valid_np, valid_np)
     token_index = torch.from_numpy(base + offs).pin_memory().to(device, non_blocking=True)
 
+    TRANSFERS["h2d"] += 8 * int(token_index.numel()) + 4 * len(frames) + sum(
+        m.numel() * m.element_size() for m in mels if not m.is_cuda)
     mel = torch.cat([m.to(device, non_blocking=True) for m in mels], dim=-1)
     if mel.dtype != torch.bfloat16:
         mel = mel.to(torch.bfloat16)

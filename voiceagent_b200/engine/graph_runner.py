@@ -21,6 +21,7 @@ import torch
 from voiceagent_b200 import kernels as kx
 from voiceagent_b200.config import EngineConfig
 from voiceagent_b200.layers.context import AttentionContext, attention_context
+from voiceagent_b200.profiling import TRANSFERS
 
 logger = logging.getLogger(__name__)
 
@@ -39,6 +40,7 @@ class GraphRunner:
         self.max_batch = self.buckets[-1]
         self.error_flag = error_flag
         self.graphs: dict[int, torch.cuda.CUDAGraph] = {}
+        self.kernels_per_replay: dict[int, int] = {}
         self.pool = None
         self._allocate()
 
@@ -104,8 +106,10 @@ class GraphRunner:
                     self._step(bucket)
                 torch.cuda.synchronize()
                 graph = torch.cuda.CUDAGraph()
+                before = kx.LAUNCHES["count"]
                 with torch.cuda.graph(graph, self.pool):
                     self.hidden[bucket] = self._step(bucket)
+                self.kernels_per_replay[bucket] = kx.LAUNCHES["count"] - before
             self.pool = self.pool or graph.pool()
             self.graphs[bucket] = graph
         torch.cuda.synchronize()
@@ -137,7 +141,10 @@ class GraphRunner:
         self._fill_padding(n)
         self.desc[:cursor].copy_(self.host_desc[:cursor], non_blocking=True)
         self.graphs[bucket].replay()
+        kx.LAUNCHES["count"] += self.kernels_per_replay[bucket]
         self.host_tokens[:n].copy_(self.token_ids[:n], non_blocking=True)
+        TRANSFERS["h2d"] += 4 * cursor
+        TRANSFERS["d2h"] += 8 * n
         torch.cuda.current_stream().synchronize()
         return self.host_tokens[:n].tolist()
 

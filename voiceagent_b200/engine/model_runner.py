@@ -21,7 +21,7 @@ from voiceagent_b200.engine.scheduler import ModelBatch
 from voiceagent_b200.layers.attention import PagedAttention
 from voiceagent_b200.layers.context import AttentionContext, attention_context
 from voiceagent_b200.layers.sampler import GREEDY_TEMPERATURE_EPS, Sampler
-from voiceagent_b200.profiling import NULL_TIMER
+from voiceagent_b200.profiling import NULL_TIMER, TRANSFERS
 from voiceagent_b200.qwen3_asr.model import Qwen3ASRForConditionalGeneration
 
 
@@ -47,6 +47,7 @@ class Staging:
             views.append((off, n))
             off += n
         self.device_buf[:total].copy_(self.host[:total], non_blocking=True)
+        TRANSFERS["h2d"] += 4 * total
         return [self.device_buf[o:o + n] for o, n in views]
 
 
@@ -230,6 +231,7 @@ class ModelRunner:
         host = self._tokens_host[:n] if n <= self._tokens_host.numel() else torch.empty(
             n, dtype=torch.int64, pin_memory=True)
         host.copy_(ids, non_blocking=True)
+        TRANSFERS["d2h"] += 8 * n
         torch.cuda.current_stream().synchronize()
         return host.tolist()
 

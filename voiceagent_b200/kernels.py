@@ -14,6 +14,14 @@ from voiceagent_b200._lib import check, lib
 
 BF16 = torch.bfloat16
 
+# Kernel launches issued through these wrappers (eager calls and calls recorded
+# while capturing a CUDA graph alike); the graph runner adds its per-replay count.
+LAUNCHES = {"count": 0}
+
+
+def _count(n: int = 1) -> None:
+    LAUNCHES["count"] += n
+
 
 def _p(t: torch.Tensor | None):
     return None if t is None else t.data_ptr()
@@ -50,6 +58,7 @@ def pack_decoder(req_start, req_end, table_off, table_len, tables, query_tokens,
     _cuda(req_start, req_end, table_off, table_len, tables, query_tokens)
     for t in (req_start, req_end, table_off, table_len, tables, query_tokens):
         _need(t.dtype == torch.int32, "pack_decoder inputs are int32")
+    _count()
     check(lib.b200asr_pack_decoder(
         _p(req_start), _p(req_end), _p(table_off), _p(table_len), _p(tables), _p(query_tokens),
         batch, total_tokens, width, block_size, _p(out["input_ids"]), _p(out["positions"]),
@@ -62,6 +71,7 @@ def pack_decode_bucket(lens, last_ids, table_off, table_len, tables, *, batch: i
                        max_blocks: int, block_size: int, input_ids, positions, slot_mapping,
                        cu_seqlens_k, block_tables) -> None:
     """``GraphRunner.run`` staging (engine/graph_runner.py:149-191) on the GPU."""
+    _count()
     check(lib.b200asr_pack_decode_bucket(
         _p(lens), _p(last_ids), _p(table_off), _p(table_len), _p(tables), batch, bucket,
         max_blocks, block_size, _p(input_ids), _p(positions), _p(slot_mapping), _p(cu_seqlens_k),
@@ -72,6 +82,7 @@ def pack_audio(mel_frames, *, chunk_frames: int, window_tokens: int, max_chunks:
                max_windows: int, out: dict, error_flag=None) -> None:
     """Metadata of ``pack_audio_batch`` (audio/batcher.py:101-141) on the GPU."""
     _need(mel_frames.dtype == torch.int32, "mel_frames is int32")
+    _count()
     check(lib.b200asr_pack_audio(
         _p(mel_frames), mel_frames.numel(), chunk_frames, window_tokens, max_chunks, max_windows,
         _p(out["chunk_lengths"]), _p(out["chunk_valid_lens"]), _p(out["chunk_start"]),
@@ -84,6 +95,7 @@ def audio_chunk_pad(mel, chunk_start, chunk_lengths, num_chunks: int, chunk_fram
     """``AudioEncoder._chunk_and_pad`` (models/audio_encoder.py:130-143): mel [bins, F]
     -> out [num_chunks, bins, chunk_frames] bf16, zero past each chunk's length."""
     _need(mel.dtype == BF16 and mel.is_contiguous() and out.dtype == BF16, "bf16 contiguous mel")
+    _count()
     check(lib.b200asr_audio_chunk_pad(
         _p(mel), mel.shape[0], mel.shape[1], _p(chunk_start), _p(chunk_lengths), num_chunks,
         chunk_frames, _p(out), _stream()), "audio_chunk_pad")
@@ -104,6 +116,7 @@ def store_kvcache(key, value, k_cache, v_cache, slot_mapping, error_flag=None) -
     _need(k_cache.stride(1) == hidden and v_cache.stride(1) == hidden, "cache slot stride")
     _need(slot_mapping.numel() == num_tokens and slot_mapping.dtype == torch.int32, "slots")
     num_slots = k_cache.numel() // hidden
+    _count()
     check(lib.b200asr_store_kvcache(
         _p(key), key.stride(0), _p(value), value.stride(0), _p(k_cache), _p(v_cache),
         _p(slot_mapping), num_tokens, num_heads, head_dim, num_slots, _p(error_flag), _stream()),
@@ -128,6 +141,7 @@ def qk_norm_rope_store(qkv, positions, *, num_heads: int, num_kv_heads: int, hea
     if slot_mapping is not None:
         _need(slot_mapping.dtype == torch.int32, "slot_mapping int32")
         num_slots = k_cache.numel() // (num_kv_heads * head_dim)
+    _count()
     check(lib.b200asr_qk_norm_rope_store(
         _p(qkv), qkv.stride(0), _p(positions), qkv.shape[0], num_heads, num_kv_heads, head_dim,
         _p(q_weight), _p(k_weight), float(eps), _p(cos_sin_cache), cos_sin_cache.shape[0],
@@ -142,6 +156,7 @@ def rmsnorm(x, weight, eps: float, residual=None, out=None) -> torch.Tensor:
     _need(x.dtype == BF16 and x.is_contiguous(), "x bf16 contiguous")
     rows, hidden = x.numel() // x.shape[-1], x.shape[-1]
     out = torch.empty_like(x) if out is None else out
+    _count()
     check(lib.b200asr_rmsnorm(_p(x), _p(residual), _p(weight), float(eps), rows, hidden, _p(out),
                               _stream()), "rmsnorm")
     return out
@@ -154,6 +169,7 @@ def silu_mul(x, out=None) -> torch.Tensor:
     rows = x.numel() // x.shape[-1]
     if out is None:
         out = torch.empty(*x.shape[:-1], inner, dtype=x.dtype, device=x.device)
+    _count()
     check(lib.b200asr_silu_mul(_p(x), rows, inner, _p(out), _stream()), "silu_mul")
     return out
 
@@ -173,6 +189,7 @@ def paged_decode(q, k_cache, v_cache, cu_seqlens_k, block_tables, *, max_seqlen_
     batch, num_heads, head_dim = q.shape
     num_blocks, block_size, num_kv_heads, _ = k_cache.shape
     _need(block_tables.dtype == torch.int32 and cu_seqlens_k.dtype == torch.int32, "int32 metadata")
+    _count(2)  # split-K pass + combine
     check(lib.b200asr_paged_decode(
         _p(q), q.stride(0), _p(k_cache), _p(v_cache), num_blocks, block_size, num_heads,
         num_kv_heads, head_dim, _p(cu_seqlens_k), _p(block_tables), block_tables.stride(0), batch,
@@ -188,6 +205,7 @@ def paged_prefill(q, k_cache, v_cache, cu_seqlens_q, cu_seqlens_k, block_tables,
     total_q, num_heads, head_dim = q.shape
     num_blocks, block_size, num_kv_heads, _ = k_cache.shape
     batch = cu_seqlens_q.numel() - 1
+    _count()
     check(lib.b200asr_paged_prefill(
         _p(q), q.stride(0), _p(k_cache), _p(v_cache), num_blocks, block_size, num_heads,
         num_kv_heads, head_dim, _p(cu_seqlens_q), _p(cu_seqlens_k), _p(block_tables),
@@ -205,6 +223,7 @@ def varlen_attention(q, k, v, cu_seqlens, max_seqlen: int, scale: float, out=Non
         _need(t.dtype == BF16 and t.stride(-1) == 1 and t.stride(1) == head_dim, "q/k/v layout")
     if out is None:
         out = torch.empty(total, num_heads, head_dim, dtype=q.dtype, device=q.device)
+    _count()
     check(lib.b200asr_varlen_attention(
         _p(q), q.stride(0), _p(k), k.stride(0), _p(v), v.stride(0), _p(cu_seqlens),
         cu_seqlens.numel() - 1, total, int(max_seqlen), num_heads, head_dim, float(scale), _p(out),
@@ -222,6 +241,7 @@ def greedy_argmax(logits, out=None) -> torch.Tensor:
     batch, vocab = logits.shape
     if out is None:
         out = torch.empty(batch, dtype=torch.int64, device=logits.device)
+    _count()
     check(lib.b200asr_greedy_argmax(_p(logits), logits.stride(0), batch, vocab, _p(out),
                                     _stream()), "greedy_argmax")
     return out

@@ -59,3 +59,7 @@ class StageTimer:
 
 
 NULL_TIMER = StageTimer(enabled=False)
+
+# Bytes the engine moves between host and device (batch descriptors, mel features,
+# token ids); read by benchmarks to report per-step transfer volume.
+TRANSFERS = {"h2d": 0, "d2h": 0}
