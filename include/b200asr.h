@@ -173,6 +173,27 @@ B200ASR_API int b200asr_paged_decode(const void *q, int64_t q_row_stride, const 
                          void *out, int64_t out_row_stride, void *workspace,
                          size_t workspace_bytes, int32_t *error_flag, b200asr_stream_t stream);
 
+/* Allocation-free variant of b200asr_paged_decode. No counterpart in the reference:
+ * it exists for callers that cannot allocate device scratch -- an FFI host without a
+ * CUDA allocator, a server whose memory pool is fully reserved up front, or code running
+ * during CUDA-graph capture, where cudaMalloc is illegal. Same arguments and results as
+ * b200asr_paged_decode minus the workspace: the split-K partials live in a static device
+ * array of B200ASR_NOALLOC_SCRATCH_BYTES held by every GPU that loads the library.
+ * Requests whose b200asr_paged_decode_workspace_size exceeds that limit are rejected
+ * with B200ASR_ERR_WORKSPACE. The first call on each device resolves the array's address
+ * (cudaGetSymbolAddress, with that device current): make it before any stream capture.
+ * Every call shares the array, so calls whose kernels overlap on the GPU race on it;
+ * serialise them (one stream, or one replay at a time). Allocates nothing.           */
+#define B200ASR_NOALLOC_SCRATCH_BYTES (24u << 20)
+B200ASR_API int b200asr_paged_decode_noalloc(const void *q, int64_t q_row_stride,
+                                 const void *k_cache, const void *v_cache, int32_t num_blocks,
+                                 int32_t block_size, int32_t num_heads, int32_t num_kv_heads,
+                                 int32_t head_dim, const int32_t *cu_seqlens_k,
+                                 const int32_t *block_tables, int32_t bt_stride, int32_t batch,
+                                 int32_t max_seqlen_k, float scale, void *out,
+                                 int64_t out_row_stride, int32_t *error_flag,
+                                 b200asr_stream_t stream);
+
 /* Varlen causal GQA attention over the paged KV cache on tcgen05 tensor cores.
  * Replaces PagedAttention.forward (layers/attention.py:87-107) for prefill and mixed
  * batches: flash_attn_varlen_func(q, k_cache, v_cache, cu_seqlens_q, cu_seqlens_k,

@@ -43,6 +43,9 @@ SIGNATURES: dict[str, tuple] = {
     "b200asr_paged_decode": (c_int32, [P, c_int64, P, P, c_int32, c_int32, c_int32, c_int32,
                                        c_int32, P, P, c_int32, c_int32, c_int32, c_float, P,
                                        c_int64, P, c_size_t, P, P]),
+    "b200asr_paged_decode_noalloc": (c_int32, [P, c_int64, P, P, c_int32, c_int32, c_int32,
+                                               c_int32, c_int32, P, P, c_int32, c_int32,
+                                               c_int32, c_float, P, c_int64, P, P]),
     "b200asr_paged_prefill": (c_int32, [P, c_int64, P, P, c_int32, c_int32, c_int32, c_int32,
                                         c_int32, P, P, P, c_int32, c_int32, c_int32, c_int32,
                                         c_float, P, c_int64, P, P]),

@@ -490,3 +490,82 @@ extern "C" int b200asr_paged_decode(const void *q, int64_t q_row_stride, const v
   set_error("paged_decode: %d query / %d KV heads unsupported", num_heads, num_kv_heads);
   return B200ASR_ERR_UNSUPPORTED;
 }
+
+// -----------------------------------------------------------------------------
+// Allocation-free paged decode.
+//
+// Some callers of this library cannot hand it device scratch memory: an FFI host that
+// owns no CUDA allocator, a serving process whose memory pool was fully reserved for the
+// KV cache at start-up, or code that runs while a CUDA graph is being captured, where a
+// cudaMalloc is not allowed. For them the split-K partials of the decode pass live in a
+// fixed array compiled into this library instead of a caller workspace.
+//
+// The array is a file-scope __device__ symbol of B200ASR_NOALLOC_SCRATCH_BYTES; every GPU
+// that loads the library holds that much memory until the process exits. Host code cannot
+// use the symbol's name as a device address, so on the first call on each device (with
+// that device current) cudaGetSymbolAddress resolves it once and the pointer is cached.
+// That first call may trigger module loading, so it must come before any stream capture.
+// All calls share the one array and nothing in it needs clearing (every partial is written
+// before it is read), so two calls whose kernels overlap on the GPU -- different streams,
+// or graphs replayed concurrently -- race on it and must be serialised by the caller.
+#include <mutex>
+
+namespace b200asr {
+
+static __device__ __align__(256) unsigned char g_decode_noalloc_scratch[B200ASR_NOALLOC_SCRATCH_BYTES];
+
+static void *noalloc_scratch(int *status) {
+  constexpr int kMaxDevices = 64;
+  static std::mutex mu;
+  static void *resolved[kMaxDevices] = {};
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    set_error("paged_decode_noalloc: no usable current device (%s)", cudaGetErrorString(e));
+    *status = B200ASR_ERR_CUDA;
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (resolved[dev] == nullptr) {
+    void *p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_decode_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      set_error("paged_decode_noalloc: cudaGetSymbolAddress failed on device %d: %s", dev,
+                cudaGetErrorString(e));
+      *status = B200ASR_ERR_CUDA;
+      return nullptr;
+    }
+    resolved[dev] = p;
+  }
+  return resolved[dev];
+}
+
+}  // namespace b200asr
+
+extern "C" int b200asr_paged_decode_noalloc(const void *q, int64_t q_row_stride,
+                                            const void *k_cache, const void *v_cache,
+                                            int32_t num_blocks, int32_t block_size,
+                                            int32_t num_heads, int32_t num_kv_heads,
+                                            int32_t head_dim, const int32_t *cu_seqlens_k,
+                                            const int32_t *block_tables, int32_t bt_stride,
+                                            int32_t batch, int32_t max_seqlen_k, float scale,
+                                            void *out, int64_t out_row_stride,
+                                            int32_t *error_flag, b200asr_stream_t stream) {
+  const size_t need =
+      b200asr_paged_decode_workspace_size(batch, max_seqlen_k, num_heads, head_dim);
+  if (need > static_cast<size_t>(B200ASR_NOALLOC_SCRATCH_BYTES)) {
+    set_error("paged_decode_noalloc: batch %d x max_seqlen_k %d x %d heads needs %zu bytes of "
+              "scratch, more than the built-in %zu; use b200asr_paged_decode with a workspace",
+              batch, max_seqlen_k, num_heads, need,
+              static_cast<size_t>(B200ASR_NOALLOC_SCRATCH_BYTES));
+    return B200ASR_ERR_WORKSPACE;
+  }
+  if (batch == 0) return B200ASR_OK;
+  int status = B200ASR_OK;
+  void *scratch = noalloc_scratch(&status);
+  if (scratch == nullptr) return status;
+  return b200asr_paged_decode(q, q_row_stride, k_cache, v_cache, num_blocks, block_size,
+                              num_heads, num_kv_heads, head_dim, cu_seqlens_k, block_tables,
+                              bt_stride, batch, max_seqlen_k, scale, out, out_row_stride, scratch,
+                              B200ASR_NOALLOC_SCRATCH_BYTES, error_flag, stream);
+}
