@@ -162,7 +162,10 @@ B200ASR_API int b200asr_silu_mul(const void *x, int32_t rows, int32_t inner, voi
  * Supported: head_dim 128, block_size 256, num_heads / num_kv_heads in {1,2,4,8},
  * num_kv_heads <= 8. workspace: device scratch of at least
  * b200asr_paged_decode_workspace_size(batch, max_seqlen_k, num_heads, head_dim)
- * bytes; its contents need no initialisation.                                     */
+ * bytes. Its first 4096 bytes hold per-sequence merge counters that must be zero
+ * before the first call with that workspace; every completed call leaves them zero
+ * (allocate it zero-filled once). Calls sharing a workspace must not overlap on the
+ * GPU.                                                                             */
 B200ASR_API size_t b200asr_paged_decode_workspace_size(int32_t batch, int32_t max_seqlen_k,
                                            int32_t num_heads, int32_t head_dim);
 B200ASR_API int b200asr_paged_decode(const void *q, int64_t q_row_stride, const void *k_cache,
@@ -184,7 +187,7 @@ B200ASR_API int b200asr_paged_decode(const void *q, int64_t q_row_stride, const 
  * (cudaGetSymbolAddress, with that device current): make it before any stream capture.
  * Every call shares the array, so calls whose kernels overlap on the GPU race on it;
  * serialise them (one stream, or one replay at a time). Allocates nothing.           */
-#define B200ASR_NOALLOC_SCRATCH_BYTES (24u << 20)
+#define B200ASR_NOALLOC_SCRATCH_BYTES (12u << 20)
 B200ASR_API int b200asr_paged_decode_noalloc(const void *q, int64_t q_row_stride,
                                  const void *k_cache, const void *v_cache, int32_t num_blocks,
                                  int32_t block_size, int32_t num_heads, int32_t num_kv_heads,

@@ -324,7 +324,7 @@ def _decode_case(rng, lens, nblocks=4096, hq=16, hkv=8, d=128):
 def _run_decode(kx, q, kc, vc, tables, cu_k, max_len, err=None):
     qd, kcd, vcd = bf16(q), bf16(kc), bf16(vc)
     out = torch.zeros_like(qd)
-    ws = torch.empty(kx.paged_decode_workspace_size(q.shape[0], max_len, q.shape[1]) // 4 + 64,
+    ws = torch.zeros(kx.paged_decode_workspace_size(q.shape[0], max_len, q.shape[1]) // 4 + 64,
                      dtype=torch.float32, device="cuda")
     kx.paged_decode(qd, kcd, vcd, dev(cu_k, torch.int32), dev(tables, torch.int32),
                     max_seqlen_k=max_len, scale=q.shape[-1] ** -0.5, out=out, workspace=ws,
@@ -344,7 +344,7 @@ def test_paged_decode_matches_reference_torch_path(kx):
     pad = lambda x: np.concatenate([x, np.zeros_like(x)], axis=-1)
     qd, kcd, vcd = bf16(pad(q)), bf16(pad(kc)), bf16(pad(vc))
     out = torch.zeros_like(qd)
-    ws = torch.empty(1 << 22, dtype=torch.float32, device="cuda")
+    ws = torch.zeros(1 << 22, dtype=torch.float32, device="cuda")
     kx.paged_decode(qd, kcd, vcd, dev(cu_k, torch.int32), dev(g["tables"], torch.int32),
                     max_seqlen_k=int(lens.max()), scale=64 ** -0.5, out=out, workspace=ws)
     assert_attn_close(out[..., :64], g["out_reference"].astype(np.float64), "decode vs reference")

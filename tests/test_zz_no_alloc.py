@@ -42,9 +42,9 @@ def _case(seed: int, batch: int, nblocks: int = 96):
     return q, kc, vc, torch.from_numpy(cu).cuda(), torch.from_numpy(tables).cuda()
 
 
-def _noalloc(lib, q, kc, vc, cu, bt, max_len, out, err=None):
+def _noalloc(lib, q, kc, vc, cu, bt, max_len, out, err=None, num_heads=16):
     return lib.b200asr_paged_decode_noalloc(
-        q.data_ptr(), q.stride(0), kc.data_ptr(), vc.data_ptr(), kc.shape[0], 256, 16, 8, 128,
+        q.data_ptr(), q.stride(0), kc.data_ptr(), vc.data_ptr(), kc.shape[0], 256, num_heads, 8, 128,
         cu.data_ptr(), bt.data_ptr(), bt.stride(0), q.shape[0], max_len, 128 ** -0.5,
         out.data_ptr(), out.stride(0), None if err is None else err.data_ptr(),
         torch.cuda.current_stream().cuda_stream)
@@ -57,7 +57,7 @@ def test_noalloc_matches_workspace_entry_point_twice():
     for seed, batch in ((1, 32), (2, 7)):
         q, kc, vc, cu, bt = _case(seed, batch)
         ref = torch.empty_like(q)
-        ws = torch.empty(kx.paged_decode_workspace_size(batch, 1280, 16) // 4 + 64,
+        ws = torch.zeros(kx.paged_decode_workspace_size(batch, 1280, 16) // 4 + 64,
                          dtype=torch.float32, device="cuda")
         kx.paged_decode(q, kc, vc, cu, bt, max_seqlen_k=1280, scale=128 ** -0.5, out=ref,
                         workspace=ws)
@@ -77,7 +77,7 @@ def test_noalloc_rejects_requests_beyond_its_scratch():
 
     q, kc, vc, cu, bt = _case(3, 4)
     out = torch.zeros_like(q)
-    rc = _noalloc(lib, q, kc, vc, cu, bt, 1 << 20, out)  # absurd max length
+    rc = _noalloc(lib, q, kc, vc, cu, bt, 1024, out, num_heads=128)  # partials beyond 12 MiB
     assert rc == 4
     assert "scratch" in lib.b200asr_last_error().decode()
     torch.cuda.synchronize()

@@ -6,385 +6,512 @@
 // K_b, V_b the first len_b rows of sequence b gathered through its block table, and
 // query head h reading KV head h / (H / H_kv).
 //
-// Design (HBM-bound; one KV row is read once for all query heads of its group):
-//  * Work item = (sequence, 64-token chunk inside one 256-token block). The K (or V)
-//    rows of a chunk are ONE contiguous range of the cache (a slot holds all KV heads),
-//    so a stage of 16 tokens is a single 32 KiB 1-D bulk copy per operand.
-//  * Persistent grid, one CTA per SM. Warp 16 is the producer: it walks the same item
-//    sequence as the consumers and keeps a 3-stage ring of K/V tiles in flight
-//    (mbarrier full/empty pairs).
-//  * 16 consumer warps: warp w % 8 owns KV head w % 8 (and its G query heads) and
-//    token half w / 8 of every stage. Lane l holds head dims 4l..4l+3. The G x 8
-//    partial dot products of a stage are summed with a butterfly reduce-scatter
-//    (each lane ends with one full score), then an fp32 online softmax in base 2.
-//  * At the end of an item the two token halves merge through shared memory. A
-//    sequence with one item writes its bf16 output directly; longer ones write an
-//    unnormalised fp32 partial (+ running max and sum) to the caller's workspace and
-//    decode_combine merges them.
+// Design (HBM-bound; every KV row is read exactly once, for all query heads of its group):
+//  * Stream-K split: the persistent grid (one CTA per SM) divides the batch's key tokens
+//    -- all sequences laid end to end -- into equal contiguous ranges, so every CTA
+//    streams the same number of bytes whatever the length mix. A range is cut into
+//    segments at sequence ends and into stages of <= 16 tokens at KV-block ends.
+//  * Producer warp: keeps a 3-deep ring of stages and publishes each stage's sequence,
+//    token count and segment flags in shared memory. A stage is 2 x H_kv x 2
+//    TMA boxes {64 dims, 1 head, 16 tokens} with the 128-byte swizzle (K and V, every
+//    KV head, both halves of the head dim) -- one box per producer lane -- plus, on an
+//    segment's first stage, a 1-D bulk copy of that sequence's query row.
+//  * One consumer warp per KV head. Scores S = Q K^T and the update O += P V run on
+//    mma.sync m16n8k16 (bf16 in, fp32 accumulate) with the group's query heads as the
+//    MMA rows: a single-token GQA group has G (= 2) query rows, far below the 64-row
+//    minimum of tcgen05, and the tensor-core fragments remove the shuffle reductions that
+//    dominated a CUDA-core version. P is reused from the score registers as the A
+//    operand (no shared-memory round trip); softmax statistics are fp32, base 2, and
+//    need only a quad (4-lane) reduction per row.
+//  * A segment covering a whole sequence writes bf16 output directly. A sequence split
+//    across CTAs leaves one unnormalised fp32 partial plus (max, sum) per CTA in the
+//    workspace; the CTA that publishes the last one (per-sequence counter in the
+//    workspace header, reset by that CTA) merges them -- no second kernel.
+#include <mutex>
+
 #include "common.cuh"
 
 namespace b200asr {
 
 constexpr int kDecD = 128;
-constexpr int kDecChunk = 64;
+constexpr int kDecMaxGrid = 256;  // CTAs of the persistent grid (<= one per SM)
 constexpr int kDecStage = 16;
 constexpr int kDecStages = 3;
-constexpr int kDecHalf = kDecStage / 2;
 constexpr int kDecMaxBatch = 1024;
+constexpr size_t kDecHeaderBytes = 4096;  // per-sequence merge counters (int32 x 1024)
 constexpr float kLog2e = 1.4426950408889634f;
 
 template <int HKV, int G>
 struct Dec {
   static constexpr int H = HKV * G;
-  static constexpr int ROW = HKV * kDecD;            // elements per slot (K or V)
-  static constexpr int ROW_BYTES = ROW * 2;
-  static constexpr int CONSUMERS = 2 * HKV;           // warps
-  static constexpr int THREADS = (CONSUMERS + 1) * 32;
-  static constexpr int STAGE_BYTES = kDecStage * ROW_BYTES;
-  static constexpr int NV = kDecHalf * G;             // partial scores per warp per stage
-  static constexpr int LOG2NV = NV == 8 ? 3 : NV == 16 ? 4 : NV == 32 ? 5 : -1;
-  static constexpr int SHIFT = 5 - LOG2NV;            // lane bits that duplicate a score
-  static constexpr int LOG2G = G == 1 ? 0 : G == 2 ? 1 : G == 4 ? 2 : -1;
-  static constexpr int MERGE_FLOATS = HKV * 32 * (4 * G) + HKV * 2 * G;
-  static constexpr size_t SMEM = 2ull * kDecStages * STAGE_BYTES + MERGE_FLOATS * 4 +
-                                 (kDecMaxBatch + 1) * 4 + 2 * kDecStages * 8 + 16;
-  static_assert(LOG2NV > 0 && LOG2G >= 0, "unsupported group size");
+  static constexpr int THREADS = (HKV + 1) * 32;       // HKV consumer warps + 1 producer
+  static constexpr int HEAD_TILE = kDecStage * kDecD * 2;  // 16 tokens x 128 dims: 4 KiB
+  static constexpr int KV_BYTES = HKV * HEAD_TILE;
+  static constexpr int Q_BYTES = ((H * kDecD * 2 + 1023) / 1024) * 1024;
+  static constexpr int STAGE_BYTES = 2 * KV_BYTES + Q_BYTES;
+  static constexpr uint32_t TX_KV = 2 * KV_BYTES;
+  static constexpr uint32_t TX_Q = H * kDecD * 2;
+  static constexpr size_t SMEM = 1024 + static_cast<size_t>(kDecStages) * STAGE_BYTES +
+                                 3 * (kDecMaxBatch + 1) * 4 + 2 * kDecStages * 8 +
+                                 kDecStages * 32 + 64;
+  static_assert(G >= 1 && G <= 8, "group size");
+  static_assert(4 * HKV <= 32, "one TMA box per producer lane");
 };
 
 struct DecodeArgs {
   const __nv_bfloat16 *q;
   int64_t q_stride;
-  const __nv_bfloat16 *k_cache;
-  const __nv_bfloat16 *v_cache;
   int num_blocks;
   int block_size;
   const int32_t *cu_seqlens_k;
   const int32_t *block_tables;
   int bt_stride;
   int batch;
-  float scale_log2;  // softmax scale * log2(e)
+  float scale_log2;
   __nv_bfloat16 *out;
   int64_t out_stride;
-  float *ws_o;   // [items_cap][H][128]
-  float *ws_ml;  // [items_cap][H][2]
-  int items_cap;
+  int *counters;  // [kDecMaxBatch], zero between calls
+  float *ws_ml;   // [parts_cap][H][2]
+  float *ws_o;    // [parts_cap][H][128]
+  int parts_cap;
   int32_t *error_flag;
 };
 
-__device__ __forceinline__ void consumer_barrier(int threads) {
+// What the producer tells the consumers about a stage (written before the stage's
+// mbarrier arrive, read after the matching wait).
+struct StageInfo {
+  int b;      // sequence, or -1 for the terminal stage
+  int ntok;   // valid tokens (1..16)
+  int flags;  // 1: first stage of a segment (q attached), 2: last stage, 4: whole sequence
+};
+
+__device__ __forceinline__ void consumer_sync(int threads) {
   asm volatile("bar.sync 1, %0;" ::"r"(threads) : "memory");
 }
 
-// Index of the sequence owning item `it` (largest b with item_start[b] <= it).
-__device__ __forceinline__ int item_seq(const int *item_start, int batch, int it) {
-  int lo = 0, hi = batch - 1;
+// Largest b in [0, n) with v[b] <= x (v non-decreasing, v[0] <= x).
+__device__ __forceinline__ int upper_index(const int *v, int n, int x) {
+  int lo = 0, hi = n - 1;
   while (lo < hi) {
     const int mid = (lo + hi + 1) >> 1;
-    if (item_start[mid] <= it) lo = mid; else hi = mid - 1;
+    if (v[mid] <= x) lo = mid; else hi = mid - 1;
   }
   return lo;
 }
 
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2,
+                                        uint32_t &r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t &r0, uint32_t &r1,
+                                          uint32_t &r2, uint32_t &r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+// D = A(16x16 bf16, rows) * B(16x8 bf16, cols) + D, fp32 accumulate.
+__device__ __forceinline__ void mma16816(float *d, uint32_t a0, uint32_t a1, uint32_t a2,
+                                         uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Byte offset of (row, 16-byte chunk) inside a 128-byte-swizzled tile (1024-aligned).
+__device__ __forceinline__ uint32_t swz(int row, int chunk) {
+  return static_cast<uint32_t>(row * 128 + ((chunk ^ (row & 7)) << 4));
+}
+
+// Stream-K partition: CTA c of g owns global key tokens [T*c/g, T*(c+1)/g).
+__device__ __forceinline__ int part_begin(int64_t total, int c, int g) {
+  return static_cast<int>(total * c / g);
+}
+// The CTA whose range contains global token x.
+__device__ __forceinline__ int owner_cta(int64_t total, int x, int g) {
+  const int64_t c = ((static_cast<int64_t>(x) + 1) * g - 1) / total;
+  return static_cast<int>(c < g - 1 ? c : g - 1);
+}
+
+// Merge the n_parts split-K partials of sequence b for the G query heads of KV head w
+// (one warp). Lane l owns head dims 4l..4l+3 of every head; lane i also holds the (max,
+// sum) of parts i, i+32, ... All loads of a batch of parts are issued before the
+// reductions that consume them, so a merge of up to 32 parts costs about two L2 round
+// trips. Partials are read with ld.global.cg: they were written by other SMs.
+template <class C>
+__device__ __forceinline__ void merge_partials(const DecodeArgs &a, int first, int n_parts,
+                                               int b, int w, int lane) {
+  constexpr int G = C::H / (C::THREADS / 32 - 1);
+  constexpr int MB = G == 1 ? 8 : (G == 2 ? 4 : 2);  // parts per batch of loads (registers)
+  const float2 *ml = reinterpret_cast<const float2 *>(a.ws_ml) +
+                     static_cast<int64_t>(first) * C::H + w * G;
+  const float4 *os = reinterpret_cast<const float4 *>(a.ws_o) +
+                     (static_cast<int64_t>(first) * C::H + w * G) * (kDecD / 4) + lane;
+  constexpr int64_t kPartStride = static_cast<int64_t>(C::H) * (kDecD / 4);
+  float2 mine[G];
+  float4 v[MB][G];
+#pragma unroll
+  for (int g = 0; g < G; ++g)
+    mine[g] = lane < n_parts ? __ldcg(ml + static_cast<int64_t>(lane) * C::H + g)
+                             : make_float2(-INFINITY, 0.f);
+#pragma unroll
+  for (int jj = 0; jj < MB; ++jj)
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+      v[jj][g] = jj < n_parts ? __ldcg(os + jj * kPartStride + g * (kDecD / 4))
+                              : make_float4(0.f, 0.f, 0.f, 0.f);
+  float mm[G], lsum[G], acc[G][4];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    float m = mine[g].x;
+    for (int i = lane + 32; i < n_parts; i += 32)
+      m = fmaxf(m, __ldcg(ml + static_cast<int64_t>(i) * C::H + g).x);
+    mm[g] = warp_max(m);
+    lsum[g] = 0.f;
+    acc[g][0] = acc[g][1] = acc[g][2] = acc[g][3] = 0.f;
+  }
+  for (int i0 = 0; i0 < n_parts; i0 += 32) {
+    float wgt[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const bool ok = i0 + lane < n_parts;
+      const float2 sm = i0 == 0 ? mine[g]
+                                : (ok ? __ldcg(ml + static_cast<int64_t>(i0 + lane) * C::H + g)
+                                      : make_float2(-INFINITY, 0.f));
+      wgt[g] = ok ? exp2f(sm.x - mm[g]) : 0.f;
+      lsum[g] += ok ? sm.y * wgt[g] : 0.f;
+    }
+    const int cnt = min(32, n_parts - i0);
+    for (int j0 = 0; j0 < cnt; j0 += MB) {
+      if (i0 + j0 > 0) {  // the first batch was loaded above
+#pragma unroll
+        for (int jj = 0; jj < MB; ++jj)
+#pragma unroll
+          for (int g = 0; g < G; ++g)
+            v[jj][g] = j0 + jj < cnt
+                           ? __ldcg(os + (i0 + j0 + jj) * kPartStride + g * (kDecD / 4))
+                           : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int jj = 0; jj < MB; ++jj)
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          const float wj = __shfl_sync(0xffffffffu, wgt[g], j0 + jj);  // 0 past cnt
+          acc[g][0] += v[jj][g].x * wj;
+          acc[g][1] += v[jj][g].y * wj;
+          acc[g][2] += v[jj][g].z * wj;
+          acc[g][3] += v[jj][g].w * wj;
+        }
+    }
+  }
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    const float inv = 1.f / warp_sum(lsum[g]);
+    __nv_bfloat16 *dst = a.out + b * a.out_stride + (w * G + g) * kDecD + lane * 4;
+    *reinterpret_cast<uint2 *>(dst) = make_uint2(pack2(acc[g][0] * inv, acc[g][1] * inv),
+                                                 pack2(acc[g][2] * inv, acc[g][3] * inv));
+  }
+}
+
 template <int HKV, int G>
 __global__ void __launch_bounds__(Dec<HKV, G>::THREADS, 1)
-    paged_decode_kernel(const DecodeArgs a) {
+    paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
+                        const __grid_constant__ CUtensorMap tm_v, const DecodeArgs a) {
   using C = Dec<HKV, G>;
-  extern __shared__ __align__(128) uint8_t smem[];
-  uint8_t *ks = smem;
-  uint8_t *vs = smem + kDecStages * C::STAGE_BYTES;
-  float *merge = reinterpret_cast<float *>(smem + 2 * kDecStages * C::STAGE_BYTES);
-  int *item_start = reinterpret_cast<int *>(merge + C::MERGE_FLOATS);
-  uint64_t *full = reinterpret_cast<uint64_t *>(item_start + kDecMaxBatch + 1 + 1);
-  // (+1 int of padding keeps the barriers 8-byte aligned for any batch)
-  full = reinterpret_cast<uint64_t *>((reinterpret_cast<uintptr_t>(full) + 7) & ~uintptr_t(7));
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                              ~uintptr_t(1023));
+  uint8_t *stages = smem;
+  int *s_cuk = reinterpret_cast<int *>(smem + kDecStages * C::STAGE_BYTES);  // [B + 1]
+  int *s_parts = s_cuk + kDecMaxBatch + 1;                                    // [B + 1]
+  int *s_first = s_parts + kDecMaxBatch + 1;                                  // [B]
+  uint64_t *full = reinterpret_cast<uint64_t *>(
+      (reinterpret_cast<uintptr_t>(s_first + kDecMaxBatch + 1) + 7) & ~uintptr_t(7));
   uint64_t *empty = full + kDecStages;
+  StageInfo *info = reinterpret_cast<StageInfo *>(empty + kDecStages);
   __shared__ int abort_flag;
+  __shared__ int merge_owner;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int B = a.batch;
 
-  // Item prefix over sequences (warp 0, 32 sequences per pass).
-  if (warp == 0) {
+  for (int i = tid; i <= B; i += blockDim.x) s_cuk[i] = a.cu_seqlens_k[i];
+  if (tid == 0) {
+    abort_flag = 0;
+    for (int s = 0; s < kDecStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], HKV);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+  const int64_t total = s_cuk[B] - s_cuk[0];
+  const int64_t by_len = total / kDecStage;  // at least a stage's worth of tokens per CTA
+  const int geff = static_cast<int>(by_len < 1 ? 1 : (by_len < gridDim.x ? by_len : gridDim.x));
+  const bool has_work = total > 0 && static_cast<int>(blockIdx.x) < geff;
+
+  if (warp == HKV) {
+    // ------------------------------------------------------------------ producer
+    if (lane == 0) {
+      prefetch_tmap(&tm_k);
+      prefetch_tmap(&tm_v);
+    }
+    uint32_t it_stage = 0;
+    auto acquire = [&](int &st) -> bool {
+      st = it_stage % kDecStages;
+      const uint32_t ph = (it_stage / kDecStages) & 1;
+      int ok = 1;
+      if (lane == 0) ok = mbar_wait(&empty[st], ph ^ 1, a.error_flag, &abort_flag);
+      return __shfl_sync(0xffffffffu, ok, 0) != 0;
+    };
+    if (has_work) {
+      const int c = blockIdx.x;
+      int pos = part_begin(total, c, geff);
+      const int end = part_begin(total, c + 1, geff);
+      int b = upper_index(s_cuk, B + 1, pos + s_cuk[0]);
+      while (pos < end) {
+        while (s_cuk[b + 1] - s_cuk[0] <= pos) ++b;  // skip empty sequences
+        const int seq0 = s_cuk[b] - s_cuk[0], seq1 = s_cuk[b + 1] - s_cuk[0];
+        const int seg1 = min(end, seq1);
+        const int p0 = pos - seq0, p1 = seg1 - seq0;
+        const bool whole = pos == seq0 && seg1 == seq1;
+        // block ids of this segment, one per lane (a segment spans few blocks)
+        const int blk0 = p0 / a.block_size;
+        const int nblk = (p1 - 1) / a.block_size - blk0 + 1;
+        int my_block = 0;
+        if (lane < nblk) {
+          my_block = a.block_tables[static_cast<int64_t>(b) * a.bt_stride + blk0 + lane];
+          if (my_block < 0 || my_block >= a.num_blocks) {
+            raise_flag(a.error_flag, B200ASR_DEVERR_BLOCK);
+            my_block = 0;
+          }
+        }
+        for (int t = p0; t < p1;) {
+          const int n = min(min(kDecStage, p1 - t), a.block_size - t % a.block_size);
+          const int blk = __shfl_sync(0xffffffffu, my_block, min(31, t / a.block_size - blk0));
+          int st;
+          if (!acquire(st)) return;
+          const bool first = t == p0, last = t + n == p1;
+          if (lane == 0) {
+            info[st] = StageInfo{b, n, (first ? 1 : 0) | (last ? 2 : 0) | (whole ? 4 : 0)};
+            mbar_arrive_expect_tx(&full[st], C::TX_KV + (first ? C::TX_Q : 0));
+          }
+          __syncwarp();
+          uint8_t *stage = stages + st * C::STAGE_BYTES;
+          const int slot = blk * a.block_size + t % a.block_size;
+          if (lane < 4 * HKV) {
+            const int kind = lane / (2 * HKV), head = (lane >> 1) % HKV, dh = lane & 1;
+            tma_load_3d(stage + kind * C::KV_BYTES + head * C::HEAD_TILE + dh * 2048,
+                        kind ? &tm_v : &tm_k, dh * 64, head, slot, &full[st]);
+          }
+          if (first && lane == 31)
+            bulk_g2s(stage + 2 * C::KV_BYTES, a.q + b * a.q_stride, C::TX_Q, &full[st]);
+          ++it_stage;
+          t += n;
+        }
+        pos = seg1;
+      }
+    }
+    int st;  // terminal stage: tells the consumers to stop
+    if (!acquire(st)) return;
+    if (lane == 0) {
+      info[st] = StageInfo{-1, 0, 0};
+      mbar_arrive(&full[st]);
+    }
+    return;
+  }
+
+  // -------------------------------------------------------------------- consumers
+  if (warp == 0) {  // per sequence: first owning CTA + prefix of partial slots
     int carry = 0;
-    for (int b0 = 0; b0 < a.batch; b0 += 32) {
+    for (int b0 = 0; b0 < B; b0 += 32) {
       const int b = b0 + lane;
-      int n = 0;
-      if (b < a.batch) n = (a.cu_seqlens_k[b + 1] - a.cu_seqlens_k[b] + kDecChunk - 1) / kDecChunk;
-      int incl = n;
+      int parts = 0, first = 0;
+      if (b < B && total > 0) {
+        const int x0 = s_cuk[b] - s_cuk[0], x1 = s_cuk[b + 1] - s_cuk[0];
+        if (x1 > x0) {
+          first = owner_cta(total, x0, geff);
+          parts = owner_cta(total, x1 - 1, geff) - first + 1;
+        }
+      }
+      int incl = parts;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
         const int y = __shfl_up_sync(0xffffffffu, incl, o);
         if (lane >= o) incl += y;
       }
-      if (b < a.batch) item_start[b] = carry + incl - n;
+      if (b < B) {
+        s_parts[b] = carry + incl - parts;
+        s_first[b] = first;
+      }
       carry += __shfl_sync(0xffffffffu, incl, 31);
     }
-    if (lane == 0) item_start[a.batch] = carry;
-  }
-  if (tid == 0) {
-    abort_flag = 0;
-    for (int s = 0; s < kDecStages; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], C::CONSUMERS);
-    }
-    fence_barrier_init();
-  }
-  __syncthreads();
-  int total = item_start[a.batch];
-  if (total > a.items_cap) {
-    if (tid == 0) raise_flag(a.error_flag, B200ASR_DEVERR_LENGTH);
-    total = a.items_cap;
-  }
-
-  if (warp == C::CONSUMERS) {
-    // ------------------------------------------------------------ producer
     if (lane == 0) {
-      uint32_t it_stage = 0;
-      for (int it = blockIdx.x; it < total; it += gridDim.x) {
-        const int b = item_seq(item_start, a.batch, it);
-        const int c = it - item_start[b];
-        const int len = a.cu_seqlens_k[b + 1] - a.cu_seqlens_k[b];
-        const int start = c * kDecChunk;
-        const int n = min(kDecChunk, len - start);
-        int block = a.block_tables[static_cast<int64_t>(b) * a.bt_stride + start / a.block_size];
-        if (block < 0 || block >= a.num_blocks) {
-          raise_flag(a.error_flag, B200ASR_DEVERR_BLOCK);
-          block = 0;
-        }
-        const int64_t slot0 = static_cast<int64_t>(block) * a.block_size + (start % a.block_size);
-        for (int s0 = 0; s0 < n; s0 += kDecStage, ++it_stage) {
-          const int st = it_stage % kDecStages;
-          const uint32_t ph = (it_stage / kDecStages) & 1;
-          if (!mbar_wait(&empty[st], ph ^ 1, a.error_flag, &abort_flag)) return;
-          const int ntok = min(kDecStage, n - s0);
-          const uint32_t bytes = ntok * C::ROW_BYTES;
-          mbar_arrive_expect_tx(&full[st], 2 * bytes);
-          const int64_t off = (slot0 + s0) * C::ROW;
-          bulk_g2s(ks + st * C::STAGE_BYTES, a.k_cache + off, bytes, &full[st]);
-          bulk_g2s(vs + st * C::STAGE_BYTES, a.v_cache + off, bytes, &full[st]);
-        }
+      s_parts[B] = carry;  // <= B + geff - 1 <= parts_cap by construction
+      if (carry > a.parts_cap) raise_flag(a.error_flag, B200ASR_DEVERR_LENGTH);
+    }
+  }
+  consumer_sync(HKV * 32);
+  const bool parts_ok = s_parts[B] <= a.parts_cap;
+  const int w = warp;               // KV head of this warp
+  const int row = lane >> 2;        // MMA row = query head within the group (valid if < G)
+  const int quad = lane & 3;
+  const bool row_valid = row < G;
+  const uint32_t stage_base = smem_addr(stages);
+  const int lm_mat = lane >> 3, lm_row = lane & 7;  // ldmatrix: matrix and row of this lane
+
+  if (blockIdx.x == 0) {  // rows with no keys: zeros (nothing else writes them)
+    for (int b = w; b < B; b += HKV) {
+      if (s_cuk[b + 1] - s_cuk[b] <= 0) {
+        for (int i = lane; i < C::H * kDecD / 8; i += 32)
+          reinterpret_cast<uint4 *>(a.out + b * a.out_stride)[i] = make_uint4(0, 0, 0, 0);
       }
     }
-    return;
   }
 
-  // -------------------------------------------------------------- consumers
-  const int w = warp % HKV;      // KV head
-  const int half = warp / HKV;   // token half of each stage
-  const int my_j = lane >> C::SHIFT;
-  const int my_t = my_j >> C::LOG2G;
-  const int my_g = my_j & (G - 1);
-  uint32_t it_stage = 0;
+  uint32_t qa[8][2];
+  float o[16][4];
+  float m_run = -INFINITY, l_run = 0.f;
+  for (uint32_t it_stage = 0;; ++it_stage) {
+    const int st = it_stage % kDecStages;
+    const uint32_t ph = (it_stage / kDecStages) & 1;
+    if (!mbar_wait(&full[st], ph, a.error_flag, &abort_flag)) return;
+    const StageInfo si = info[st];
+    if (si.b < 0) break;
+    const int ntok = si.ntok;
+    const uint32_t k_tile = stage_base + st * C::STAGE_BYTES + w * C::HEAD_TILE;
+    const uint32_t v_tile = k_tile + C::KV_BYTES;
 
-  for (int it = blockIdx.x; it < total; it += gridDim.x) {
-    const int b = item_seq(item_start, a.batch, it);
-    const int c = it - item_start[b];
-    const int len = a.cu_seqlens_k[b + 1] - a.cu_seqlens_k[b];
-    const int n = min(kDecChunk, len - c * kDecChunk);
-    const bool single = len <= kDecChunk;
-
-    float qv[G][4];
+    if (si.flags & 1) {  // first stage of a segment: fresh state + this sequence's query
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-      const uint2 u = *reinterpret_cast<const uint2 *>(
-          a.q + b * a.q_stride + (w * G + g) * kDecD + lane * 4);
-      qv[g][0] = __uint_as_float(u.x << 16) * a.scale_log2;
-      qv[g][1] = __uint_as_float(u.x & 0xffff0000u) * a.scale_log2;
-      qv[g][2] = __uint_as_float(u.y << 16) * a.scale_log2;
-      qv[g][3] = __uint_as_float(u.y & 0xffff0000u) * a.scale_log2;
+      for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+      m_run = -INFINITY;
+      l_run = 0.f;
+      const uint8_t *qs = stages + st * C::STAGE_BYTES + 2 * C::KV_BYTES +
+                          (w * G + (row_valid ? row : 0)) * kDecD * 2;
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        const uint32_t lo = *reinterpret_cast<const uint32_t *>(qs + (kk * 16 + quad * 2) * 2);
+        const uint32_t hi = *reinterpret_cast<const uint32_t *>(qs + (kk * 16 + 8 + quad * 2) * 2);
+        qa[kk][0] = row_valid ? lo : 0u;
+        qa[kk][1] = row_valid ? hi : 0u;
+      }
     }
-    float acc[G][4], m[G], l[G];
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-      m[g] = -INFINITY;
-      l[g] = 0.f;
-#pragma unroll
-      for (int k = 0; k < 4; ++k) acc[g][k] = 0.f;
-    }
-
-    for (int s0 = 0; s0 < n; s0 += kDecStage, ++it_stage) {
-      const int st = it_stage % kDecStages;
-      const uint32_t ph = (it_stage / kDecStages) & 1;
-      if (!mbar_wait(&full[st], ph, a.error_flag, &abort_flag)) return;
-      const int ntok = min(kDecStage, n - s0);
-      const uint8_t *kt = ks + st * C::STAGE_BYTES + (w * kDecD + lane * 4) * 2;
-      const uint8_t *vt = vs + st * C::STAGE_BYTES + (w * kDecD + lane * 4) * 2;
-
-      // Partial dot products of this lane's 4 dims for 8 tokens x G heads.
-      float part[C::NV];
-#pragma unroll
-      for (int t = 0; t < kDecHalf; ++t) {
-        const int tt = half * kDecHalf + t;
-        float kf[4] = {0.f, 0.f, 0.f, 0.f};
-        if (tt < ntok) {
-          const uint2 u = *reinterpret_cast<const uint2 *>(kt + tt * C::ROW_BYTES);
-          kf[0] = __uint_as_float(u.x << 16);
-          kf[1] = __uint_as_float(u.x & 0xffff0000u);
-          kf[2] = __uint_as_float(u.y << 16);
-          kf[3] = __uint_as_float(u.y & 0xffff0000u);
-        }
-#pragma unroll
-        for (int g = 0; g < G; ++g)
-          part[t * G + g] = qv[g][0] * kf[0] + qv[g][1] * kf[1] + qv[g][2] * kf[2] + qv[g][3] * kf[3];
-      }
-      // Butterfly reduce-scatter: lane ends with the full score of index lane >> SHIFT.
-#pragma unroll
-      for (int step = 0; step < C::LOG2NV; ++step) {
-        const int hn = C::NV >> (step + 1);
-        const int mask = 16 >> step;
-        const bool upper = (lane & mask) != 0;
-#pragma unroll
-        for (int i = 0; i < hn; ++i) {
-          const float send = upper ? part[i] : part[i + hn];
-          const float keep = upper ? part[i + hn] : part[i];
-          part[i] = keep + __shfl_xor_sync(0xffffffffu, send, mask);
-        }
-      }
-#pragma unroll
-      for (int mask = 16 >> C::LOG2NV; mask >= 1; mask >>= 1)
-        part[0] += __shfl_xor_sync(0xffffffffu, part[0], mask);
-
-      const bool valid = half * kDecHalf + my_t < ntok;
-      const float s = valid ? part[0] : -INFINITY;
-      // Per-head max over this half's tokens: reduce across the lane bits that hold t.
-      float mx = s;
-#pragma unroll
-      for (int bit = C::SHIFT + C::LOG2G; bit < 5; ++bit)
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1 << bit));
-      float alpha[G], mnew[G];
-#pragma unroll
-      for (int g = 0; g < G; ++g) {
-        const float ms = __shfl_sync(0xffffffffu, mx, g << C::SHIFT);
-        mnew[g] = fmaxf(m[g], ms);
-        alpha[g] = mnew[g] == -INFINITY ? 1.f : exp2f(m[g] - mnew[g]);
-      }
-      float mine_m = mnew[0];
-#pragma unroll
-      for (int g = 1; g < G; ++g)
-        if (my_g == g) mine_m = mnew[g];
-      const float p = (valid && mine_m != -INFINITY) ? exp2f(s - mine_m) : 0.f;
-      float ps = p;
-#pragma unroll
-      for (int bit = C::SHIFT + C::LOG2G; bit < 5; ++bit)
-        ps += __shfl_xor_sync(0xffffffffu, ps, 1 << bit);
-#pragma unroll
-      for (int g = 0; g < G; ++g) {
-        const float ls = __shfl_sync(0xffffffffu, ps, g << C::SHIFT);
-        l[g] = l[g] * alpha[g] + ls;
-        m[g] = mnew[g];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) acc[g][k] *= alpha[g];
-      }
-      // P V for this half's tokens.
-#pragma unroll
-      for (int t = 0; t < kDecHalf; ++t) {
-        const int tt = half * kDecHalf + t;
-        if (tt < ntok) {
-          const uint2 u = *reinterpret_cast<const uint2 *>(vt + tt * C::ROW_BYTES);
-          const float v0 = __uint_as_float(u.x << 16), v1 = __uint_as_float(u.x & 0xffff0000u);
-          const float v2 = __uint_as_float(u.y << 16), v3 = __uint_as_float(u.y & 0xffff0000u);
-#pragma unroll
-          for (int g = 0; g < G; ++g) {
-            const float pg = __shfl_sync(0xffffffffu, p, ((t * G + g) << C::SHIFT));
-            acc[g][0] += pg * v0;
-            acc[g][1] += pg * v1;
-            acc[g][2] += pg * v2;
-            acc[g][3] += pg * v3;
-          }
-        }
+    if (ntok < kDecStage) {  // clear V rows past the end so 0 * stale bytes stays 0
+      uint8_t *vt = stages + st * C::STAGE_BYTES + C::KV_BYTES + w * C::HEAD_TILE;
+      for (int i = lane; i < (kDecStage - ntok) * 16; i += 32) {
+        const int r = ntok + i / 16, ch = i % 16;
+        *reinterpret_cast<uint4 *>(vt + (ch >> 3) * 2048 + swz(r, ch & 7)) = make_uint4(0, 0, 0, 0);
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[st]);
     }
 
-    // Merge the two token halves of this item.
-    float *mine = merge + (w * 32 + lane) * (4 * G);
-    float *ml = merge + HKV * 32 * (4 * G) + w * 2 * G;
-    if (half == 1) {
+    // S = Q K^T for tokens 0-7 (n-tile 0) and 8-15 (n-tile 1).
+    float s[2][4];
 #pragma unroll
-      for (int g = 0; g < G; ++g) {
+    for (int nt = 0; nt < 2; ++nt) {
+      s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
 #pragma unroll
-        for (int k = 0; k < 4; ++k) mine[g * 4 + k] = acc[g][k];
-        if (lane == 0) {
-          ml[2 * g] = m[g];
-          ml[2 * g + 1] = l[g];
-        }
+      for (int kp = 0; kp < 4; ++kp) {  // k-steps 2kp, 2kp+1 = 16-byte chunks 4kp..4kp+3
+        const int chunk = 4 * kp + lm_mat;
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4(k_tile + (chunk >> 3) * 2048 + swz(nt * 8 + lm_row, chunk & 7), b0, b1, b2, b3);
+        mma16816(s[nt], qa[2 * kp][0], 0u, qa[2 * kp][1], 0u, b0, b1);
+        mma16816(s[nt], qa[2 * kp + 1][0], 0u, qa[2 * kp + 1][1], 0u, b2, b3);
       }
     }
-    consumer_barrier(C::CONSUMERS * 32);
-    if (half == 0) {
+    // Online softmax on rows (one query head per quad), base 2.
+    float mx = -INFINITY;
 #pragma unroll
-      for (int g = 0; g < G; ++g) {
-        const float m1 = ml[2 * g], l1 = ml[2 * g + 1];
-        const float mm = fmaxf(m[g], m1);
-        const float a0 = m[g] == -INFINITY ? 0.f : exp2f(m[g] - mm);
-        const float a1 = m1 == -INFINITY ? 0.f : exp2f(m1 - mm);
-        const float lt = l[g] * a0 + l1 * a1;
-        float o[4];
+    for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-        for (int k = 0; k < 4; ++k) o[k] = acc[g][k] * a0 + mine[g * 4 + k] * a1;
-        const int h = w * G + g;
-        if (single) {
-          const float inv = 1.f / lt;
-          uint2 u;
-          u.x = pack2(o[0] * inv, o[1] * inv);
-          u.y = pack2(o[2] * inv, o[3] * inv);
-          *reinterpret_cast<uint2 *>(a.out + b * a.out_stride + h * kDecD + lane * 4) = u;
-        } else {
-          float4 *dst = reinterpret_cast<float4 *>(a.ws_o + (static_cast<int64_t>(it) * C::H + h) * kDecD) + lane;
-          *dst = make_float4(o[0], o[1], o[2], o[3]);
-          if (lane == 0) {
-            a.ws_ml[(static_cast<int64_t>(it) * C::H + h) * 2] = mm;
-            a.ws_ml[(static_cast<int64_t>(it) * C::H + h) * 2 + 1] = lt;
-          }
-        }
+      for (int e = 0; e < 2; ++e) {
+        const int t = nt * 8 + quad * 2 + e;
+        s[nt][e] = t < ntok ? s[nt][e] * a.scale_log2 : -INFINITY;
+        mx = fmaxf(mx, s[nt][e]);
       }
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    const float m_new = fmaxf(m_run, mx);  // token 0 of every stage is valid: finite
+    const float alpha = exp2f(m_run - m_new);
+    float p[2][2], sum = 0.f;
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        p[nt][e] = exp2f(s[nt][e] - m_new);
+        sum += p[nt][e];
+      }
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+    l_run = l_run * alpha + sum;
+    m_run = m_new;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      o[j][0] *= alpha;
+      o[j][1] *= alpha;
     }
-    consumer_barrier(C::CONSUMERS * 32);
-  }
-}
+    // O += P V: P (16 rows x 16 tokens) straight from the score registers.
+    const uint32_t pa0 = row_valid ? pack2(p[0][0], p[0][1]) : 0u;
+    const uint32_t pa2 = row_valid ? pack2(p[1][0], p[1][1]) : 0u;
+#pragma unroll
+    for (int nd = 0; nd < 8; ++nd) {  // 16 head dims = chunks 2nd, 2nd+1
+      const int chunk = 2 * nd + (lm_mat >> 1);
+      const int trow = (lm_mat & 1) * 8 + lm_row;
+      uint32_t b0, b1, b2, b3;
+      ldsm_x4_t(v_tile + (chunk >> 3) * 2048 + swz(trow, chunk & 7), b0, b1, b2, b3);
+      mma16816(o[2 * nd], pa0, 0u, pa2, 0u, b0, b1);
+      mma16816(o[2 * nd + 1], pa0, 0u, pa2, 0u, b2, b3);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[st]);
+    if (!(si.flags & 2)) continue;
 
-// Merge the per-item partials of every sequence longer than one item.
-// One CTA per sequence, H x 32 threads; thread (h, lane) owns dims 4*lane..+3.
-template <int H>
-__global__ void decode_combine_kernel(const DecodeArgs a) {
-  const int b = blockIdx.x;
-  const int h = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // Items before this sequence: warp-parallel sum over the preceding lengths.
-  int first = 0;
-  for (int i0 = 0; i0 < b; i0 += 32) {
-    const int i = i0 + lane;
-    int n_i = 0;
-    if (i < b) n_i = (a.cu_seqlens_k[i + 1] - a.cu_seqlens_k[i] + kDecChunk - 1) / kDecChunk;
-    first += n_i;
-  }
+    // ---------------------------------------------------------- segment epilogue
+    const int b = si.b;
+    const int h = w * G + row;
+    if (si.flags & 4) {
+      if (row_valid) {
+        const float inv = 1.f / l_run;
+        __nv_bfloat16 *dst = a.out + b * a.out_stride + h * kDecD + quad * 2;
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) first += __shfl_xor_sync(0xffffffffu, first, o);
-  const int len = a.cu_seqlens_k[b + 1] - a.cu_seqlens_k[b];
-  const int n = (len + kDecChunk - 1) / kDecChunk;
-  __nv_bfloat16 *dst = a.out + b * a.out_stride + h * kDecD + lane * 4;
-  if (n == 1) return;
-  if (n <= 0 || first + n > a.items_cap) {
-    *reinterpret_cast<uint2 *>(dst) = make_uint2(0u, 0u);
-    return;
+        for (int j = 0; j < 16; ++j)
+          *reinterpret_cast<uint32_t *>(dst + j * 8) = pack2(o[j][0] * inv, o[j][1] * inv);
+      }
+      continue;
+    }
+    if (!parts_ok) continue;
+    const int part = s_parts[b] + (static_cast<int>(blockIdx.x) - s_first[b]);
+    if (row_valid) {
+      float *dst = a.ws_o + (static_cast<int64_t>(part) * C::H + h) * kDecD + quad * 2;
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+        *reinterpret_cast<float2 *>(dst + j * 8) = make_float2(o[j][0], o[j][1]);
+      if (quad == 0)
+        *reinterpret_cast<float2 *>(a.ws_ml + (static_cast<int64_t>(part) * C::H + h) * 2) =
+            make_float2(m_run, l_run);
+    }
+    const int n_parts = s_parts[b + 1] - s_parts[b];
+    consumer_sync(HKV * 32);
+    if (tid == 0) {
+      // Release this CTA's partial (cumulative over the barrier) and count it; the CTA
+      // that brings the count to n_parts acquires every other partial and merges.
+      int done;
+      asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;"
+                   : "=r"(done)
+                   : "l"(a.counters + b)
+                   : "memory");
+      merge_owner = done == n_parts - 1;
+      if (merge_owner) a.counters[b] = 0;  // every partial has arrived: ready for the next call
+    }
+    consumer_sync(HKV * 32);
+    if (merge_owner) merge_partials<C>(a, s_parts[b], n_parts, b, w, lane);
   }
-  float mm = -INFINITY;
-#pragma unroll 8
-  for (int i = 0; i < n; ++i) mm = fmaxf(mm, a.ws_ml[(static_cast<int64_t>(first + i) * H + h) * 2]);
-  float lt = 0.f, o[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 8
-  for (int i = 0; i < n; ++i) {
-    const int64_t base = static_cast<int64_t>(first + i) * H + h;
-    const float mi = a.ws_ml[base * 2];
-    const float w = mi == -INFINITY ? 0.f : exp2f(mi - mm);
-    lt += a.ws_ml[base * 2 + 1] * w;
-    const float4 v = reinterpret_cast<const float4 *>(a.ws_o + base * kDecD)[lane];
-    o[0] += v.x * w;
-    o[1] += v.y * w;
-    o[2] += v.z * w;
-    o[3] += v.w * w;
-  }
-  const float inv = 1.f / lt;
-  *reinterpret_cast<uint2 *>(dst) = make_uint2(pack2(o[0] * inv, o[1] * inv), pack2(o[2] * inv, o[3] * inv));
 }
 
 int num_sms() {
@@ -399,7 +526,8 @@ int num_sms() {
 }
 
 template <int HKV, int G>
-int launch_decode(const DecodeArgs &a, cudaStream_t stream) {
+int launch_decode(const DecodeArgs &a, const void *k_cache, const void *v_cache,
+                  int64_t num_slots, cudaStream_t stream) {
   using C = Dec<HKV, G>;
   static bool configured = false;
   if (!configured) {
@@ -413,17 +541,20 @@ int launch_decode(const DecodeArgs &a, cudaStream_t stream) {
     }
     configured = true;
   }
-  const int grid = std::max(1, std::min(a.items_cap, num_sms()));
-  paged_decode_kernel<HKV, G><<<grid, C::THREADS, C::SMEM, stream>>>(a);
+  CUtensorMap tk, tv;
+  if (!make_tmap_3d_bf16(&tk, k_cache, kDecD, HKV, num_slots, kDecD * 2, HKV * kDecD * 2ull, 64,
+                         1, kDecStage) ||
+      !make_tmap_3d_bf16(&tv, v_cache, kDecD, HKV, num_slots, kDecD * 2, HKV * kDecD * 2ull, 64,
+                         1, kDecStage))
+    return B200ASR_ERR_CUDA;
+  const int grid = std::min(num_sms(), kDecMaxGrid);
+  paged_decode_kernel<HKV, G><<<grid, C::THREADS, C::SMEM, stream>>>(tk, tv, a);
   B200_CUDA_LAUNCH_CHECK("paged_decode");
-  decode_combine_kernel<C::H><<<a.batch, C::H * 32, 0, stream>>>(a);
-  B200_CUDA_LAUNCH_CHECK("paged_decode_combine");
   return B200ASR_OK;
 }
 
-size_t decode_items_cap(int batch, int max_seqlen_k) {
-  return static_cast<size_t>(batch) * ((std::max(max_seqlen_k, 1) + kDecChunk - 1) / kDecChunk);
-}
+// Partials: every sequence contributes at most one per CTA boundary it straddles plus one.
+size_t decode_parts_cap(int batch) { return static_cast<size_t>(batch) + kDecMaxGrid; }
 
 }  // namespace b200asr
 
@@ -432,8 +563,9 @@ using namespace b200asr;
 extern "C" size_t b200asr_paged_decode_workspace_size(int32_t batch, int32_t max_seqlen_k,
                                                       int32_t num_heads, int32_t head_dim) {
   if (batch <= 0 || num_heads <= 0 || head_dim <= 0) return 0;
-  const size_t items = decode_items_cap(batch, max_seqlen_k);
-  return items * num_heads * (static_cast<size_t>(head_dim) + 2) * sizeof(float) + 256;
+  (void)max_seqlen_k;  // the stream-K split bounds the partials by batch + grid, not length
+  const size_t parts = decode_parts_cap(batch);
+  return kDecHeaderBytes + parts * num_heads * (static_cast<size_t>(head_dim) + 2) * sizeof(float);
 }
 
 extern "C" int b200asr_paged_decode(const void *q, int64_t q_row_stride, const void *k_cache,
@@ -448,17 +580,17 @@ extern "C" int b200asr_paged_decode(const void *q, int64_t q_row_stride, const v
   B200_REQUIRE(batch >= 0 && batch <= kDecMaxBatch, "paged_decode: batch %d not in [0, %d]",
                batch, kDecMaxBatch);
   if (batch == 0) return B200ASR_OK;
-  B200_REQUIRE(block_size >= kDecChunk && block_size % kDecChunk == 0,
-               "paged_decode: block_size %d must be a multiple of %d", block_size, kDecChunk);
+  B200_REQUIRE(block_size >= kDecStage && block_size % kDecStage == 0,
+               "paged_decode: block_size %d must be a multiple of %d", block_size, kDecStage);
   B200_REQUIRE(num_blocks >= 1 && bt_stride >= 1 && max_seqlen_k >= 1,
                "paged_decode: bad table geometry");
   B200_REQUIRE(q && k_cache && v_cache && cu_seqlens_k && block_tables && out && workspace,
                "paged_decode: null pointer");
-  B200_REQUIRE(q_row_stride % 4 == 0 && out_row_stride % 4 == 0 &&
-                   (reinterpret_cast<uintptr_t>(q) & 7) == 0 &&
-                   (reinterpret_cast<uintptr_t>(out) & 7) == 0 && aligned16(k_cache) &&
-                   aligned16(v_cache) && aligned16(workspace),
-               "paged_decode: misaligned tensor");
+  B200_REQUIRE(q_row_stride >= static_cast<int64_t>(num_heads) * head_dim && q_row_stride % 8 == 0 &&
+                   out_row_stride % 4 == 0 && aligned16(q) && aligned16(k_cache) &&
+                   aligned16(v_cache) && aligned16(workspace) &&
+                   (reinterpret_cast<uintptr_t>(out) & 7) == 0,
+               "paged_decode: misaligned tensor (q rows must be contiguous and 16-byte aligned)");
   const size_t need = b200asr_paged_decode_workspace_size(batch, max_seqlen_k, num_heads, head_dim);
   if (workspace_bytes < need) {
     set_error("paged_decode: workspace %zu bytes < %zu needed", workspace_bytes, need);
@@ -467,8 +599,6 @@ extern "C" int b200asr_paged_decode(const void *q, int64_t q_row_stride, const v
   DecodeArgs a;
   a.q = static_cast<const __nv_bfloat16 *>(q);
   a.q_stride = q_row_stride;
-  a.k_cache = static_cast<const __nv_bfloat16 *>(k_cache);
-  a.v_cache = static_cast<const __nv_bfloat16 *>(v_cache);
   a.num_blocks = num_blocks;
   a.block_size = block_size;
   a.cu_seqlens_k = cu_seqlens_k;
@@ -478,15 +608,17 @@ extern "C" int b200asr_paged_decode(const void *q, int64_t q_row_stride, const v
   a.scale_log2 = scale * kLog2e;
   a.out = static_cast<__nv_bfloat16 *>(out);
   a.out_stride = out_row_stride;
-  a.items_cap = static_cast<int>(decode_items_cap(batch, max_seqlen_k));
-  a.ws_o = static_cast<float *>(workspace);
-  a.ws_ml = a.ws_o + static_cast<size_t>(a.items_cap) * num_heads * head_dim;
+  a.parts_cap = static_cast<int>(decode_parts_cap(batch));
+  a.counters = static_cast<int *>(workspace);
+  a.ws_ml = reinterpret_cast<float *>(static_cast<uint8_t *>(workspace) + kDecHeaderBytes);
+  a.ws_o = a.ws_ml + static_cast<size_t>(a.parts_cap) * num_heads * 2;
   a.error_flag = error_flag;
-  if (num_kv_heads == 8 && num_heads == 16) return launch_decode<8, 2>(a, stream);
-  if (num_kv_heads == 8 && num_heads == 8) return launch_decode<8, 1>(a, stream);
-  if (num_kv_heads == 4 && num_heads == 16) return launch_decode<4, 4>(a, stream);
-  if (num_kv_heads == 4 && num_heads == 8) return launch_decode<4, 2>(a, stream);
-  if (num_kv_heads == 2 && num_heads == 4) return launch_decode<2, 2>(a, stream);
+  const int64_t slots = static_cast<int64_t>(num_blocks) * block_size;
+  if (num_kv_heads == 8 && num_heads == 16) return launch_decode<8, 2>(a, k_cache, v_cache, slots, stream);
+  if (num_kv_heads == 8 && num_heads == 8) return launch_decode<8, 1>(a, k_cache, v_cache, slots, stream);
+  if (num_kv_heads == 4 && num_heads == 16) return launch_decode<4, 4>(a, k_cache, v_cache, slots, stream);
+  if (num_kv_heads == 4 && num_heads == 8) return launch_decode<4, 2>(a, k_cache, v_cache, slots, stream);
+  if (num_kv_heads == 2 && num_heads == 4) return launch_decode<2, 2>(a, k_cache, v_cache, slots, stream);
   set_error("paged_decode: %d query / %d KV heads unsupported", num_heads, num_kv_heads);
   return B200ASR_ERR_UNSUPPORTED;
 }
@@ -503,16 +635,16 @@ extern "C" int b200asr_paged_decode(const void *q, int64_t q_row_stride, const v
 // The array is a file-scope __device__ symbol of B200ASR_NOALLOC_SCRATCH_BYTES; every GPU
 // that loads the library holds that much memory until the process exits. Host code cannot
 // use the symbol's name as a device address, so on the first call on each device (with
-// that device current) cudaGetSymbolAddress resolves it once and the pointer is cached.
-// That first call may trigger module loading, so it must come before any stream capture.
-// All calls share the one array and nothing in it needs clearing (every partial is written
-// before it is read), so two calls whose kernels overlap on the GPU -- different streams,
-// or graphs replayed concurrently -- race on it and must be serialised by the caller.
-#include <mutex>
-
-namespace b200asr {
+// that device current) cudaGetSymbolAddress resolves it once, the per-sequence merge
+// counters at its head are cleared (they must start at zero; the kernel leaves them at
+// zero), and the pointer is cached. That first call may trigger module loading and
+// synchronises the device, so it must come before any stream capture. All calls share the
+// one array, so two calls whose kernels overlap on the GPU -- different streams, or graphs
+// replayed concurrently -- race on it and must be serialised by the caller.
 
 static __device__ __align__(256) unsigned char g_decode_noalloc_scratch[B200ASR_NOALLOC_SCRATCH_BYTES];
+
+namespace b200asr {
 
 static void *noalloc_scratch(int *status) {
   constexpr int kMaxDevices = 64;
@@ -529,8 +661,9 @@ static void *noalloc_scratch(int *status) {
   if (resolved[dev] == nullptr) {
     void *p = nullptr;
     e = cudaGetSymbolAddress(&p, g_decode_noalloc_scratch);
+    if (e == cudaSuccess && p != nullptr) e = cudaMemset(p, 0, kDecHeaderBytes);
     if (e != cudaSuccess || p == nullptr) {
-      set_error("paged_decode_noalloc: cudaGetSymbolAddress failed on device %d: %s", dev,
+      set_error("paged_decode_noalloc: set-up of the static scratch failed on device %d: %s", dev,
                 cudaGetErrorString(e));
       *status = B200ASR_ERR_CUDA;
       return nullptr;
@@ -554,9 +687,9 @@ extern "C" int b200asr_paged_decode_noalloc(const void *q, int64_t q_row_stride,
   const size_t need =
       b200asr_paged_decode_workspace_size(batch, max_seqlen_k, num_heads, head_dim);
   if (need > static_cast<size_t>(B200ASR_NOALLOC_SCRATCH_BYTES)) {
-    set_error("paged_decode_noalloc: batch %d x max_seqlen_k %d x %d heads needs %zu bytes of "
-              "scratch, more than the built-in %zu; use b200asr_paged_decode with a workspace",
-              batch, max_seqlen_k, num_heads, need,
+    set_error("paged_decode_noalloc: batch %d x %d heads needs %zu bytes of scratch, more than "
+              "the built-in %zu; use b200asr_paged_decode with a workspace",
+              batch, num_heads, need,
               static_cast<size_t>(B200ASR_NOALLOC_SCRATCH_BYTES));
     return B200ASR_ERR_WORKSPACE;
   }

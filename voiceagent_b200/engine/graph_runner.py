@@ -61,7 +61,7 @@ class GraphRunner:
         self.hidden: dict[int, torch.Tensor] = {}
         ws_bytes = kx.paged_decode_workspace_size(m, self.config.max_model_len,
                                                   self.config.model_config.text.num_attention_heads)
-        self.workspace = torch.empty(ws_bytes // 4 + 64, dtype=torch.float32, device=dev)
+        self.workspace = torch.zeros(ws_bytes // 4 + 64, dtype=torch.float32, device=dev)
 
     def _desc_views(self, bucket: int):
         m = self.max_batch

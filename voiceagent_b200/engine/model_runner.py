@@ -72,7 +72,7 @@ class ModelRunner:
         # Split-K workspace so eager decode-only batches run the same kernel as the graphs.
         heads = config.model_config.text.num_attention_heads
         ws = kx.paged_decode_workspace_size(config.max_num_seqs, config.max_model_len, heads)
-        self.decode_workspace = torch.empty(ws // 4 + 64, dtype=torch.float32, device=self.device)
+        self.decode_workspace = torch.zeros(ws // 4 + 64, dtype=torch.float32, device=self.device)
 
     # ------------------------------------------------------------------ cache
 

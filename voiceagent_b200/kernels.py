@@ -189,7 +189,7 @@ def paged_decode(q, k_cache, v_cache, cu_seqlens_k, block_tables, *, max_seqlen_
     batch, num_heads, head_dim = q.shape
     num_blocks, block_size, num_kv_heads, _ = k_cache.shape
     _need(block_tables.dtype == torch.int32 and cu_seqlens_k.dtype == torch.int32, "int32 metadata")
-    _count(2)  # split-K pass + combine
+    _count()  # one stream-K launch; the merge is fused into it
     check(lib.b200asr_paged_decode(
         _p(q), q.stride(0), _p(k_cache), _p(v_cache), num_blocks, block_size, num_heads,
         num_kv_heads, head_dim, _p(cu_seqlens_k), _p(block_tables), block_tables.stride(0), batch,
