@@ -294,6 +294,10 @@ using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_
                                    const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
                                    const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
                                    CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+// Tiled bf16 tensor map (128-byte swizzle, no interleave, zero OOB fill) of rank <= 5:
+// dims[0] is contiguous; strides_bytes[i] is the byte stride of dims[i + 1] (any order).
+bool make_tmap_bf16(CUtensorMap *map, const void *base, int rank, const uint64_t *dims,
+                    const uint64_t *strides_bytes, const uint32_t *box);
 EncodeTiledFn encode_tiled_fn();  // defined in capi.cu
 
 // 3-D bf16 tensor map: dims {d0 (contiguous), d1, d2}, strides in bytes for d1, d2,

@@ -44,7 +44,8 @@ constexpr float kLog2e = 1.4426950408889634f;
 template <int HKV, int G>
 struct Dec {
   static constexpr int H = HKV * G;
-  static constexpr int THREADS = (HKV + 1) * 32;       // HKV consumer warps + 1 producer
+  static constexpr int CONSUMERS = HKV * 32;           // one consumer warp per KV head
+  static constexpr int THREADS = CONSUMERS + 32;       // + 1 producer warp
   static constexpr int HEAD_TILE = kDecStage * kDecD * 2;  // 16 tokens x 128 dims: 4 KiB
   static constexpr int KV_BYTES = HKV * HEAD_TILE;
   static constexpr int Q_BYTES = ((H * kDecD * 2 + 1023) / 1024) * 1024;
@@ -52,10 +53,10 @@ struct Dec {
   static constexpr uint32_t TX_KV = 2 * KV_BYTES;
   static constexpr uint32_t TX_Q = H * kDecD * 2;
   static constexpr size_t SMEM = 1024 + static_cast<size_t>(kDecStages) * STAGE_BYTES +
-                                 3 * (kDecMaxBatch + 1) * 4 + 2 * kDecStages * 8 +
+                                 4 * (kDecMaxBatch + 1) * 4 + 2 * kDecStages * 8 +
                                  kDecStages * 32 + 64;
   static_assert(G >= 1 && G <= 8, "group size");
-  static_assert(4 * HKV <= 32, "one TMA box per producer lane");
+  static_assert(HKV <= 8, "a stage box holds at most 8 KV heads");
 };
 
 struct DecodeArgs {
@@ -138,80 +139,87 @@ __device__ __forceinline__ int owner_cta(int64_t total, int x, int g) {
   return static_cast<int>(c < g - 1 ? c : g - 1);
 }
 
-// Merge the n_parts split-K partials of sequence b for the G query heads of KV head w
-// (one warp). Lane l owns head dims 4l..4l+3 of every head; lane i also holds the (max,
-// sum) of parts i, i+32, ... All loads of a batch of parts are issued before the
-// reductions that consume them, so a merge of up to 32 parts costs about two L2 round
-// trips. Partials are read with ld.global.cg: they were written by other SMs.
+__device__ __forceinline__ void cp_async16(uint32_t saddr, const void *gptr) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(saddr), "l"(gptr) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+
+// 4-D tiled tensor load (no multicast) into shared memory.
+__device__ __forceinline__ void tma_load_4d(void *dst, const CUtensorMap *map, int32_t c0,
+                                            int32_t c1, int32_t c2, int32_t c3, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3),
+      "r"(smem_addr(bar))
+      : "memory");
+}
+
+// Merge the n_parts split-K partials of sequence b (workspace slots first..first+n_parts-1)
+// for the G query heads of KV head w (one warp each). Runs after this CTA's last stage,
+// when the stage buffers are free: all consumer threads stage a chunk of partials --
+// (max, sum) rows and fp32 accumulators, contiguous in the workspace -- with 16-byte
+// cp.async.cg (L2, never a stale L1 line: other SMs wrote them), so a chunk costs one L2
+// round trip. Lane l owns dims 4l..4l+3 of every head; the online rescale carries
+// across chunks, so any number of partials merges.
 template <class C>
-__device__ __forceinline__ void merge_partials(const DecodeArgs &a, int first, int n_parts,
-                                               int b, int w, int lane) {
-  constexpr int G = C::H / (C::THREADS / 32 - 1);
-  constexpr int MB = G == 1 ? 8 : (G == 2 ? 4 : 2);  // parts per batch of loads (registers)
-  const float2 *ml = reinterpret_cast<const float2 *>(a.ws_ml) +
-                     static_cast<int64_t>(first) * C::H + w * G;
-  const float4 *os = reinterpret_cast<const float4 *>(a.ws_o) +
-                     (static_cast<int64_t>(first) * C::H + w * G) * (kDecD / 4) + lane;
-  constexpr int64_t kPartStride = static_cast<int64_t>(C::H) * (kDecD / 4);
-  float2 mine[G];
-  float4 v[MB][G];
-#pragma unroll
-  for (int g = 0; g < G; ++g)
-    mine[g] = lane < n_parts ? __ldcg(ml + static_cast<int64_t>(lane) * C::H + g)
-                             : make_float2(-INFINITY, 0.f);
-#pragma unroll
-  for (int jj = 0; jj < MB; ++jj)
-#pragma unroll
-    for (int g = 0; g < G; ++g)
-      v[jj][g] = jj < n_parts ? __ldcg(os + jj * kPartStride + g * (kDecD / 4))
-                              : make_float4(0.f, 0.f, 0.f, 0.f);
-  float mm[G], lsum[G], acc[G][4];
+__device__ __forceinline__ void merge_staged(const DecodeArgs &a, uint8_t *buf, int first,
+                                             int n_parts, int b, int w, int lane, int tid) {
+  constexpr int H = C::H;
+  constexpr int NT = C::CONSUMERS;
+  constexpr int G = H / (NT / 32);
+  constexpr int PART_BYTES = H * (kDecD + 2) * 4;
+  constexpr int CAP = kDecStages * C::STAGE_BYTES / PART_BYTES;
+  const uint32_t sbuf = smem_addr(buf);
+  float m[G], l[G], acc[G][4];
 #pragma unroll
   for (int g = 0; g < G; ++g) {
-    float m = mine[g].x;
-    for (int i = lane + 32; i < n_parts; i += 32)
-      m = fmaxf(m, __ldcg(ml + static_cast<int64_t>(i) * C::H + g).x);
-    mm[g] = warp_max(m);
-    lsum[g] = 0.f;
+    m[g] = -INFINITY;
+    l[g] = 0.f;
     acc[g][0] = acc[g][1] = acc[g][2] = acc[g][3] = 0.f;
   }
-  for (int i0 = 0; i0 < n_parts; i0 += 32) {
-    float wgt[G];
+  for (int c0 = 0; c0 < n_parts; c0 += CAP) {
+    const int n = min(CAP, n_parts - c0);
+    const int ml_bytes = n * H * 8, o_bytes = n * H * kDecD * 4;
+    const uint8_t *gml = reinterpret_cast<const uint8_t *>(a.ws_ml + static_cast<int64_t>(first + c0) * H * 2);
+    const uint8_t *go = reinterpret_cast<const uint8_t *>(a.ws_o + static_cast<int64_t>(first + c0) * H * kDecD);
+    for (int i = tid * 16; i < ml_bytes; i += NT * 16) cp_async16(sbuf + i, gml + i);
+    for (int i = tid * 16; i < o_bytes; i += NT * 16) cp_async16(sbuf + ml_bytes + i, go + i);
+    cp_async_wait_all();
+    consumer_sync(NT);
+    const float2 *sml = reinterpret_cast<const float2 *>(buf);
+    const float4 *so = reinterpret_cast<const float4 *>(buf + ml_bytes);
 #pragma unroll
     for (int g = 0; g < G; ++g) {
-      const bool ok = i0 + lane < n_parts;
-      const float2 sm = i0 == 0 ? mine[g]
-                                : (ok ? __ldcg(ml + static_cast<int64_t>(i0 + lane) * C::H + g)
-                                      : make_float2(-INFINITY, 0.f));
-      wgt[g] = ok ? exp2f(sm.x - mm[g]) : 0.f;
-      lsum[g] += ok ? sm.y * wgt[g] : 0.f;
-    }
-    const int cnt = min(32, n_parts - i0);
-    for (int j0 = 0; j0 < cnt; j0 += MB) {
-      if (i0 + j0 > 0) {  // the first batch was loaded above
-#pragma unroll
-        for (int jj = 0; jj < MB; ++jj)
-#pragma unroll
-          for (int g = 0; g < G; ++g)
-            v[jj][g] = j0 + jj < cnt
-                           ? __ldcg(os + (i0 + j0 + jj) * kPartStride + g * (kDecD / 4))
-                           : make_float4(0.f, 0.f, 0.f, 0.f);
+      const int hh = w * G + g;
+      float cm = -INFINITY;
+      for (int i = lane; i < n; i += 32) cm = fmaxf(cm, sml[i * H + hh].x);
+      const float mn = fmaxf(m[g], warp_max(cm));
+      const float sc = exp2f(m[g] - mn);
+      l[g] *= sc;
+      acc[g][0] *= sc;
+      acc[g][1] *= sc;
+      acc[g][2] *= sc;
+      acc[g][3] *= sc;
+      for (int i = 0; i < n; ++i) {
+        const float2 st = sml[i * H + hh];
+        const float wgt = exp2f(st.x - mn);
+        const float4 v = so[(i * H + hh) * (kDecD / 4) + lane];
+        l[g] += st.y * wgt;
+        acc[g][0] += v.x * wgt;
+        acc[g][1] += v.y * wgt;
+        acc[g][2] += v.z * wgt;
+        acc[g][3] += v.w * wgt;
       }
-#pragma unroll
-      for (int jj = 0; jj < MB; ++jj)
-#pragma unroll
-        for (int g = 0; g < G; ++g) {
-          const float wj = __shfl_sync(0xffffffffu, wgt[g], j0 + jj);  // 0 past cnt
-          acc[g][0] += v[jj][g].x * wj;
-          acc[g][1] += v[jj][g].y * wj;
-          acc[g][2] += v[jj][g].z * wj;
-          acc[g][3] += v[jj][g].w * wj;
-        }
+      m[g] = mn;
     }
+    consumer_sync(NT);  // the next chunk (or merge) overwrites the buffer
   }
 #pragma unroll
   for (int g = 0; g < G; ++g) {
-    const float inv = 1.f / warp_sum(lsum[g]);
+    const float inv = 1.f / l[g];
     __nv_bfloat16 *dst = a.out + b * a.out_stride + (w * G + g) * kDecD + lane * 4;
     *reinterpret_cast<uint2 *>(dst) = make_uint2(pack2(acc[g][0] * inv, acc[g][1] * inv),
                                                  pack2(acc[g][2] * inv, acc[g][3] * inv));
@@ -228,14 +236,16 @@ __global__ void __launch_bounds__(Dec<HKV, G>::THREADS, 1)
                                               ~uintptr_t(1023));
   uint8_t *stages = smem;
   int *s_cuk = reinterpret_cast<int *>(smem + kDecStages * C::STAGE_BYTES);  // [B + 1]
-  int *s_parts = s_cuk + kDecMaxBatch + 1;                                    // [B + 1]
-  int *s_first = s_parts + kDecMaxBatch + 1;                                  // [B]
+  int *s_sp = s_cuk + kDecMaxBatch + 1;      // [B + 1] first stage of each sequence
+  int *s_parts = s_sp + kDecMaxBatch + 1;    // [B + 1] first partial slot of each sequence
+  int *s_first = s_parts + kDecMaxBatch + 1;  // [B] first CTA of each sequence
   uint64_t *full = reinterpret_cast<uint64_t *>(
       (reinterpret_cast<uintptr_t>(s_first + kDecMaxBatch + 1) + 7) & ~uintptr_t(7));
   uint64_t *empty = full + kDecStages;
   StageInfo *info = reinterpret_cast<StageInfo *>(empty + kDecStages);
   __shared__ int abort_flag;
-  __shared__ int merge_owner;
+  __shared__ int s_pending[2];  // sequences this CTA merges after its last stage
+  __shared__ int s_npending;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int B = a.batch;
@@ -243,24 +253,41 @@ __global__ void __launch_bounds__(Dec<HKV, G>::THREADS, 1)
   for (int i = tid; i <= B; i += blockDim.x) s_cuk[i] = a.cu_seqlens_k[i];
   if (tid == 0) {
     abort_flag = 0;
+    s_npending = 0;
     for (int s = 0; s < kDecStages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], HKV);
     }
     fence_barrier_init();
   }
+  if (warp == HKV && lane == 0) {
+    prefetch_tmap(&tm_k);
+    prefetch_tmap(&tm_v);
+  }
   __syncthreads();
-  const int64_t total = s_cuk[B] - s_cuk[0];
-  const int64_t by_len = total / kDecStage;  // at least a stage's worth of tokens per CTA
-  const int geff = static_cast<int>(by_len < 1 ? 1 : (by_len < gridDim.x ? by_len : gridDim.x));
-  const bool has_work = total > 0 && static_cast<int>(blockIdx.x) < geff;
 
   if (warp == HKV) {
     // ------------------------------------------------------------------ producer
-    if (lane == 0) {
-      prefetch_tmap(&tm_k);
-      prefetch_tmap(&tm_v);
+    // Stage prefix: sequence b owns ceil(len_b / 16) stages, laid end to end. Published
+    // to the consumers through named barrier 2 (arrive here, sync there).
+    int carry = 0;
+    for (int b0 = 0; b0 < B; b0 += 32) {
+      const int b = b0 + lane;
+      const int len = b < B ? s_cuk[b + 1] - s_cuk[b] : 0;
+      const int ns = len > 0 ? (len + kDecStage - 1) / kDecStage : 0;
+      int incl = ns;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+      }
+      if (b < B) s_sp[b] = carry + incl - ns;
+      carry += __shfl_sync(0xffffffffu, incl, 31);
     }
+    if (lane == 0) s_sp[B] = carry;
+    __syncwarp();
+    asm volatile("bar.arrive 2, %0;" ::"r"(C::THREADS) : "memory");
+
     uint32_t it_stage = 0;
     auto acquire = [&](int &st) -> bool {
       st = it_stage % kDecStages;
@@ -269,52 +296,58 @@ __global__ void __launch_bounds__(Dec<HKV, G>::THREADS, 1)
       if (lane == 0) ok = mbar_wait(&empty[st], ph ^ 1, a.error_flag, &abort_flag);
       return __shfl_sync(0xffffffffu, ok, 0) != 0;
     };
-    if (has_work) {
+    const int S = carry;
+    const int geff = S < 1 ? 1 : (S < static_cast<int>(gridDim.x) ? S : static_cast<int>(gridDim.x));
+    if (S > 0 && static_cast<int>(blockIdx.x) < geff) {
       const int c = blockIdx.x;
-      int pos = part_begin(total, c, geff);
-      const int end = part_begin(total, c + 1, geff);
-      int b = upper_index(s_cuk, B + 1, pos + s_cuk[0]);
-      while (pos < end) {
-        while (s_cuk[b + 1] - s_cuk[0] <= pos) ++b;  // skip empty sequences
-        const int seq0 = s_cuk[b] - s_cuk[0], seq1 = s_cuk[b + 1] - s_cuk[0];
-        const int seg1 = min(end, seq1);
-        const int p0 = pos - seq0, p1 = seg1 - seq0;
-        const bool whole = pos == seq0 && seg1 == seq1;
-        // block ids of this segment, one per lane (a segment spans few blocks)
-        const int blk0 = p0 / a.block_size;
-        const int nblk = (p1 - 1) / a.block_size - blk0 + 1;
-        int my_block = 0;
-        if (lane < nblk) {
-          my_block = a.block_tables[static_cast<int64_t>(b) * a.bt_stride + blk0 + lane];
-          if (my_block < 0 || my_block >= a.num_blocks) {
-            raise_flag(a.error_flag, B200ASR_DEVERR_BLOCK);
-            my_block = 0;
+      const int j0 = part_begin(S, c, geff), j1 = part_begin(S, c + 1, geff);
+      for (int wb = j0; wb < j1; wb += 32) {
+        // Lane i describes stage wb + i: sequence, token count, flags and cache slot
+        // (the block-table reads of 32 stages are in flight together).
+        const int j = wb + lane;
+        int d_b = 0, d_n = 0, d_fl = 0, d_slot = 0;
+        if (j < j1) {
+          const int b = upper_index(s_sp, B + 1, j);  // s_sp[b] <= j < s_sp[b + 1]
+          const int len = s_cuk[b + 1] - s_cuk[b];
+          const int t0 = (j - s_sp[b]) * kDecStage;
+          d_n = min(kDecStage, len - t0);
+          const bool first = t0 == 0 || j == j0, last = t0 + d_n == len || j == j1 - 1;
+          const bool whole = s_sp[b] >= j0 && s_sp[b + 1] <= j1;
+          const int col = t0 / a.block_size;
+          int blk = 0;
+          if (col >= a.bt_stride) {  // context longer than its block-table row
+            raise_flag(a.error_flag, B200ASR_DEVERR_LENGTH);
+          } else {
+            blk = a.block_tables[static_cast<int64_t>(b) * a.bt_stride + col];
+            if (blk < 0 || blk >= a.num_blocks) {
+              raise_flag(a.error_flag, B200ASR_DEVERR_BLOCK);
+              blk = 0;
+            }
           }
+          d_b = b;
+          d_fl = (first ? 1 : 0) | (last ? 2 : 0) | (whole ? 4 : 0);
+          d_slot = blk * a.block_size + t0 % a.block_size;
         }
-        for (int t = p0; t < p1;) {
-          const int n = min(min(kDecStage, p1 - t), a.block_size - t % a.block_size);
-          const int blk = __shfl_sync(0xffffffffu, my_block, min(31, t / a.block_size - blk0));
+        const int nw = min(32, j1 - wb);
+        for (int i = 0; i < nw; ++i) {
+          const int b = __shfl_sync(0xffffffffu, d_b, i);
+          const int n = __shfl_sync(0xffffffffu, d_n, i);
+          const int fl = __shfl_sync(0xffffffffu, d_fl, i);
+          const int slot = __shfl_sync(0xffffffffu, d_slot, i);
           int st;
           if (!acquire(st)) return;
-          const bool first = t == p0, last = t + n == p1;
           if (lane == 0) {
-            info[st] = StageInfo{b, n, (first ? 1 : 0) | (last ? 2 : 0) | (whole ? 4 : 0)};
-            mbar_arrive_expect_tx(&full[st], C::TX_KV + (first ? C::TX_Q : 0));
+            info[st] = StageInfo{b, n, fl};
+            mbar_arrive_expect_tx(&full[st], C::TX_KV + ((fl & 1) ? C::TX_Q : 0));
           }
           __syncwarp();
           uint8_t *stage = stages + st * C::STAGE_BYTES;
-          const int slot = blk * a.block_size + t % a.block_size;
-          if (lane < 4 * HKV) {
-            const int kind = lane / (2 * HKV), head = (lane >> 1) % HKV, dh = lane & 1;
-            tma_load_3d(stage + kind * C::KV_BYTES + head * C::HEAD_TILE + dh * 2048,
-                        kind ? &tm_v : &tm_k, dh * 64, head, slot, &full[st]);
-          }
-          if (first && lane == 31)
+          // One box per operand: 16 tokens x every KV head x both 64-dim halves (32 KiB).
+          if (lane < 2) tma_load_4d(stage + lane * C::KV_BYTES, lane ? &tm_v : &tm_k, 0, slot, 0, 0, &full[st]);
+          if ((fl & 1) && lane == 2)
             bulk_g2s(stage + 2 * C::KV_BYTES, a.q + b * a.q_stride, C::TX_Q, &full[st]);
           ++it_stage;
-          t += n;
         }
-        pos = seg1;
       }
     }
     int st;  // terminal stage: tells the consumers to stop
@@ -327,17 +360,17 @@ __global__ void __launch_bounds__(Dec<HKV, G>::THREADS, 1)
   }
 
   // -------------------------------------------------------------------- consumers
+  asm volatile("bar.sync 2, %0;" ::"r"(C::THREADS) : "memory");  // stage prefix ready
+  const int S = s_sp[B];
+  const int geff = S < 1 ? 1 : (S < static_cast<int>(gridDim.x) ? S : static_cast<int>(gridDim.x));
   if (warp == 0) {  // per sequence: first owning CTA + prefix of partial slots
     int carry = 0;
     for (int b0 = 0; b0 < B; b0 += 32) {
       const int b = b0 + lane;
       int parts = 0, first = 0;
-      if (b < B && total > 0) {
-        const int x0 = s_cuk[b] - s_cuk[0], x1 = s_cuk[b + 1] - s_cuk[0];
-        if (x1 > x0) {
-          first = owner_cta(total, x0, geff);
-          parts = owner_cta(total, x1 - 1, geff) - first + 1;
-        }
+      if (b < B && s_sp[b + 1] > s_sp[b]) {
+        first = owner_cta(S, s_sp[b], geff);
+        parts = owner_cta(S, s_sp[b + 1] - 1, geff) - first + 1;
       }
       int incl = parts;
 #pragma unroll
@@ -356,7 +389,7 @@ __global__ void __launch_bounds__(Dec<HKV, G>::THREADS, 1)
       if (carry > a.parts_cap) raise_flag(a.error_flag, B200ASR_DEVERR_LENGTH);
     }
   }
-  consumer_sync(HKV * 32);
+  consumer_sync(C::CONSUMERS);
   const bool parts_ok = s_parts[B] <= a.parts_cap;
   const int w = warp;               // KV head of this warp
   const int row = lane >> 2;        // MMA row = query head within the group (valid if < G)
@@ -497,20 +530,26 @@ __global__ void __launch_bounds__(Dec<HKV, G>::THREADS, 1)
             make_float2(m_run, l_run);
     }
     const int n_parts = s_parts[b + 1] - s_parts[b];
-    consumer_sync(HKV * 32);
+    consumer_sync(C::CONSUMERS);
     if (tid == 0) {
       // Release this CTA's partial (cumulative over the barrier) and count it; the CTA
-      // that brings the count to n_parts acquires every other partial and merges.
+      // that brings the count to n_parts has acquired every other partial and merges
+      // them after its last stage. A CTA's only partial segments are its first and last.
       int done;
       asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;"
                    : "=r"(done)
                    : "l"(a.counters + b)
                    : "memory");
-      merge_owner = done == n_parts - 1;
-      if (merge_owner) a.counters[b] = 0;  // every partial has arrived: ready for the next call
+      if (done == n_parts - 1) {
+        a.counters[b] = 0;  // every partial has arrived: ready for the next call
+        if (s_npending < 2) s_pending[s_npending++] = b;
+      }
     }
-    consumer_sync(HKV * 32);
-    if (merge_owner) merge_partials<C>(a, s_parts[b], n_parts, b, w, lane);
+  }
+  consumer_sync(C::CONSUMERS);  // all stages consumed: the stage buffers are free
+  for (int k = 0; k < s_npending; ++k) {
+    const int b = s_pending[k];
+    merge_staged<C>(a, stages, s_parts[b], s_parts[b + 1] - s_parts[b], b, w, lane, tid);
   }
 }
 
@@ -541,11 +580,17 @@ int launch_decode(const DecodeArgs &a, const void *k_cache, const void *v_cache,
     }
     configured = true;
   }
+  // The cache [slots][HKV][128] bf16 viewed as {64 dims, slots, 2 halves, HKV heads}: one
+  // box of {64, 16, 2, HKV} lands in shared memory as [head][half][token][64 dims], i.e.
+  // per head a 16 x 128 K (or V) tile in two 128-byte-swizzled halves. A single large box
+  // per operand matters: an SM keeps only a limited number of TMA boxes in flight, and
+  // with 2 boxes per stage (rather than 4 * HKV) all stages of the ring stream at once.
   CUtensorMap tk, tv;
-  if (!make_tmap_3d_bf16(&tk, k_cache, kDecD, HKV, num_slots, kDecD * 2, HKV * kDecD * 2ull, 64,
-                         1, kDecStage) ||
-      !make_tmap_3d_bf16(&tv, v_cache, kDecD, HKV, num_slots, kDecD * 2, HKV * kDecD * 2ull, 64,
-                         1, kDecStage))
+  const uint64_t dims[4] = {64, static_cast<uint64_t>(num_slots), 2, HKV};
+  const uint64_t strides[3] = {HKV * kDecD * 2ull, 128, 256};
+  const uint32_t box[4] = {64, kDecStage, 2, HKV};
+  if (!make_tmap_bf16(&tk, k_cache, 4, dims, strides, box) ||
+      !make_tmap_bf16(&tv, v_cache, 4, dims, strides, box))
     return B200ASR_ERR_CUDA;
   const int grid = std::min(num_sms(), kDecMaxGrid);
   paged_decode_kernel<HKV, G><<<grid, C::THREADS, C::SMEM, stream>>>(tk, tv, a);
