@@ -12,18 +12,21 @@ request (EOS ignored), CUDA-graph decode on. A step transcribes one slice of
 
 * ``value``    audio-s/s with each clip's mel features already resident in HBM
                (device-timed with CUDA events, max over ranks, all ranks summed);
-* ``e2e``      the same through the public API from host waveforms: CPU mel
-               frontend, host-to-device copies and token read-back inside the timing;
+* ``e2e``      the same through the public API from host waveforms: waveform copies,
+               GPU log-mel frontend and token read-back inside the timing;
 * ``roofline`` the paged decode attention kernel (stream-K split with fused merge) on config 1
                (B = 32, ctx ~ U[64, 1024], 4096-block pool), timed live here with CUDA
-               events and L2 flushed between launches; bytes = algorithmic KV/q/out;
+               events around a graph of back-to-back launches over rotating KV sets that
+               together exceed L2; bytes = algorithmic KV/q/out;
 * ``cpu_baseline`` the CPU fp32 restatement of the upstream model (oracle/model.py)
                transcribing a bounded sample of the same workload on the host cores.
 
 Multi-GPU: independent engine replicas (weak scaling), no collective on the data
 path; torch.distributed (NCCL) is used only for barriers and the max-over-ranks
 timing. ``--impl reference`` times the CPU restatement of the reference's path on
-rank 0 with all host threads (other ranks exit 0).
+rank 0 with all host threads (other ranks exit 0). ``--impl reference-engine`` runs
+the reference's own GPU engine (``qwen_asr_vllm.AsrEngine``, installed under
+baseline/_ref) on the same workload for a like-for-like e2e comparison.
 """
 
 from __future__ import annotations
@@ -53,7 +56,7 @@ def parse_args():
     p.add_argument("--gpus", type=int, default=1)
     p.add_argument("--steps", type=int, default=4)
     p.add_argument("--warmup", type=int, default=3)
-    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--impl", choices=["ours", "reference", "reference-engine"], default="ours")
     p.add_argument("--clips", type=int, default=512)
     p.add_argument("--clips-per-step", type=int, default=128)
     p.add_argument("--concurrency", type=int, default=32)
@@ -321,6 +324,103 @@ def run_reference_arm(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+class _TemplateTokenizer:
+    """Stands in for the checkpoint tokenizer, which does not exist offline.
+
+    The reference engine only asks its tokenizer to encode the chat template (once per
+    context/language pair), for the EOS id, and to decode output text. This returns the
+    same template ids as ``voiceagent_b200.prompt`` (pinned by the reference's
+    tests/test_prompt.py) so both engines see prompts of identical length; text output
+    is empty. Everything after the prompt -- frontend, scheduler, model, flash-attn,
+    Triton store, CUDA graphs -- is the reference's own, unmodified code.
+    """
+
+    eos_token_id = 151645
+
+    @classmethod
+    def from_pretrained(cls, *args, **kwargs):
+        return cls()
+
+    def encode(self, text: str) -> list[int]:
+        from voiceagent_b200.prompt import PromptBuilder
+
+        head, sep, tail = text.partition("<|im_start|>assistant\n")
+        if not sep or "<|im_start|>system\n<|im_end|>" not in head:
+            raise ValueError("template tokenizer: only the empty-context ASR template is known")
+        language = tail[len("language "):].replace("<asr_text>", "") if tail else None
+        return PromptBuilder().template(None, language or None)[0]
+
+    def decode(self, ids, skip_special_tokens: bool = True) -> str:
+        return ""
+
+
+def run_reference_engine(args) -> None:
+    """The reference's own GPU engine (``qwen_asr_vllm.AsrEngine`` from baseline/_ref) on
+    the config-3 workload, for comparison with our e2e number: same seeded random
+    weights (written as a safetensors checkpoint), clips, concurrency and sampling."""
+    ref = Path(__file__).resolve().parent / "baseline" / "_ref"
+    if not (ref / "qwen_asr_vllm").is_dir():
+        print(json.dumps({"impl": "reference-engine", "unavailable":
+                          "baseline/_ref is not installed (pip install --target baseline/_ref)"}))
+        return
+    sys.path.insert(0, str(ref))
+    import torch
+
+    import qwen_asr_vllm.prompt as ref_prompt
+    from qwen_asr_vllm import AsrEngine as RefEngine
+    from qwen_asr_vllm.engine.request import SamplingParams as RefSampling
+
+    from voiceagent_b200.checkpoint import write_checkpoint
+    from voiceagent_b200.workload import config3_clips, lognormal_durations
+
+    ref_prompt.AutoTokenizer = _TemplateTokenizer
+    dist = Dist()
+    rank, world, local = dist.rank, dist.world, dist.local
+    torch.cuda.set_device(local)
+    ckpt = write_checkpoint(Path(tempfile.mkdtemp(prefix="b200asr_ref_")) / "ckpt", args.preset,
+                            seed=0, weights=True)
+    engine = RefEngine(model=str(ckpt), max_num_seqs=args.concurrency, max_model_len=4096,
+                       max_num_batched_tokens=8192, max_audio_batch_size=args.concurrency,
+                       num_kvcache_blocks=1024, device=f"cuda:{local}")
+    sampling = RefSampling(max_new_tokens=args.decode_tokens, ignore_eos=True)
+    clips = config3_clips(args.clips, seed=rank)
+    durations = lognormal_durations(args.clips, seed=rank)
+    n_slices = max(1, args.clips // args.clips_per_step)
+    slices = [list(range(i * args.clips_per_step, (i + 1) * args.clips_per_step))
+              for i in range(n_slices)]
+
+    def run(i):
+        return engine.transcribe([clips[j] for j in slices[i % n_slices]], language="en",
+                                 sampling=sampling)
+
+    for i in range(args.warmup):
+        run(i)
+    dist.barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    outs = [run(i) for i in range(args.steps)]
+    torch.cuda.synchronize()
+    sec = time.perf_counter() - t0
+    dist.barrier()
+    toks = sum(len(o.output_token_ids) for batch in outs for o in batch)
+    audio = float(sum(durations[j] for i in range(args.steps) for j in slices[i % n_slices]))
+    sec_max = dist.max(sec)
+    value = dist.sum(audio) / sec_max
+    if rank == 0:
+        print(json.dumps({
+            "impl": "reference-engine", "metric": METRIC, "value": value, "unit": UNIT,
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 1000.0 * sec_max / args.steps, "higher_is_better": True,
+            "scaling": "weak", "dtype": "bf16",
+            "data": "synthetic (seeded noise + sines; random-init weights, seed 0)",
+            "config": {"workload": "config3 through qwen_asr_vllm.AsrEngine.transcribe "
+                                   "(flash-attn + Triton, CUDA-graph decode), wall clock, "
+                                   "max over ranks", "clips_per_step": args.clips_per_step,
+                       "concurrency": args.concurrency, "output_tokens": toks},
+        }), flush=True)
+    dist.close()
+
+
 def run_ours(args) -> None:
     import torch
 
@@ -354,7 +454,9 @@ def run_ours(args) -> None:
         return slices[i % len(slices)]
 
     # Mel features on the host once (for the HBM-resident run), then moved to the GPU.
-    host_feats = build_features(clips, engine.frontend, torch)
+    from voiceagent_b200.audio.frontend import AudioFrontend
+
+    host_feats = build_features(clips, AudioFrontend(str(ckpt)), torch)
     dev_feats = []
     for f in host_feats:
         g = type(f)(mel=f.mel.to(device=device, dtype=torch.bfloat16), mel_frames=f.mel_frames,
@@ -414,8 +516,9 @@ def run_ours(args) -> None:
                "h2d_bytes_per_step": int(xfer["h2d"] / args.steps),
                "d2h_bytes_per_step": int(xfer["d2h"] / args.steps),
                "ms_per_step": ms_e_max / args.steps,
-               "note": "AsrEngine.transcribe from host float32 waveforms: CPU mel frontend, "
-                       "host-to-device copies and token read-back inside the timing"}
+               "note": "AsrEngine.transcribe from host float32 waveforms: waveform copies "
+                       "(one pinned copy per encode batch), GPU log-mel, token read-back "
+                       "inside the timing"}
     clock_info = clocks.stop() if rank == 0 else None
 
     roof = decode_roofline(torch, device)
@@ -485,6 +588,8 @@ def main():
         run_roofline_only()
     elif args.impl == "reference":
         run_reference_arm(args)
+    elif args.impl == "reference-engine":
+        run_reference_engine(args)
     else:
         run_ours(args)
 

@@ -235,6 +235,27 @@ B200ASR_API int b200asr_varlen_attention(const void *q, int64_t q_row_stride, co
 B200ASR_API int b200asr_greedy_argmax(const void *logits, int64_t row_stride, int32_t batch,
                           int32_t vocab, int64_t *out_ids, b200asr_stream_t stream);
 
+/* ------------------------------------------------------------- mel frontend ----
+ * Replaces AudioFrontend.__call__ (audio/frontend.py:71-94), the stock Whisper log-mel
+ * extractor run per clip on the host: centred STFT (reflect pad 200), periodic Hann
+ * window, n_fft 400, hop 160, power of bins 0..200, last frame dropped (n / 160 frames
+ * for n samples), mel = filters^T power, log10(max(mel, 1e-10)), per clip
+ * max(x, clip max - 8), (x + 4) / 4, rounded to bf16.
+ *   waveform     fp32 clips laid end to end; cu_samples int64 [batch + 1] (each clip
+ *                longer than 200 samples, else B200ASR_DEVERR_LENGTH)
+ *   frame_start  int32 [batch + 1] prefix sums of n_b / 160; total_frames its last entry
+ *   tables       fp32 [1200]: Hann window[400], cos[400], sin[400] of 2*pi*j/400
+ *   mel_filters  fp32 [201][128]; filter_range int32 [128][2] first nonzero bin, count
+ *   out          bf16 [128][out_stride]; clip b fills columns out_col[b] .. + frames_b
+ *   workspace    >= b200asr_log_mel_workspace_size(batch, total_frames) bytes, 256-byte
+ *                aligned (per-clip maxima + fp32 log-mel scratch)                     */
+B200ASR_API size_t b200asr_log_mel_workspace_size(int32_t batch, int32_t total_frames);
+B200ASR_API int b200asr_log_mel(const float *waveform, const int64_t *cu_samples,
+                    const int32_t *frame_start, int32_t batch, int32_t total_frames,
+                    const float *tables, const float *mel_filters, const int32_t *filter_range,
+                    void *workspace, size_t workspace_bytes, void *out, int64_t out_stride,
+                    const int32_t *out_col, int32_t *error_flag, b200asr_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -351,3 +351,29 @@ def silu_mul(x) -> np.ndarray:
 def greedy_argmax(logits) -> np.ndarray:
     """``layers/sampler.py:16-20``: argmax of fp32 logits, first index on ties."""
     return np.argmax(np.asarray(logits, dtype=np.float32), axis=-1).astype(np.int64)
+
+
+def log_mel(waveform, mel_filters, n_fft: int = 400, hop: int = 160) -> np.ndarray:
+    """Whisper log-mel features ``[128, n // hop]`` of one clip, in float64.
+
+    Follows AudioFrontend.__call__ (audio/frontend.py:71-94), which calls the stock
+    transformers WhisperFeatureExtractor (transformers 5.5.0 here; the reference pins
+    4.57.6, same algorithm): centred STFT with reflect padding ``n_fft // 2``, periodic
+    Hann window, power spectrum of the ``n_fft // 2 + 1`` bins, the last STFT frame
+    dropped, ``mel_filters^T power``, ``log10(max(mel, 1e-10))``, then per clip
+    ``max(x, max(x) - 8)`` and ``(x + 4) / 4``. ``mel_filters`` is the extractor's
+    ``[201, 128]`` filterbank.
+    """
+    x = np.asarray(waveform, dtype=np.float64).reshape(-1)
+    if x.size <= n_fft // 2:
+        raise ValueError(f"clip of {x.size} samples is too short for reflect padding")
+    padded = np.pad(x, n_fft // 2, mode="reflect")
+    frames = x.size // hop
+    idx = np.arange(frames)[:, None] * hop + np.arange(n_fft)[None, :]
+    window = 0.5 - 0.5 * np.cos(2.0 * np.pi * np.arange(n_fft) / n_fft)
+    spec = np.fft.rfft(padded[idx] * window, axis=1)
+    power = spec.real ** 2 + spec.imag ** 2
+    mel = power @ np.asarray(mel_filters, dtype=np.float64)
+    logm = np.log10(np.maximum(mel, 1e-10))
+    logm = np.maximum(logm, logm.max() - 8.0)
+    return ((logm + 4.0) / 4.0).T

@@ -21,6 +21,7 @@ the TTS paged decode) on the CPU interpreter. What each fixture pins:
 * ``elementwise.npz``   -- fused add-RMSNorm and SiluAndMul (layernorm.py, activation.py)
 * ``sampler.npz``       -- greedy ``Sampler`` (sampler.py:16-27)
 * ``model_tiny.npz``    -- upstream HF Qwen3-ASR thinker on a tiny seeded config
+* ``frontend.npz``      -- ``AudioFrontend`` log-mel features (audio/frontend.py:71-94)
 """
 
 from __future__ import annotations
@@ -516,6 +517,30 @@ def gen_model_tiny(out: Path):
                         first_logits=_f32(logits0), seed=np.asarray(11))
 
 
+def gen_frontend(out: Path):
+    """The reference's AudioFrontend (Whisper log-mel) on seeded clips of awkward lengths:
+    a config-0 style mix of noise and sines, a clip that is not a multiple of the hop,
+    a quiet one (the clip-max clamp bites) and the shortest that reflect padding allows."""
+    import tempfile
+
+    from qwen_asr_vllm.audio.frontend import AudioFrontend
+    from voiceagent_b200.checkpoint import write_checkpoint
+    from voiceagent_b200.workload import synthetic_waveform
+
+    ckpt = write_checkpoint(Path(tempfile.mkdtemp()) / "ckpt", "tiny", weights=False)
+    fe = AudioFrontend(str(ckpt))
+    rng = np.random.default_rng(21)
+    clips = [synthetic_waveform(1.0, rng), synthetic_waveform(0.77, rng)[:12321],
+             (synthetic_waveform(0.5, rng) * 1e-4).astype(np.float32),
+             rng.normal(0.0, 0.3, size=201).astype(np.float32)]
+    mels = [fe(c, 16000).mel.float().numpy() for c in clips]
+    lens = np.asarray([c.size for c in clips], np.int64)
+    np.savez_compressed(out / "frontend.npz", wave=np.concatenate(clips), lens=lens,
+                        mel=np.concatenate(mels, axis=1).astype(np.float32),
+                        frames=np.asarray([m.shape[1] for m in mels], np.int64),
+                        mel_filters=fe.extractor.mel_filters.astype(np.float32))
+
+
 GENERATORS = {
     "audio_pack": gen_audio_pack,
     "decoder_pack": gen_decoder_pack,
@@ -527,6 +552,7 @@ GENERATORS = {
     "elementwise": gen_elementwise,
     "sampler": gen_sampler,
     "model_tiny": gen_model_tiny,
+    "frontend": gen_frontend,
 }
 
 

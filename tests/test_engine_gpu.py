@@ -50,12 +50,21 @@ def _run(engine, clips, n_tokens=24):
                              sampling=SamplingParams(max_new_tokens=n_tokens, ignore_eos=True))
 
 
+def _host_frontend(engine):
+    """The reference's frontend: the Whisper extractor on the host (the engine itself
+    renders log-mel on the GPU by default, so this also checks that kernel end to end)."""
+    from voiceagent_b200.audio.frontend import AudioFrontend
+
+    return AudioFrontend(engine.config.model)
+
+
 def _agreement_with_reference(engine, clips, outputs):
     from tests import reference_path as ref
 
+    host = _host_frontend(engine)
     agree = total = 0
     for clip, out in zip(clips, outputs):
-        feats = engine.frontend(clip)
+        feats = host(clip)
         layout = engine.prompt_builder.build(feats.num_audio_tokens, language="English")
         audio = ref.encode_audio(engine.model, feats.mel)
         seq = layout.token_ids + out.output_token_ids[:-1]
@@ -80,14 +89,25 @@ def test_encoder_matches_reference_path(tiny_dir, clips):
     from voiceagent_b200.audio.batcher import pack_audio_batch
 
     engine = _engine(tiny_dir)
-    feats = [engine.frontend(c) for c in clips]
-    batch = pack_audio_batch([f.mel for f in feats], 800, "cuda")
+    host = _host_frontend(engine)
+    deferred = [engine.frontend(c) for c in clips]  # GPU log-mel rendered while packing
+    batch = pack_audio_batch(deferred, 800, "cuda", renderer=engine.frontend)
     packed = engine.model.encode_audio(batch)
-    for f, got in zip(feats, packed):
-        want = ref.encode_audio(engine.model, f.mel)
+    for clip, got in zip(clips, packed):
+        want = ref.encode_audio(engine.model, host(clip).mel)
         err = (got.float() - want.float()).abs()
         scale = want.float().abs().max().item()
         assert err.max().item() <= 2e-2 * max(1.0, scale), err.max().item()
+
+
+def test_gpu_frontend_matches_host_frontend(tiny_dir, clips):
+    """Same engine, log-mel on the GPU vs the host Whisper extractor: same tokens."""
+    gpu = _run(_engine(tiny_dir), clips)
+    cpu = _run(_engine(tiny_dir, frontend="cpu"), clips)
+    same = sum(int(a == b) for g, c in zip(gpu, cpu)
+               for a, b in zip(g.output_token_ids, c.output_token_ids))
+    total = sum(len(c.output_token_ids) for c in cpu)
+    assert same / total >= 0.99, same / total
 
 
 def test_graph_decode_equals_eager(tiny_dir, clips):
@@ -136,7 +156,7 @@ def test_config0_full_size_against_reference_and_oracle(tmp_path):
     assert rate >= 0.99, f"agreement with the bf16 reference path {rate:.4f}"
 
     oracle = M.OracleThinker(PRESETS["0.6b"], M.init_weights(PRESETS["0.6b"], seed=0))
-    feats = engine.frontend(clip)
+    feats = _host_frontend(engine)(clip)
     layout = engine.prompt_builder.build(feats.num_audio_tokens, language="English")
     audio = oracle.encode_audio(feats.mel.float())
     _, argmaxes = oracle.greedy(layout.token_ids, audio, 48, forced=out.output_token_ids)

@@ -464,3 +464,78 @@ def test_varlen_window_attention_matches_oracle(kx, token_lens):
     ref = K.varlen_attention(qkv[:, 0], qkv[:, 1], qkv[:, 2], cu, 64 ** -0.5)
     assert_attn_close(out, ref, f"window {token_lens}")
     assert err.item() == 0
+
+
+# ------------------------------------------------------------------ mel frontend
+
+
+def _bf16_ulp_close(got, want, atol=1e-3):
+    """(fraction of bit-identical bf16 values, all within one bf16 ulp or ``atol``, worst).
+
+    The absolute floor covers values near zero: (x + 4) / 4 cancels there, a bf16 ulp
+    shrinks with the value, and fp32 STFT rounding (~1e-6) can exceed it."""
+    w = torch.as_tensor(np.ascontiguousarray(want, dtype=np.float32)).to(torch.bfloat16).float()
+    g = got.float().cpu()
+    exact = (g == w).float().mean().item()
+    ulp = torch.exp2(torch.floor(torch.log2(w.abs().clamp_min(1e-30))) - 7)
+    err = (g - w).abs()
+    ok = err <= torch.maximum(ulp, torch.full_like(ulp, atol))
+    i = int(torch.argmax(err / torch.maximum(ulp, torch.full_like(ulp, atol))))
+    worst = (float(g.flatten()[i]), float(w.flatten()[i]), float(err.flatten()[i]))
+    return exact, bool(ok.all()), worst
+
+
+def _render(frontend, clips, columns=None, width=None):
+    feats = [frontend(c) for c in clips]
+    frames = [f.mel_frames for f in feats]
+    if columns is None:
+        columns = list(np.concatenate([[0], np.cumsum(frames)])[:-1])
+        width = int(sum(frames))
+    out = torch.full((128, width), float("nan"), dtype=torch.bfloat16, device="cuda")
+    frontend.render(feats, out, [int(c) for c in columns])
+    torch.cuda.synchronize()
+    return out, frames
+
+
+@pytest.fixture(scope="module")
+def gpu_frontend():
+    from voiceagent_b200.audio.frontend import GpuMelFrontend
+
+    return GpuMelFrontend(None)
+
+
+def test_log_mel_matches_reference_frontend(gpu_frontend):
+    z = load_npz("frontend.npz")
+    off = np.concatenate([[0], np.cumsum(z["lens"])])
+    clips = [z["wave"][off[i]:off[i + 1]] for i in range(len(z["lens"]))]
+    out, frames = _render(gpu_frontend, clips)
+    assert frames == list(z["frames"])
+    exact, within, worst = _bf16_ulp_close(out, z["mel"])
+    assert exact >= 0.995 and within, (exact, worst)
+
+
+def test_log_mel_matches_oracle_on_mixed_lengths(gpu_frontend):
+    from voiceagent_b200.workload import config0_clip, synthetic_waveform
+
+    rng = np.random.default_rng(5)
+    clips = [config0_clip(0), synthetic_waveform(2.3456, rng), rng.normal(0, 0.2, 201).astype(np.float32),
+             (synthetic_waveform(0.9, rng) * 1e-5).astype(np.float32), synthetic_waveform(12.0, rng)]
+    filters = np.asarray(gpu_frontend.extractor.mel_filters)
+    # scattered, out-of-order output columns with untouched gaps between them
+    frames = [c.size // 160 for c in clips]
+    columns, at = [], 7
+    for f in reversed(frames):
+        columns.insert(0, at)
+        at += f + 5
+    out, _ = _render(gpu_frontend, clips, columns=columns, width=at)
+    covered = torch.zeros(at, dtype=torch.bool)
+    for c, f, clip in zip(columns, frames, clips):
+        exact, within, worst = _bf16_ulp_close(out[:, c:c + f], K.log_mel(clip, filters))
+        assert exact >= 0.995 and within, (exact, worst, clip.size)
+        covered[c:c + f] = True
+    assert torch.isnan(out[:, ~covered.cuda()].float()).all()  # nothing written outside
+
+
+def test_log_mel_rejects_short_clips(gpu_frontend):
+    with pytest.raises(ValueError):
+        gpu_frontend(np.zeros(200, np.float32))

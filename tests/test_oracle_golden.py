@@ -225,3 +225,20 @@ def test_model_oracle_matches_hf_thinker():
     np.testing.assert_allclose(audio.numpy(), g["audio_features"], atol=2e-5, rtol=1e-4)
     tokens, _ = thinker.greedy(g["prompt"].tolist(), audio, steps=len(g["greedy"]))
     assert tokens == g["greedy"].tolist()
+
+
+def test_log_mel_oracle_matches_reference_frontend():
+    """oracle.log_mel (float64) vs the reference AudioFrontend (fp32 torch STFT)."""
+    z = load_npz("frontend.npz")
+    off = np.concatenate([[0], np.cumsum(z["lens"])])
+    col = np.concatenate([[0], np.cumsum(z["frames"])])
+    for i in range(len(z["lens"])):
+        want = z["mel"][:, col[i]:col[i + 1]]
+        got = K.log_mel(z["wave"][off[i]:off[i + 1]], z["mel_filters"])
+        assert got.shape == want.shape == (128, z["lens"][i] // 160)
+        assert np.abs(got - want).max() <= 5e-5
+
+
+def test_log_mel_oracle_rejects_clips_too_short_to_reflect():
+    with pytest.raises(ValueError):
+        K.log_mel(np.zeros(200, np.float32), np.zeros((201, 128)))

@@ -39,6 +39,9 @@ SIGNATURES: dict[str, tuple] = {
                                              c_int64, P, P]),
     "b200asr_rmsnorm": (c_int32, [P, P, P, c_float, c_int32, c_int32, P, P]),
     "b200asr_silu_mul": (c_int32, [P, c_int32, c_int32, P, P]),
+    "b200asr_log_mel_workspace_size": (c_size_t, [c_int32, c_int32]),
+    "b200asr_log_mel": (c_int32, [P, P, P, c_int32, c_int32, P, P, P, P, c_size_t, P, c_int64, P,
+                                  P, P]),
     "b200asr_paged_decode_workspace_size": (c_size_t, [c_int32, c_int32, c_int32, c_int32]),
     "b200asr_paged_decode": (c_int32, [P, c_int64, P, P, c_int32, c_int32, c_int32, c_int32,
                                        c_int32, P, P, c_int32, c_int32, c_int32, c_float, P,

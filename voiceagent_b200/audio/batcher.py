@@ -45,12 +45,19 @@ class PackedAudioBatch:
         return list(torch.split(packed, self.audio_token_lens, dim=0))
 
 
-def pack_audio_batch(mels: list[torch.Tensor], n_window_infer: int, device,
-                     chunk_frames: int = CHUNK_FRAMES) -> PackedAudioBatch:
-    """Pack per-request mel features ``(bins, frames)`` into one encoder batch."""
-    if not mels:
+def pack_audio_batch(items: list, n_window_infer: int, device, chunk_frames: int = CHUNK_FRAMES,
+                     renderer=None, error_flag: torch.Tensor | None = None) -> PackedAudioBatch:
+    """Pack per-request features into one encoder batch.
+
+    Each item is a mel tensor ``(bins, frames)`` or an ``AudioFeatures``; features whose
+    mel is still deferred (``mel is None``, waveform attached) are rendered on the GPU by
+    ``renderer`` (a ``GpuMelFrontend``) straight into the packed bf16 input.
+    """
+    if not items:
         raise ValueError("pack_audio_batch requires at least one request")
-    frames = [int(m.shape[-1]) for m in mels]
+    mels = [it if isinstance(it, torch.Tensor) else it.mel for it in items]
+    frames = [int(it.shape[-1]) if isinstance(it, torch.Tensor) else int(it.mel_frames)
+              for it in items]
     window = attention_window_tokens(n_window_infer, chunk_frames)
     tokens = [num_audio_tokens(f, chunk_frames) for f in frames]
     n_chunks = sum(num_chunks(f, chunk_frames) for f in frames)
@@ -68,13 +75,28 @@ def pack_audio_batch(mels: list[torch.Tensor], n_window_infer: int, device,
     base = np.repeat(np.arange(len(valid_np), dtype=np.int64) * TOKENS_PER_FULL_CHUNK, valid_np)
     offs = np.arange(base.size, dtype=np.int64) - np.repeat(np.cumsum(valid_np) - valid_np, valid_np)
     token_index = torch.from_numpy(base + offs).pin_memory().to(device, non_blocking=True)
-
     TRANSFERS["h2d"] += 8 * int(token_index.numel()) + 4 * len(frames) + sum(
-        m.numel() * m.element_size() for m in mels if not m.is_cuda)
-    mel = torch.cat([m.to(device, non_blocking=True) for m in mels], dim=-1)
-    if mel.dtype != torch.bfloat16:
-        mel = mel.to(torch.bfloat16)
-    mel = mel.contiguous()
+        m.numel() * m.element_size() for m in mels if m is not None and not m.is_cuda)
+
+    if all(m is not None for m in mels):
+        mel = torch.cat([m.to(device, non_blocking=True) for m in mels], dim=-1)
+        if mel.dtype != torch.bfloat16:
+            mel = mel.to(torch.bfloat16)
+        mel = mel.contiguous()
+    else:
+        if renderer is None:
+            raise ValueError("deferred mel features need a GPU frontend to render them")
+        bins = next((int(m.shape[0]) for m in mels if m is not None), renderer.num_mel_bins)
+        cols = np.concatenate([[0], np.cumsum(frames)]).astype(np.int64)
+        mel = torch.empty(bins, int(cols[-1]), dtype=torch.bfloat16, device=device)
+        deferred, where = [], []
+        for i, m in enumerate(mels):
+            if m is None:
+                deferred.append(items[i])
+                where.append(int(cols[i]))
+            else:
+                mel[:, cols[i]:cols[i + 1]].copy_(m.to(device, non_blocking=True))
+        TRANSFERS["h2d"] += renderer.render(deferred, mel, where, error_flag)
     mel_frames = torch.tensor(frames, dtype=torch.int32).pin_memory().to(device, non_blocking=True)
     out = {
         "chunk_lengths": torch.empty(n_chunks, dtype=torch.int64, device=device),

@@ -135,11 +135,16 @@ class EngineConfig:
     enable_prefix_cache: bool = True
     enforce_eager: bool = False
     frontend_threads: int = 8
+    # "gpu": log-mel on the GPU at encode time (b200asr_log_mel); "cpu": the host
+    # Whisper extractor per request, as the reference does.
+    frontend: str = "gpu"
     device: str = "cuda"
     dtype: Any = None
     model_config: Qwen3ASRConfig | None = None
 
     def __post_init__(self):
+        if self.frontend not in ("gpu", "cpu"):
+            raise ValueError(f"frontend must be 'gpu' or 'cpu', got {self.frontend!r}")
         if self.num_kvcache_blocks == 0 or self.num_kvcache_blocks < -1:
             raise ValueError("num_kvcache_blocks must be -1 or positive")
         if self.model_config is None:

@@ -19,13 +19,15 @@ class AudioRunner:
         self.config = config
         self.device = torch.device(config.device)
         self.n_window_infer = config.model_config.audio.n_window_infer
+        self.renderer = None  # GpuMelFrontend when requests defer their mel to the GPU
 
     @torch.inference_mode()
     def encode(self, requests: list[AsrRequest]) -> None:
         if not requests:
             return
-        batch = pack_audio_batch([r.features.mel for r in requests],
-                                 n_window_infer=self.n_window_infer, device=self.device)
+        batch = pack_audio_batch([r.features for r in requests],
+                                 n_window_infer=self.n_window_infer, device=self.device,
+                                 renderer=self.renderer)
         embeddings = self.model.encode_audio(batch)
         for request, embeds in zip(requests, embeddings):
             if embeds.size(0) != request.layout.audio_length:

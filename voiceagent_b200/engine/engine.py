@@ -17,7 +17,7 @@ from typing import Iterable, Sequence
 import numpy as np
 import torch
 
-from voiceagent_b200.audio.frontend import AudioFeatures, AudioFrontend
+from voiceagent_b200.audio.frontend import AudioFeatures, AudioFrontend, GpuMelFrontend
 from voiceagent_b200.audio.tokens import num_audio_tokens
 from voiceagent_b200.checkpoint import random_state_dict
 from voiceagent_b200.config import EngineConfig
@@ -70,7 +70,10 @@ class AsrEngine:
         if device.type == "cuda" and device.index is not None:
             torch.cuda.set_device(device)
         self._limit_frontend_threads()
-        self.frontend = AudioFrontend(self.config.model)
+        if self.config.frontend == "gpu":
+            self.frontend = GpuMelFrontend(self.config.model, device=device)
+        else:
+            self.frontend = AudioFrontend(self.config.model)
         self.prompt_builder = PromptBuilder(self.config.model_config.audio_token_id,
                                             self.config.model_config.stop_token_ids
                                             or (151643, 151645))
@@ -81,6 +84,8 @@ class AsrEngine:
         self.model_runner.capture_graphs()
         self.num_kvcache_blocks = num_blocks
         self.audio_runner = AudioRunner(self.model, self.config)
+        if isinstance(self.frontend, GpuMelFrontend):
+            self.audio_runner.renderer = self.frontend
         self.block_manager = BlockManager(num_blocks, self.config.kvcache_block_size,
                                           self.config.enable_prefix_cache)
         self.scheduler = Scheduler(self.config, self.block_manager)

@@ -245,3 +245,32 @@ def greedy_argmax(logits, out=None) -> torch.Tensor:
     check(lib.b200asr_greedy_argmax(_p(logits), logits.stride(0), batch, vocab, _p(out),
                                     _stream()), "greedy_argmax")
     return out
+
+
+# ------------------------------------------------------------------ frontend
+
+
+def log_mel_workspace_size(batch: int, total_frames: int) -> int:
+    return int(lib.b200asr_log_mel_workspace_size(batch, total_frames))
+
+
+def log_mel(waveform, cu_samples, frame_start, *, total_frames: int, tables, mel_filters,
+            filter_range, out, out_col, workspace, error_flag=None) -> None:
+    """Whisper log-mel of every clip into bf16 ``out[128, cols]`` (audio/frontend.py:71-94).
+
+    waveform f32 [S]; cu_samples i64 [B+1]; frame_start i32 [B+1]; out_col i32 [B]."""
+    _cuda(waveform, cu_samples, frame_start, tables, mel_filters, filter_range, out, out_col,
+          workspace)
+    _need(waveform.dtype == torch.float32 and waveform.is_contiguous(), "f32 contiguous waveform")
+    _need(cu_samples.dtype == torch.int64 and frame_start.dtype == torch.int32
+          and out_col.dtype == torch.int32 and filter_range.dtype == torch.int32,
+          "int64 cu_samples, int32 frame_start/out_col/filter_range")
+    _need(out.dtype == BF16 and out.dim() == 2 and out.shape[0] == 128 and out.stride(1) == 1,
+          "bf16 [128, cols] output with contiguous rows")
+    batch = cu_samples.numel() - 1
+    _count(2)  # log-mel + finish (plus a memset of the per-clip maxima)
+    check(lib.b200asr_log_mel(
+        _p(waveform), _p(cu_samples), _p(frame_start), batch, int(total_frames), _p(tables),
+        _p(mel_filters), _p(filter_range), _p(workspace),
+        workspace.numel() * workspace.element_size(), _p(out), out.stride(0), _p(out_col),
+        _p(error_flag), _stream()), "log_mel")
