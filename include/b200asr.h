@@ -54,6 +54,16 @@ enum {
 B200ASR_API int b200asr_version(void);
 B200ASR_API const char *b200asr_last_error(void);
 
+/* Programmatic dependent launch (no reference counterpart; default off). When on,
+ * the decode-path kernels (rmsnorm, qk_norm_rope_store, paged_decode, linear_small,
+ * silu_mul, store_kvcache, greedy_argmax) are launched so that each may begin its
+ * prologue -- shared-memory and TMEM set-up, tensor-map and weight loads -- while the
+ * previous kernel in the stream finishes; each waits for that kernel's results before
+ * reading them or writing global memory. A CUDA graph captured with it on keeps the
+ * overlap. Process-wide; set it before capturing graphs.                            */
+B200ASR_API void b200asr_set_pdl(int32_t enable);
+B200ASR_API int32_t b200asr_pdl_enabled(void);
+
 /* ---------------------------------------------------------------- packers ----
  * Replaces ModelRunner._prepare (engine/model_runner.py:183-233): builds the ragged
  * decoder metadata of a mixed prefill/decode batch on the GPU.
@@ -234,6 +244,19 @@ B200ASR_API int b200asr_varlen_attention(const void *q, int64_t q_row_stride, co
  * fp32, first index on ties, NaN counted as the maximum.                          */
 B200ASR_API int b200asr_greedy_argmax(const void *logits, int64_t row_stride, int32_t batch,
                           int32_t vocab, int64_t *out_ids, b200asr_stream_t stream);
+
+/* -------------------------------------------------------- decode linears ----
+ * The decoder's dense projections at decode batch sizes (qkv_proj / o_proj /
+ * gate_up_proj + SiluAndMul / down_proj of models/qwen3.py:20-69 and
+ * layers/activation.py:11-14, called from the CUDA-graph decode with 1..64 rows):
+ *   y[r, j] = sum_k x[r, k] * w[j, k]   (bf16 in/out, fp32 accumulation), r < m <= 64
+ * w is [n, k] row-major (k % 64 == 0, n % 128 == 0). With silu_inner = I > 0 the
+ * weight is the fused [gate; up] of 2I rows (I % 64 == 0) and
+ *   y[r, j] = bf16(bf16(silu(bf16(gate))) * bf16(up)),  j < I.
+ * No workspace; launches thread-block clusters (split-K reduced on chip).           */
+B200ASR_API int b200asr_linear_small(const void *x, int64_t x_row_stride, int32_t m, int32_t k,
+                         const void *w, int32_t n, int32_t silu_inner, void *y,
+                         int64_t y_row_stride, int32_t *error_flag, b200asr_stream_t stream);
 
 /* ------------------------------------------------------------- mel frontend ----
  * Replaces AudioFrontend.__call__ (audio/frontend.py:71-94), the stock Whisper log-mel

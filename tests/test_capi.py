@@ -114,3 +114,16 @@ def test_product_path_has_no_oracle_dependency():
     for path in (REPO / "voiceagent_b200").rglob("*.py"):
         text = path.read_text()
         assert "import oracle" not in text and "from oracle" not in text, path
+
+
+def test_linear_small_validates_on_the_host(lib):
+    dummy = ctypes.c_void_p(256)
+    assert lib.b200asr_linear_small(dummy, 1024, 65, 1024, dummy, 4096, 0, dummy, 4096, None,
+                                    None) == 1 and "64" in _err(lib)
+    assert lib.b200asr_linear_small(dummy, 1024, 8, 1000, dummy, 4096, 0, dummy, 4096, None,
+                                    None) == 1 and "multiple" in _err(lib)
+    assert lib.b200asr_linear_small(dummy, 1024, 8, 1024, dummy, 4000, 0, dummy, 4096, None,
+                                    None) == 1
+    assert lib.b200asr_linear_small(dummy, 1024, 8, 1024, dummy, 6000, 3000, dummy, 3000, None,
+                                    None) == 1 and "SiLU" in _err(lib)
+    assert lib.b200asr_linear_small(None, 0, 0, 1024, None, 128, 0, None, 0, None, None) == 0

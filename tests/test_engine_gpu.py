@@ -110,6 +110,20 @@ def test_gpu_frontend_matches_host_frontend(tiny_dir, clips):
     assert same / total >= 0.99, same / total
 
 
+def test_pdl_launches_do_not_change_tokens(tiny_dir, clips):
+    """Programmatic dependent launch only overlaps prologues: tokens are identical."""
+    from voiceagent_b200 import kernels as kx
+
+    try:
+        with_pdl = _run(_engine(tiny_dir, pdl=True), clips)
+        assert kx.pdl_enabled()
+        without = _run(_engine(tiny_dir, pdl=False), clips)
+        assert not kx.pdl_enabled()
+    finally:
+        kx.set_pdl(False)
+    assert [o.output_token_ids for o in with_pdl] == [o.output_token_ids for o in without]
+
+
 def test_graph_decode_equals_eager(tiny_dir, clips):
     eager = _run(_engine(tiny_dir, enforce_eager=True), clips)
     graphed_engine = _engine(tiny_dir)

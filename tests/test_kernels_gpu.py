@@ -539,3 +539,83 @@ def test_log_mel_matches_oracle_on_mixed_lengths(gpu_frontend):
 def test_log_mel_rejects_short_clips(gpu_frontend):
     with pytest.raises(ValueError):
         gpu_frontend(np.zeros(200, np.float32))
+
+
+# ------------------------------------------------------------------ decode linears
+
+
+def _close_to(got, ref, rel=1e-2):
+    """bf16 GEMM output vs an fp32 reference of the same math."""
+    scale = ref.abs().max().item()
+    err = (got.float() - ref).abs()
+    ulp_ok = (got.float() == ref.bfloat16().float()).float().mean().item()
+    return err.max().item() <= rel * scale and err.mean().item() <= 2e-3 * scale, ulp_ok
+
+
+@pytest.mark.parametrize("m,k,n", [(1, 1024, 4096), (7, 1024, 1024), (32, 2048, 1024),
+                                   (32, 3072, 1024), (33, 1024, 4096), (64, 2048, 2048),
+                                   (16, 6144, 2048)])
+def test_linear_small_matches_fp32_matmul(kx, m, k, n):
+    g = torch.Generator(device="cuda").manual_seed(m * 7 + k + n)
+    base = torch.randn(m, k + 64, device="cuda", generator=g).bfloat16()
+    x = base[:, :k]  # row stride k + 64: a strided view
+    w = (torch.randn(n, k, device="cuda", generator=g) * k ** -0.5).bfloat16()
+    y = kx.linear_small(x, w)
+    ref = x.float() @ w.float().T
+    ok, exact = _close_to(y, ref)
+    assert ok and exact >= 0.98, exact
+
+
+@pytest.mark.parametrize("m,k,inner", [(1, 1024, 3072), (32, 1024, 3072), (64, 2048, 6144)])
+def test_linear_small_fused_silu_mul(kx, m, k, inner):
+    import torch.nn.functional as F
+
+    g = torch.Generator(device="cuda").manual_seed(m + inner)
+    x = torch.randn(m, k, device="cuda", generator=g).bfloat16()
+    w = (torch.randn(2 * inner, k, device="cuda", generator=g) * k ** -0.5).bfloat16()
+    y = kx.linear_small(x, w, silu=True)
+    proj = (x.float() @ w.float().T).bfloat16().float()  # the unfused path's bf16 projection
+    gate, up = proj[:, :inner], proj[:, inner:]
+    ref = (F.silu(gate).bfloat16().float() * up)
+    ok, exact = _close_to(y, ref, rel=2e-2)
+    assert y.shape == (m, inner) and ok and exact >= 0.97, exact
+
+
+def test_linear_small_lm_head_width(kx):
+    g = torch.Generator(device="cuda").manual_seed(3)
+    x = torch.randn(32, 1024, device="cuda", generator=g).bfloat16()
+    w = (torch.randn(151936, 1024, device="cuda", generator=g) * 0.03).bfloat16()
+    y = kx.linear_small(x, w)
+    ok, exact = _close_to(y, x.float() @ w.float().T)
+    assert ok and exact >= 0.98, exact
+
+
+def test_linear_small_chain_with_pdl_in_a_graph(kx):
+    """Dependent linear_small / rmsnorm launches with PDL, captured in a graph, give the
+    same bytes as without PDL (the waits order every read after its producer)."""
+    g = torch.Generator(device="cuda").manual_seed(9)
+    x = torch.randn(32, 1024, device="cuda", generator=g).bfloat16()
+    ws = [(torch.randn(1024, 1024, device="cuda", generator=g) * 0.03).bfloat16() for _ in range(6)]
+    nw = torch.ones(1024, device="cuda", dtype=torch.bfloat16)
+
+    def chain():
+        h = x
+        for w in ws:
+            h = kx.rmsnorm(kx.linear_small(h, w), nw, 1e-6)
+        return h
+
+    outs = []
+    for pdl in (False, True):
+        kx.set_pdl(pdl)
+        try:
+            chain()
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                y = chain()
+            graph.replay()
+            torch.cuda.synchronize()
+            outs.append(y.clone())
+        finally:
+            kx.set_pdl(False)
+    assert torch.equal(outs[0], outs[1])

@@ -25,6 +25,8 @@ P = c_void_p  # every pointer (device memory or stream) crosses as void*
 SIGNATURES: dict[str, tuple] = {
     "b200asr_version": (c_int32, []),
     "b200asr_last_error": (c_char_p, []),
+    "b200asr_set_pdl": (None, [c_int32]),
+    "b200asr_pdl_enabled": (c_int32, []),
     "b200asr_pack_decoder": (c_int32, [P, P, P, P, P, P, c_int32, c_int32, c_int32, c_int32,
                                        P, P, P, P, P, P, P, P, P]),
     "b200asr_pack_decode_bucket": (c_int32, [P, P, P, P, P, c_int32, c_int32, c_int32, c_int32,
@@ -39,6 +41,8 @@ SIGNATURES: dict[str, tuple] = {
                                              c_int64, P, P]),
     "b200asr_rmsnorm": (c_int32, [P, P, P, c_float, c_int32, c_int32, P, P]),
     "b200asr_silu_mul": (c_int32, [P, c_int32, c_int32, P, P]),
+    "b200asr_linear_small": (c_int32, [P, c_int64, c_int32, c_int32, P, c_int32, c_int32, P,
+                                       c_int64, P, P]),
     "b200asr_log_mel_workspace_size": (c_size_t, [c_int32, c_int32]),
     "b200asr_log_mel": (c_int32, [P, P, P, c_int32, c_int32, P, P, P, P, c_size_t, P, c_int64, P,
                                   P, P]),

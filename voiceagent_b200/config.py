@@ -138,6 +138,9 @@ class EngineConfig:
     # "gpu": log-mel on the GPU at encode time (b200asr_log_mel); "cpu": the host
     # Whisper extractor per request, as the reference does.
     frontend: str = "gpu"
+    # Programmatic dependent launch between the decode-path kernels (overlaps each
+    # kernel's launch and prologue with its predecessor, also inside CUDA graphs).
+    pdl: bool = True
     device: str = "cuda"
     dtype: Any = None
     model_config: Qwen3ASRConfig | None = None

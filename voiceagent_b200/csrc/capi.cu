@@ -1,4 +1,5 @@
 // C-ABI plumbing: error reporting, version, TMA tensor-map encoding.
+#include <atomic>
 #include <mutex>
 
 #include "common.cuh"
@@ -6,6 +7,9 @@
 namespace b200asr {
 
 static thread_local std::string g_last_error;
+static std::atomic<int> g_pdl{0};
+
+bool pdl_enabled() { return g_pdl.load(std::memory_order_relaxed) != 0; }
 
 void set_error(const char *fmt, ...) {
   char buf[512];
@@ -83,5 +87,9 @@ bool make_tmap_3d_bf16(CUtensorMap *map, const void *base, uint64_t d0, uint64_t
 }  // namespace b200asr
 
 extern "C" int b200asr_version(void) { return 100; }
+
+extern "C" void b200asr_set_pdl(int32_t enable) { b200asr::g_pdl.store(enable ? 1 : 0); }
+
+extern "C" int32_t b200asr_pdl_enabled(void) { return b200asr::pdl_enabled() ? 1 : 0; }
 
 extern "C" const char *b200asr_last_error(void) { return b200asr::g_last_error.c_str(); }

@@ -45,7 +45,58 @@ void set_error(const char *fmt, ...);  // defined in capi.cu (thread-local messa
 
 inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// ---------------------------------------------------- programmatic dependent launch
+// With PDL on (b200asr_set_pdl), the decode-path kernels are launched with the
+// programmatic-stream-serialization attribute: a kernel may start while its predecessor
+// in the stream is still running. Each such kernel calls pdl_trigger() first (letting its
+// own successor launch early) and pdl_wait() in every thread before it reads data that
+// an earlier kernel produced or writes global memory; before that it only sets up shared
+// memory, tensor maps, TMEM and loads of static data (weights). Without the attribute
+// both instructions are no-ops.
+bool pdl_enabled();  // defined in capi.cu
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                          cudaStream_t stream, bool pdl, unsigned cluster_x, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  unsigned n = 0;
+  if (pdl && pdl_enabled()) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  if (cluster_x > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = cluster_x;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
+#define B200_LAUNCH_CHECK_ERR(err, what)                                             \
+  do {                                                                             \
+    cudaError_t e__ = (err);                                                       \
+    if (e__ != cudaSuccess) {                                                      \
+      ::b200asr::set_error("%s: launch failed: %s", what, cudaGetErrorString(e__)); \
+      return B200ASR_ERR_CUDA;                                                     \
+    }                                                                              \
+  } while (0)
+
 // ------------------------------------------------------------------ device math
+
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 __device__ __forceinline__ float bf2f(__nv_bfloat16 x) { return __bfloat162float(x); }
 __device__ __forceinline__ __nv_bfloat16 f2bf(float x) { return __float2bfloat16_rn(x); }

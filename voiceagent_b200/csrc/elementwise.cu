@@ -22,6 +22,8 @@ __global__ void store_kvcache_kernel(const __nv_bfloat16 *__restrict__ key, int6
                                      __nv_bfloat16 *__restrict__ v_cache,
                                      const int32_t *__restrict__ slot_mapping, int num_tokens,
                                      int hidden, int64_t num_slots, int32_t *error_flag) {
+  pdl_trigger();
+  pdl_wait();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= 2 * num_tokens) return;
@@ -55,10 +57,12 @@ __global__ void qk_norm_rope_store_kernel(
     __nv_bfloat16 *__restrict__ v_cache, const int32_t *__restrict__ slot_mapping,
     int64_t num_slots, int32_t *error_flag) {
   constexpr int D = EPL * 32;
+  pdl_trigger();
   const int tasks_per_token = num_heads + 2 * num_kv_heads;
   const int64_t task = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (task >= static_cast<int64_t>(num_tokens) * tasks_per_token) return;
+  pdl_wait();
   const int t = static_cast<int>(task / tasks_per_token);
   const int j = static_cast<int>(task - static_cast<int64_t>(t) * tasks_per_token);
   const int kv_hidden = num_kv_heads * D;
@@ -152,9 +156,13 @@ __global__ void rmsnorm_kernel(const __nv_bfloat16 *__restrict__ x, __nv_bfloat1
                                const __nv_bfloat16 *__restrict__ weight, float eps, int hidden,
                                __nv_bfloat16 *__restrict__ out) {
   __shared__ float red[32];
+  pdl_trigger();
   const int64_t row = blockIdx.x;
   const int i8 = threadIdx.x;
   const bool active = i8 * 8 < hidden;
+  float w[8];
+  if (active) unpack8(*reinterpret_cast<const uint4 *>(weight + i8 * 8), w);  // static
+  pdl_wait();
   float v[8] = {0, 0, 0, 0, 0, 0, 0, 0};
   if (active) {
     unpack8(*reinterpret_cast<const uint4 *>(x + row * hidden + i8 * 8), v);
@@ -182,8 +190,6 @@ __global__ void rmsnorm_kernel(const __nv_bfloat16 *__restrict__ x, __nv_bfloat1
   __syncthreads();
   const float r = rsqrtf(red[0] / static_cast<float>(hidden) + eps);
   if (!active) return;
-  float w[8];
-  unpack8(*reinterpret_cast<const uint4 *>(weight + i8 * 8), w);
   float y[8];
 #pragma unroll
   for (int e = 0; e < 8; ++e) y[e] = bf2f(f2bf(bf2f(f2bf(v[e] * r)) * w[e]));
@@ -194,6 +200,8 @@ __global__ void rmsnorm_kernel(const __nv_bfloat16 *__restrict__ x, __nv_bfloat1
 // ------------------------------------------------------------------- SiLU*mul
 __global__ void silu_mul_kernel(const __nv_bfloat16 *__restrict__ x, int64_t rows, int inner,
                                 __nv_bfloat16 *__restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
   const int64_t n8 = rows * (inner / 8);
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n8;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -232,12 +240,13 @@ extern "C" int b200asr_store_kvcache(const void *key, int64_t key_row_stride, co
                hidden, (long long)key_row_stride, (long long)value_row_stride);
   const int64_t threads = 2LL * num_tokens * 32;
   const int block = 256;
-  store_kvcache_kernel<<<static_cast<unsigned>((threads + block - 1) / block), block, 0, stream>>>(
-      static_cast<const __nv_bfloat16 *>(key), key_row_stride,
-      static_cast<const __nv_bfloat16 *>(value), value_row_stride,
-      static_cast<__nv_bfloat16 *>(k_cache), static_cast<__nv_bfloat16 *>(v_cache), slot_mapping,
-      num_tokens, hidden, num_slots, error_flag);
-  B200_CUDA_LAUNCH_CHECK("store_kvcache");
+  B200_LAUNCH_CHECK_ERR(
+      launch_kernel(store_kvcache_kernel, dim3(static_cast<unsigned>((threads + block - 1) / block)),
+                    dim3(block), 0, stream, true, 1, static_cast<const __nv_bfloat16 *>(key),
+                    key_row_stride, static_cast<const __nv_bfloat16 *>(value), value_row_stride,
+                    static_cast<__nv_bfloat16 *>(k_cache), static_cast<__nv_bfloat16 *>(v_cache),
+                    slot_mapping, num_tokens, hidden, num_slots, error_flag),
+      "store_kvcache");
   return B200ASR_OK;
 }
 
@@ -263,14 +272,15 @@ extern "C" int b200asr_qk_norm_rope_store(
   const int block = 256;
   const unsigned grid = static_cast<unsigned>((warps * 32 + block - 1) / block);
   auto kfn = head_dim == 128 ? qk_norm_rope_store_kernel<4> : qk_norm_rope_store_kernel<2>;
-  kfn<<<grid, block, 0, stream>>>(
-      static_cast<const __nv_bfloat16 *>(qkv), qkv_row_stride, positions, num_tokens, num_heads,
-      num_kv_heads, static_cast<const __nv_bfloat16 *>(q_norm_weight),
-      static_cast<const __nv_bfloat16 *>(k_norm_weight), eps, cos_sin_cache, max_position,
-      static_cast<__nv_bfloat16 *>(q_out), q_out_row_stride, static_cast<__nv_bfloat16 *>(k_out),
-      static_cast<__nv_bfloat16 *>(k_cache), static_cast<__nv_bfloat16 *>(v_cache), slot_mapping,
-      num_slots, error_flag);
-  B200_CUDA_LAUNCH_CHECK("qk_norm_rope_store");
+  B200_LAUNCH_CHECK_ERR(
+      launch_kernel(kfn, dim3(grid), dim3(block), 0, stream, true, 1,
+                    static_cast<const __nv_bfloat16 *>(qkv), qkv_row_stride, positions, num_tokens,
+                    num_heads, num_kv_heads, static_cast<const __nv_bfloat16 *>(q_norm_weight),
+                    static_cast<const __nv_bfloat16 *>(k_norm_weight), eps, cos_sin_cache,
+                    max_position, static_cast<__nv_bfloat16 *>(q_out), q_out_row_stride,
+                    static_cast<__nv_bfloat16 *>(k_out), static_cast<__nv_bfloat16 *>(k_cache),
+                    static_cast<__nv_bfloat16 *>(v_cache), slot_mapping, num_slots, error_flag),
+      "qk_norm_rope_store");
   return B200ASR_OK;
 }
 
@@ -284,10 +294,12 @@ extern "C" int b200asr_rmsnorm(const void *x, void *residual, const void *weight
                    (residual == nullptr || aligned16(residual)),
                "rmsnorm: tensors must be 16-byte aligned");
   const int threads = ((hidden / 8) + 31) / 32 * 32;
-  rmsnorm_kernel<<<rows, threads, 0, stream>>>(
-      static_cast<const __nv_bfloat16 *>(x), static_cast<__nv_bfloat16 *>(residual),
-      static_cast<const __nv_bfloat16 *>(weight), eps, hidden, static_cast<__nv_bfloat16 *>(out));
-  B200_CUDA_LAUNCH_CHECK("rmsnorm");
+  B200_LAUNCH_CHECK_ERR(
+      launch_kernel(rmsnorm_kernel, dim3(rows), dim3(threads), 0, stream, true, 1,
+                    static_cast<const __nv_bfloat16 *>(x), static_cast<__nv_bfloat16 *>(residual),
+                    static_cast<const __nv_bfloat16 *>(weight), eps, hidden,
+                    static_cast<__nv_bfloat16 *>(out)),
+      "rmsnorm");
   return B200ASR_OK;
 }
 
@@ -299,8 +311,10 @@ extern "C" int b200asr_silu_mul(const void *x, int32_t rows, int32_t inner, void
   B200_REQUIRE(x && out && aligned16(x) && aligned16(out), "silu_mul: null or unaligned pointer");
   const int64_t n8 = static_cast<int64_t>(rows) * (inner / 8);
   const unsigned grid = static_cast<unsigned>(std::min<int64_t>((n8 + 255) / 256, 148 * 32));
-  silu_mul_kernel<<<grid, 256, 0, stream>>>(static_cast<const __nv_bfloat16 *>(x), rows, inner,
-                                            static_cast<__nv_bfloat16 *>(out));
-  B200_CUDA_LAUNCH_CHECK("silu_mul");
+  B200_LAUNCH_CHECK_ERR(
+      launch_kernel(silu_mul_kernel, dim3(grid), dim3(256), 0, stream, true, 1,
+                    static_cast<const __nv_bfloat16 *>(x), static_cast<int64_t>(rows), inner,
+                    static_cast<__nv_bfloat16 *>(out)),
+      "silu_mul");
   return B200ASR_OK;
 }

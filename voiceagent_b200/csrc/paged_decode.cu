@@ -250,7 +250,7 @@ __global__ void __launch_bounds__(Dec<HKV, G>::THREADS, 1)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int B = a.batch;
 
-  for (int i = tid; i <= B; i += blockDim.x) s_cuk[i] = a.cu_seqlens_k[i];
+  pdl_trigger();
   if (tid == 0) {
     abort_flag = 0;
     s_npending = 0;
@@ -264,6 +264,8 @@ __global__ void __launch_bounds__(Dec<HKV, G>::THREADS, 1)
     prefetch_tmap(&tm_k);
     prefetch_tmap(&tm_v);
   }
+  pdl_wait();  // q, the new token's K/V and the batch metadata come from earlier kernels
+  for (int i = tid; i <= B; i += blockDim.x) s_cuk[i] = a.cu_seqlens_k[i];
   __syncthreads();
 
   if (warp == HKV) {
@@ -593,8 +595,9 @@ int launch_decode(const DecodeArgs &a, const void *k_cache, const void *v_cache,
       !make_tmap_bf16(&tv, v_cache, 4, dims, strides, box))
     return B200ASR_ERR_CUDA;
   const int grid = std::min(num_sms(), kDecMaxGrid);
-  paged_decode_kernel<HKV, G><<<grid, C::THREADS, C::SMEM, stream>>>(tk, tv, a);
-  B200_CUDA_LAUNCH_CHECK("paged_decode");
+  B200_LAUNCH_CHECK_ERR(launch_kernel(paged_decode_kernel<HKV, G>, dim3(grid), dim3(C::THREADS),
+                                      C::SMEM, stream, true, 1, tk, tv, a),
+                        "paged_decode");
   return B200ASR_OK;
 }
 

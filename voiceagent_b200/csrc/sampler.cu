@@ -37,6 +37,8 @@ __global__ void __cluster_dims__(kArgmaxCluster, 1, 1) __launch_bounds__(kArgmax
                          int64_t *__restrict__ out_ids) {
   __shared__ Best warp_best[kArgmaxThreads / 32];
   __shared__ Best cta_best;
+  pdl_trigger();
+  pdl_wait();
   cg::cluster_group cluster = cg::this_cluster();
   const int rank = static_cast<int>(cluster.block_rank());
   const int row = blockIdx.y;
@@ -114,8 +116,9 @@ extern "C" int b200asr_greedy_argmax(const void *logits, int64_t row_stride, int
   B200_REQUIRE(batch <= 65535, "greedy_argmax: batch %d too large", batch);
   B200_REQUIRE(logits && out_ids, "greedy_argmax: null pointer");
   dim3 grid(kArgmaxCluster, batch);
-  greedy_argmax_kernel<<<grid, kArgmaxThreads, 0, stream>>>(
-      static_cast<const __nv_bfloat16 *>(logits), row_stride, vocab, out_ids);
-  B200_CUDA_LAUNCH_CHECK("greedy_argmax");
+  B200_LAUNCH_CHECK_ERR(launch_kernel(greedy_argmax_kernel, grid, dim3(kArgmaxThreads), 0,
+                                      stream, true, 1, static_cast<const __nv_bfloat16 *>(logits),
+                                      row_stride, vocab, out_ids),
+                        "greedy_argmax");
   return B200ASR_OK;
 }

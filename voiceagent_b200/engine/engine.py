@@ -17,6 +17,7 @@ from typing import Iterable, Sequence
 import numpy as np
 import torch
 
+from voiceagent_b200 import kernels as kx
 from voiceagent_b200.audio.frontend import AudioFeatures, AudioFrontend, GpuMelFrontend
 from voiceagent_b200.audio.tokens import num_audio_tokens
 from voiceagent_b200.checkpoint import random_state_dict
@@ -70,6 +71,7 @@ class AsrEngine:
         if device.type == "cuda" and device.index is not None:
             torch.cuda.set_device(device)
         self._limit_frontend_threads()
+        kx.set_pdl(self.config.pdl)  # before any graph capture
         if self.config.frontend == "gpu":
             self.frontend = GpuMelFrontend(self.config.model, device=device)
         else:
@@ -84,6 +86,7 @@ class AsrEngine:
         self.model_runner.capture_graphs()
         self.num_kvcache_blocks = num_blocks
         self.audio_runner = AudioRunner(self.model, self.config)
+        self.model.audio_tower.warm_up()
         if isinstance(self.frontend, GpuMelFrontend):
             self.audio_runner.renderer = self.frontend
         self.block_manager = BlockManager(num_blocks, self.config.kvcache_block_size,
@@ -116,6 +119,9 @@ class AsrEngine:
             load_tensors(model, random_state_dict(preset, seed).items(), prefixed=False)
         else:
             raise ValueError(f"unknown weights source {weights!r}")
+        for module in model.modules():  # the encoder's convolutions run channels-last
+            if isinstance(module, torch.nn.Conv2d):
+                module.to(memory_format=torch.channels_last)
         return model.eval()
 
     def _limit_frontend_threads(self) -> None:

@@ -14,6 +14,7 @@ import numpy as np
 import torch
 
 from voiceagent_b200 import kernels as kx
+from voiceagent_b200.shapes import padded_rows
 from voiceagent_b200.config import EngineConfig
 from voiceagent_b200.engine.graph_runner import GraphRunner
 from voiceagent_b200.engine.request import AsrRequest
@@ -154,10 +155,11 @@ class ModelRunner:
             [starts, ends, toffs, tlens, np.asarray(tables, np.int32),
              np.asarray(tokens, np.int32)])
         dev = self.device
+        rows = padded_rows(total)  # bucketed (shape-stable GEMMs); see voiceagent_b200.shapes
         out = {
-            "input_ids": torch.empty(total, dtype=torch.int64, device=dev),
-            "positions": torch.empty(total, dtype=torch.int64, device=dev),
-            "slot_mapping": torch.empty(total, dtype=torch.int32, device=dev),
+            "input_ids": torch.empty(rows, dtype=torch.int64, device=dev),
+            "positions": torch.empty(rows, dtype=torch.int64, device=dev),
+            "slot_mapping": torch.empty(rows, dtype=torch.int32, device=dev),
             "cu_seqlens_q": torch.empty(n + 1, dtype=torch.int32, device=dev),
             "cu_seqlens_k": torch.empty(n + 1, dtype=torch.int32, device=dev),
             "max_seqlen": torch.empty(2, dtype=torch.int32, device=dev),
@@ -166,6 +168,10 @@ class ModelRunner:
         }
         kx.pack_decoder(d_start, d_end, d_toff, d_tlen, d_tables, d_tokens, total_tokens=total,
                         width=width, block_size=self.block_size, out=out)
+        if rows > total:  # padding rows: token 0 at position 0, never stored (slot -1)
+            out["input_ids"][total:].zero_()
+            out["positions"][total:].zero_()
+            out["slot_mapping"][total:].fill_(-1)
         max_q = int((ends - starts).max())
         decode_only = max_q == 1 and n <= self.config.max_num_seqs
         ctx = AttentionContext(
@@ -219,7 +225,12 @@ class ModelRunner:
 
     def _forward_eager(self, batch: ModelBatch) -> torch.Tensor:
         hidden, packed = self._forward_hidden(batch)
-        return self.model.compute_logits(hidden.index_select(0, packed["last_token_index"]))
+        last = packed["last_token_index"]
+        n = last.numel()
+        rows = padded_rows(n)
+        if rows > n:  # bucketed lm_head rows; the extra rows repeat row 0 and are dropped
+            last = torch.cat([last, last[:1].expand(rows - n)])
+        return self.model.compute_logits(hidden.index_select(0, last))[:n]
 
     def _sample(self, logits: torch.Tensor, requests) -> list[int]:
         temps = [r.sampling.temperature for r in requests]

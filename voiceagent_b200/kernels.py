@@ -184,11 +184,14 @@ def paged_decode_workspace_size(batch: int, max_seqlen_k: int, num_heads: int,
 
 def paged_decode(q, k_cache, v_cache, cu_seqlens_k, block_tables, *, max_seqlen_k: int,
                  scale: float, out, workspace, error_flag=None) -> torch.Tensor:
-    """One-token paged decode (split-K). q/out: [B, H, D]; caches [N, bs, Hkv, D]."""
+    """One-token paged decode (split-K). q/out: [>= B, H, D] (rows past B, e.g. bucket
+    padding, are left alone); B = cu_seqlens_k.numel() - 1; caches [N, bs, Hkv, D]."""
     _cuda(q, k_cache, v_cache, cu_seqlens_k, block_tables, out, workspace)
-    batch, num_heads, head_dim = q.shape
+    rows, num_heads, head_dim = q.shape
+    batch = cu_seqlens_k.numel() - 1
     num_blocks, block_size, num_kv_heads, _ = k_cache.shape
     _need(block_tables.dtype == torch.int32 and cu_seqlens_k.dtype == torch.int32, "int32 metadata")
+    _need(batch <= rows and batch <= block_tables.shape[0], "cu_seqlens_k longer than the batch")
     _count()  # one stream-K launch; the merge is fused into it
     check(lib.b200asr_paged_decode(
         _p(q), q.stride(0), _p(k_cache), _p(v_cache), num_blocks, block_size, num_heads,
@@ -274,3 +277,46 @@ def log_mel(waveform, cu_samples, frame_start, *, total_frames: int, tables, mel
         _p(mel_filters), _p(filter_range), _p(workspace),
         workspace.numel() * workspace.element_size(), _p(out), out.stride(0), _p(out_col),
         _p(error_flag), _stream()), "log_mel")
+
+
+# ------------------------------------------------------------------- linears
+
+LINEAR_SMALL_MAX_ROWS = 64
+
+
+def linear_small_ok(x, weight, silu: bool = False) -> bool:
+    """Whether ``linear_small`` takes this projection (decode batch sizes, aligned dims)."""
+    if x.dim() != 2 or x.dtype != BF16 or weight.dtype != BF16 or not weight.is_contiguous():
+        return False
+    m, k = x.shape
+    n = weight.shape[0]
+    if not (1 <= m <= LINEAR_SMALL_MAX_ROWS and k % 64 == 0 and weight.shape[1] == k
+            and x.stride(1) == 1 and x.stride(0) % 8 == 0):
+        return False
+    return (n % 2 == 0 and (n // 2) % 64 == 0) if silu else n % 128 == 0
+
+
+def linear_small(x, weight, *, silu: bool = False, out=None, error_flag=None) -> torch.Tensor:
+    """``x @ weight.T`` for 1..64 rows on tcgen05 (fused SiLU*mul when ``silu``)."""
+    _cuda(x, weight)
+    _need(linear_small_ok(x, weight, silu), "linear_small: unsupported shape/layout")
+    m, k = x.shape
+    n = weight.shape[0]
+    cols = n // 2 if silu else n
+    if out is None:
+        out = torch.empty(m, cols, dtype=BF16, device=x.device)
+    _count()
+    check(lib.b200asr_linear_small(_p(x), x.stride(0), m, k, _p(weight), n, cols if silu else 0,
+                                   _p(out), out.stride(0), _p(error_flag), _stream()),
+          "linear_small")
+    return out
+
+
+
+def set_pdl(enable: bool) -> None:
+    """Programmatic dependent launch for the decode-path kernels (process-wide)."""
+    lib.b200asr_set_pdl(1 if enable else 0)
+
+
+def pdl_enabled() -> bool:
+    return bool(lib.b200asr_pdl_enabled())

@@ -5,6 +5,13 @@ Differences from the reference, all numerically neutral: the chunk padding is th
 (``qkv_proj`` = [q | k | v] rows, loaded from the checkpoint's three tensors), the
 valid-token gather uses host-known indices instead of a boolean mask (no device
 sync), and window attention is the tcgen05 ``varlen_attention`` kernel.
+
+The convolutional downsampler runs on groups of a few fixed sizes (8, 16, 32 or 64
+chunks, the last group zero-padded) in channels-last layout. Every encode batch has a
+different chunk count, and cuDNN builds an execution plan per new input shape -- tens
+of milliseconds of host time that dwarfed the few milliseconds of GPU work; with fixed
+group shapes the plans are built once. Chunks are independent through the convolutions
+(padding only ever adds whole zero chunks), so the grouping does not change results.
 """
 
 from __future__ import annotations
@@ -19,6 +26,7 @@ from voiceagent_b200 import kernels as kx
 from voiceagent_b200.audio.batcher import PackedAudioBatch
 from voiceagent_b200.config import AudioEncoderConfig
 from voiceagent_b200.layers.attention import VarlenSelfAttention
+from voiceagent_b200.shapes import padded_rows
 
 
 def sinusoid_table(length: int, channels: int, max_timescale: float = 10000.0) -> torch.Tensor:
@@ -89,27 +97,57 @@ class AudioEncoder(nn.Module):
         self.proj1 = nn.Linear(config.d_model, config.d_model)
         self.proj2 = nn.Linear(config.d_model, config.output_dim)
 
-    def _downsample(self, padded: torch.Tensor) -> torch.Tensor:
+    CONV_GROUPS = (8, 16, 32, 64)  # chunk counts of the conv launches (shape-stable)
+
+    @classmethod
+    def conv_rows(cls, num_chunks: int) -> int:
+        """Rows to allocate for ``num_chunks`` chunks: whole fixed-size groups."""
+        g = cls.conv_group(num_chunks)
+        return -(-num_chunks // g) * g
+
+    @classmethod
+    def conv_group(cls, num_chunks: int) -> int:
+        return next((g for g in cls.CONV_GROUPS if g >= num_chunks), cls.CONV_GROUPS[-1])
+
+    def _downsample(self, padded: torch.Tensor, num_chunks: int) -> torch.Tensor:
+        g = self.conv_group(num_chunks)
         outs = []
-        for part in padded.split(self.config.conv_chunksize, dim=0):
-            h = F.gelu(self.conv2d1(part))
+        for part in padded.split(g, dim=0):
+            h = F.gelu(self.conv2d1(part.contiguous(memory_format=torch.channels_last)))
             h = F.gelu(self.conv2d2(h))
             outs.append(F.gelu(self.conv2d3(h)))
         x = torch.cat(outs, dim=0) if len(outs) > 1 else outs[0]
+        x = x[:num_chunks]
         n, c, f, t = x.shape
         return self.conv_out(x.permute(0, 3, 1, 2).reshape(n, t, c * f))
 
     @torch.inference_mode()
+    def warm_up(self) -> None:
+        """Build the cuDNN plans of every conv group shape once, at engine start."""
+        p = next(self.parameters())
+        for g in self.CONV_GROUPS:
+            self._downsample(torch.zeros(g, 1, self.config.num_mel_bins, self.chunk_frames,
+                                         dtype=p.dtype, device=p.device), g)
+
+    @torch.inference_mode()
     def forward(self, batch: PackedAudioBatch) -> torch.Tensor:
         """Encode a packed batch into (total audio tokens, output_dim)."""
-        padded = torch.empty(batch.num_chunks, self.config.num_mel_bins, self.chunk_frames,
+        rows = self.conv_rows(batch.num_chunks)
+        padded = torch.empty(rows, self.config.num_mel_bins, self.chunk_frames,
                              dtype=batch.mel.dtype, device=batch.mel.device)
+        if rows > batch.num_chunks:
+            padded[batch.num_chunks:].zero_()
         kx.audio_chunk_pad(batch.mel, batch.chunk_start, batch.chunk_lengths, batch.num_chunks,
                            self.chunk_frames, padded)
-        embed = self._downsample(padded.unsqueeze(1))
+        embed = self._downsample(padded.unsqueeze(1), batch.num_chunks)
         embed = embed + self.positional_embedding[: embed.shape[1]].unsqueeze(0).to(embed.dtype)
-        hidden = embed.reshape(-1, embed.shape[-1]).index_select(0, batch.token_index)
+        flat = embed.reshape(-1, embed.shape[-1])
+        t = batch.token_index.numel()
+        # bucketed row count (shape-stable GEMMs); rows t.. are zeros that attention never
+        # reads (cu_seqlens covers the first t) and that are dropped at the end
+        hidden = flat.new_zeros(padded_rows(t), flat.shape[-1])
+        torch.index_select(flat, 0, batch.token_index, out=hidden[:t])
         for layer in self.layers:
             hidden = layer(hidden, batch.cu_seqlens, batch.max_seqlen)
-        hidden = self.ln_post(hidden)
+        hidden = self.ln_post(hidden[:t])
         return self.proj2(F.gelu(self.proj1(hidden)))

@@ -1,8 +1,10 @@
 """Qwen3 text decoder (models/qwen3.py of the reference).
 
-Dense projections stay on torch matmul (cuBLAS). Per layer the b200asr kernels do:
-input / post-attention RMSNorm (the latter fused with the residual add), per-head
-q/k RMSNorm + RoPE fused with the KV-cache store, paged attention and SiLU*mul.
+Per layer the b200asr kernels do: input / post-attention RMSNorm (the latter fused
+with the residual add), per-head q/k RMSNorm + RoPE fused with the KV-cache store,
+paged attention and SiLU*mul. Dense projections run on torch matmul (cuBLAS) for
+prefill-sized batches and on the weight-streaming ``linear_small`` kernel for decode
+batches of up to 64 rows, where gate_up_proj also applies SiLU*mul in its epilogue.
 """
 
 from __future__ import annotations
@@ -15,6 +17,13 @@ from voiceagent_b200.config import TextConfig
 from voiceagent_b200.layers.attention import PagedAttention
 from voiceagent_b200.layers.context import get_attention_context
 from voiceagent_b200.layers.norm import RMSNorm, SiluAndMul
+
+
+def project(x: torch.Tensor, layer: nn.Linear) -> torch.Tensor:
+    """``layer(x)``: decode-size batches on ``linear_small``, larger ones on cuBLAS."""
+    if layer.bias is None and kx.linear_small_ok(x, layer.weight):
+        return kx.linear_small(x, layer.weight, error_flag=get_attention_context().error_flag)
+    return layer(x)
 
 
 class Qwen3Attention(nn.Module):
@@ -37,7 +46,7 @@ class Qwen3Attention(nn.Module):
 
     def forward(self, positions: torch.Tensor, hidden_states: torch.Tensor) -> torch.Tensor:
         ctx = get_attention_context()
-        qkv = self.qkv_proj(hidden_states)
+        qkv = project(hidden_states, self.qkv_proj)
         t = qkv.shape[0]
         q = torch.empty(t, self.num_heads, self.head_dim, dtype=qkv.dtype, device=qkv.device)
         # q/k RMSNorm + RoPE; K and V go straight into the paged cache.
@@ -47,7 +56,7 @@ class Qwen3Attention(nn.Module):
             eps=self.eps, cos_sin_cache=self.rope.table, q_out=q, k_cache=self.attn.k_cache,
             v_cache=self.attn.v_cache, slot_mapping=ctx.slot_mapping, error_flag=ctx.error_flag)
         attn_out = self.attn(q)
-        return self.o_proj(attn_out.view(t, self.q_size))
+        return project(attn_out.view(t, self.q_size), self.o_proj)
 
 
 class Qwen3MLP(nn.Module):
@@ -60,7 +69,12 @@ class Qwen3MLP(nn.Module):
         self.act_fn = SiluAndMul()
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        return self.down_proj(self.act_fn(self.gate_up_proj(x)))
+        w = self.gate_up_proj.weight
+        if kx.linear_small_ok(x, w, silu=True):  # SiLU*mul fused into the projection
+            act = kx.linear_small(x, w, silu=True, error_flag=get_attention_context().error_flag)
+        else:
+            act = self.act_fn(self.gate_up_proj(x))
+        return project(act, self.down_proj)
 
 
 class Qwen3DecoderLayer(nn.Module):

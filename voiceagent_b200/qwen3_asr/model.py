@@ -13,7 +13,7 @@ from torch import nn
 from voiceagent_b200.audio.batcher import PackedAudioBatch
 from voiceagent_b200.config import Qwen3ASRConfig
 from voiceagent_b200.qwen3_asr.audio_encoder import AudioEncoder
-from voiceagent_b200.qwen3_asr.decoder import Qwen3Model
+from voiceagent_b200.qwen3_asr.decoder import Qwen3Model, project
 
 
 class Qwen3ASRForConditionalGeneration(nn.Module):
@@ -44,4 +44,4 @@ class Qwen3ASRForConditionalGeneration(nn.Module):
         return self.model(input_ids, positions, inputs_embeds=inputs_embeds)
 
     def compute_logits(self, hidden_states: torch.Tensor) -> torch.Tensor:
-        return self.lm_head(hidden_states)
+        return project(hidden_states, self.lm_head)
