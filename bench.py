@@ -188,68 +188,15 @@ def ncu_traffic() -> int | None:
 # ------------------------------------------------------------------ roofline
 
 
-def decode_roofline(torch, device, iters: int = 64, warm: int = 8, sets: int = 4) -> dict:
-    """Config 1 paged decode kernel timed back to back with CUDA events on its stream.
+def decode_roofline(torch, device) -> dict:
+    """Config 1 paged decode kernel, timed live (voiceagent_b200.microbench.decode_config1:
+    CUDA events around a graph of back-to-back launches over rotating KV sets > L2)."""
+    from voiceagent_b200.microbench import decode_config1
 
-    ``sets`` batches with the same lengths but disjoint KV blocks rotate, so every launch
-    streams keys and values that the previous ``sets - 1`` launches did not touch: 4 x 75 MB
-    exceeds the 126 MB L2, and no launch finds its KV rows cached (the block tables and
-    lengths, a few KB, stay in L2 as they do after the packer in a real decode step).
-    """
-    from voiceagent_b200 import kernels as kx
-
-    rng = np.random.default_rng(0)
-    b, h, hkv, d, nb = 32, 16, 8, 128, 4096
-    lens = rng.integers(64, 1025, size=b)
-    need = int(sum((lens + 255) // 256))
-    gen = torch.Generator(device=device).manual_seed(0)
-    kc = (torch.randn(nb, 256, hkv, d, device=device, generator=gen) / d ** 0.5).bfloat16()
-    vc = (torch.randn(nb, 256, hkv, d, device=device, generator=gen) / d ** 0.5).bfloat16()
-    q = (torch.randn(b, h, d, device=device, generator=gen) / d ** 0.5).bfloat16()
-    perm = rng.permutation(nb)
-    assert sets * need <= nb
-    cu = torch.from_numpy(np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)).to(device)
-    tables = []
-    for k in range(sets):
-        t = np.zeros((b, 16), np.int32)
-        c = k * need
-        for i, n in enumerate(lens):
-            m = (int(n) + 255) // 256
-            t[i, :m] = perm[c:c + m]
-            c += m
-        tables.append(torch.from_numpy(t).to(device))
-    out = torch.empty_like(q)
-    ws = torch.zeros(kx.paged_decode_workspace_size(b, 4096, h) // 4 + 64, dtype=torch.float32,
-                     device=device)
-    stream = torch.cuda.current_stream()  # replays run here
-
-    def op(i):
-        kx.paged_decode(q, kc, vc, cu, tables[i % sets], max_seqlen_k=4096, scale=d ** -0.5,
-                        out=out, workspace=ws)
-
-    for i in range(warm):
-        op(i)
-    torch.cuda.synchronize()
-    graph = torch.cuda.CUDAGraph()  # the launches replay without host overhead between them
-    with torch.cuda.graph(graph):
-        for i in range(iters):
-            op(i)
-    graph.replay()
-    torch.cuda.synchronize()
-    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s.record(stream)
-    graph.replay()
-    e.record(stream)
-    e.synchronize()
-    ms = s.elapsed_time(e) / iters
-    del graph
-    sumctx = int(lens.sum())
-    algo = sumctx * hkv * d * 2 * 2 + 2 * b * h * d * 2 + 4 * need + 4 * b
-    del kc, vc
-    torch.cuda.empty_cache()
-    return {"ms": ms, "algo_bytes": algo, "sum_ctx": sumctx, "launches": iters,
-            "l2": f"CUDA events around a graph of {iters} back-to-back launches over {sets} rotating "
-                  f"KV sets of {algo / 1e6:.0f} MB each (together > L2)"}
+    with torch.cuda.device(device):
+        r = decode_config1()
+    return {"ms": r["us"] / 1000.0, "algo_bytes": r["algo_bytes"], "sum_ctx": r["sum_ctx"],
+            "l2": r["timing"]}
 
 
 # ----------------------------------------------------------------- workloads

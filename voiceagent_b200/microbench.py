@@ -1,0 +1,378 @@
+"""Per-kernel microbenchmarks of the hot path on one B200.
+
+    python -m voiceagent_b200.microbench [--only decode prefill ...]
+
+prints one JSON line per kernel configuration: device time per launch, algorithmic
+bytes (and FLOPs for the attention contractions), achieved GB/s (TFLOP/s) and the
+fraction of the measured peaks in MEASURED_PEAKS.json (copy bandwidth; cuBLAS bf16
+GEMM burst throughput). Timing: the launches are captured back to back in a CUDA
+graph and timed with CUDA events around a replay (no host gaps); kernels that stream
+HBM rotate over input sets that together exceed the 126 MB L2, so no launch finds
+its inputs cached. Latency-bound kernels (packers, decode-size rows) are reported
+the same way and labelled ``latency``.
+
+Workloads follow the reference's benchmark configurations: config 1 (paged decode,
+B = 32, ctx ~ U[64, 1024], 4096-block pool), config 2 (32 clips of U(2, 30) s: the
+decoder prefill over L = 13 s + 24 tokens each and the encoder's 104-token windows),
+and the config-3 decode step shapes (32 rows, Qwen3-ASR-0.6B projections).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+from pathlib import Path
+
+import numpy as np
+import torch
+
+from voiceagent_b200 import kernels as kx
+from voiceagent_b200.audio.tokens import attention_window_tokens, num_audio_tokens
+
+REPO = Path(__file__).resolve().parents[1]
+L2_BYTES = 126 * 2**20
+
+
+def measured_peaks() -> dict:
+    path = REPO / "MEASURED_PEAKS.json"
+    if path.exists():
+        d = json.loads(path.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+def graph_time_us(launches, reps: int = 3) -> float:
+    """Mean device time per callable when ``launches`` replay back to back in a graph."""
+    for f in launches:
+        f()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for f in launches:
+            f()
+    graph.replay()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(reps):
+        graph.replay()
+    e.record()
+    e.synchronize()
+    del graph
+    return s.elapsed_time(e) * 1000.0 / reps / len(launches)
+
+
+def _line(kernel, config, us, nbytes, flops=None, bound="hbm", **extra) -> dict:
+    peaks = measured_peaks()
+    out = {"kernel": kernel, "config": config, "us": round(us, 3), "algo_bytes": int(nbytes),
+           "gbs": round(nbytes / us / 1e3, 1), "frac_hbm": round(nbytes / us / 1e3 / peaks["hbm_gbs"], 4),
+           "bound": bound, "peak_source": peaks["source"]}
+    if flops is not None:
+        tf = flops / us / 1e6
+        out.update(flops=int(flops), tflops=round(tf, 1), frac_tensor=round(tf / peaks["bf16_tflops"], 4))
+    out.update(extra)
+    return out
+
+
+def _sets(per_set_bytes: int) -> int:
+    return max(2, -(-2 * L2_BYTES // max(per_set_bytes, 1)))
+
+
+# ------------------------------------------------------------------ config 1
+
+
+def decode_config1(iters: int = 64, sets: int = 4) -> dict:
+    """Paged decode, config 1: B = 32, ctx ~ U[64, 1024], 4096-block pool (2 GiB per K/V),
+    block tables = slices of a random permutation; ``sets`` disjoint table sets rotate."""
+    dev = torch.device("cuda")
+    rng = np.random.default_rng(0)
+    b, h, hkv, d, nb = 32, 16, 8, 128, 4096
+    lens = rng.integers(64, 1025, size=b)
+    need = int(sum((lens + 255) // 256))
+    gen = torch.Generator(device=dev).manual_seed(0)
+    kc = (torch.randn(nb, 256, hkv, d, device=dev, generator=gen) / d ** 0.5).bfloat16()
+    vc = (torch.randn(nb, 256, hkv, d, device=dev, generator=gen) / d ** 0.5).bfloat16()
+    q = (torch.randn(b, h, d, device=dev, generator=gen) / d ** 0.5).bfloat16()
+    perm = rng.permutation(nb)
+    cu = torch.from_numpy(np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)).to(dev)
+    tables = []
+    for k in range(sets):
+        t = np.zeros((b, 16), np.int32)
+        c = k * need
+        for i, n in enumerate(lens):
+            m = (int(n) + 255) // 256
+            t[i, :m] = perm[c:c + m]
+            c += m
+        tables.append(torch.from_numpy(t).to(dev))
+    out = torch.empty_like(q)
+    ws = torch.zeros(kx.paged_decode_workspace_size(b, 4096, h) // 4 + 64, dtype=torch.float32,
+                     device=dev)
+
+    def op(i):
+        return lambda: kx.paged_decode(q, kc, vc, cu, tables[i % sets], max_seqlen_k=4096,
+                                       scale=d ** -0.5, out=out, workspace=ws)
+
+    us = graph_time_us([op(i) for i in range(iters)])
+    sumctx = int(lens.sum())
+    algo = sumctx * hkv * d * 2 * 2 + 2 * b * h * d * 2 + 4 * need + 4 * b
+    del kc, vc
+    torch.cuda.empty_cache()
+    return _line("paged_decode", "config1 B=32 ctx~U[64,1024] Hq16/Hkv8 d128", us, algo,
+                 sum_ctx=sumctx, timing=f"graph of {iters} launches over {sets} rotating KV sets "
+                                           f"of {algo / 1e6:.0f} MB each (together > L2)")
+
+
+# ------------------------------------------------------------------ config 2
+
+
+def _config2_lengths():
+    rng = np.random.default_rng(0)
+    secs = rng.uniform(2.0, 30.0, size=32)
+    dec = [num_audio_tokens(int(100 * s)) + 24 for s in secs]
+    enc = [num_audio_tokens(int(100 * s)) for s in secs]
+    return dec, enc
+
+
+def prefill_config2() -> dict:
+    """Varlen causal GQA prefill over the paged cache, config 2 decoder lengths."""
+    dev = torch.device("cuda")
+    lens, _ = _config2_lengths()
+    t = sum(lens)
+    nblk = [(n + 255) // 256 for n in lens]
+    per_set = t * (16 + 8 + 8 + 16) * 128 * 2
+    sets = _sets(per_set)
+    gen = torch.Generator(device=dev).manual_seed(1)
+    cu = torch.from_numpy(np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)).to(dev)
+    runs = []
+    for k in range(sets):
+        q = torch.randn(t, 16, 128, device=dev, generator=gen).bfloat16()
+        kc = torch.randn(sum(nblk) + 1, 256, 8, 128, device=dev, generator=gen).bfloat16()
+        vc = torch.randn_like(kc)
+        tb = np.zeros((32, max(nblk)), np.int32)
+        c = 0
+        for i, n in enumerate(nblk):
+            tb[i, :n] = np.arange(c, c + n)
+            c += n
+        out = torch.empty_like(q)
+        runs.append((q, kc, vc, torch.from_numpy(tb).to(dev), out))
+
+    def op(r):
+        q, kc, vc, tb, out = r
+        return lambda: kx.paged_prefill(q, kc, vc, cu, cu, tb, max_seqlen_q=max(lens),
+                                        scale=128 ** -0.5, out=out)
+
+    us = graph_time_us([op(runs[i % sets]) for i in range(4 * sets)])
+    flops = sum(4096 * n * (n + 1) for n in lens)  # causal QK^T + PV, 16 heads, d 128
+    return _line("paged_prefill", "config2 decoder 32 prompts L=13s+24, s~U(2,30), Hq16/Hkv8 d128",
+                 us, per_set, flops=flops, bound="hbm (below the bf16 ridge)", tokens=t,
+                 timing=f"graph over {sets} rotating input sets of {per_set / 1e6:.0f} MB")
+
+
+def _window_bounds(tokens, window: int) -> np.ndarray:
+    """cu_seqlens of the encoder's attention windows: each clip cut into ``window``-token
+    segments, the last one ragged (audio/batcher.py build_window_boundaries)."""
+    cu = [0]
+    for t in tokens:
+        full, rem = divmod(int(t), window)
+        base = cu[-1]
+        cu.extend(base + window * (i + 1) for i in range(full))
+        if rem:
+            cu.append(cu[-1] + rem)
+    return np.asarray(cu, np.int32)
+
+
+def window_config2() -> dict:
+    """Encoder windowed bidirectional attention, config 2 clips (104-token windows)."""
+    dev = torch.device("cuda")
+    _, toks = _config2_lengths()
+    cuw = _window_bounds(toks, attention_window_tokens(800))
+    t = int(cuw[-1])
+    per_set = t * 4 * 896 * 2
+    sets = _sets(per_set)
+    gen = torch.Generator(device=dev).manual_seed(2)
+    cu = torch.from_numpy(cuw).to(dev)
+    runs = []
+    for _ in range(sets):
+        qkv = torch.randn(t, 3 * 896, device=dev, generator=gen).bfloat16()
+        views = [qkv[:, i * 896:(i + 1) * 896].unflatten(1, (14, 64)) for i in range(3)]
+        runs.append((views, torch.empty(t, 14, 64, device=dev, dtype=torch.bfloat16)))
+
+    def op(r):
+        (q, k, v), out = r
+        return lambda: kx.varlen_attention(q, k, v, cu, int(np.diff(cuw).max()), 64 ** -0.5, out=out)
+
+    us = graph_time_us([op(runs[i % sets]) for i in range(4 * sets)])
+    flops = sum(4 * int(w) * int(w) * 64 * 14 for w in np.diff(cuw))
+    return _line("varlen_window", "config2 encoder windows (104 tokens), 14 heads d64", us, per_set,
+                 flops=flops, bound="hbm", tokens=t, windows=len(cuw) - 1,
+                 timing=f"graph over {sets} rotating input sets of {per_set / 1e6:.0f} MB")
+
+
+# --------------------------------------------------------------- store / pack
+
+
+def store_rows(rows: int) -> dict:
+    dev = torch.device("cuda")
+    per_set = 4 * rows * 2048
+    sets = _sets(per_set) if rows >= 1024 else 8
+    nb = max(64, -(-rows * sets // 256) + 1)
+    kc = torch.zeros(nb, 256, 8, 128, device=dev, dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    runs = []
+    for k in range(sets):
+        qkv = torch.randn(rows, 4096, device=dev).bfloat16()
+        key = qkv[:, 2048:3072].unflatten(1, (8, 128))
+        val = qkv[:, 3072:].unflatten(1, (8, 128))
+        slots = torch.arange(k * rows, (k + 1) * rows, dtype=torch.int32, device=dev)
+        runs.append((key, val, slots))
+
+    def op(r):
+        key, val, slots = r
+        return lambda: kx.store_kvcache(key, val, kc, vc, slots)
+
+    us = graph_time_us([op(runs[i % sets]) for i in range(4 * sets)])
+    return _line("store_kvcache", f"{rows} rows x 8 KV heads x 128 (K and V)", us, per_set,
+                 bound="hbm" if rows >= 1024 else "latency")
+
+
+def qk_norm_rope_rows(rows: int) -> dict:
+    from voiceagent_b200.layers.norm import rope_table
+
+    dev = torch.device("cuda")
+    sets = 8 if rows < 1024 else 4
+    nb = -(-rows * sets // 256) + 1
+    kc = torch.zeros(nb, 256, 8, 128, device=dev, dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    table = rope_table(128, 4096, 1e6, None).to(dev)
+    qw = torch.ones(128, device=dev, dtype=torch.bfloat16)
+    runs = []
+    for k in range(sets):
+        qkv = torch.randn(rows, 4096, device=dev).bfloat16()
+        pos = torch.randint(0, 4096, (rows,), device=dev)
+        slots = torch.arange(k * rows, (k + 1) * rows, dtype=torch.int32, device=dev)
+        q = torch.empty(rows, 16, 128, device=dev, dtype=torch.bfloat16)
+        runs.append((qkv, pos, slots, q))
+
+    def op(r):
+        qkv, pos, slots, q = r
+        return lambda: kx.qk_norm_rope_store(qkv, pos, num_heads=16, num_kv_heads=8, head_dim=128,
+                                             q_weight=qw, k_weight=qw, eps=1e-6,
+                                             cos_sin_cache=table, q_out=q, k_cache=kc,
+                                             v_cache=vc, slot_mapping=slots)
+
+    us = graph_time_us([op(runs[i % sets]) for i in range(4 * sets)])
+    nbytes = rows * (4096 * 2 + 2048 * 2 + 2048 * 2 + 8 + 4)  # qkv in; q out; k,v to cache
+    return _line("qk_norm_rope_store", f"{rows} rows, 16/8 heads d128", us, nbytes,
+                 bound="hbm" if rows >= 1024 else "latency")
+
+
+def pack_decoder_batch() -> dict:
+    """Mixed prefill batch metadata: 32 requests, ~4200 query tokens (config 3 prefill)."""
+    dev = torch.device("cuda")
+    rng = np.random.default_rng(3)
+    n = 32
+    starts = np.zeros(n, np.int32)
+    ends = rng.integers(60, 260, size=n).astype(np.int32)
+    tlen = ((ends + 255) // 256).astype(np.int32)
+    toff = np.concatenate([[0], np.cumsum(tlen)[:-1]]).astype(np.int32)
+    tables = rng.permutation(4096)[:int(tlen.sum())].astype(np.int32)
+    total = int(ends.sum())
+    tokens = rng.integers(0, 150000, size=total).astype(np.int32)
+    d = [torch.from_numpy(a).to(dev) for a in (starts, ends, toff, tlen, tables, tokens)]
+    width = int(tlen.max())
+    out = {"input_ids": torch.empty(total, dtype=torch.int64, device=dev),
+           "positions": torch.empty(total, dtype=torch.int64, device=dev),
+           "slot_mapping": torch.empty(total, dtype=torch.int32, device=dev),
+           "cu_seqlens_q": torch.empty(n + 1, dtype=torch.int32, device=dev),
+           "cu_seqlens_k": torch.empty(n + 1, dtype=torch.int32, device=dev),
+           "max_seqlen": torch.empty(2, dtype=torch.int32, device=dev),
+           "block_tables": torch.empty(n, width, dtype=torch.int32, device=dev),
+           "last_token_index": torch.empty(n, dtype=torch.int64, device=dev)}
+    us = graph_time_us([lambda: kx.pack_decoder(*d, total_tokens=total, width=width,
+                                                block_size=256, out=out)] * 16)
+    nbytes = total * (8 + 8 + 4) + n * (width * 4 + 16) + total * 4 + n * 16 + int(tlen.sum()) * 4
+    return _line("pack_decoder", f"{n} requests, {total} query tokens", us, nbytes, bound="latency")
+
+
+def linear_decode(m: int = 32) -> list[dict]:
+    """Decode-step projections (0.6B shapes, ``m`` rows), 28 rotating layers of weights."""
+    dev = torch.device("cuda")
+    shapes = {"qkv_proj": (1024, 4096, False), "o_proj": (2048, 1024, False),
+              "gate_up_proj+silu": (1024, 6144, True), "down_proj": (3072, 1024, False)}
+    lines = []
+    for name, (k, n, silu) in shapes.items():
+        x = torch.randn(m, k, device=dev).bfloat16()
+        ws = [(torch.randn(n, k, device=dev) * 0.02).bfloat16() for _ in range(28)]
+        us = graph_time_us([(lambda w=w: kx.linear_small(x, w, silu=silu)) for w in ws])
+        nbytes = n * k * 2 + m * k * 2 + m * (n // 2 if silu else n) * 2
+        flops = 2 * m * n * k
+        lines.append(_line("linear_small", f"{name} m={m} k={k} n={n}", us, nbytes, flops=flops,
+                           bound="hbm (weight streaming)"))
+        del ws
+    torch.cuda.empty_cache()
+    return lines
+
+
+def argmax_rows(rows: int = 32) -> dict:
+    dev = torch.device("cuda")
+    per = rows * 151936 * 2
+    sets = _sets(per)
+    logits = [torch.randn(rows, 151936, device=dev).bfloat16() for _ in range(sets)]
+    out = torch.empty(rows, dtype=torch.int64, device=dev)
+    us = graph_time_us([(lambda l=l: kx.greedy_argmax(l, out=out)) for l in logits * 2])
+    return _line("greedy_argmax", f"{rows} x 151936 bf16 logits", us, per + rows * 8)
+
+
+def log_mel_config3() -> dict:
+    from voiceagent_b200.audio.frontend import GpuMelFrontend
+    from voiceagent_b200.workload import config3_clips
+
+    dev = torch.device("cuda")
+    fe = GpuMelFrontend(None)
+    clips = config3_clips(128, seed=0)
+    lens = np.asarray([c.size for c in clips], np.int64)
+    frames = lens // 160
+    wave = torch.from_numpy(np.concatenate(clips)).to(dev)
+    cu = torch.from_numpy(np.concatenate([[0], np.cumsum(lens)])).to(dev)
+    fs = torch.from_numpy(np.concatenate([[0], np.cumsum(frames)]).astype(np.int32)).to(dev)
+    col = fs[:-1].clone()
+    total = int(frames.sum())
+    out = torch.empty(128, total, device=dev, dtype=torch.bfloat16)
+    ws = torch.empty(kx.log_mel_workspace_size(len(clips), total), dtype=torch.uint8, device=dev)
+    us = graph_time_us([lambda: kx.log_mel(wave, cu, fs, total_frames=total, tables=fe.tables,
+                                           mel_filters=fe.filters, filter_range=fe.filter_range,
+                                           out=out, out_col=col, workspace=ws)] * 4)
+    nbytes = int(lens.sum()) * 4 + total * 128 * (2 + 4 + 4)  # waveform, out, scratch w+r
+    flops = total * (201 * 400 * 4 + 2 * 201 * 128)
+    return _line("log_mel (2 kernels)", f"config3 128 clips, {lens.sum() / 16000:.0f} s of audio",
+                 us, nbytes, flops=flops, bound="fp32 DFT on CUDA cores",
+                 audio_seconds_per_ms=round(float(lens.sum()) / 16000 / (us / 1000), 1))
+
+
+BENCHES = {
+    "decode": lambda: [decode_config1()],
+    "prefill": lambda: [prefill_config2()],
+    "window": lambda: [window_config2()],
+    "store": lambda: [store_rows(32), store_rows(8192)],
+    "rope": lambda: [qk_norm_rope_rows(32), qk_norm_rope_rows(4096)],
+    "pack": lambda: [pack_decoder_batch()],
+    "linear": lambda: linear_decode(32),
+    "argmax": lambda: [argmax_rows(32)],
+    "log_mel": lambda: [log_mel_config3()],
+}
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--only", nargs="*", choices=sorted(BENCHES), default=None)
+    args = ap.parse_args()
+    torch.cuda.set_device(0)
+    for name, fn in BENCHES.items():
+        if args.only and name not in args.only:
+            continue
+        for line in fn():
+            print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()
