@@ -74,48 +74,16 @@ def parse_args():
 
 
 def dist_env():
-    rank = int(os.environ.get("RANK", 0))
-    world = int(os.environ.get("WORLD_SIZE", 1))
-    local = int(os.environ.get("LOCAL_RANK", 0))
-    return rank, world, local
+    from voiceagent_b200.replicas import rank_env
+
+    return rank_env()
 
 
-class Dist:
-    def __init__(self):
-        import torch
+def Dist():
+    """The replicas' process group (NCCL; one rank per GPU)."""
+    from voiceagent_b200.replicas import ReplicaGroup
 
-        self.rank, self.world, self.local = dist_env()
-        self.torch = torch
-        self.pg = None
-        if self.world > 1:
-            import torch.distributed as dist
-
-            torch.cuda.set_device(self.local)
-            dist.init_process_group("nccl", timeout=timedelta(seconds=600),
-                                    device_id=torch.device("cuda", self.local))
-            self.pg = dist
-
-    def barrier(self):
-        if self.pg is not None:
-            self.pg.barrier()
-
-    def max(self, value: float) -> float:
-        if self.pg is None:
-            return value
-        t = self.torch.tensor([value], dtype=self.torch.float64, device="cuda")
-        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
-        return float(t.item())
-
-    def sum(self, value: float) -> float:
-        if self.pg is None:
-            return value
-        t = self.torch.tensor([value], dtype=self.torch.float64, device="cuda")
-        self.pg.all_reduce(t, op=self.pg.ReduceOp.SUM)
-        return float(t.item())
-
-    def close(self):
-        if self.pg is not None:
-            self.pg.destroy_process_group()
+    return ReplicaGroup("nccl")
 
 
 class ClockSampler:
