@@ -43,11 +43,38 @@ __global__ void store_kvcache_kernel(const __nv_bfloat16 *__restrict__ key, int6
 }
 
 // ------------------------------------------------------ QK norm + RoPE + store
-// One warp per (token, head-vector). Tasks 0..H-1: query heads; H..H+Hkv-1: key
-// heads; H+Hkv..H+2Hkv-1: value heads (plain copy into the cache).
-// Lane l holds EPL = head_dim/32 consecutive elements starting at l*EPL; the RoPE
+// A warp takes TPW consecutive (token, head-vector) tasks and issues all their loads
+// before computing: TPW = 4 for prefill-sized batches, where it keeps more loads in flight
+// per warp, and 1 for decode-sized ones, where spreading the few tasks over more warps is
+// what keeps the latency down. Task j of a token: 0..H-1
+// query heads, H..H+Hkv-1 key heads, H+Hkv..H+2Hkv-1 value heads (plain copy into the
+// cache). Lane l holds EPL = head_dim/32 consecutive elements starting at l*EPL; the RoPE
 // partner of element d (< D/2) is d + D/2, which lives in lane l ^ 16.
+
 template <int EPL>
+__device__ __forceinline__ void load_epl(const __nv_bfloat16 *src, float *x) {
+  if constexpr (EPL == 4) {
+    const uint2 u = *reinterpret_cast<const uint2 *>(src);
+    x[0] = __uint_as_float(u.x << 16);
+    x[1] = __uint_as_float(u.x & 0xffff0000u);
+    x[2] = __uint_as_float(u.y << 16);
+    x[3] = __uint_as_float(u.y & 0xffff0000u);
+  } else {
+    const uint32_t u = *reinterpret_cast<const uint32_t *>(src);
+    x[0] = __uint_as_float(u << 16);
+    x[1] = __uint_as_float(u & 0xffff0000u);
+  }
+}
+
+template <int EPL>
+__device__ __forceinline__ void store_epl(__nv_bfloat16 *dst, const float *o) {
+  if constexpr (EPL == 4)
+    *reinterpret_cast<uint2 *>(dst) = make_uint2(pack2(o[0], o[1]), pack2(o[2], o[3]));
+  else
+    *reinterpret_cast<uint32_t *>(dst) = pack2(o[0], o[1]);
+}
+
+template <int EPL, int TPW>
 __global__ void qk_norm_rope_store_kernel(
     const __nv_bfloat16 *__restrict__ qkv, int64_t qkv_stride, const int64_t *__restrict__ positions,
     int num_tokens, int num_heads, int num_kv_heads, const __nv_bfloat16 *__restrict__ qw,
@@ -59,95 +86,87 @@ __global__ void qk_norm_rope_store_kernel(
   constexpr int D = EPL * 32;
   pdl_trigger();
   const int tasks_per_token = num_heads + 2 * num_kv_heads;
-  const int64_t task = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int64_t total = static_cast<int64_t>(num_tokens) * tasks_per_token;
+  const int64_t first = ((static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5) * TPW;
   const int lane = threadIdx.x & 31;
-  if (task >= static_cast<int64_t>(num_tokens) * tasks_per_token) return;
+  if (first >= total) return;
+  float wq[EPL], wk[EPL];  // static weights: before the wait
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) {
+    wq[e] = bf2f(qw[lane * EPL + e]);
+    wk[e] = bf2f(kw[lane * EPL + e]);
+  }
   pdl_wait();
-  const int t = static_cast<int>(task / tasks_per_token);
-  const int j = static_cast<int>(task - static_cast<int64_t>(t) * tasks_per_token);
   const int kv_hidden = num_kv_heads * D;
-  const __nv_bfloat16 *row = qkv + t * qkv_stride;
 
-  float x[EPL];
-  const __nv_bfloat16 *src = row + static_cast<int64_t>(j) * D + lane * EPL;
-  if constexpr (EPL == 4) {
-    const uint2 u = *reinterpret_cast<const uint2 *>(src);
-    x[0] = __uint_as_float(u.x << 16);
-    x[1] = __uint_as_float(u.x & 0xffff0000u);
-    x[2] = __uint_as_float(u.y << 16);
-    x[3] = __uint_as_float(u.y & 0xffff0000u);
-  } else {
+  int tok[TPW], head[TPW];
+  float x[TPW][EPL];
+  int64_t pos[TPW], slot[TPW];
 #pragma unroll
-    for (int e = 0; e < EPL; ++e) x[e] = bf2f(src[e]);
+  for (int i = 0; i < TPW; ++i) {  // every load of the warp's tasks first
+    const int64_t task = first + i < total ? first + i : first;
+    tok[i] = static_cast<int>(task / tasks_per_token);
+    head[i] = static_cast<int>(task - static_cast<int64_t>(tok[i]) * tasks_per_token);
+    load_epl<EPL>(qkv + tok[i] * qkv_stride + static_cast<int64_t>(head[i]) * D + lane * EPL, x[i]);
+    pos[i] = positions[tok[i]];
+    slot[i] = slot_mapping ? slot_mapping[tok[i]] : -1;
   }
-
-  if (j >= num_heads + num_kv_heads) {  // value head: copy into the cache
-    const int64_t slot = slot_mapping ? slot_mapping[t] : -1;
-    if (slot == -1) return;
-    if (slot < 0 || slot >= num_slots) {
-      if (lane == 0) raise_flag(error_flag, B200ASR_DEVERR_SLOT);
-      return;
+#pragma unroll
+  for (int i = 0; i < TPW; ++i) {
+    if (first + i >= total) break;
+    const int t = tok[i], j = head[i];
+    if (j >= num_heads + num_kv_heads) {  // value head: copy into the cache
+      if (slot[i] == -1) continue;
+      if (slot[i] < 0 || slot[i] >= num_slots) {
+        if (lane == 0) raise_flag(error_flag, B200ASR_DEVERR_SLOT);
+        continue;
+      }
+      const int h = j - num_heads - num_kv_heads;
+      store_epl<EPL>(v_cache + slot[i] * kv_hidden + h * D + lane * EPL, x[i]);
+      continue;
     }
-    const int h = j - num_heads - num_kv_heads;
-    __nv_bfloat16 *dst = v_cache + slot * kv_hidden + h * D + lane * EPL;
+    const bool is_q = j < num_heads;
+    float ss = 0.f;
 #pragma unroll
-    for (int e = 0; e < EPL; ++e) dst[e] = src[e];
-    return;
-  }
-
-  const bool is_q = j < num_heads;
-  const __nv_bfloat16 *w = is_q ? qw : kw;
-  float ss = 0.f;
+    for (int e = 0; e < EPL; ++e) ss += x[i][e] * x[i][e];
+    ss = warp_sum(ss);
+    const float r = rsqrtf(ss / static_cast<float>(D) + eps);
+    float y[EPL];
 #pragma unroll
-  for (int e = 0; e < EPL; ++e) ss += x[e] * x[e];
-  ss = warp_sum(ss);
-  const float r = rsqrtf(ss / static_cast<float>(D) + eps);
-  float y[EPL];
+    for (int e = 0; e < EPL; ++e) {
+      const float n = bf2f(f2bf(x[i][e] * r));                   // x.to(bf16)
+      y[e] = bf2f(f2bf(n * (is_q ? wq[e] : wk[e])));             // .mul_(weight)
+    }
+    int64_t p = pos[i];
+    if (p < 0 || p >= max_position) {
+      if (lane == 0) raise_flag(error_flag, B200ASR_DEVERR_POSITION);
+      p = 0;
+    }
+    const float *cs = cos_sin + p * D;
+    const bool first_half = lane < 16;
+    float o[EPL];
 #pragma unroll
-  for (int e = 0; e < EPL; ++e) {
-    const float n = bf2f(f2bf(x[e] * r));                      // x.to(bf16)
-    y[e] = bf2f(f2bf(n * bf2f(w[lane * EPL + e])));             // .mul_(weight)
+    for (int e = 0; e < EPL; ++e) {
+      const float partner = __shfl_xor_sync(0xffffffffu, y[e], 16);
+      const int dd = (lane & 15) * EPL + e;  // index within the half
+      const float c = cs[dd], sn = cs[D / 2 + dd];
+      // first*cos - second*sin | second*cos + first*sin, each product rounded (no FMA)
+      o[e] = first_half ? __fsub_rn(__fmul_rn(y[e], c), __fmul_rn(partner, sn))
+                        : __fadd_rn(__fmul_rn(y[e], c), __fmul_rn(partner, sn));
+    }
+    if (is_q) {
+      store_epl<EPL>(q_out + t * q_out_stride + static_cast<int64_t>(j) * D + lane * EPL, o);
+      continue;
+    }
+    const int h = j - num_heads;
+    if (k_out != nullptr) store_epl<EPL>(k_out + static_cast<int64_t>(t) * kv_hidden + h * D + lane * EPL, o);
+    if (slot[i] == -1) continue;
+    if (slot[i] < 0 || slot[i] >= num_slots) {
+      if (lane == 0) raise_flag(error_flag, B200ASR_DEVERR_SLOT);
+      continue;
+    }
+    store_epl<EPL>(k_cache + slot[i] * kv_hidden + h * D + lane * EPL, o);
   }
-  int64_t pos = positions[t];
-  if (pos < 0 || pos >= max_position) {
-    if (lane == 0) raise_flag(error_flag, B200ASR_DEVERR_POSITION);
-    pos = 0;
-  }
-  const float *cs = cos_sin + pos * D;
-  const bool first_half = lane < 16;
-  float o[EPL];
-#pragma unroll
-  for (int e = 0; e < EPL; ++e) {
-    const float partner = __shfl_xor_sync(0xffffffffu, y[e], 16);
-    const int dd = (lane & 15) * EPL + e;  // index within the half
-    const float c = cs[dd], s = cs[D / 2 + dd];
-    // first*cos - second*sin | second*cos + first*sin, each product rounded (no FMA)
-    o[e] = first_half ? __fsub_rn(__fmul_rn(y[e], c), __fmul_rn(partner, s))
-                      : __fadd_rn(__fmul_rn(y[e], c), __fmul_rn(partner, s));
-  }
-
-  __nv_bfloat16 *dst;
-  if (is_q) {
-    dst = q_out + t * q_out_stride + static_cast<int64_t>(j) * D + lane * EPL;
-#pragma unroll
-    for (int e = 0; e < EPL; ++e) dst[e] = f2bf(o[e]);
-    return;
-  }
-  const int h = j - num_heads;
-  if (k_out != nullptr) {
-    dst = k_out + static_cast<int64_t>(t) * kv_hidden + h * D + lane * EPL;
-#pragma unroll
-    for (int e = 0; e < EPL; ++e) dst[e] = f2bf(o[e]);
-  }
-  const int64_t slot = slot_mapping ? slot_mapping[t] : -1;
-  if (slot == -1) return;
-  if (slot < 0 || slot >= num_slots) {
-    if (lane == 0) raise_flag(error_flag, B200ASR_DEVERR_SLOT);
-    return;
-  }
-  dst = k_cache + slot * kv_hidden + h * D + lane * EPL;
-#pragma unroll
-  for (int e = 0; e < EPL; ++e) dst[e] = f2bf(o[e]);
 }
 
 // ------------------------------------------------------------------- RMSNorm
@@ -268,10 +287,18 @@ extern "C" int b200asr_qk_norm_rope_store(
                "qk_norm_rope_store: slot_mapping given without caches");
   B200_REQUIRE(qkv_row_stride % 4 == 0 && (reinterpret_cast<uintptr_t>(qkv) & 7) == 0,
                "qk_norm_rope_store: qkv rows must be 8-byte aligned");
-  const int64_t warps = static_cast<int64_t>(num_tokens) * (num_heads + 2 * num_kv_heads);
+  B200_REQUIRE(q_out_row_stride % 4 == 0 && (reinterpret_cast<uintptr_t>(q_out) & 7) == 0 &&
+                   (reinterpret_cast<uintptr_t>(k_out) & 7) == 0 &&
+                   (reinterpret_cast<uintptr_t>(k_cache) & 7) == 0 &&
+                   (reinterpret_cast<uintptr_t>(v_cache) & 7) == 0,
+               "qk_norm_rope_store: outputs must be 8-byte aligned (q_out rows too)");
+  const int64_t tasks = static_cast<int64_t>(num_tokens) * (num_heads + 2 * num_kv_heads);
+  const bool wide = num_tokens > 256;  // prefill-sized: 4 tasks per warp
+  const int64_t warps = wide ? (tasks + 3) / 4 : tasks;
   const int block = 256;
   const unsigned grid = static_cast<unsigned>((warps * 32 + block - 1) / block);
-  auto kfn = head_dim == 128 ? qk_norm_rope_store_kernel<4> : qk_norm_rope_store_kernel<2>;
+  auto kfn = head_dim == 128 ? (wide ? qk_norm_rope_store_kernel<4, 4> : qk_norm_rope_store_kernel<4, 1>)
+                             : (wide ? qk_norm_rope_store_kernel<2, 4> : qk_norm_rope_store_kernel<2, 1>);
   B200_LAUNCH_CHECK_ERR(
       launch_kernel(kfn, dim3(grid), dim3(block), 0, stream, true, 1,
                     static_cast<const __nv_bfloat16 *>(qkv), qkv_row_stride, positions, num_tokens,

@@ -18,6 +18,7 @@ namespace b200asr {
 
 constexpr int kArgmaxCluster = 8;
 constexpr int kArgmaxThreads = 512;
+constexpr int kArgmaxUnroll = 8;
 
 struct Best {
   float v;
@@ -52,21 +53,46 @@ __global__ void __cluster_dims__(kArgmaxCluster, 1, 1) __launch_bounds__(kArgmax
   float bv = -INFINITY;
   int bi = INT_MAX;
   const bool vec_ok = (row_stride % 8 == 0) && ((reinterpret_cast<uintptr_t>(logits) & 15) == 0);
-  for (int c = lo8 + threadIdx.x; c < hi8; c += blockDim.x) {
-    const int base = c * 8;
-    float v[8];
-    if (vec_ok && base + 8 <= vocab) {
-      unpack8(__ldg(reinterpret_cast<const uint4 *>(x + base)), v);
-    } else {
+  // kArgmaxUnroll 16-byte loads per thread are in flight before the first compare (the
+  // slice is a handful of loads per thread, so issuing them one by one would serialise
+  // that many DRAM round trips). Ties resolve by index, so the visiting order is free.
+  for (int c0 = lo8 + threadIdx.x; c0 < hi8; c0 += kArgmaxUnroll * blockDim.x) {
+    uint4 raw[kArgmaxUnroll];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) v[e] = base + e < vocab ? bf2f(x[base + e]) : -INFINITY;
+    for (int u = 0; u < kArgmaxUnroll; ++u) {
+      const int c = c0 + u * static_cast<int>(blockDim.x);
+      if (vec_ok && c < hi8 && c * 8 + 8 <= vocab)
+        raw[u] = __ldg(reinterpret_cast<const uint4 *>(x + c * 8));
     }
 #pragma unroll
-    for (int e = 0; e < 8; ++e)
-      if (base + e < vocab && better(v[e], base + e, bv, bi)) {
-        bv = v[e];
-        bi = base + e;
+    for (int u = 0; u < kArgmaxUnroll; ++u) {
+      const int c = c0 + u * static_cast<int>(blockDim.x);
+      if (c >= hi8) break;
+      const int base = c * 8;
+      float v[8];
+      if (vec_ok && base + 8 <= vocab) {
+        unpack8(raw[u], v);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[e] = base + e < vocab ? bf2f(x[base + e]) : -INFINITY;
       }
+      // Fast reject: a thread visits its indices in increasing order, so a vector can only
+      // change its best if it holds a strictly larger number or a NaN.
+      float m = v[0];
+      bool nan = v[0] != v[0];
+#pragma unroll
+      for (int e = 1; e < 8; ++e) {
+        m = fmaxf(m, v[e]);
+        nan |= v[e] != v[e];
+      }
+      if (!nan && !(m > bv)) continue;
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        if (base + e < vocab && better(v[e], base + e, bv, bi)) {
+          bv = v[e];
+          bi = base + e;
+        }
+    }
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
