@@ -619,3 +619,34 @@ def test_linear_small_chain_with_pdl_in_a_graph(kx):
         finally:
             kx.set_pdl(False)
     assert torch.equal(outs[0], outs[1])
+
+
+def test_paged_decode_reuses_its_workspace_across_calls(kx):
+    """Config-1-sized calls three times in a row on one workspace with different data: the
+    merge counters the kernel leaves behind must not leak into the next call."""
+    rng = np.random.default_rng(41)
+    b, h, hkv, d, nb = 32, 16, 8, 128, 320
+    ws = torch.zeros(kx.paged_decode_workspace_size(b, 4096, h) // 4 + 64, dtype=torch.float32,
+                     device="cuda")
+    for call in range(3):
+        lens = rng.integers(64, 1025, size=b)
+        kc = K.bf16_round(rng.standard_normal((nb, 256, hkv, d)).astype(np.float32) / 11.3)
+        vc = K.bf16_round(rng.standard_normal((nb, 256, hkv, d)).astype(np.float32) / 11.3)
+        q = K.bf16_round(rng.standard_normal((b, h, d)).astype(np.float32) / 11.3)
+        perm = rng.permutation(nb)
+        tables = np.zeros((b, 5), np.int32)
+        c = 0
+        for i, n in enumerate(lens):
+            m = (int(n) + 255) // 256
+            tables[i, :m] = perm[c:c + m]
+            c += m
+        cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+        out = torch.full((b, h, d), float("nan"), dtype=torch.bfloat16, device="cuda")
+        err = torch.zeros(1, dtype=torch.int32, device="cuda")
+        kx.paged_decode(bf16(q), bf16(kc), bf16(vc), dev(cu, torch.int32), dev(tables, torch.int32),
+                        max_seqlen_k=4096, scale=d ** -0.5, out=out, workspace=ws, error_flag=err)
+        ref = K.paged_attention(q, kc, vc, np.arange(b + 1), cu, tables, d ** -0.5)
+        e = np.abs(out.float().cpu().numpy() - ref)
+        assert err.item() == 0
+        assert e.max() <= ATOL_MAX and e.mean() <= ATOL_MEAN, (call, e.max())
+    assert int(ws[:4096 // 4].view(torch.int32).abs().sum().item()) == 0  # header left at zero
