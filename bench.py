@@ -61,6 +61,8 @@ def parse_args():
     p.add_argument("--clips-per-step", type=int, default=128)
     p.add_argument("--concurrency", type=int, default=32)
     p.add_argument("--decode-tokens", type=int, default=64)
+    p.add_argument("--decode-steps", type=int, default=4,
+                   help="decode steps per CUDA-graph call (EngineConfig.decode_steps)")
     p.add_argument("--preset", default="0.6b")
     p.add_argument("--cpu-sample-clips", type=int, default=2)
     p.add_argument("--no-cpu-baseline", action="store_true")
@@ -356,7 +358,7 @@ def run_ours(args) -> None:
     engine = AsrEngine(str(ckpt), weights="random", seed=0, device=f"cuda:{local}",
                        max_num_seqs=args.concurrency, max_model_len=4096,
                        max_num_batched_tokens=8192, max_audio_batch_size=args.concurrency,
-                       num_kvcache_blocks=1024)
+                       num_kvcache_blocks=1024, decode_steps=args.decode_steps)
     sampling = SamplingParams(max_new_tokens=args.decode_tokens, ignore_eos=True)
 
     clips = config3_clips(args.clips, seed=rank)

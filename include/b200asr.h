@@ -98,6 +98,15 @@ B200ASR_API int b200asr_pack_decode_bucket(const int32_t *lens, const int32_t *l
                                int32_t *cu_seqlens_k, int32_t *block_tables,
                                b200asr_stream_t stream);
 
+/* Advances the first four descriptor arrays of b200asr_pack_decode_bucket by one
+ * generated token, on the device: for rows with table_len > 0, lens += 1 and
+ * last_ids = (int32) sampled (the greedy_argmax output). Used to replay a decode
+ * graph several times in a row without a host round trip (the caller allocates the
+ * blocks those steps write ahead of time); no reference counterpart.              */
+B200ASR_API int b200asr_advance_decode_bucket(int32_t *lens, int32_t *last_ids,
+                                  const int32_t *table_len, const int64_t *sampled,
+                                  int32_t bucket, b200asr_stream_t stream);
+
 /* Replaces the metadata of pack_audio_batch (audio/batcher.py:101-141) and
  * num_audio_tokens/chunk_lengths_for (audio/tokens.py:30-52).
  *   mel_frames[b] > 0 for each request.

@@ -124,6 +124,16 @@ def test_pdl_launches_do_not_change_tokens(tiny_dir, clips):
     assert [o.output_token_ids for o in with_pdl] == [o.output_token_ids for o in without]
 
 
+def test_multi_step_decode_gives_the_same_tokens(tiny_dir, clips):
+    """Several graph replays per host round trip (device-side token feedback) vs one."""
+    multi_engine = _engine(tiny_dir, decode_steps=4)
+    multi = _run(multi_engine, clips)
+    single = _run(_engine(tiny_dir, decode_steps=1), clips)
+    assert [o.output_token_ids for o in multi] == [o.output_token_ids for o in single]
+    assert multi_engine.scheduler.stats.num_decoded_tokens == sum(
+        o.num_output_tokens - 1 for o in multi)  # every decode token was counted once
+
+
 def test_graph_decode_equals_eager(tiny_dir, clips):
     eager = _run(_engine(tiny_dir, enforce_eager=True), clips)
     graphed_engine = _engine(tiny_dir)

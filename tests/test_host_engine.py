@@ -339,3 +339,73 @@ def test_audio_token_accounting_matches_oracle():
         assert T.num_audio_tokens(f) == K.num_audio_tokens(f)
         assert T.chunk_lengths_for(f) == K.chunk_lengths_for(f)
     assert T.attention_window_tokens(800) == 104
+
+
+# ------------------------------------------------------------ multi-step decode
+
+
+def test_may_append_matches_reference_rule_and_is_idempotent():
+    manager = BlockManager(64, BS, enable_prefix_cache=False)
+    r = make_request(BS - 1)
+    manager.allocate(r)
+    for _ in range(3 * BS):
+        held = len(r.block_table)
+        r.append_token(7)
+        manager.may_append(r)
+        assert len(r.block_table) - held == (1 if len(r) % BS == 1 else 0)  # reference rule
+        manager.may_append(r)  # again: nothing more
+        assert len(r.block_table) == r.num_blocks
+
+
+def test_lookahead_blocks_cover_every_written_position():
+    manager = BlockManager(64, BS, enable_prefix_cache=False)
+    r = make_request(BS - 2)
+    manager.allocate(r)
+    for steps in (1, 2, 3, 4):
+        need = manager.blocks_ahead(r, steps)
+        assert need == max(0, -(-(len(r) + steps - 1) // BS) - len(r.block_table))
+    manager.append_ahead(r, 4)  # positions len-1 .. len+2 cross into the next block
+    assert len(r.block_table) * BS >= len(r) + 3
+    assert manager.blocks_ahead(r, 4) == 0
+
+
+def test_decode_steps_bounded_by_budget_length_blocks_and_cancel(config):
+    manager = BlockManager(64, BS)
+    scheduler = Scheduler(config(), manager)
+    a, b = make_request(60, max_new_tokens=10), make_request(70, max_new_tokens=3)
+    for r in (a, b):
+        start_decoding(scheduler, manager, r)
+    batch = scheduler.schedule_model()
+    assert batch.decode == [a, b]
+    assert scheduler.decode_steps_for(batch, 4, max_model_len=4096) == 3  # b: 3 tokens of budget
+    assert scheduler.decode_steps_for(batch, 4, max_model_len=len(a)) == 1  # model length
+    assert scheduler.decode_steps_for(batch, 1, max_model_len=4096) == 1
+    b.cancel_requested = True
+    assert scheduler.decode_steps_for(batch, 4, max_model_len=4096) == 1
+
+
+def test_multi_step_postprocess_equals_single_steps(config):
+    def run(multi):
+        manager = BlockManager(64, BS)
+        scheduler = Scheduler(config(), manager)
+        reqs = [make_request(BS - 2 + i, max_new_tokens=6) for i in range(3)]
+        for r in reqs:
+            start_decoding(scheduler, manager, r)
+        rng = np.random.default_rng(5)
+        tokens = [[int(t) for t in rng.integers(100, 200, size=3)] for _ in range(3)]
+        tokens[1][2] = 151645  # request 2 stops on EOS at the second step
+        batch = scheduler.schedule_model()
+        finished = []
+        if multi:
+            assert scheduler.decode_steps_for(batch, 3, max_model_len=4096) == 3
+            finished += scheduler.postprocess_steps(batch, tokens)
+        else:
+            for k in range(3):
+                step = [tokens[k][reqs.index(r)] for r in batch.decode]
+                finished += scheduler.postprocess(batch, step)
+                batch = scheduler.schedule_model()
+        state = [(list(r.token_ids), r.stage, len(r.block_table)) for r in reqs]
+        return state, [r.request_id - reqs[0].request_id for r in finished], manager.num_free_blocks
+    single, multi = run(False), run(True)
+    assert single == multi
+    assert multi[1] == [2]  # the EOS request finished; its third token was discarded

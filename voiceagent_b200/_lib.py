@@ -31,6 +31,7 @@ SIGNATURES: dict[str, tuple] = {
                                        P, P, P, P, P, P, P, P, P]),
     "b200asr_pack_decode_bucket": (c_int32, [P, P, P, P, P, c_int32, c_int32, c_int32, c_int32,
                                              P, P, P, P, P, P]),
+    "b200asr_advance_decode_bucket": (c_int32, [P, P, P, P, c_int32, P]),
     "b200asr_pack_audio": (c_int32, [P, c_int32, c_int32, c_int32, c_int32, c_int32,
                                      P, P, P, P, P, P, P, P]),
     "b200asr_audio_chunk_pad": (c_int32, [P, c_int32, c_int32, P, P, c_int32, c_int32, P, P]),

@@ -141,11 +141,17 @@ class EngineConfig:
     # Programmatic dependent launch between the decode-path kernels (overlaps each
     # kernel's launch and prologue with its predecessor, also inside CUDA graphs).
     pdl: bool = True
+    # Decode steps per CUDA-graph call when every running request can take them: the
+    # graph is replayed back to back with the sampled tokens fed back on the device and
+    # the host syncs once per call (1 = one host round trip per token).
+    decode_steps: int = 4
     device: str = "cuda"
     dtype: Any = None
     model_config: Qwen3ASRConfig | None = None
 
     def __post_init__(self):
+        if self.decode_steps < 1:
+            raise ValueError("decode_steps must be >= 1")
         if self.frontend not in ("gpu", "cpu"):
             raise ValueError(f"frontend must be 'gpu' or 'cpu', got {self.frontend!r}")
         if self.num_kvcache_blocks == 0 or self.num_kvcache_blocks < -1:

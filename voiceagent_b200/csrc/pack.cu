@@ -252,6 +252,23 @@ __global__ void audio_chunk_pad_kernel(const __nv_bfloat16 *__restrict__ mel, in
   }
 }
 
+// Advances a decode-bucket descriptor by one generated token on the device: for every
+// real row (non-empty block table) the length grows by one and the last token becomes
+// the one just sampled. Lets consecutive decode-graph replays run without a host round
+// trip when their block tables already cover the next positions.
+__global__ void advance_decode_bucket_kernel(int32_t *__restrict__ lens,
+                                             int32_t *__restrict__ last_ids,
+                                             const int32_t *__restrict__ table_len,
+                                             const int64_t *__restrict__ sampled, int bucket) {
+  pdl_trigger();
+  pdl_wait();
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < bucket && table_len[i] > 0) {
+    lens[i] += 1;
+    last_ids[i] = static_cast<int32_t>(sampled[i]);
+  }
+}
+
 }  // namespace b200asr
 
 using namespace b200asr;
@@ -300,6 +317,19 @@ extern "C" int b200asr_pack_decode_bucket(const int32_t *lens, const int32_t *la
       lens, last_ids, table_off, table_len, tables, batch, bucket, max_blocks, block_size,
       input_ids, positions, slot_mapping, cu_seqlens_k, block_tables);
   B200_CUDA_LAUNCH_CHECK("pack_decode_bucket");
+  return B200ASR_OK;
+}
+
+extern "C" int b200asr_advance_decode_bucket(int32_t *lens, int32_t *last_ids,
+                                             const int32_t *table_len, const int64_t *sampled,
+                                             int32_t bucket, b200asr_stream_t stream) {
+  B200_REQUIRE(bucket >= 0, "advance_decode_bucket: negative bucket");
+  if (bucket == 0) return B200ASR_OK;
+  B200_REQUIRE(lens && last_ids && table_len && sampled, "advance_decode_bucket: null pointer");
+  B200_LAUNCH_CHECK_ERR(launch_kernel(advance_decode_bucket_kernel, dim3((bucket + 127) / 128),
+                                      dim3(128), 0, stream, true, 1, lens, last_ids, table_len,
+                                      sampled, static_cast<int>(bucket)),
+                        "advance_decode_bucket");
   return B200ASR_OK;
 }
 

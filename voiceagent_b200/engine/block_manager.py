@@ -115,5 +115,18 @@ class BlockManager:
         return self.num_free_blocks >= (1 if len(request) % self.block_size == 1 else 0)
 
     def may_append(self, request: AsrRequest) -> None:
-        if len(request) % self.block_size == 1:
+        """Cover the position the next decode step writes (len - 1). Equivalent to the
+        reference's ``len % block_size == 1`` test, and a no-op when the block was
+        already taken ahead (multi-step decode)."""
+        if len(request.block_table) < request.num_blocks:
+            request.block_table.append(self._take_any().block_id)
+
+    def blocks_ahead(self, request: AsrRequest, steps: int) -> int:
+        """New blocks the positions written by ``steps`` decode steps need beyond those
+        already held (the step at length L writes position L - 1)."""
+        needed = -(-(len(request) + steps - 1) // self.block_size)
+        return max(0, needed - len(request.block_table))
+
+    def append_ahead(self, request: AsrRequest, steps: int) -> None:
+        for _ in range(self.blocks_ahead(request, steps)):
             request.block_table.append(self._take_any().block_id)

@@ -209,15 +209,25 @@ class AsrEngine:
         batch = self.scheduler.schedule_model()
         if batch:
             started = time.perf_counter()
+            steps = 1
+            if self.model_runner.can_use_graph(batch):
+                steps = self.scheduler.decode_steps_for(batch, self.model_runner.max_decode_steps,
+                                                        self.config.max_model_len)
             try:
-                token_ids = self.model_runner.run(batch)
+                if steps > 1:
+                    tokens = self.model_runner.run_steps(batch, steps)
+                else:
+                    token_ids = self.model_runner.run(batch)
             except OutOfMemoryError:
                 logger.warning("decoder step ran out of memory on %d requests; rolling back",
                                len(batch.requests))
                 self._recover_from_oom()
                 self.scheduler.on_model_oom(batch)
             else:
-                finished = self.scheduler.postprocess(batch, token_ids)
+                if steps > 1:
+                    finished = self.scheduler.postprocess_steps(batch, tokens)
+                else:
+                    finished = self.scheduler.postprocess(batch, token_ids)
                 self.scheduler.relax_limits()
             self.stage_seconds["model_step"] += time.perf_counter() - started
         return [self._finalize(r) for r in self.scheduler.drain_aborted() + finished]

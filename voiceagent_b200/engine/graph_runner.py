@@ -4,8 +4,10 @@ One graph per batch bucket. Each graph holds the WHOLE decode step: the
 ``pack_decode_bucket`` kernel (building input ids, positions, slot mapping,
 cu_seqlens_k and block tables from a static device descriptor), the 28-layer
 decoder with the split-K paged decode attention, the final norm, the lm_head GEMM
-and the greedy argmax. Per step the host fills a pinned descriptor, issues one
-host-to-device copy, replays, and reads back the bucket's token ids.
+and the greedy argmax, then advances the device descriptor by the sampled tokens
+(length + 1, last token). Per call the host fills a pinned descriptor, issues one
+host-to-device copy, replays ``steps`` times in a row (the blocks those steps write are
+allocated beforehand) and reads back the tokens of every step with one sync.
 
 Padding rows are encoded in the descriptor as (length 1, empty block table), which
 the packer turns into the reference's padding: slot -1, key length 1, an all-zero
@@ -57,7 +59,8 @@ class GraphRunner:
         self.cu_seqlens_k = torch.zeros(m + 1, dtype=torch.int32, device=dev)
         self.block_tables = torch.zeros(m, self.max_blocks, dtype=torch.int32, device=dev)
         self.token_ids = torch.zeros(m, dtype=torch.int64, device=dev)
-        self.host_tokens = torch.zeros(m, dtype=torch.int64, pin_memory=True)
+        self.max_steps = max(1, int(getattr(self.config, "decode_steps", 1)))
+        self.host_tokens = torch.zeros(self.max_steps, m, dtype=torch.int64, pin_memory=True)
         self.hidden: dict[int, torch.Tensor] = {}
         ws_bytes = kx.paged_decode_workspace_size(m, self.config.max_model_len,
                                                   self.config.model_config.text.num_attention_heads)
@@ -86,6 +89,7 @@ class GraphRunner:
         hidden = self.model(self.input_ids[:bucket], self.positions[:bucket])
         logits = self.model.compute_logits(hidden)
         kx.greedy_argmax(logits, out=self.token_ids[:bucket])
+        kx.advance_decode_bucket(lens, last_ids, tlen, self.token_ids[:bucket], bucket=bucket)
         return hidden
 
     def _fill_padding(self, start: int) -> None:
@@ -122,12 +126,16 @@ class GraphRunner:
         return None
 
     @torch.inference_mode()
-    def run(self, requests) -> list[int]:
-        """Replay one decode step for `requests`; returns their sampled token ids."""
+    def run(self, requests, steps: int = 1) -> list[int] | list[list[int]]:
+        """Replay ``steps`` decode steps for ``requests`` (their block tables must already
+        cover every position those steps write). Returns the sampled ids of the one step,
+        or one list per step when ``steps > 1``."""
         n = len(requests)
         bucket = self.bucket_for(n)
         if bucket is None:
             raise ValueError(f"no captured graph for a batch of {n}")
+        if not 1 <= steps <= self.max_steps:
+            raise ValueError(f"steps must be in [1, {self.max_steps}], got {steps}")
         m, h = self.max_batch, self._host_np
         cursor = 4 * m
         for i, r in enumerate(requests):
@@ -140,13 +148,16 @@ class GraphRunner:
             cursor += len(table)
         self._fill_padding(n)
         self.desc[:cursor].copy_(self.host_desc[:cursor], non_blocking=True)
-        self.graphs[bucket].replay()
-        kx.LAUNCHES["count"] += self.kernels_per_replay[bucket]
-        self.host_tokens[:n].copy_(self.token_ids[:n], non_blocking=True)
+        for k in range(steps):
+            self.graphs[bucket].replay()
+            self.host_tokens[k, :n].copy_(self.token_ids[:n], non_blocking=True)
+        kx.LAUNCHES["count"] += steps * self.kernels_per_replay[bucket]
         TRANSFERS["h2d"] += 4 * cursor
-        TRANSFERS["d2h"] += 8 * n
+        TRANSFERS["d2h"] += 8 * n * steps
         torch.cuda.current_stream().synchronize()
-        return self.host_tokens[:n].tolist()
+        if steps == 1:
+            return self.host_tokens[0, :n].tolist()
+        return self.host_tokens[:steps, :n].tolist()
 
     def release(self) -> None:
         self.graphs.clear()

@@ -206,6 +206,19 @@ class ModelRunner:
             return "llm_mixed"
         return "llm_prefill" if batch.prefill else "llm_decode"
 
+    @property
+    def max_decode_steps(self) -> int:
+        return self.graph_runner.max_steps if self.graph_runner is not None else 1
+
+    @torch.inference_mode()
+    def run_steps(self, batch: ModelBatch, steps: int) -> list[list[int]]:
+        """``steps`` CUDA-graph decode steps of a decode-only batch in one host round trip
+        (its block tables already cover every position they write)."""
+        if not self.can_use_graph(batch) or batch.prefill:
+            raise ValueError("multi-step decode needs a graph-eligible decode-only batch")
+        with self.timer.phase("llm_decode"):
+            return self.graph_runner.run(batch.decode, steps)
+
     @torch.inference_mode()
     def run(self, batch: ModelBatch) -> list[int]:
         with self.timer.phase(self._phase_name(batch)):

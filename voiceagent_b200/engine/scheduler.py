@@ -218,6 +218,63 @@ class Scheduler:
             self.audio_frame_limit = min(self.config.max_audio_batch_frames,
                                          self.audio_frame_limit * 2)
 
+    def decode_steps_for(self, batch: ModelBatch, limit: int, max_model_len: int) -> int:
+        """How many decode steps a decode-only batch can run in one call (>= 1): bounded
+        by ``limit``, every request's remaining token budget and the model length, and
+        by free blocks for the positions those steps write (taken when > 1 is returned).
+
+        Running several steps before the host sees their tokens changes no output: a
+        request that stops early (EOS) has its later tokens discarded. It can delay the
+        admission of a waiting request by up to ``steps - 1`` steps."""
+        if limit <= 1 or batch.prefill or not batch.decode:
+            return 1
+        steps = limit
+        for r in batch.decode:
+            if r.cancel_requested:
+                return 1
+            steps = min(steps, r.sampling.max_new_tokens - r.num_output_tokens,
+                        max_model_len - len(r) + 1)
+        if steps <= 1:
+            return 1
+        need = sum(self.block_manager.blocks_ahead(r, steps) for r in batch.decode)
+        if need > self.block_manager.num_free_blocks:
+            return 1
+        for r in batch.decode:
+            self.block_manager.append_ahead(r, steps)
+        return steps
+
+    def postprocess_steps(self, batch: ModelBatch, tokens: list[list[int]]) -> list[AsrRequest]:
+        """``postprocess`` for several decode steps of a decode-only batch: tokens[k][i] is
+        request i's token of step k; a request stops at its first finishing token."""
+        requests = batch.decode
+        if batch.prefill or any(len(step) != len(requests) for step in tokens):
+            raise ValueError("multi-step results do not match the decode batch")
+        finished: list[AsrRequest] = []
+        for i, request in enumerate(requests):
+            done = False
+            for step in tokens:
+                request.num_computed_tokens = len(request)
+                request.append_token(step[i])
+                if request.cancel_requested:
+                    request.finish("cancelled")
+                    done = True
+                elif request.check_finished():
+                    done = True
+                if done:
+                    break
+            if not done:
+                self.block_manager.may_append(request)
+                self.running.append(request)
+                continue
+            self.block_manager.deallocate(request)
+            request.audio_embeds = None
+            self.tracked.pop(request.request_id, None)
+            finished.append(request)
+        extra = len(tokens) - 1
+        self.stats.num_model_steps += extra
+        self.stats.num_decoded_tokens += extra * len(requests)
+        return finished
+
     def postprocess(self, batch: ModelBatch, token_ids: list[int]) -> list[AsrRequest]:
         requests = batch.requests
         if len(requests) != len(token_ids):

@@ -78,6 +78,13 @@ def pack_decode_bucket(lens, last_ids, table_off, table_len, tables, *, batch: i
         _p(block_tables), _stream()), "pack_decode_bucket")
 
 
+def advance_decode_bucket(lens, last_ids, table_len, sampled, *, bucket: int) -> None:
+    """One generated token onto a decode-bucket descriptor, on the device."""
+    _count()
+    check(lib.b200asr_advance_decode_bucket(_p(lens), _p(last_ids), _p(table_len), _p(sampled),
+                                            bucket, _stream()), "advance_decode_bucket")
+
+
 def pack_audio(mel_frames, *, chunk_frames: int, window_tokens: int, max_chunks: int,
                max_windows: int, out: dict, error_flag=None) -> None:
     """Metadata of ``pack_audio_batch`` (audio/batcher.py:101-141) on the GPU."""
