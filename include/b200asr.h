@@ -181,7 +181,10 @@ B200ASR_API int b200asr_silu_mul(const void *x, int32_t rows, int32_t inner, voi
  * Supported: head_dim 128, block_size 256, num_heads / num_kv_heads in {1,2,4,8},
  * num_kv_heads <= 8. workspace: device scratch of at least
  * b200asr_paged_decode_workspace_size(batch, max_seqlen_k, num_heads, head_dim)
- * bytes. Its first 4096 bytes hold per-sequence merge counters that must be zero
+ * bytes. max_seqlen_k <= 512 (with block_size % 64 == 0) selects a kernel with one CTA
+ * per (sequence, KV head) and no split, the faster choice for short contexts; larger
+ * bounds select the stream-K split over the whole batch.
+ * Its first 4096 bytes hold per-sequence merge counters that must be zero
  * before the first call with that workspace; every completed call leaves them zero
  * (allocate it zero-filled once). Calls sharing a workspace must not overlap on the
  * GPU.                                                                             */

@@ -109,9 +109,10 @@ def encode_audio(model, mel: torch.Tensor) -> torch.Tensor:
 
 
 @torch.inference_mode()
-def greedy_predictions(model, token_ids: list[int], audio_embeds: torch.Tensor,
-                       audio_offset: int) -> torch.Tensor:
-    """Argmax at every position of ``token_ids`` (teacher forced), reference ops."""
+def greedy_logits(model, token_ids: list[int], audio_embeds: torch.Tensor,
+                  audio_offset: int) -> torch.Tensor:
+    """Logits (fp32 view of the bf16 lm_head output) at every position of ``token_ids``,
+    teacher forced, reference ops."""
     dec = model.model
     dev = dec.embed_tokens.weight.device
     ids = torch.tensor(token_ids, dtype=torch.long, device=dev)
@@ -143,4 +144,10 @@ def greedy_predictions(model, token_ids: list[int], audio_embeds: torch.Tensor,
         gate, up = layer.mlp.gate_up_proj(h).chunk(2, dim=-1)
         h = layer.mlp.down_proj(F.silu(gate) * up)
     h, _ = _add_rms(h, residual, dec.norm.weight, dec.norm.eps)
-    return model.compute_logits(h).float().argmax(-1)
+    return model.compute_logits(h).float()
+
+
+def greedy_predictions(model, token_ids: list[int], audio_embeds: torch.Tensor,
+                       audio_offset: int) -> torch.Tensor:
+    """Argmax at every position of ``token_ids`` (teacher forced), reference ops."""
+    return greedy_logits(model, token_ids, audio_embeds, audio_offset).argmax(-1)

@@ -354,12 +354,42 @@ def test_paged_decode_matches_reference_torch_path(kx):
     [1], [63], [64], [65], [255], [256], [257], [1023, 1024, 1025], [4096],
     [1, 2, 3, 4, 5, 300, 700, 128],
 ])
-def test_paged_decode_edges(kx, lens):
+@pytest.mark.parametrize("max_len", ["tight", 4096])
+def test_paged_decode_edges(kx, lens, max_len):
+    """Both decode kernels: max_seqlen_k <= 512 selects one CTA per (sequence, KV head),
+    larger bounds the stream-K split."""
     rng = np.random.default_rng(sum(lens))
     q, kc, vc, tables, cu_k = _decode_case(rng, lens, nblocks=64)
-    out = _run_decode(kx, q, kc, vc, tables, cu_k, max(lens))
+    out = _run_decode(kx, q, kc, vc, tables, cu_k, max(lens) if max_len == "tight" else max_len)
     ref = K.paged_attention(q, kc, vc, np.arange(len(lens) + 1), cu_k, tables, 128 ** -0.5)
-    assert_attn_close(out, ref, f"decode {lens}")
+    assert_attn_close(out, ref, f"decode {lens} max_seqlen_k={max_len}")
+
+
+@pytest.mark.parametrize("max_len", [512, 4096])
+def test_paged_decode_step_shape_both_kernels(kx, max_len):
+    """Config-3 decode-step shape (32 sequences of 80-250 tokens, random tables) through
+    the short-context kernel (512) and the stream-K kernel (4096)."""
+    rng = np.random.default_rng(77)
+    lens = rng.integers(80, 251, size=32)
+    q, kc, vc, tables, cu_k = _decode_case(rng, lens, nblocks=128)
+    out = _run_decode(kx, q, kc, vc, tables, cu_k, max_len)
+    ref = K.paged_attention(q, kc, vc, np.arange(33), cu_k, tables, 128 ** -0.5)
+    assert_attn_close(out, ref, f"decode step shape max_seqlen_k={max_len}")
+
+
+@pytest.mark.parametrize("max_len", [512, 4096])
+def test_paged_decode_peaked_scores(kx, max_len):
+    """Scores with a spread of ~9 (q, k ~ 3 N(0, 1) after the 1/sqrt(d) scale): the
+    running-max rescale across stages and the split merge carry the result, not a
+    near-uniform average. Lengths cross stage, 64-token and block boundaries."""
+    rng = np.random.default_rng(9)
+    lens = [70, 118, 1, 1, 257, 500, 33, 190]
+    q, kc, vc, tables, cu_k = _decode_case(rng, lens, nblocks=64)
+    q, kc = K.bf16_round(q * 3 * np.sqrt(128)), K.bf16_round(kc * 3 * np.sqrt(128))
+    vc = vc * 8  # values ~ N(0, 0.5); a power of two keeps them exact in bf16
+    out = _run_decode(kx, q, kc, vc, tables, cu_k, max_len)
+    ref = K.paged_attention(q, kc, vc, np.arange(len(lens) + 1), cu_k, tables, 128 ** -0.5)
+    assert_attn_close(out, ref, f"decode peaked scores max_seqlen_k={max_len}")
 
 
 def test_paged_decode_config1(kx):

@@ -566,6 +566,322 @@ int num_sms() {
   return sms;
 }
 
+// =============================================================================
+// Short contexts: one CTA per (sequence, KV head), no cross-CTA merge.
+//
+// With contexts of a few hundred tokens (the decode steps of ASR requests) the stream-K
+// split above leaves every CTA a couple of stages and nearly every sequence split, so the
+// partial writes, the counter round trip and the merge dominate the launch. Here a work
+// unit is one KV head of one sequence: stages of 64 tokens of that head (one 16 KiB TMA
+// box for K and one for V: {64 dims, 64 tokens, 2 halves, 1 head}), four consumer warps
+// taking 16 tokens each with the same mma.sync QK^T / PV as above, and at the unit's end
+// the four warps' softmax states combine in shared memory and the G query rows are
+// written directly. B x H_kv units (256 for 32 sequences) keep the SMs busy without
+// splitting any sequence's softmax across CTAs.
+// =============================================================================
+constexpr int kShortTok = 64;
+constexpr int kShortStages = 3;
+constexpr int kShortWarps = 4;
+constexpr int kShortMaxCtx = 512;  // the host picks this kernel for max_seqlen_k <= 512
+
+template <int G>
+struct Short {
+  static constexpr int HALF = kShortTok * 128;  // 64 tokens x 64 dims x 2 B = 8 KiB
+  static constexpr int KV_BYTES = 2 * HALF;     // one head's K (or V) stage: 16 KiB
+  static constexpr int Q_BYTES = ((G * kDecD * 2 + 1023) / 1024) * 1024;
+  static constexpr int STAGE_BYTES = 2 * KV_BYTES + Q_BYTES;
+  static constexpr int CONSUMERS = kShortWarps * 32;
+  static constexpr int THREADS = CONSUMERS + 32;
+  static constexpr int SCRATCH_BYTES = kShortWarps * G * (kDecD + 2) * 4;
+  static constexpr size_t SMEM = 1024 + static_cast<size_t>(kShortStages) * STAGE_BYTES +
+                                 SCRATCH_BYTES + 2 * kShortStages * 8 + kShortStages * 16 + 64;
+};
+
+struct ShortStage {
+  int b, h, ntok, flags;  // flags 1: first stage of the unit (q attached), 2: last
+};
+
+template <int G>
+__global__ void __launch_bounds__(Short<G>::THREADS, 2)
+    paged_decode_short_kernel(const __grid_constant__ CUtensorMap tm_k,
+                              const __grid_constant__ CUtensorMap tm_v, const DecodeArgs a,
+                              int hkv) {
+  using C = Short<G>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                              ~uintptr_t(1023));
+  uint8_t *stages = smem;
+  float *scratch = reinterpret_cast<float *>(smem + kShortStages * C::STAGE_BYTES);
+  uint64_t *full = reinterpret_cast<uint64_t *>(reinterpret_cast<uint8_t *>(scratch) + C::SCRATCH_BYTES);
+  uint64_t *empty = full + kShortStages;
+  ShortStage *info = reinterpret_cast<ShortStage *>(empty + kShortStages);
+  __shared__ int abort_flag;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int B = a.batch, units = a.batch * hkv;
+  pdl_trigger();
+  if (tid == 0) {
+    abort_flag = 0;
+    for (int s = 0; s < kShortStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kShortWarps);
+    }
+    fence_barrier_init();
+  }
+  if (warp == kShortWarps && lane == 0) {
+    prefetch_tmap(&tm_k);
+    prefetch_tmap(&tm_v);
+  }
+  pdl_wait();  // q, the new token's K/V and the batch metadata come from earlier kernels
+  __syncthreads();
+
+  if (warp == kShortWarps) {
+    // ------------------------------------------------------------------ producer
+    uint32_t it_stage = 0;
+    auto acquire = [&](int &st) -> bool {
+      st = it_stage % kShortStages;
+      const uint32_t ph = (it_stage / kShortStages) & 1;
+      int ok = 1;
+      if (lane == 0) ok = mbar_wait(&empty[st], ph ^ 1, a.error_flag, &abort_flag);
+      return __shfl_sync(0xffffffffu, ok, 0) != 0;
+    };
+    for (int u = blockIdx.x; u < units; u += gridDim.x) {
+      const int b = u / hkv, h = u - (u / hkv) * hkv;
+      const int len = a.cu_seqlens_k[b + 1] - a.cu_seqlens_k[b];
+      if (len <= 0) continue;  // zero rows: written by CTA 0's consumers
+      const int nst = (len + kShortTok - 1) / kShortTok;
+      for (int wb = 0; wb < nst; wb += 32) {
+        // lane i: cache slot of stage wb + i (block-table reads in flight together)
+        const int s = wb + lane;
+        int d_slot = 0;
+        if (s < nst) {
+          const int t0 = s * kShortTok;
+          const int col = t0 / a.block_size;
+          int blk = 0;
+          if (col >= a.bt_stride) {
+            raise_flag(a.error_flag, B200ASR_DEVERR_LENGTH);
+          } else {
+            blk = a.block_tables[static_cast<int64_t>(b) * a.bt_stride + col];
+            if (blk < 0 || blk >= a.num_blocks) {
+              raise_flag(a.error_flag, B200ASR_DEVERR_BLOCK);
+              blk = 0;
+            }
+          }
+          d_slot = blk * a.block_size + t0 % a.block_size;
+        }
+        const int nw = min(32, nst - wb);
+        for (int i = 0; i < nw; ++i) {
+          const int j = wb + i;
+          const int slot = __shfl_sync(0xffffffffu, d_slot, i);
+          const int n = min(kShortTok, len - j * kShortTok);
+          const int fl = (j == 0 ? 1 : 0) | (j == nst - 1 ? 2 : 0);
+          int st;
+          if (!acquire(st)) return;
+          if (lane == 0) {
+            info[st] = ShortStage{b, h, n, fl};
+            mbar_arrive_expect_tx(&full[st], 2 * C::KV_BYTES + ((fl & 1) ? G * kDecD * 2 : 0));
+          }
+          __syncwarp();
+          uint8_t *stage = stages + st * C::STAGE_BYTES;
+          if (lane < 2) tma_load_4d(stage + lane * C::KV_BYTES, lane ? &tm_v : &tm_k, 0, slot, 0, h, &full[st]);
+          if ((fl & 1) && lane == 2)
+            bulk_g2s(stage + 2 * C::KV_BYTES, a.q + b * a.q_stride + h * G * kDecD,
+                     G * kDecD * 2, &full[st]);
+          ++it_stage;
+        }
+      }
+    }
+    int st;  // terminal stage
+    if (!acquire(st)) return;
+    if (lane == 0) {
+      info[st] = ShortStage{-1, 0, 0, 0};
+      mbar_arrive(&full[st]);
+    }
+    return;
+  }
+
+  // -------------------------------------------------------------------- consumers
+  const int w = warp;               // token slice [16w, 16w + 16) of every stage
+  const int row = lane >> 2;        // MMA row = query head within the group (valid if < G)
+  const int quad = lane & 3;
+  const bool row_valid = row < G;
+  const uint32_t stage_base = smem_addr(stages);
+  const int lm_mat = lane >> 3, lm_row = lane & 7;
+  constexpr int H = G;  // query rows of a unit
+
+  if (blockIdx.x == 0) {  // rows with no keys: zeros
+    for (int b = w; b < B; b += kShortWarps) {
+      if (a.cu_seqlens_k[b + 1] - a.cu_seqlens_k[b] <= 0) {
+        for (int i = lane; i < hkv * G * kDecD / 8; i += 32)
+          reinterpret_cast<uint4 *>(a.out + b * a.out_stride)[i] = make_uint4(0, 0, 0, 0);
+      }
+    }
+  }
+
+  uint32_t qa[8][2];
+  float o[16][4];
+  float m_run = -INFINITY, l_run = 0.f;
+  for (uint32_t it_stage = 0;; ++it_stage) {
+    const int st = it_stage % kShortStages;
+    const uint32_t ph = (it_stage / kShortStages) & 1;
+    if (!mbar_wait(&full[st], ph, a.error_flag, &abort_flag)) return;
+    const ShortStage si = info[st];
+    if (si.b < 0) break;
+    const int ntok = min(16, max(0, si.ntok - 16 * w));  // this warp's tokens in the stage
+    const uint32_t k_tile = stage_base + st * C::STAGE_BYTES + w * 16 * 128;
+    const uint32_t v_tile = k_tile + C::KV_BYTES;
+
+    if (si.flags & 1) {  // first stage of a unit: fresh state + the unit's query rows
+#pragma unroll
+      for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+      m_run = -INFINITY;
+      l_run = 0.f;
+      const uint8_t *qs = stages + st * C::STAGE_BYTES + 2 * C::KV_BYTES + (row_valid ? row : 0) * kDecD * 2;
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        const uint32_t lo = *reinterpret_cast<const uint32_t *>(qs + (kk * 16 + quad * 2) * 2);
+        const uint32_t hi = *reinterpret_cast<const uint32_t *>(qs + (kk * 16 + 8 + quad * 2) * 2);
+        qa[kk][0] = row_valid ? lo : 0u;
+        qa[kk][1] = row_valid ? hi : 0u;
+      }
+    }
+    if (ntok > 0) {
+      if (ntok < 16) {  // clear V rows past the end so 0 * stale bytes stays 0
+        uint8_t *vt = stages + st * C::STAGE_BYTES + C::KV_BYTES + w * 16 * 128;
+        for (int i = lane; i < (16 - ntok) * 16; i += 32) {
+          const int r = ntok + i / 16, ch = i % 16;
+          *reinterpret_cast<uint4 *>(vt + (ch >> 3) * C::HALF + swz(r, ch & 7)) = make_uint4(0, 0, 0, 0);
+        }
+        __syncwarp();
+      }
+      float s[2][4];
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+        s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
+#pragma unroll
+        for (int kp = 0; kp < 4; ++kp) {
+          const int chunk = 4 * kp + lm_mat;
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4(k_tile + (chunk >> 3) * C::HALF + swz(nt * 8 + lm_row, chunk & 7), b0, b1, b2, b3);
+          mma16816(s[nt], qa[2 * kp][0], 0u, qa[2 * kp][1], 0u, b0, b1);
+          mma16816(s[nt], qa[2 * kp + 1][0], 0u, qa[2 * kp + 1][1], 0u, b2, b3);
+        }
+      }
+      float mx = -INFINITY;
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int t = nt * 8 + quad * 2 + e;
+          s[nt][e] = t < ntok ? s[nt][e] * a.scale_log2 : -INFINITY;
+          mx = fmaxf(mx, s[nt][e]);
+        }
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      const float m_new = fmaxf(m_run, mx);  // token 0 of the slice is valid: finite
+      const float alpha = exp2f(m_run - m_new);
+      float p[2][2], sum = 0.f;
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          p[nt][e] = exp2f(s[nt][e] - m_new);
+          sum += p[nt][e];
+        }
+      sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+      sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+      l_run = l_run * alpha + sum;
+      m_run = m_new;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        o[j][0] *= alpha;
+        o[j][1] *= alpha;
+      }
+      const uint32_t pa0 = row_valid ? pack2(p[0][0], p[0][1]) : 0u;
+      const uint32_t pa2 = row_valid ? pack2(p[1][0], p[1][1]) : 0u;
+#pragma unroll
+      for (int nd = 0; nd < 8; ++nd) {
+        const int chunk = 2 * nd + (lm_mat >> 1);
+        const int trow = (lm_mat & 1) * 8 + lm_row;
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4_t(v_tile + (chunk >> 3) * C::HALF + swz(trow, chunk & 7), b0, b1, b2, b3);
+        mma16816(o[2 * nd], pa0, 0u, pa2, 0u, b0, b1);
+        mma16816(o[2 * nd + 1], pa0, 0u, pa2, 0u, b2, b3);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[st]);
+    if (!(si.flags & 2)) continue;
+
+    // ----------------------------------------------- unit end: combine the 4 warps
+    float *sm = scratch + w * H * (kDecD + 2);  // [H][2] (m, l) then [H][128] o
+    if (row_valid) {
+      if (quad == 0) {
+        sm[row * 2] = m_run;
+        sm[row * 2 + 1] = l_run;
+      }
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        sm[2 * H + row * kDecD + j * 8 + quad * 2] = o[j][0];
+        sm[2 * H + row * kDecD + j * 8 + quad * 2 + 1] = o[j][1];
+      }
+    }
+    consumer_sync(C::CONSUMERS);
+    for (int idx = threadIdx.x; idx < H * kDecD / 2; idx += C::CONSUMERS) {
+      const int g = idx / (kDecD / 2), d = (idx % (kDecD / 2)) * 2;
+      float mm = -INFINITY;
+#pragma unroll
+      for (int v = 0; v < kShortWarps; ++v) mm = fmaxf(mm, scratch[v * H * (kDecD + 2) + g * 2]);
+      float l = 0.f, o0 = 0.f, o1 = 0.f;
+#pragma unroll
+      for (int v = 0; v < kShortWarps; ++v) {
+        const float *sv = scratch + v * H * (kDecD + 2);
+        const float wgt = exp2f(sv[g * 2] - mm);  // 0 for a warp that saw no token
+        l += sv[g * 2 + 1] * wgt;
+        o0 += sv[2 * H + g * kDecD + d] * wgt;
+        o1 += sv[2 * H + g * kDecD + d + 1] * wgt;
+      }
+      const float inv = 1.f / l;
+      *reinterpret_cast<uint32_t *>(a.out + si.b * a.out_stride + (si.h * G + g) * kDecD + d) =
+          pack2(o0 * inv, o1 * inv);
+    }
+    consumer_sync(C::CONSUMERS);  // scratch is reused by the next unit
+  }
+}
+
+template <int G>
+int launch_decode_short(const DecodeArgs &a, int hkv, const void *k_cache, const void *v_cache,
+                        int64_t num_slots, cudaStream_t stream) {
+  using C = Short<G>;
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(paged_decode_short_kernel<G>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(C::SMEM));
+    if (e != cudaSuccess) {
+      set_error("paged_decode: cannot reserve %zu bytes of shared memory: %s", C::SMEM,
+                cudaGetErrorString(e));
+      return B200ASR_ERR_CUDA;
+    }
+    configured = true;
+  }
+  // {64 dims, slots, 2 halves, hkv heads}; box {64, 64 tokens, 2, 1 head} lands as
+  // [half][token][64 dims] with the 128-byte swizzle: one head's 64-token K or V tile.
+  CUtensorMap tk, tv;
+  const uint64_t dims[4] = {64, static_cast<uint64_t>(num_slots), 2, static_cast<uint64_t>(hkv)};
+  const uint64_t strides[3] = {static_cast<uint64_t>(hkv) * kDecD * 2, 128, 256};
+  const uint32_t box[4] = {64, kShortTok, 2, 1};
+  if (!make_tmap_bf16(&tk, k_cache, 4, dims, strides, box) ||
+      !make_tmap_bf16(&tv, v_cache, 4, dims, strides, box))
+    return B200ASR_ERR_CUDA;
+  const int units = a.batch * hkv;
+  const int grid = std::min(units, 2 * num_sms());
+  B200_LAUNCH_CHECK_ERR(launch_kernel(paged_decode_short_kernel<G>, dim3(grid), dim3(C::THREADS),
+                                      C::SMEM, stream, true, 1, tk, tv, a, hkv),
+                        "paged_decode (short contexts)");
+  return B200ASR_OK;
+}
+
 template <int HKV, int G>
 int launch_decode(const DecodeArgs &a, const void *k_cache, const void *v_cache,
                   int64_t num_slots, cudaStream_t stream) {
@@ -662,6 +978,14 @@ extern "C" int b200asr_paged_decode(const void *q, int64_t q_row_stride, const v
   a.ws_o = a.ws_ml + static_cast<size_t>(a.parts_cap) * num_heads * 2;
   a.error_flag = error_flag;
   const int64_t slots = static_cast<int64_t>(num_blocks) * block_size;
+  // Contexts of at most kShortMaxCtx tokens: one CTA per (sequence, KV head).
+  if (max_seqlen_k <= kShortMaxCtx && block_size % kShortTok == 0 &&
+      num_heads % num_kv_heads == 0 && num_kv_heads <= 8) {
+    const int g = num_heads / num_kv_heads;
+    if (g == 1) return launch_decode_short<1>(a, num_kv_heads, k_cache, v_cache, slots, stream);
+    if (g == 2) return launch_decode_short<2>(a, num_kv_heads, k_cache, v_cache, slots, stream);
+    if (g == 4) return launch_decode_short<4>(a, num_kv_heads, k_cache, v_cache, slots, stream);
+  }
   if (num_kv_heads == 8 && num_heads == 16) return launch_decode<8, 2>(a, k_cache, v_cache, slots, stream);
   if (num_kv_heads == 8 && num_heads == 8) return launch_decode<8, 1>(a, k_cache, v_cache, slots, stream);
   if (num_kv_heads == 4 && num_heads == 16) return launch_decode<4, 4>(a, k_cache, v_cache, slots, stream);

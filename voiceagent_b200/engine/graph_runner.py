@@ -12,6 +12,11 @@ allocated beforehand) and reads back the tokens of every step with one sync.
 Padding rows are encoded in the descriptor as (length 1, empty block table), which
 the packer turns into the reference's padding: slot -1, key length 1, an all-zero
 block-table row.
+
+Each bucket has two graphs: one whose attention is bounded to contexts of at most
+``kernels.DECODE_SHORT_CTX`` tokens (paged decode with one CTA per sequence and KV head)
+and one for any length up to max_model_len (the stream-K split); a call picks the
+short one when every context, including the steps it adds, fits.
 """
 
 from __future__ import annotations
@@ -41,8 +46,8 @@ class GraphRunner:
         self.buckets = tuple(b for b in buckets if b <= config.max_num_seqs) or (config.max_num_seqs,)
         self.max_batch = self.buckets[-1]
         self.error_flag = error_flag
-        self.graphs: dict[int, torch.cuda.CUDAGraph] = {}
-        self.kernels_per_replay: dict[int, int] = {}
+        self.graphs: dict[tuple[int, bool], torch.cuda.CUDAGraph] = {}
+        self.kernels_per_replay: dict[tuple[int, bool], int] = {}
         self.pool = None
         self._allocate()
 
@@ -72,10 +77,11 @@ class GraphRunner:
         return (d[0:bucket], d[m:m + bucket], d[2 * m:2 * m + bucket], d[3 * m:3 * m + bucket],
                 d[4 * m:])
 
-    def _context(self, bucket: int) -> AttentionContext:
+    def _context(self, bucket: int, short: bool) -> AttentionContext:
+        max_k = min(kx.DECODE_SHORT_CTX, self.config.max_model_len) if short else self.config.max_model_len
         return AttentionContext(
             cu_seqlens_q=self.cu_seqlens_q[:bucket + 1], cu_seqlens_k=self.cu_seqlens_k[:bucket + 1],
-            max_seqlen_q=1, max_seqlen_k=self.config.max_model_len,
+            max_seqlen_q=1, max_seqlen_k=max_k,
             slot_mapping=self.slot_mapping[:bucket], block_tables=self.block_tables[:bucket],
             decode_only=True, decode_workspace=self.workspace, error_flag=self.error_flag)
 
@@ -105,19 +111,25 @@ class GraphRunner:
         self._fill_padding(0)
         self.desc.copy_(self.host_desc)
         for bucket in reversed(self.buckets):
-            with attention_context(self._context(bucket)):
-                for _ in range(2):
-                    self._step(bucket)
-                torch.cuda.synchronize()
-                graph = torch.cuda.CUDAGraph()
-                before = kx.LAUNCHES["count"]
-                with torch.cuda.graph(graph, self.pool):
-                    self.hidden[bucket] = self._step(bucket)
-                self.kernels_per_replay[bucket] = kx.LAUNCHES["count"] - before
-            self.pool = self.pool or graph.pool()
-            self.graphs[bucket] = graph
+            for short in (False, True):
+                with attention_context(self._context(bucket, short)):
+                    for _ in range(2):
+                        self._step(bucket)
+                    torch.cuda.synchronize()
+                    graph = torch.cuda.CUDAGraph()
+                    before = kx.LAUNCHES["count"]
+                    with torch.cuda.graph(graph, self.pool):
+                        self.hidden[(bucket, short)] = self._step(bucket)
+                    self.kernels_per_replay[(bucket, short)] = kx.LAUNCHES["count"] - before
+                self.pool = self.pool or graph.pool()
+                self.graphs[(bucket, short)] = graph
         torch.cuda.synchronize()
-        logger.info("captured decode graphs for buckets %s", sorted(self.graphs))
+        logger.info("captured decode graphs for buckets %s", sorted({b for b, _ in self.graphs}))
+
+    def uses_short_graph(self, max_len: int, steps: int = 1) -> bool:
+        """Whether every context of a call (longest ``max_len`` before it, growing by one
+        per step) fits the short-context attention."""
+        return max_len + steps - 1 <= min(kx.DECODE_SHORT_CTX, self.config.max_model_len)
 
     def bucket_for(self, batch_size: int) -> int | None:
         for b in self.buckets:
@@ -148,10 +160,11 @@ class GraphRunner:
             cursor += len(table)
         self._fill_padding(n)
         self.desc[:cursor].copy_(self.host_desc[:cursor], non_blocking=True)
+        key = (bucket, self.uses_short_graph(max(len(r) for r in requests), steps))
         for k in range(steps):
-            self.graphs[bucket].replay()
+            self.graphs[key].replay()
             self.host_tokens[k, :n].copy_(self.token_ids[:n], non_blocking=True)
-        kx.LAUNCHES["count"] += steps * self.kernels_per_replay[bucket]
+        kx.LAUNCHES["count"] += steps * self.kernels_per_replay[key]
         TRANSFERS["h2d"] += 4 * cursor
         TRANSFERS["d2h"] += 8 * n * steps
         torch.cuda.current_stream().synchronize()

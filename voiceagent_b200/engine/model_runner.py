@@ -177,8 +177,11 @@ class ModelRunner:
         ctx = AttentionContext(
             cu_seqlens_q=out["cu_seqlens_q"], cu_seqlens_k=out["cu_seqlens_k"],
             max_seqlen_q=max_q,
-            # decode rows use the graph's baked max so both paths split work identically
-            max_seqlen_k=self.config.max_model_len if decode_only else int(ends.max()),
+            # decode rows use the bound the graph would bake in, so both paths pick the same
+            # attention kernel (short contexts: one CTA per sequence and KV head)
+            max_seqlen_k=(min(kx.DECODE_SHORT_CTX, self.config.max_model_len)
+                          if int(ends.max()) <= min(kx.DECODE_SHORT_CTX, self.config.max_model_len)
+                          else self.config.max_model_len) if decode_only else int(ends.max()),
             slot_mapping=out["slot_mapping"], block_tables=out["block_tables"],
             decode_only=decode_only, decode_workspace=self.decode_workspace,
             error_flag=self.error_flag)

@@ -189,6 +189,11 @@ def paged_decode_workspace_size(batch: int, max_seqlen_k: int, num_heads: int,
     return int(lib.b200asr_paged_decode_workspace_size(batch, max_seqlen_k, num_heads, head_dim))
 
 
+# max_seqlen_k at or below this selects the short-context decode kernel (one CTA per
+# sequence and KV head, no split-K); must match kShortMaxCtx in csrc/paged_decode.cu.
+DECODE_SHORT_CTX = 512
+
+
 def paged_decode(q, k_cache, v_cache, cu_seqlens_k, block_tables, *, max_seqlen_k: int,
                  scale: float, out, workspace, error_flag=None) -> torch.Tensor:
     """One-token paged decode (split-K). q/out: [>= B, H, D] (rows past B, e.g. bucket

@@ -81,13 +81,15 @@ def _sets(per_set_bytes: int) -> int:
 # ------------------------------------------------------------------ config 1
 
 
-def decode_config1(iters: int = 64, sets: int = 4) -> dict:
-    """Paged decode, config 1: B = 32, ctx ~ U[64, 1024], 4096-block pool (2 GiB per K/V),
-    block tables = slices of a random permutation; ``sets`` disjoint table sets rotate."""
+def decode_config1(iters: int = 64, sets: int = 4, lo: int = 64, hi: int = 1024,
+                   label: str = "config1 B=32 ctx~U[64,1024] Hq16/Hkv8 d128",
+                   max_seqlen_k: int = 4096) -> dict:
+    """Paged decode, config 1: B = 32, ctx ~ U[lo, hi] (64-1024), 4096-block pool (2 GiB per
+    K/V), block tables = slices of a random permutation; ``sets`` disjoint table sets rotate."""
     dev = torch.device("cuda")
     rng = np.random.default_rng(0)
     b, h, hkv, d, nb = 32, 16, 8, 128, 4096
-    lens = rng.integers(64, 1025, size=b)
+    lens = rng.integers(lo, hi + 1, size=b)
     need = int(sum((lens + 255) // 256))
     gen = torch.Generator(device=dev).manual_seed(0)
     kc = (torch.randn(nb, 256, hkv, d, device=dev, generator=gen) / d ** 0.5).bfloat16()
@@ -109,7 +111,7 @@ def decode_config1(iters: int = 64, sets: int = 4) -> dict:
                      device=dev)
 
     def op(i):
-        return lambda: kx.paged_decode(q, kc, vc, cu, tables[i % sets], max_seqlen_k=4096,
+        return lambda: kx.paged_decode(q, kc, vc, cu, tables[i % sets], max_seqlen_k=max_seqlen_k,
                                        scale=d ** -0.5, out=out, workspace=ws)
 
     us = graph_time_us([op(i) for i in range(iters)])
@@ -117,7 +119,7 @@ def decode_config1(iters: int = 64, sets: int = 4) -> dict:
     algo = sumctx * hkv * d * 2 * 2 + 2 * b * h * d * 2 + 4 * need + 4 * b
     del kc, vc
     torch.cuda.empty_cache()
-    return _line("paged_decode", "config1 B=32 ctx~U[64,1024] Hq16/Hkv8 d128", us, algo,
+    return _line("paged_decode", label, us, algo,
                  sum_ctx=sumctx, timing=f"graph of {iters} launches over {sets} rotating KV sets "
                                            f"of {algo / 1e6:.0f} MB each (together > L2)")
 
@@ -351,6 +353,11 @@ def log_mel_config3() -> dict:
 
 BENCHES = {
     "decode": lambda: [decode_config1()],
+    "decode_step": lambda: [
+        decode_config1(lo=80, hi=250, sets=16, max_seqlen_k=512,
+                       label="config3 decode-step shape B=32 ctx~U[80,250], short-context kernel"),
+        decode_config1(lo=80, hi=250, sets=16, max_seqlen_k=4096,
+                       label="config3 decode-step shape B=32 ctx~U[80,250], stream-K kernel")],
     "prefill": lambda: [prefill_config2()],
     "window": lambda: [window_config2()],
     "store": lambda: [store_rows(32), store_rows(8192)],
