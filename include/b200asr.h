@@ -270,6 +270,49 @@ B200ASR_API int b200asr_linear_small(const void *x, int64_t x_row_stride, int32_
                          const void *w, int32_t n, int32_t silu_inner, void *y,
                          int64_t y_row_stride, int32_t *error_flag, b200asr_stream_t stream);
 
+/* ------------------------------------------- decode-step RMSNorm fusions ----
+ * The decoder layer's add + RMSNorm (RMSNorm._add_norm / _norm, layers/layernorm.py:19-36)
+ * split across the projections around it, for 1..64 rows. Between them a row is carried
+ * as h (fp32, the pre-norm sum) plus ss[r][t] (fp32 [rows][hidden / 128], row-major): the
+ * sum of h[r]^2 over columns 128t .. 128t + 127. The RMSNorm of that row is
+ *   bf16(bf16(h * rsqrt(sum_t ss[r][t] / hidden + eps)) * weight)   (t summed in order).
+ *
+ * linear_small_add (o_proj / down_proj + the residual add of the next norm):
+ *   h[r, j] = bf16(y[r, j]) + residual[r, j] (fp32), residual[r, j] <- bf16(h), h_out, ss_out
+ *   with y = x w^T as in b200asr_linear_small (n % 128 == 0, n / 128 <= 64).
+ * linear_small_norm (qkv_proj / gate_up_proj after the norm): y = RMSNorm(h) w^T, with
+ *   silu_inner as in b200asr_linear_small; k = hidden, ss_tiles = hidden / 128 (hidden a
+ *   multiple of 512 up to 4096: the normalised slice of each CTA must fit its ring).
+ * linear_small_norm_qk_rope (qkv_proj + Qwen3Attention.forward's q/k norm and RoPE,
+ *   models/qwen3.py:43-48, + the KV store of PagedAttention.forward, attention.py:90):
+ *   the projection of RMSNorm(h), then per head exactly what b200asr_qk_norm_rope_store
+ *   does (q heads to q_out, K and V into the cache at slot_mapping; slot -1 skipped);
+ *   head_dim 128.
+ * rms_stats: h and ss of x (+ residual, updated in place to bf16(x + residual)) -- the
+ *   layer-0 input norm, whose input is the embedding.
+ * norm_apply: out = RMSNorm of (h, ss) -- the model's final norm before lm_head.     */
+B200ASR_API int b200asr_linear_small_add(const void *x, int64_t x_row_stride, int32_t m, int32_t k,
+                             const void *w, int32_t n, void *residual,
+                             int64_t residual_row_stride, float *h_out, int64_t h_row_stride,
+                             float *ss_out, int32_t *error_flag, b200asr_stream_t stream);
+B200ASR_API int b200asr_linear_small_norm(const float *h, int64_t h_row_stride, const float *ss,
+                              int32_t ss_tiles, const void *norm_weight, float eps, int32_t m,
+                              int32_t k, const void *w, int32_t n, int32_t silu_inner, void *y,
+                              int64_t y_row_stride, int32_t *error_flag,
+                              b200asr_stream_t stream);
+B200ASR_API int b200asr_linear_small_norm_qk_rope(
+    const float *h, int64_t h_row_stride, const float *ss, int32_t ss_tiles,
+    const void *norm_weight, float eps, int32_t m, int32_t k, const void *w, int32_t num_heads,
+    int32_t num_kv_heads, int32_t head_dim, const void *q_norm_weight, const void *k_norm_weight,
+    float qk_eps, const int64_t *positions, const float *cos_sin_cache, int32_t max_position,
+    void *q_out, int64_t q_out_row_stride, void *k_cache, void *v_cache,
+    const int32_t *slot_mapping, int64_t num_slots, int32_t *error_flag,
+    b200asr_stream_t stream);
+B200ASR_API int b200asr_rms_stats(const void *x, void *residual, int32_t rows, int32_t hidden,
+                      float *h_out, float *ss_out, b200asr_stream_t stream);
+B200ASR_API int b200asr_norm_apply(const float *h, const float *ss, const void *weight, float eps,
+                       int32_t rows, int32_t hidden, void *out, b200asr_stream_t stream);
+
 /* ------------------------------------------------------------- mel frontend ----
  * Replaces AudioFrontend.__call__ (audio/frontend.py:71-94), the stock Whisper log-mel
  * extractor run per clip on the host: centred STFT (reflect pad 200), periodic Hann

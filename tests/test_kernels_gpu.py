@@ -620,6 +620,125 @@ def test_linear_small_lm_head_width(kx):
     assert ok and exact >= 0.98, exact
 
 
+def _within_one_ulp(got, ref, exact_frac=0.99):
+    """bf16 tensors that differ only by fp32 summation order upstream."""
+    g, r = got.float(), ref.float()
+    same = (g == r).float().mean().item()
+    ulp = r.abs().clamp_min(1e-30) * 2.0 ** -7
+    return same >= exact_frac and bool(((g - r).abs() <= ulp).all()), same
+
+
+@pytest.mark.parametrize("m", [1, 17, 32, 64])
+def test_linear_small_add_matches_unfused(kx, m):
+    """o_proj / down_proj + residual add: residual and h bit-exact against linear_small
+    followed by the add of rmsnorm; tile sums of h^2 against float64."""
+    g = torch.Generator(device="cuda").manual_seed(m)
+    for k, n in ((2048, 1024), (3072, 1024)):
+        x = torch.randn(m, k, device="cuda", generator=g).bfloat16()
+        w = (torch.randn(n, k, device="cuda", generator=g) * k ** -0.5).bfloat16()
+        res = torch.randn(m, n, device="cuda", generator=g).bfloat16()
+        state = kx.NormState(m, n, "cuda")
+        res_fused = res.clone()
+        kx.linear_small_add(x, w, res_fused, state)
+        y = kx.linear_small(x, w)
+        h_ref = y.float() + res.float()
+        assert torch.equal(state.h, h_ref)
+        assert torch.equal(res_fused, h_ref.bfloat16())
+        ss_ref = (h_ref.double() ** 2).reshape(m, n // 128, 128).sum(-1)
+        torch.testing.assert_close(state.ss.double(), ss_ref, rtol=1e-5, atol=1e-6)
+
+
+@pytest.mark.parametrize("m", [1, 32, 64])
+@pytest.mark.parametrize("silu", [False, True])
+def test_linear_small_norm_matches_unfused(kx, m, silu):
+    """RMSNorm prologue: the same as rmsnorm(y, residual) then linear_small, up to the
+    order of the fp32 sum of squares (outputs within one bf16 ulp, nearly all equal)."""
+    g = torch.Generator(device="cuda").manual_seed(100 + m)
+    hidden, n = 1024, (6144 if silu else 4096)
+    y = torch.randn(m, hidden, device="cuda", generator=g).bfloat16()
+    res = torch.randn(m, hidden, device="cuda", generator=g).bfloat16()
+    nw = (1 + 0.1 * torch.randn(hidden, device="cuda", generator=g)).bfloat16()
+    w = (torch.randn(n, hidden, device="cuda", generator=g) * hidden ** -0.5).bfloat16()
+    state = kx.rms_stats(y, kx.NormState(m, hidden, "cuda"), residual=res.clone())
+    fused = kx.linear_small_norm(state, nw, 1e-6, w, silu=silu)
+    normed = kx.rmsnorm(y, nw, 1e-6, residual=res.clone())
+    # the normalised activation itself, as the prologue builds it
+    ok, same = _within_one_ulp(kx.norm_apply(state, nw, 1e-6), normed, 0.995)
+    assert ok, same
+    unfused = kx.linear_small(normed, w, silu=silu)
+    ok, same = _within_one_ulp(fused, unfused, 0.97)
+    if not ok:  # an input that moved by one ulp moves the sum by more: bound it instead
+        err = (fused.float() - unfused.float()).abs().max().item()
+        assert err <= 2e-2 * unfused.float().abs().max().item() and same >= 0.97, (err, same)
+
+
+@pytest.mark.parametrize("m", [1, 32, 64])
+def test_linear_small_norm_qk_rope_matches_unfused(kx, m):
+    """qkv_proj (RMSNorm prologue) + q/k norm + RoPE + KV store in one kernel: q, K and V
+    bit-exact against linear_small_norm followed by qk_norm_rope_store (same K split,
+    same per-head arithmetic); slot -1 rows leave the cache untouched."""
+    g = torch.Generator(device="cuda").manual_seed(7 + m)
+    hidden, hq, hkv, d = 1024, 16, 8, 128
+    y = torch.randn(m, hidden, device="cuda", generator=g).bfloat16()
+    nw = (1 + 0.1 * torch.randn(hidden, device="cuda", generator=g)).bfloat16()
+    w = (torch.randn((hq + 2 * hkv) * d, hidden, device="cuda", generator=g) * 0.03).bfloat16()
+    qw = (1 + 0.1 * torch.randn(d, device="cuda", generator=g)).bfloat16()
+    kw = (1 + 0.1 * torch.randn(d, device="cuda", generator=g)).bfloat16()
+    positions = torch.randint(0, 4096, (m,), device="cuda", generator=g)
+    nslots = 4 * 256
+    slots = torch.randperm(nslots, device="cuda", generator=g)[:m].int()
+    slots[::5] = -1
+    from voiceagent_b200.layers.norm import rope_table
+
+    table = rope_table(d, 4096, 1e6, "cuda")
+    state = kx.rms_stats(y, kx.NormState(m, hidden, "cuda"))
+    outs = []
+    for fused in (True, False):
+        kc = torch.full((4, 256, hkv, d), 7.0, device="cuda").bfloat16()
+        vc = kc.clone()
+        q = torch.empty(m, hq, d, device="cuda", dtype=torch.bfloat16)
+        if fused:
+            kx.linear_small_norm_qk_rope(state, nw, 1e-6, w, positions, num_heads=hq,
+                                         num_kv_heads=hkv, head_dim=d, q_weight=qw, k_weight=kw,
+                                         qk_eps=1e-6, cos_sin_cache=table, q_out=q, k_cache=kc,
+                                         v_cache=vc, slot_mapping=slots)
+        else:
+            qkv = kx.linear_small_norm(state, nw, 1e-6, w)
+            kx.qk_norm_rope_store(qkv, positions, num_heads=hq, num_kv_heads=hkv, head_dim=d,
+                                  q_weight=qw, k_weight=kw, eps=1e-6, cos_sin_cache=table,
+                                  q_out=q, k_cache=kc, v_cache=vc, slot_mapping=slots)
+        outs.append((q, kc, vc))
+    for a, b in zip(*outs):
+        assert torch.equal(a, b)
+    untouched = torch.ones(nslots, dtype=torch.bool, device="cuda")
+    untouched[slots[slots >= 0].long()] = False
+    assert bool((outs[0][1].view(nslots, -1)[untouched] == 7.0).all())
+
+
+def test_fused_step_rejects_bad_slot(kx):
+    """An out-of-range slot raises the error flag and stores nothing (memory safe)."""
+    hidden, hq, hkv, d, m = 1024, 16, 8, 128, 4
+    y = torch.randn(m, hidden, device="cuda").bfloat16()
+    ones = torch.ones(hidden, device="cuda", dtype=torch.bfloat16)
+    w = (torch.randn((hq + 2 * hkv) * d, hidden, device="cuda") * 0.03).bfloat16()
+    from voiceagent_b200.layers.norm import rope_table
+
+    kc = torch.zeros(2, 256, hkv, d, device="cuda", dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    state = kx.rms_stats(y, kx.NormState(m, hidden, "cuda"))
+    kx.linear_small_norm_qk_rope(
+        state, ones, 1e-6, w, torch.zeros(m, dtype=torch.int64, device="cuda"), num_heads=hq,
+        num_kv_heads=hkv, head_dim=d, q_weight=ones[:d], k_weight=ones[:d], qk_eps=1e-6,
+        cos_sin_cache=rope_table(d, 16, 1e6, "cuda"),
+        q_out=torch.empty(m, hq, d, device="cuda", dtype=torch.bfloat16), k_cache=kc, v_cache=vc,
+        slot_mapping=torch.tensor([0, 1, 512, -1], dtype=torch.int32, device="cuda"),
+        error_flag=err)
+    torch.cuda.synchronize()
+    assert err.item() != 0
+    assert bool((kc.view(512, -1)[2:] == 0).all()) and bool((vc.view(512, -1)[2:] == 0).all())
+
+
 def test_linear_small_chain_with_pdl_in_a_graph(kx):
     """Dependent linear_small / rmsnorm launches with PDL, captured in a graph, give the
     same bytes as without PDL (the waits order every read after its producer)."""

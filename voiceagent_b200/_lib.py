@@ -44,6 +44,16 @@ SIGNATURES: dict[str, tuple] = {
     "b200asr_silu_mul": (c_int32, [P, c_int32, c_int32, P, P]),
     "b200asr_linear_small": (c_int32, [P, c_int64, c_int32, c_int32, P, c_int32, c_int32, P,
                                        c_int64, P, P]),
+    "b200asr_linear_small_add": (c_int32, [P, c_int64, c_int32, c_int32, P, c_int32, P, c_int64,
+                                           P, c_int64, P, P, P]),
+    "b200asr_linear_small_norm": (c_int32, [P, c_int64, P, c_int32, P, c_float, c_int32, c_int32,
+                                            P, c_int32, c_int32, P, c_int64, P, P]),
+    "b200asr_linear_small_norm_qk_rope": (c_int32, [P, c_int64, P, c_int32, P, c_float, c_int32,
+                                                    c_int32, P, c_int32, c_int32, c_int32, P, P,
+                                                    c_float, P, P, c_int32, P, c_int64, P, P, P,
+                                                    c_int64, P, P]),
+    "b200asr_rms_stats": (c_int32, [P, P, c_int32, c_int32, P, P, P]),
+    "b200asr_norm_apply": (c_int32, [P, P, P, c_float, c_int32, c_int32, P, P]),
     "b200asr_log_mel_workspace_size": (c_size_t, [c_int32, c_int32]),
     "b200asr_log_mel": (c_int32, [P, P, P, c_int32, c_int32, P, P, P, P, c_size_t, P, c_int64, P,
                                   P, P]),

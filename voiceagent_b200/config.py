@@ -145,6 +145,10 @@ class EngineConfig:
     # graph is replayed back to back with the sampled tokens fed back on the device and
     # the host syncs once per call (1 = one host round trip per token).
     decode_steps: int = 4
+    # Decode-sized batches (<= 64 rows) on the fused projections: each RMSNorm split
+    # across the projections around it, q/k norm + RoPE + KV store in qkv_proj's
+    # epilogue (five launches per decoder layer instead of eight).
+    fused_decode: bool = True
     device: str = "cuda"
     dtype: Any = None
     model_config: Qwen3ASRConfig | None = None

@@ -19,6 +19,22 @@
 //    epilogue writes silu(gate) * up directly, with the rounding of the unfused path
 //    (bf16 projections, bf16 silu, bf16 product).
 //
+//  * Decode-step fusions around the decoder layer's RMSNorms (layers/layernorm.py:19-36)
+//    and q/k norm + RoPE + KV store (models/qwen3.py:43-48, attention.py:90):
+//      - residual-add epilogue (o_proj, down_proj): h = bf16(y) + residual in fp32,
+//        residual <- bf16(h), h kept in fp32 and, per 128-column tile, the row's partial
+//        sum of squares of h (a warp reduction in a fixed order: deterministic);
+//      - RMSNorm prologue (qkv_proj, gate_up_proj): the CTA's K slice of the normalised
+//        activation bf16(bf16(h * rsqrt(sum / K + eps)) * w) is computed from that fp32 h
+//        and the tile partials (summed in tile order) and written straight into shared
+//        memory in the 128-byte-swizzled layout the MMA reads, instead of a TMA load;
+//      - q/k-norm + RoPE + store epilogue (qkv_proj): a 128-row tile is one head, so the
+//        per-head RMSNorm, the rotation (partner dims in lane ^ 16) and the paged-cache
+//        store of K and V happen on the reduced tile, with the rounding of the unfused
+//        kernels (bf16 projection, bf16 after the norm, after the weight, after RoPE).
+//    A decode layer is then qkv (norm + rope + store) -> attention -> o_proj (+residual)
+//    -> gate_up (norm, SiLU*mul) -> down (+residual): five launches instead of eight.
+//
 // No TMA multicast is used. Every CTA arrives at both cluster barriers whatever happens
 // (a timed-out mbarrier wait only skips work), so no CTA waits for one that left.
 #include "common.cuh"
@@ -50,6 +66,37 @@ struct LinearArgs {
   __nv_bfloat16 *y;
   int64_t y_stride;
   int32_t *error_flag;
+};
+
+enum : int { kEpiPlain = 0, kEpiSilu = 1, kEpiAdd = 2, kEpiQkRope = 3 };
+
+struct LinearFuse {
+  // RMSNorm prologue: x[r, k] = bf16(bf16(h[r, k] * rsqrt(sum_t ss[t][r] / K + eps)) * w[k])
+  const float *h;          // fp32 [m, >= K], row stride h_stride
+  int64_t h_stride;
+  const float *ss;         // [m][ss_tiles] partial sums of squares (row-major, 16-B rows)
+  int ss_tiles;
+  const __nv_bfloat16 *norm_w;
+  float norm_eps;
+  int norm_k;              // K of the normalised row (the full hidden size)
+  // residual-add epilogue
+  __nv_bfloat16 *residual;
+  int64_t res_stride;
+  float *h_out;            // fp32 [m, N], row stride h_out_stride
+  int64_t h_out_stride;
+  float *ss_out;           // [m][N / 128]
+  // q/k-norm + RoPE + store epilogue (head_dim 128 = one tile)
+  int num_heads, num_kv_heads;
+  const __nv_bfloat16 *q_w, *k_w;
+  float qk_eps;
+  const int64_t *positions;
+  const float *cos_sin;    // fp32 [max_position, 128]: cos | sin
+  int max_position;
+  __nv_bfloat16 *q_out;
+  int64_t q_out_stride;
+  __nv_bfloat16 *k_cache, *v_cache;
+  const int32_t *slot_mapping;
+  int64_t num_slots;
 };
 
 __device__ __forceinline__ uint32_t cluster_rank() {
@@ -87,10 +134,187 @@ __device__ __forceinline__ float silu_mul1(float g, float u) {
   return bf2f(f2bf(gb / (1.0f + expf(-gb)))) * ub;
 }
 
+constexpr int kNormMaxTiles = 32;  // RMSNorm prologue: hidden <= 32 x 128
+constexpr int kEpiPre = 2;         // epilogue rows per warp whose operands are prefetched
+static_assert(kEpiPre == 2, "the epilogue selects pre[0] / pre[1] by name");
+
+// This thread's norm weights for the RMSNorm prologue (static: read before the wait on
+// the previous kernel). Thread t owns chunks (t & 3) and (t & 3) + 4 of every stage.
+__device__ __forceinline__ void norm_in_weights(uint4 (&wv)[kLnStages][2], const LinearArgs &a,
+                                                const LinearFuse &f, int k0) {
+  const int tid = threadIdx.x;
+#pragma unroll
+  for (int s = 0; s < kLnStages; ++s)
+#pragma unroll
+    for (int jj = 0; jj < 2; ++jj)
+      wv[s][jj] = s < a.steps ? *reinterpret_cast<const uint4 *>(
+                                    f.norm_w + k0 + s * kLnBK + ((tid & 3) + 4 * jj) * 8)
+                              : make_uint4(0, 0, 0, 0);
+}
+
+// The CTA's K slice of the RMS-normalised activation, written into the x halves of the
+// first a.steps stages in the layout a 128-byte-swizzled TMA box {64, MP} would leave:
+// row r at r * 128 bytes, its 16-byte chunk j at chunk j ^ (r & 7). Rows >= m are zero.
+// Thread t owns row t / 4 (and + 32 for MP = 64). The row's tile sums (row-major, 16-byte
+// vectors) and its h values are requested together: one L2 round trip per row.
 template <int MP>
+__device__ __forceinline__ void norm_in_fill(uint8_t *stages, const LinearArgs &a,
+                                             const LinearFuse &f, int k0,
+                                             const uint4 (&wv)[kLnStages][2]) {
+  using C = Ln<MP>;
+  const int tid = threadIdx.x;
+#pragma unroll
+  for (int rr = 0; rr < MP / 32; ++rr) {
+    const int r = (tid >> 2) + rr * 32;
+    uint8_t *xrow = stages + C::W_BYTES + r * 128;
+    if (r >= a.m) {
+#pragma unroll
+      for (int s = 0; s < kLnStages; ++s)
+#pragma unroll
+        for (int jj = 0; jj < 2; ++jj) {
+          const int j = (tid & 3) + 4 * jj;
+          if (s < a.steps)
+            *reinterpret_cast<uint4 *>(xrow + s * C::STAGE + ((j ^ (r & 7)) << 4)) =
+                make_uint4(0, 0, 0, 0);
+        }
+      continue;
+    }
+    const float4 *srow = reinterpret_cast<const float4 *>(f.ss + r * f.ss_tiles);
+    const float *hrow = f.h + r * f.h_stride;
+    float4 sv[kNormMaxTiles / 4];
+    float4 hv[kLnStages][2][2];
+#pragma unroll
+    for (int i = 0; i < kNormMaxTiles / 4; ++i)
+      if (4 * i < f.ss_tiles) sv[i] = srow[i];
+#pragma unroll
+    for (int s = 0; s < kLnStages; ++s)
+#pragma unroll
+      for (int jj = 0; jj < 2; ++jj) {
+        const int kc = k0 + s * kLnBK + ((tid & 3) + 4 * jj) * 8;
+        if (s < a.steps) {
+          hv[s][jj][0] = *reinterpret_cast<const float4 *>(hrow + kc);
+          hv[s][jj][1] = *reinterpret_cast<const float4 *>(hrow + kc + 4);
+        }
+      }
+    float ss = 0.f;  // tile order, as norm_apply sums
+#pragma unroll
+    for (int i = 0; i < kNormMaxTiles / 4; ++i)
+      if (4 * i < f.ss_tiles) {
+        ss += sv[i].x;
+        ss += sv[i].y;
+        ss += sv[i].z;
+        ss += sv[i].w;
+      }
+    const float rs = rsqrtf(ss / static_cast<float>(f.norm_k) + f.norm_eps);
+#pragma unroll
+    for (int s = 0; s < kLnStages; ++s)
+#pragma unroll
+      for (int jj = 0; jj < 2; ++jj) {
+        if (s >= a.steps) continue;
+        const int j = (tid & 3) + 4 * jj;
+        float w[8];
+        unpack8(wv[s][jj], w);
+        const float h[8] = {hv[s][jj][0].x, hv[s][jj][0].y, hv[s][jj][0].z, hv[s][jj][0].w,
+                            hv[s][jj][1].x, hv[s][jj][1].y, hv[s][jj][1].z, hv[s][jj][1].w};
+        float y[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) y[e] = bf2f(f2bf(bf2f(f2bf(h[e] * rs)) * w[e]));
+        *reinterpret_cast<uint4 *>(xrow + s * C::STAGE + ((j ^ (r & 7)) << 4)) =
+            make_uint4(pack2(y[0], y[1]), pack2(y[2], y[3]), pack2(y[4], y[5]), pack2(y[6], y[7]));
+      }
+  }
+}
+
+// Operands of one epilogue row that do not depend on this kernel's result.
+struct EpiRow {
+  int64_t slot;   // q/k-rope: cache slot (-1: none)
+  float cs[8];    // q/k-rope: cos of dims 4*(lane&15)+e, then sin
+  uint2 res;      // residual add: this lane's 4 residual values
+};
+
+template <int EPI>
+__device__ __forceinline__ void epi_fetch(EpiRow &o, const LinearFuse &f, const LinearArgs &a,
+                                          int c, int tile, int lane) {
+  if (EPI == kEpiAdd) {
+    o.res = *reinterpret_cast<const uint2 *>(f.residual + c * f.res_stride + tile * kLnRows + lane * 4);
+  } else if (EPI == kEpiQkRope) {
+    o.slot = f.slot_mapping ? f.slot_mapping[c] : -1;
+    if (tile < f.num_heads + f.num_kv_heads) {
+      int64_t p = f.positions[c];
+      if (p < 0 || p >= f.max_position) {
+        if (lane == 0) raise_flag(a.error_flag, B200ASR_DEVERR_POSITION);
+        p = 0;
+      }
+      const float4 cv = *reinterpret_cast<const float4 *>(f.cos_sin + p * kLnRows + (lane & 15) * 4);
+      const float4 sv = *reinterpret_cast<const float4 *>(f.cos_sin + p * kLnRows + kLnRows / 2 +
+                                                          (lane & 15) * 4);
+      o.cs[0] = cv.x; o.cs[1] = cv.y; o.cs[2] = cv.z; o.cs[3] = cv.w;
+      o.cs[4] = sv.x; o.cs[5] = sv.y; o.cs[6] = sv.z; o.cs[7] = sv.w;
+    }
+  }
+}
+
+// q/k RMSNorm + RoPE + paged store of one head vector: lane holds dims 4*lane .. +3 of
+// row c of head `head` (0..H-1 query, H..H+Hkv-1 key, then value heads); nw = this lane's
+// 4 q- or k-norm weights.
+__device__ __forceinline__ void qk_rope_store4(const LinearFuse &f, const LinearArgs &a, int c,
+                                               int head, int lane, const float *acc,
+                                               const EpiRow &pre, const float *nw) {
+  constexpr int D = kLnRows;
+  float x[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) x[e] = bf2f(f2bf(acc[e]));  // the bf16 projection output
+  const int kv_hidden = f.num_kv_heads * D;
+  const int64_t slot = pre.slot;
+  const bool slot_bad = slot != -1 && (slot < 0 || slot >= f.num_slots);
+  if (head >= f.num_heads + f.num_kv_heads) {  // value head: copy into the cache
+    if (slot == -1) return;
+    if (slot_bad) {
+      if (lane == 0) raise_flag(a.error_flag, B200ASR_DEVERR_SLOT);
+      return;
+    }
+    const int hv = head - f.num_heads - f.num_kv_heads;
+    *reinterpret_cast<uint2 *>(f.v_cache + slot * kv_hidden + hv * D + lane * 4) =
+        make_uint2(pack2(x[0], x[1]), pack2(x[2], x[3]));
+    return;
+  }
+  const bool is_q = head < f.num_heads;
+  float ss = 0.f;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) ss += x[e] * x[e];
+  ss = warp_sum(ss);
+  const float r = rsqrtf(ss / static_cast<float>(D) + f.qk_eps);
+  float y[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) y[e] = bf2f(f2bf(bf2f(f2bf(x[e] * r)) * nw[e]));
+  const bool first_half = lane < 16;
+  float o[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float partner = __shfl_xor_sync(0xffffffffu, y[e], 16);
+    const float cv = pre.cs[e], sv = pre.cs[4 + e];
+    o[e] = first_half ? __fsub_rn(__fmul_rn(y[e], cv), __fmul_rn(partner, sv))
+                      : __fadd_rn(__fmul_rn(y[e], cv), __fmul_rn(partner, sv));
+  }
+  const uint2 packed = make_uint2(pack2(o[0], o[1]), pack2(o[2], o[3]));
+  if (is_q) {
+    *reinterpret_cast<uint2 *>(f.q_out + c * f.q_out_stride + head * D + lane * 4) = packed;
+    return;
+  }
+  if (slot == -1) return;
+  if (slot_bad) {
+    if (lane == 0) raise_flag(a.error_flag, B200ASR_DEVERR_SLOT);
+    return;
+  }
+  *reinterpret_cast<uint2 *>(f.k_cache + slot * kv_hidden + (head - f.num_heads) * D +
+                             lane * 4) = packed;
+}
+
+template <int MP, bool NORM_IN, int EPI>
 __global__ void __launch_bounds__(kLnThreads)
     linear_small_kernel(const __grid_constant__ CUtensorMap tm_w,
-                        const __grid_constant__ CUtensorMap tm_x, const LinearArgs a) {
+                        const __grid_constant__ CUtensorMap tm_x, const LinearArgs a,
+                        const __grid_constant__ LinearFuse f) {
   using C = Ln<MP>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -110,7 +334,7 @@ __global__ void __launch_bounds__(kLnThreads)
   const int tile = blockIdx.x / ks;
   const int k0 = kz * a.steps * kLnBK;
   int r0, r1;  // first weight row of the two 64-row boxes
-  if (a.silu_inner) {
+  if (EPI == kEpiSilu) {
     r0 = tile * 64;
     r1 = a.silu_inner + tile * 64;
   } else {
@@ -138,17 +362,36 @@ __global__ void __launch_bounds__(kLnThreads)
 
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&tm_w);
-    prefetch_tmap(&tm_x);
+    if (!NORM_IN) prefetch_tmap(&tm_x);
     // The weights are static: the first ring's worth is requested before waiting for
-    // the kernel that produces x (programmatic dependent launch).
+    // the kernel that produces x (programmatic dependent launch). With the RMSNorm
+    // prologue the whole K slice fits the ring (the host guarantees steps <= stages).
     const int first = a.steps < kLnStages ? a.steps : kLnStages;
     for (int s = 0; s < first; ++s) {
       uint8_t *w = stages + s * C::STAGE;
       const int kc = k0 + s * kLnBK;
-      mbar_arrive_expect_tx(&full[s], C::STAGE);
+      mbar_arrive_expect_tx(&full[s], NORM_IN ? C::W_BYTES : C::STAGE);
       tma_load_2d(w, &tm_w, kc, r0, &full[s]);
       tma_load_2d(w + C::W_BYTES / 2, &tm_w, kc, r1, &full[s]);
     }
+  }
+  // static epilogue operand: this lane's q- or k-norm weights (the tile is one head)
+  float qk_nw[4] = {0.f, 0.f, 0.f, 0.f};
+  if (EPI == kEpiQkRope && tile < f.num_heads + f.num_kv_heads) {
+    const __nv_bfloat16 *nw = (tile < f.num_heads ? f.q_w : f.k_w) + lane * 4;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) qk_nw[e] = bf2f(nw[e]);
+  }
+  if (NORM_IN) {
+    uint4 wv[kLnStages][2];
+    norm_in_weights(wv, a, f, k0);
+    pdl_wait();  // h and the tile sums come from the previous kernel
+    __syncwarp();
+    norm_in_fill<MP>(stages, a, f, k0, wv);
+    fence_proxy_async_smem();  // generic-proxy stores -> visible to the tensor core
+    __syncthreads();
+  } else if (warp == 0 && lane == 0) {
+    const int first = a.steps < kLnStages ? a.steps : kLnStages;
     pdl_wait();
     for (int s = 0; s < first; ++s)
       tma_load_2d(stages + s * C::STAGE + C::W_BYTES, &tm_x, k0 + s * kLnBK, 0, &full[s]);
@@ -162,7 +405,8 @@ __global__ void __launch_bounds__(kLnThreads)
       tma_load_2d(w + C::W_BYTES / 2, &tm_w, kc, r1, &full[st]);
       tma_load_2d(w + C::W_BYTES, &tm_x, kc, 0, &full[st]);
     }
-  } else if (warp == 1 && lane == 0) {
+  }
+  if (warp == 1 && lane == 0) {
     constexpr uint32_t idesc = idesc_bf16_f32(kLnRows, MP, false, false);
     bool ok = true;
     for (int s = 0; s < a.steps && ok; ++s) {
@@ -182,6 +426,17 @@ __global__ void __launch_bounds__(kLnThreads)
 
   // Every thread: its TMEM lane = weight row (w*32 + lane) of the tile -> partial[.][row].
   __syncwarp();  // the producer / MMA lanes rejoin their warps (tcgen05.ld is warp-aligned)
+  // While the MMAs run: the epilogue operands of this warp's first rows (inputs written by
+  // earlier kernels; the wait returns at once, x or h was already waited for).
+  EpiRow pre[kEpiPre];
+  if (EPI == kEpiAdd || EPI == kEpiQkRope) {
+    pdl_wait();
+#pragma unroll
+    for (int i = 0; i < kEpiPre; ++i) {
+      const int c = kz + warp * ks + i * 4 * ks;
+      if (c < a.m) epi_fetch<EPI>(pre[i], f, a, c, tile, lane);
+    }
+  }
   const int row = warp * 32 + lane;
   const bool have = __all_sync(0xffffffffu, mbar_wait(done, 0, a.error_flag, &abort_flag));
   if (have) {
@@ -203,7 +458,7 @@ __global__ void __launch_bounds__(kLnThreads)
   // This CTA reduces batch rows kz, kz + ks, ...; warp w takes every 4th of them and each
   // lane 4 consecutive tile rows (128 rows = 32 lanes x 4).
   const uint32_t red_base = smem_addr(red);
-  for (int c = kz + warp * ks; c < a.m; c += 4 * ks) {
+  for (int c = kz + warp * ks, i = 0; c < a.m; c += 4 * ks, ++i) {
     // all ks loads in flight before the first add (one DSMEM round trip, not ks)
     const uint32_t at = red_base + (c * kLnRows + lane * 4) * 4;
     float4 part[kLnMaxSplit];
@@ -221,7 +476,7 @@ __global__ void __launch_bounds__(kLnThreads)
       }
     }
     if (!have) continue;
-    if (a.silu_inner) {  // lanes 0-15: gate rows 0-63; lanes 16-31: the matching up rows
+    if (EPI == kEpiSilu) {  // lanes 0-15: gate rows 0-63; lanes 16-31: the matching up rows
       const float ux = __shfl_down_sync(0xffffffffu, acc.x, 16);
       const float uy = __shfl_down_sync(0xffffffffu, acc.y, 16);
       const float uz = __shfl_down_sync(0xffffffffu, acc.z, 16);
@@ -232,6 +487,35 @@ __global__ void __launch_bounds__(kLnThreads)
             make_uint2(pack2(silu_mul1(acc.x, ux), silu_mul1(acc.y, uy)),
                        pack2(silu_mul1(acc.z, uz), silu_mul1(acc.w, uw)));
       }
+    } else if (EPI == kEpiAdd) {
+      const int col = tile * kLnRows + lane * 4;
+      __nv_bfloat16 *rp = f.residual + c * f.res_stride + col;
+      EpiRow cur;
+      if (i == 0) cur = pre[0];
+      else if (i == 1) cur = pre[1];
+      else epi_fetch<EPI>(cur, f, a, c, tile, lane);
+      const uint2 rv = cur.res;
+      const float y[4] = {acc.x, acc.y, acc.z, acc.w};
+      const float rr[4] = {__uint_as_float(rv.x << 16), __uint_as_float(rv.x & 0xffff0000u),
+                           __uint_as_float(rv.y << 16), __uint_as_float(rv.y & 0xffff0000u)};
+      float h[4], ss = 0.f;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        h[e] = bf2f(f2bf(y[e])) + rr[e];  // bf16 projection output + residual, in fp32
+        ss += h[e] * h[e];
+      }
+      *reinterpret_cast<uint2 *>(rp) = make_uint2(pack2(h[0], h[1]), pack2(h[2], h[3]));
+      *reinterpret_cast<float4 *>(f.h_out + c * f.h_out_stride + col) =
+          make_float4(h[0], h[1], h[2], h[3]);
+      ss = warp_sum(ss);
+      if (lane == 0) f.ss_out[c * (gridDim.x / ks) + tile] = ss;
+    } else if (EPI == kEpiQkRope) {
+      const float v4[4] = {acc.x, acc.y, acc.z, acc.w};
+      EpiRow cur;
+      if (i == 0) cur = pre[0];
+      else if (i == 1) cur = pre[1];
+      else epi_fetch<EPI>(cur, f, a, c, tile, lane);
+      qk_rope_store4(f, a, c, tile, lane, v4, cur, qk_nw);
     } else {
       __nv_bfloat16 *dst = a.y + c * a.y_stride + tile * kLnRows + lane * 4;
       *reinterpret_cast<uint2 *>(dst) = make_uint2(pack2(acc.x, acc.y), pack2(acc.z, acc.w));
@@ -243,6 +527,67 @@ __global__ void __launch_bounds__(kLnThreads)
     tc_fence_after();
     tmem_dealloc(tmem, C::TMEM_COLS);
   }
+}
+
+// Rows of x (+ residual, updated in place) as the residual-add epilogue would leave them:
+// h (fp32) and per-128-column partial sums of squares, for a following RMSNorm prologue
+// or norm_apply. One warp per (row, 128 columns).
+__global__ void rms_stats_kernel(const __nv_bfloat16 *__restrict__ x, __nv_bfloat16 *residual,
+                                 int rows, int hidden, float *__restrict__ h_out,
+                                 float *__restrict__ ss_out) {
+  pdl_trigger();
+  pdl_wait();
+  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  const int tiles = hidden / kLnRows;
+  if (gw >= rows * tiles) return;
+  const int r = gw / tiles, t = gw - (gw / tiles) * tiles;
+  const int col = t * kLnRows + lane * 4;
+  const uint2 xv = *reinterpret_cast<const uint2 *>(x + static_cast<int64_t>(r) * hidden + col);
+  float h[4] = {__uint_as_float(xv.x << 16), __uint_as_float(xv.x & 0xffff0000u),
+                __uint_as_float(xv.y << 16), __uint_as_float(xv.y & 0xffff0000u)};
+  if (residual != nullptr) {
+    uint2 *rp = reinterpret_cast<uint2 *>(residual + static_cast<int64_t>(r) * hidden + col);
+    const uint2 rv = *rp;
+    h[0] += __uint_as_float(rv.x << 16);
+    h[1] += __uint_as_float(rv.x & 0xffff0000u);
+    h[2] += __uint_as_float(rv.y << 16);
+    h[3] += __uint_as_float(rv.y & 0xffff0000u);
+    *rp = make_uint2(pack2(h[0], h[1]), pack2(h[2], h[3]));
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) ss += h[e] * h[e];
+  *reinterpret_cast<float4 *>(h_out + static_cast<int64_t>(r) * hidden + col) =
+      make_float4(h[0], h[1], h[2], h[3]);
+  ss = warp_sum(ss);
+  if (lane == 0) ss_out[r * tiles + t] = ss;
+}
+
+// out = bf16(bf16(h * rsqrt(sum_t ss[t][r] / hidden + eps)) * w): the RMSNorm of rows
+// held as h + tile sums (the model's final norm in a decode step).
+__global__ void norm_apply_kernel(const float *__restrict__ h, const float *__restrict__ ss,
+                                  const __nv_bfloat16 *__restrict__ weight, float eps, int rows,
+                                  int hidden, __nv_bfloat16 *__restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
+  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  const int tiles = hidden / kLnRows;
+  if (gw >= rows * tiles) return;
+  const int r = gw / tiles, t = gw - (gw / tiles) * tiles;
+  float sum = 0.f;
+  for (int i = 0; i < tiles; ++i) sum += ss[r * tiles + i];
+  const float rs = rsqrtf(sum / static_cast<float>(hidden) + eps);
+  const int col = t * kLnRows + lane * 4;
+  const float4 hv = *reinterpret_cast<const float4 *>(h + static_cast<int64_t>(r) * hidden + col);
+  const uint2 wv = *reinterpret_cast<const uint2 *>(weight + col);
+  const float w[4] = {__uint_as_float(wv.x << 16), __uint_as_float(wv.x & 0xffff0000u),
+                      __uint_as_float(wv.y << 16), __uint_as_float(wv.y & 0xffff0000u)};
+  const float hh[4] = {hv.x, hv.y, hv.z, hv.w};
+  float y[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) y[e] = bf2f(f2bf(bf2f(f2bf(hh[e] * rs)) * w[e]));
+  *reinterpret_cast<uint2 *>(out + static_cast<int64_t>(r) * hidden + col) =
+      make_uint2(pack2(y[0], y[1]), pack2(y[2], y[3]));
 }
 
 // Smallest split (power of two dividing the K stages, <= 16) that puts >= 120 CTAs on
@@ -257,18 +602,17 @@ int linear_split(int tiles, int k_steps) {
   return best;
 }
 
-template <int MP>
+template <int MP, bool NORM_IN, int EPI>
 int launch_linear(const void *x, int64_t x_stride, int m, int k, const void *w, int n,
-                  const LinearArgs &proto, int tiles, cudaStream_t stream) {
+                  const LinearArgs &proto, const LinearFuse &fuse, int tiles,
+                  cudaStream_t stream) {
   using C = Ln<MP>;
+  auto kfn = linear_small_kernel<MP, NORM_IN, EPI>;
   static bool configured = false;
   if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(linear_small_kernel<MP>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(C::SMEM));
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(linear_small_kernel<MP>,
-                               cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(kfn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     if (e != cudaSuccess) {
       set_error("linear_small: kernel configuration failed: %s", cudaGetErrorString(e));
       return B200ASR_ERR_CUDA;
@@ -279,11 +623,15 @@ int launch_linear(const void *x, int64_t x_stride, int m, int k, const void *w, 
   const uint64_t wdims[2] = {static_cast<uint64_t>(k), static_cast<uint64_t>(n)};
   const uint64_t wstr[1] = {static_cast<uint64_t>(k) * 2};
   const uint32_t wbox[2] = {kLnBK, 64};
-  const uint64_t xdims[2] = {static_cast<uint64_t>(k), static_cast<uint64_t>(m)};
-  const uint64_t xstr[1] = {static_cast<uint64_t>(x_stride) * 2};
-  const uint32_t xbox[2] = {kLnBK, MP};
-  if (!make_tmap_bf16(&tw, w, 2, wdims, wstr, wbox) || !make_tmap_bf16(&tx, x, 2, xdims, xstr, xbox))
-    return B200ASR_ERR_CUDA;
+  if (!make_tmap_bf16(&tw, w, 2, wdims, wstr, wbox)) return B200ASR_ERR_CUDA;
+  if (NORM_IN) {
+    tx = tw;  // unused: the prologue builds x in shared memory
+  } else {
+    const uint64_t xdims[2] = {static_cast<uint64_t>(k), static_cast<uint64_t>(m)};
+    const uint64_t xstr[1] = {static_cast<uint64_t>(x_stride) * 2};
+    const uint32_t xbox[2] = {kLnBK, MP};
+    if (!make_tmap_bf16(&tx, x, 2, xdims, xstr, xbox)) return B200ASR_ERR_CUDA;
+  }
   LinearArgs a = proto;
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[2];
@@ -295,15 +643,20 @@ int launch_linear(const void *x, int64_t x_stride, int m, int k, const void *w, 
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  // Halve a split whose cluster cannot be resident (16 CTAs is a non-portable size).
+  // Halve a split whose cluster cannot be resident (16 CTAs is a non-portable size). The
+  // RMSNorm prologue needs the whole K slice in the ring, so it cannot go below that.
+  const int min_split = NORM_IN ? (k / kLnBK + kLnStages - 1) / kLnStages : 1;
   while (a.k_split > 1) {
     attr[0].val.clusterDim.x = a.k_split;
     cfg.gridDim = dim3(tiles * a.k_split, 1, 1);
     int clusters = 0;
-    if (cudaOccupancyMaxActiveClusters(&clusters, linear_small_kernel<MP>, &cfg) == cudaSuccess &&
-        clusters > 0)
+    if (cudaOccupancyMaxActiveClusters(&clusters, kfn, &cfg) == cudaSuccess && clusters > 0)
       break;
     cudaGetLastError();
+    if (a.k_split / 2 < min_split) {
+      set_error("linear_small: a cluster of %d CTAs cannot be resident", a.k_split);
+      return B200ASR_ERR_UNSUPPORTED;
+    }
     a.k_split /= 2;
   }
   a.steps = k / kLnBK / a.k_split;
@@ -314,7 +667,7 @@ int launch_linear(const void *x, int64_t x_stride, int m, int k, const void *w, 
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.numAttrs = 2;
   }
-  cudaError_t e = cudaLaunchKernelEx(&cfg, linear_small_kernel<MP>, tw, tx, a);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kfn, tw, tx, a, fuse);
   if (e != cudaSuccess) {
     set_error("linear_small: launch failed (%d x %d CTAs, cluster %d): %s", tiles, a.k_split,
               a.k_split, cudaGetErrorString(e));
@@ -323,9 +676,72 @@ int launch_linear(const void *x, int64_t x_stride, int m, int k, const void *w, 
   return B200ASR_OK;
 }
 
+// K split for the RMSNorm prologue: at least enough CTAs that each K slice fits the
+// ring; a power of two dividing the K stages, at most 16. 0 when none exists.
+int norm_in_split(int tiles, int k_steps) {
+  int ks = linear_split(tiles, k_steps);
+  while (ks <= kLnMaxSplit && (k_steps % ks != 0 || k_steps / ks > kLnStages)) ks *= 2;
+  return ks <= kLnMaxSplit && k_steps % ks == 0 ? ks : 0;
+}
+
+template <bool NORM_IN, int EPI>
+int dispatch_linear(const void *x, int64_t x_stride, int m, int k, const void *w, int n,
+                    const LinearArgs &a, const LinearFuse &f, int tiles, cudaStream_t st) {
+  return m <= 32 ? launch_linear<32, NORM_IN, EPI>(x, x_stride, m, k, w, n, a, f, tiles, st)
+                 : launch_linear<64, NORM_IN, EPI>(x, x_stride, m, k, w, n, a, f, tiles, st);
+}
+
 }  // namespace b200asr
 
 using namespace b200asr;
+
+namespace {
+
+bool valid_weight_rows(int n, int silu_inner, int *tiles) {
+  if (silu_inner) {
+    if (silu_inner <= 0 || silu_inner % 64 != 0 || n != 2 * silu_inner) return false;
+    *tiles = silu_inner / 64;
+  } else {
+    if (n <= 0 || n % kLnRows != 0) return false;
+    *tiles = n / kLnRows;
+  }
+  return true;
+}
+
+LinearArgs make_args(int m, int k_split, int silu_inner, void *y, int64_t y_stride,
+                     int32_t *error_flag) {
+  LinearArgs a;
+  a.m = m;
+  a.steps = 0;
+  a.k_split = k_split;
+  a.silu_inner = silu_inner;
+  a.y = static_cast<__nv_bfloat16 *>(y);
+  a.y_stride = y_stride;
+  a.error_flag = error_flag;
+  return a;
+}
+
+// Shared checks of the RMSNorm prologue's inputs; fills the prologue part of f.
+int norm_in_args(const float *h, int64_t h_stride, const float *ss, int32_t ss_tiles,
+                 const void *norm_weight, float eps, int32_t m, int32_t k, LinearFuse *f) {
+  B200_REQUIRE(h && ss && norm_weight, "linear_small (RMSNorm prologue): null pointer");
+  B200_REQUIRE(aligned16(h) && h_stride >= k && h_stride % 4 == 0 && aligned16(norm_weight),
+               "linear_small (RMSNorm prologue): misaligned h or weight");
+  B200_REQUIRE(ss_tiles >= 4 && ss_tiles <= kNormMaxTiles && ss_tiles % 4 == 0 && aligned16(ss),
+               "linear_small: ss_tiles %d must be a multiple of 4 in [4, %d] (hidden %% 512 == 0)",
+               ss_tiles, kNormMaxTiles);
+  f->h = h;
+  f->h_stride = h_stride;
+  f->ss = ss;
+  f->ss_tiles = ss_tiles;
+  f->norm_w = static_cast<const __nv_bfloat16 *>(norm_weight);
+  f->norm_eps = eps;
+  f->norm_k = k;
+  (void)m;
+  return B200ASR_OK;
+}
+
+}  // namespace
 
 extern "C" int b200asr_linear_small(const void *x, int64_t x_row_stride, int32_t m, int32_t k,
                                     const void *w, int32_t n, int32_t silu_inner, void *y,
@@ -338,29 +754,154 @@ extern "C" int b200asr_linear_small(const void *x, int64_t x_row_stride, int32_t
   B200_REQUIRE(aligned16(x) && aligned16(w) && aligned16(y) && x_row_stride >= k &&
                    x_row_stride % 8 == 0 && y_row_stride % 4 == 0,
                "linear_small: misaligned tensor");
-  int tiles;
-  if (silu_inner) {
-    B200_REQUIRE(silu_inner > 0 && silu_inner % 64 == 0 && n == 2 * silu_inner,
-                 "linear_small: SiLU*mul needs 2 x I weight rows with I %% 64 == 0 (I=%d, N=%d)",
-                 silu_inner, n);
-    B200_REQUIRE(y_row_stride >= silu_inner, "linear_small: output row stride too small");
-    tiles = silu_inner / 64;
-  } else {
-    B200_REQUIRE(n > 0 && n % kLnRows == 0, "linear_small: N %d must be a multiple of %d", n,
-                 kLnRows);
-    B200_REQUIRE(y_row_stride >= n, "linear_small: output row stride too small");
-    tiles = n / kLnRows;
-  }
-  LinearArgs a;
-  a.m = m;
-  a.steps = 0;
-  a.k_split = linear_split(tiles, k / kLnBK);
-  a.silu_inner = silu_inner;
-  a.y = static_cast<__nv_bfloat16 *>(y);
-  a.y_stride = y_row_stride;
-  a.error_flag = error_flag;
+  int tiles = 0;
+  B200_REQUIRE(valid_weight_rows(n, silu_inner, &tiles),
+               "linear_small: N %d / SiLU inner %d unsupported (N %% 128 == 0, or N = 2 I with "
+               "I %% 64 == 0)", n, silu_inner);
+  B200_REQUIRE(y_row_stride >= (silu_inner ? silu_inner : n),
+               "linear_small: output row stride too small");
+  const LinearArgs a = make_args(m, linear_split(tiles, k / kLnBK), silu_inner, y, y_row_stride,
+                                 error_flag);
+  const LinearFuse f = {};
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  return m <= 32 ? launch_linear<32>(x, x_row_stride, m, k, w, n, a, tiles, st)
-                 : launch_linear<64>(x, x_row_stride, m, k, w, n, a, tiles, st);
+  return silu_inner ? dispatch_linear<false, kEpiSilu>(x, x_row_stride, m, k, w, n, a, f, tiles, st)
+                    : dispatch_linear<false, kEpiPlain>(x, x_row_stride, m, k, w, n, a, f, tiles, st);
 }
 
+extern "C" int b200asr_linear_small_add(const void *x, int64_t x_row_stride, int32_t m, int32_t k,
+                                        const void *w, int32_t n, void *residual,
+                                        int64_t residual_row_stride, float *h_out,
+                                        int64_t h_row_stride, float *ss_out,
+                                        int32_t *error_flag, b200asr_stream_t stream) {
+  B200_REQUIRE(m >= 0 && m <= 64, "linear_small_add: %d rows (at most 64)", m);
+  if (m == 0) return B200ASR_OK;
+  B200_REQUIRE(k > 0 && k % kLnBK == 0, "linear_small_add: K %d must be a multiple of %d", k, kLnBK);
+  B200_REQUIRE(n > 0 && n % kLnRows == 0 && n / kLnRows <= 64,
+               "linear_small_add: N %d must be a multiple of %d (at most 64 tiles)", n, kLnRows);
+  B200_REQUIRE(x && w && residual && h_out && ss_out, "linear_small_add: null pointer");
+  B200_REQUIRE(aligned16(x) && aligned16(w) && aligned16(residual) && aligned16(h_out) &&
+                   x_row_stride >= k && x_row_stride % 8 == 0 && residual_row_stride >= n &&
+                   residual_row_stride % 8 == 0 && h_row_stride >= n && h_row_stride % 4 == 0,
+               "linear_small_add: misaligned tensor");
+  const int tiles = n / kLnRows;
+  const LinearArgs a = make_args(m, linear_split(tiles, k / kLnBK), 0, nullptr, 0, error_flag);
+  LinearFuse f = {};
+  f.residual = static_cast<__nv_bfloat16 *>(residual);
+  f.res_stride = residual_row_stride;
+  f.h_out = h_out;
+  f.h_out_stride = h_row_stride;
+  f.ss_out = ss_out;
+  return dispatch_linear<false, kEpiAdd>(x, x_row_stride, m, k, w, n, a, f, tiles,
+                                         static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int b200asr_linear_small_norm(const float *h, int64_t h_row_stride, const float *ss,
+                                         int32_t ss_tiles, const void *norm_weight, float eps,
+                                         int32_t m, int32_t k, const void *w, int32_t n,
+                                         int32_t silu_inner, void *y, int64_t y_row_stride,
+                                         int32_t *error_flag, b200asr_stream_t stream) {
+  B200_REQUIRE(m >= 0 && m <= 64, "linear_small_norm: %d rows (at most 64)", m);
+  if (m == 0) return B200ASR_OK;
+  B200_REQUIRE(k > 0 && k % kLnBK == 0, "linear_small_norm: K %d must be a multiple of %d", k, kLnBK);
+  B200_REQUIRE(w && y && aligned16(w) && aligned16(y) && y_row_stride % 4 == 0,
+               "linear_small_norm: null or misaligned tensor");
+  LinearFuse f = {};
+  const int rc = norm_in_args(h, h_row_stride, ss, ss_tiles, norm_weight, eps, m, k, &f);
+  if (rc != B200ASR_OK) return rc;
+  int tiles = 0;
+  B200_REQUIRE(valid_weight_rows(n, silu_inner, &tiles),
+               "linear_small_norm: N %d / SiLU inner %d unsupported", n, silu_inner);
+  B200_REQUIRE(y_row_stride >= (silu_inner ? silu_inner : n),
+               "linear_small_norm: output row stride too small");
+  const int ks = norm_in_split(tiles, k / kLnBK);
+  B200_REQUIRE(ks > 0, "linear_small_norm: K %d too large for the RMSNorm prologue", k);
+  const LinearArgs a = make_args(m, ks, silu_inner, y, y_row_stride, error_flag);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  return silu_inner ? dispatch_linear<true, kEpiSilu>(nullptr, 0, m, k, w, n, a, f, tiles, st)
+                    : dispatch_linear<true, kEpiPlain>(nullptr, 0, m, k, w, n, a, f, tiles, st);
+}
+
+extern "C" int b200asr_linear_small_norm_qk_rope(
+    const float *h, int64_t h_row_stride, const float *ss, int32_t ss_tiles,
+    const void *norm_weight, float eps, int32_t m, int32_t k, const void *w, int32_t num_heads,
+    int32_t num_kv_heads, int32_t head_dim, const void *q_norm_weight, const void *k_norm_weight,
+    float qk_eps, const int64_t *positions, const float *cos_sin_cache, int32_t max_position,
+    void *q_out, int64_t q_out_row_stride, void *k_cache, void *v_cache,
+    const int32_t *slot_mapping, int64_t num_slots, int32_t *error_flag,
+    b200asr_stream_t stream) {
+  B200_REQUIRE(m >= 0 && m <= 64, "linear_small_norm_qk_rope: %d rows (at most 64)", m);
+  if (m == 0) return B200ASR_OK;
+  B200_REQUIRE(head_dim == kLnRows, "linear_small_norm_qk_rope: head_dim %d (needs %d)", head_dim,
+               kLnRows);
+  B200_REQUIRE(num_heads > 0 && num_kv_heads > 0 && num_heads % num_kv_heads == 0,
+               "linear_small_norm_qk_rope: bad head counts %d / %d", num_heads, num_kv_heads);
+  B200_REQUIRE(k > 0 && k % kLnBK == 0, "linear_small_norm_qk_rope: K %d must be a multiple of %d",
+               k, kLnBK);
+  B200_REQUIRE(w && aligned16(w) && q_norm_weight && k_norm_weight && positions && cos_sin_cache &&
+                   q_out && aligned16(q_out) && q_out_row_stride >= num_heads * head_dim &&
+                   q_out_row_stride % 4 == 0 && k_cache && v_cache && aligned16(k_cache) &&
+                   aligned16(v_cache) && max_position > 0,
+               "linear_small_norm_qk_rope: null or misaligned tensor");
+  LinearFuse f = {};
+  const int rc = norm_in_args(h, h_row_stride, ss, ss_tiles, norm_weight, eps, m, k, &f);
+  if (rc != B200ASR_OK) return rc;
+  const int n = (num_heads + 2 * num_kv_heads) * head_dim;
+  const int tiles = n / kLnRows;
+  const int ks = norm_in_split(tiles, k / kLnBK);
+  B200_REQUIRE(ks > 0, "linear_small_norm_qk_rope: K %d too large for the RMSNorm prologue", k);
+  f.num_heads = num_heads;
+  f.num_kv_heads = num_kv_heads;
+  f.q_w = static_cast<const __nv_bfloat16 *>(q_norm_weight);
+  f.k_w = static_cast<const __nv_bfloat16 *>(k_norm_weight);
+  f.qk_eps = qk_eps;
+  f.positions = positions;
+  f.cos_sin = cos_sin_cache;
+  f.max_position = max_position;
+  f.q_out = static_cast<__nv_bfloat16 *>(q_out);
+  f.q_out_stride = q_out_row_stride;
+  f.k_cache = static_cast<__nv_bfloat16 *>(k_cache);
+  f.v_cache = static_cast<__nv_bfloat16 *>(v_cache);
+  f.slot_mapping = slot_mapping;
+  f.num_slots = num_slots;
+  const LinearArgs a = make_args(m, ks, 0, nullptr, 0, error_flag);
+  return dispatch_linear<true, kEpiQkRope>(nullptr, 0, m, k, w, n, a, f, tiles,
+                                           static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int b200asr_rms_stats(const void *x, void *residual, int32_t rows, int32_t hidden,
+                                 float *h_out, float *ss_out, b200asr_stream_t stream) {
+  B200_REQUIRE(rows >= 0 && rows <= 64, "rms_stats: %d rows (at most 64)", rows);
+  if (rows == 0) return B200ASR_OK;
+  B200_REQUIRE(hidden > 0 && hidden % kLnRows == 0 && hidden / kLnRows <= 64,
+               "rms_stats: hidden %d must be a multiple of %d", hidden, kLnRows);
+  B200_REQUIRE(x && h_out && ss_out && aligned16(x) && aligned16(h_out) &&
+                   (residual == nullptr || aligned16(residual)),
+               "rms_stats: null or misaligned tensor");
+  const int warps = rows * (hidden / kLnRows);
+  B200_LAUNCH_CHECK_ERR(
+      launch_kernel(rms_stats_kernel, dim3((warps + 7) / 8), dim3(256), 0,
+                    static_cast<cudaStream_t>(stream), true, 1,
+                    static_cast<const __nv_bfloat16 *>(x), static_cast<__nv_bfloat16 *>(residual),
+                    static_cast<int>(rows), static_cast<int>(hidden), h_out, ss_out),
+      "rms_stats");
+  return B200ASR_OK;
+}
+
+extern "C" int b200asr_norm_apply(const float *h, const float *ss, const void *weight, float eps,
+                                  int32_t rows, int32_t hidden, void *out,
+                                  b200asr_stream_t stream) {
+  B200_REQUIRE(rows >= 0 && rows <= 64, "norm_apply: %d rows (at most 64)", rows);
+  if (rows == 0) return B200ASR_OK;
+  B200_REQUIRE(hidden > 0 && hidden % kLnRows == 0 && hidden / kLnRows <= 64,
+               "norm_apply: hidden %d must be a multiple of %d", hidden, kLnRows);
+  B200_REQUIRE(h && ss && weight && out && aligned16(h) && aligned16(out),
+               "norm_apply: null or misaligned tensor");
+  const int warps = rows * (hidden / kLnRows);
+  B200_LAUNCH_CHECK_ERR(
+      launch_kernel(norm_apply_kernel, dim3((warps + 7) / 8), dim3(256), 0,
+                    static_cast<cudaStream_t>(stream), true, 1, h, ss,
+                    static_cast<const __nv_bfloat16 *>(weight), eps, static_cast<int>(rows),
+                    static_cast<int>(hidden), static_cast<__nv_bfloat16 *>(out)),
+      "norm_apply");
+  return B200ASR_OK;
+}

@@ -324,6 +324,111 @@ def linear_small(x, weight, *, silu: bool = False, out=None, error_flag=None) ->
     return out
 
 
+# ---------------------------------------------------------------- decode-step fusions
+# A decoder row between the projections of a decode step is carried as ``h`` (fp32
+# [m, hidden], the pre-norm residual sum) and ``ss`` (fp32 [m, hidden / 128], per
+# 128-column partial sums of h^2); the RMSNorm is applied by the next projection.
+
+
+class NormState:
+    """``h`` and ``ss`` buffers of a decode step (rows <= 64)."""
+
+    def __init__(self, rows: int, hidden: int, device):
+        self.rows, self.hidden = rows, hidden
+        self.h = torch.empty(rows, hidden, dtype=torch.float32, device=device)
+        self.ss = torch.empty(rows, hidden // 128, dtype=torch.float32, device=device)
+
+    @property
+    def tiles(self) -> int:
+        return self.hidden // 128
+
+
+def fused_decode_ok(m: int, hidden: int, intermediate: int, num_heads: int, num_kv_heads: int,
+                    head_dim: int) -> bool:
+    """Whether the fused decode-step projections take a batch of ``m`` rows."""
+    return (1 <= m <= LINEAR_SMALL_MAX_ROWS and head_dim == 128 and hidden % 512 == 0
+            and hidden <= 4096 and intermediate % 64 == 0 and intermediate <= 4096
+            and (num_heads * head_dim) % 64 == 0 and num_heads % num_kv_heads == 0)
+
+
+def rms_stats(x, state: NormState, residual=None) -> NormState:
+    """h = x (+ residual, updated in place to bf16(x + residual)) and its tile sums."""
+    _cuda(x, residual)
+    _need(x.dtype == BF16 and x.is_contiguous() and x.shape == state.h.shape, "x bf16 [m, hidden]")
+    _count()
+    check(lib.b200asr_rms_stats(_p(x), _p(residual), x.shape[0], x.shape[1], _p(state.h),
+                                _p(state.ss), _stream()), "rms_stats")
+    return state
+
+
+def norm_apply(state: NormState, weight, eps: float, out=None) -> torch.Tensor:
+    """RMSNorm (layers/layernorm.py:19-25) of rows held as (h, ss)."""
+    if out is None:
+        out = torch.empty(state.rows, state.hidden, dtype=BF16, device=state.h.device)
+    _count()
+    check(lib.b200asr_norm_apply(_p(state.h), _p(state.ss), _p(weight), float(eps), state.rows,
+                                 state.hidden, _p(out), _stream()), "norm_apply")
+    return out
+
+
+def linear_small_add(x, weight, residual, state: NormState, error_flag=None) -> NormState:
+    """``x @ weight.T`` + the residual add of the following RMSNorm: residual <- bf16(h),
+    state <- (h, tile sums of h^2)."""
+    _cuda(x, weight, residual)
+    _need(linear_small_ok(x, weight), "linear_small_add: unsupported shape/layout")
+    m, k = x.shape
+    n = weight.shape[0]
+    _need(residual.dtype == BF16 and residual.shape == (m, n) and residual.stride(1) == 1
+          and state.h.shape == (m, n), "linear_small_add: residual / state shape")
+    _count()
+    check(lib.b200asr_linear_small_add(_p(x), x.stride(0), m, k, _p(weight), n, _p(residual),
+                                       residual.stride(0), _p(state.h), state.h.stride(0),
+                                       _p(state.ss), _p(error_flag), _stream()),
+          "linear_small_add")
+    return state
+
+
+def linear_small_norm(state: NormState, norm_weight, eps: float, weight, *, silu: bool = False,
+                      out=None, error_flag=None) -> torch.Tensor:
+    """``RMSNorm(h) @ weight.T`` (fused SiLU*mul when ``silu``)."""
+    _cuda(norm_weight, weight)
+    m, k = state.rows, state.hidden
+    n = weight.shape[0]
+    _need(weight.dtype == BF16 and weight.is_contiguous() and weight.shape[1] == k,
+          "linear_small_norm: weight [n, hidden] bf16")
+    cols = n // 2 if silu else n
+    if out is None:
+        out = torch.empty(m, cols, dtype=BF16, device=weight.device)
+    _count()
+    check(lib.b200asr_linear_small_norm(_p(state.h), state.h.stride(0), _p(state.ss), state.tiles,
+                                        _p(norm_weight), float(eps), m, k, _p(weight), n,
+                                        cols if silu else 0, _p(out), out.stride(0),
+                                        _p(error_flag), _stream()), "linear_small_norm")
+    return out
+
+
+def linear_small_norm_qk_rope(state: NormState, norm_weight, eps: float, weight, positions, *,
+                              num_heads: int, num_kv_heads: int, head_dim: int, q_weight,
+                              k_weight, qk_eps: float, cos_sin_cache, q_out, k_cache, v_cache,
+                              slot_mapping, error_flag=None) -> torch.Tensor:
+    """qkv_proj of RMSNorm(h), then q/k RMSNorm + RoPE and the K/V cache store per head."""
+    _cuda(norm_weight, weight, positions, q_weight, k_weight, cos_sin_cache, q_out, k_cache,
+          v_cache, slot_mapping)
+    _need(positions.dtype == torch.int64 and slot_mapping.dtype == torch.int32,
+          "positions int64, slot_mapping int32")
+    _need(cos_sin_cache.dtype == torch.float32 and cos_sin_cache.is_contiguous(), "fp32 rope table")
+    _need(weight.dtype == BF16 and weight.is_contiguous() and weight.shape[1] == state.hidden,
+          "qkv weight [n, hidden] bf16")
+    num_slots = k_cache.numel() // (num_kv_heads * head_dim)
+    _count()
+    check(lib.b200asr_linear_small_norm_qk_rope(
+        _p(state.h), state.h.stride(0), _p(state.ss), state.tiles, _p(norm_weight), float(eps),
+        state.rows, state.hidden, _p(weight), num_heads, num_kv_heads, head_dim, _p(q_weight),
+        _p(k_weight), float(qk_eps), _p(positions), _p(cos_sin_cache), cos_sin_cache.shape[0],
+        _p(q_out), q_out.stride(0), _p(k_cache), _p(v_cache), _p(slot_mapping), num_slots,
+        _p(error_flag), _stream()), "linear_small_norm_qk_rope")
+    return q_out
+
 
 def set_pdl(enable: bool) -> None:
     """Programmatic dependent launch for the decode-path kernels (process-wide)."""

@@ -351,6 +351,61 @@ def log_mel_config3() -> dict:
                  audio_seconds_per_ms=round(float(lens.sum()) / 16000 / (us / 1000), 1))
 
 
+class _DecodeRow:
+    """The three things GraphRunner.run reads of a running request."""
+
+    def __init__(self, length: int, block_table: list[int]):
+        self.length, self.block_table, self.token_ids = length, block_table, [100]
+
+    def __len__(self) -> int:
+        return self.length
+
+
+def decode_graph_step(fused: bool, iters: int = 64) -> dict:
+    """One whole decode step of Qwen3-ASR-0.6B (random init) as the engine replays it:
+    the bucket-32 CUDA graph (28 layers of projections, norms, RoPE + KV store, paged
+    attention, lm_head, argmax, descriptor advance) over 32 rows of contexts U[80, 250],
+    with the decoder's projections fused (five launches per layer) or not (eight)."""
+    import tempfile
+
+    from voiceagent_b200.checkpoint import write_checkpoint
+    from voiceagent_b200.engine.engine import AsrEngine
+
+    path = write_checkpoint(Path(tempfile.mkdtemp()) / "c06", "0.6b", weights=False)
+    eng = AsrEngine(str(path), weights="random", seed=0, max_num_seqs=32, max_model_len=1024,
+                    num_kvcache_blocks=96, fused_decode=fused)
+    gr = eng.model_runner.graph_runner
+    rng = np.random.default_rng(3)
+    lens = rng.integers(80, 251, size=32)
+    rows = [_DecodeRow(int(n), [3 * i, 3 * i + 1, 3 * i + 2]) for i, n in enumerate(lens)]
+    gr.run(rows, 1)  # uploads the descriptor; each replay then advances it on the device
+    graph = gr.graphs[(32, True)]
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(iters):
+        graph.replay()
+    e.record()
+    e.synchronize()
+    us = s.elapsed_time(e) * 1000.0 / iters
+    t = eng.config.model_config.text
+    hd = t.head_dim or t.hidden_size // t.num_attention_heads
+    per_layer = (t.hidden_size * (t.num_attention_heads + 2 * t.num_key_value_heads) * hd
+                 + t.num_attention_heads * hd * t.hidden_size + 3 * t.hidden_size * t.intermediate_size) * 2
+    weights = t.num_hidden_layers * per_layer + t.vocab_size * t.hidden_size * 2
+    ctx = int(lens.sum()) + 32 * (3 + iters // 2)  # mean context over the timed replays
+    kv = ctx * t.num_hidden_layers * t.num_key_value_heads * hd * 2 * 2
+    launches = gr.kernels_per_replay[(32, True)]
+    del eng, gr, graph
+    torch.cuda.empty_cache()
+    return _line("decode_step_graph", f"0.6B decode step, 32 rows ctx~U[80,250], "
+                 f"{'fused' if fused else 'unfused'} projections", us, weights + kv,
+                 bound="hbm (weights + KV, latency-bound)", launches_per_step=launches,
+                 timing=f"{iters} replays of the bucket-32 graph back to back")
+
+
 BENCHES = {
     "decode": lambda: [decode_config1()],
     "decode_step": lambda: [
@@ -358,6 +413,7 @@ BENCHES = {
                        label="config3 decode-step shape B=32 ctx~U[80,250], short-context kernel"),
         decode_config1(lo=80, hi=250, sets=16, max_seqlen_k=4096,
                        label="config3 decode-step shape B=32 ctx~U[80,250], stream-K kernel")],
+    "step": lambda: [decode_graph_step(True), decode_graph_step(False)],
     "prefill": lambda: [prefill_config2()],
     "window": lambda: [window_config2()],
     "store": lambda: [store_rows(32), store_rows(8192)],

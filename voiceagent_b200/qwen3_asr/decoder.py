@@ -3,8 +3,10 @@
 Per layer the b200asr kernels do: input / post-attention RMSNorm (the latter fused
 with the residual add), per-head q/k RMSNorm + RoPE fused with the KV-cache store,
 paged attention and SiLU*mul. Dense projections run on torch matmul (cuBLAS) for
-prefill-sized batches and on the weight-streaming ``linear_small`` kernel for decode
-batches of up to 64 rows, where gate_up_proj also applies SiLU*mul in its epilogue.
+prefill-sized batches. Decode-sized batches (up to 64 rows) take the fused step: the
+weight-streaming ``linear_small`` kernels with each RMSNorm split across the
+projections around it, q/k norm + RoPE + the KV store in qkv_proj's epilogue and
+SiLU*mul in gate_up_proj's -- five launches per layer.
 """
 
 from __future__ import annotations
@@ -116,13 +118,69 @@ class Qwen3Model(nn.Module):
         self.layers = nn.ModuleList(
             [Qwen3DecoderLayer(config, self.rope) for _ in range(config.num_hidden_layers)])
         self.norm = RMSNorm(config.hidden_size, eps=config.rms_norm_eps)
+        self.fused_decode = True  # decode-sized batches on the fused projections
+        self._plain: bool | None = None  # projections without bias, bf16, contiguous
 
     def forward(self, input_ids, positions, inputs_embeds=None) -> torch.Tensor:
         if (input_ids is None) == (inputs_embeds is None):
             raise ValueError("pass exactly one of input_ids or inputs_embeds")
         hidden = self.embed_tokens(input_ids) if inputs_embeds is None else inputs_embeds
+        if self.fused_step_ok(hidden.shape[0]):
+            # the residual stream is updated in place: never the caller's tensor
+            return self._forward_fused(positions, hidden if inputs_embeds is None else hidden.clone())
         residual = None
         for layer in self.layers:
             hidden, residual = layer(positions, hidden, residual)
         hidden, _ = self.norm(hidden, residual)
         return hidden
+
+    def fused_step_ok(self, rows: int) -> bool:
+        """Decode-sized batches run the fused projections (five launches per layer)."""
+        if not self.fused_decode or not self.layers:
+            return False
+        a = self.layers[0].self_attn
+        return kx.fused_decode_ok(rows, self.embed_tokens.embedding_dim,
+                                  self.layers[0].mlp.down_proj.in_features, a.num_heads,
+                                  a.num_kv_heads, a.head_dim) and self._plain_projections
+
+    def _forward_fused(self, positions, residual: torch.Tensor) -> torch.Tensor:
+        """The same layer stack with each RMSNorm split across the projections around it
+        (kernels.linear_small_add / linear_small_norm*): qkv (norm, q/k norm, RoPE, K/V
+        store) -> attention -> o_proj (+ residual) -> gate_up (norm, SiLU*mul) -> down
+        (+ residual); the rows travel between them as fp32 h plus tile sums of h^2."""
+        ctx = get_attention_context()
+        m, hidden = residual.shape
+        state = kx.NormState(m, hidden, residual.device)
+        kx.rms_stats(residual, state)  # layer 0's input norm reads the embeddings
+        for layer in self.layers:
+            attn, mlp = layer.self_attn, layer.mlp
+            q = torch.empty(m, attn.num_heads, attn.head_dim, dtype=residual.dtype,
+                            device=residual.device)
+            kx.linear_small_norm_qk_rope(
+                state, layer.input_layernorm.weight, layer.input_layernorm.eps,
+                attn.qkv_proj.weight, positions, num_heads=attn.num_heads,
+                num_kv_heads=attn.num_kv_heads, head_dim=attn.head_dim,
+                q_weight=attn.q_norm.weight, k_weight=attn.k_norm.weight, qk_eps=attn.eps,
+                cos_sin_cache=attn.rope.table, q_out=q, k_cache=attn.attn.k_cache,
+                v_cache=attn.attn.v_cache, slot_mapping=ctx.slot_mapping,
+                error_flag=ctx.error_flag)
+            o = attn.attn(q)
+            kx.linear_small_add(o.view(m, attn.q_size), attn.o_proj.weight, residual, state,
+                                error_flag=ctx.error_flag)
+            act = kx.linear_small_norm(state, layer.post_attention_layernorm.weight,
+                                       layer.post_attention_layernorm.eps,
+                                       mlp.gate_up_proj.weight, silu=True,
+                                       error_flag=ctx.error_flag)
+            kx.linear_small_add(act, mlp.down_proj.weight, residual, state,
+                                error_flag=ctx.error_flag)
+        return kx.norm_apply(state, self.norm.weight, self.norm.eps)
+
+    @property
+    def _plain_projections(self) -> bool:
+        if self._plain is None:
+            self._plain = all(
+                lin.bias is None and lin.weight.dtype == torch.bfloat16 and lin.weight.is_contiguous()
+                for layer in self.layers
+                for lin in (layer.self_attn.qkv_proj, layer.self_attn.o_proj,
+                            layer.mlp.gate_up_proj, layer.mlp.down_proj))
+        return self._plain
