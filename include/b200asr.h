@@ -60,7 +60,14 @@ B200ASR_API const char *b200asr_last_error(void);
  * prologue -- shared-memory and TMEM set-up, tensor-map and weight loads -- while the
  * previous kernel in the stream finishes; each waits for that kernel's results before
  * reading them or writing global memory. A CUDA graph captured with it on keeps the
- * overlap. Process-wide; set it before capturing graphs.                            */
+ * overlap. Process-wide; set it before capturing graphs.
+ * Two reads happen before that wait, on data a decode step fixes before its decoder
+ * kernels run: paged_decode with max_seqlen_k <= 512 reads cu_seqlens_k, block_tables
+ * and the cached K/V rows of every position but each sequence's newest, and
+ * linear_small_norm_qk_rope's optional KV prefetch reads cu_seqlens_k / block_tables.
+ * With PDL on, those must have been written before the nearest preceding launch in the
+ * stream that is not itself a PDL launch (the engine's embedding kernel follows the
+ * step's packer); the newest row may be written by the kernel right before.          */
 B200ASR_API void b200asr_set_pdl(int32_t enable);
 B200ASR_API int32_t b200asr_pdl_enabled(void);
 
@@ -287,7 +294,12 @@ B200ASR_API int b200asr_linear_small(const void *x, int64_t x_row_stride, int32_
  *   models/qwen3.py:43-48, + the KV store of PagedAttention.forward, attention.py:90):
  *   the projection of RMSNorm(h), then per head exactly what b200asr_qk_norm_rope_store
  *   does (q heads to q_out, K and V into the cache at slot_mapping; slot -1 skipped);
- *   head_dim 128.
+ *   head_dim 128. Optional (prefetch_cu_seqlens_k non-NULL, decode steps): the cached
+ *   K/V rows of the prefetch_batch sequences described by prefetch_cu_seqlens_k /
+ *   prefetch_block_tables (row stride prefetch_bt_stride, block_size tokens per block)
+ *   are requested into L2 for the attention that follows; they are read before the
+ *   wait on the previous kernel, so they must have been written by an earlier
+ *   non-overlapping launch (the step's packer). Out-of-pool block ids are skipped.
  * rms_stats: h and ss of x (+ residual, updated in place to bf16(x + residual)) -- the
  *   layer-0 input norm, whose input is the embedding.
  * norm_apply: out = RMSNorm of (h, ss) -- the model's final norm before lm_head.     */
@@ -306,8 +318,9 @@ B200ASR_API int b200asr_linear_small_norm_qk_rope(
     int32_t num_kv_heads, int32_t head_dim, const void *q_norm_weight, const void *k_norm_weight,
     float qk_eps, const int64_t *positions, const float *cos_sin_cache, int32_t max_position,
     void *q_out, int64_t q_out_row_stride, void *k_cache, void *v_cache,
-    const int32_t *slot_mapping, int64_t num_slots, int32_t *error_flag,
-    b200asr_stream_t stream);
+    const int32_t *slot_mapping, int64_t num_slots, const int32_t *prefetch_cu_seqlens_k,
+    const int32_t *prefetch_block_tables, int32_t prefetch_bt_stride, int32_t prefetch_batch,
+    int32_t block_size, int32_t *error_flag, b200asr_stream_t stream);
 B200ASR_API int b200asr_rms_stats(const void *x, void *residual, int32_t rows, int32_t hidden,
                       float *h_out, float *ss_out, b200asr_stream_t stream);
 B200ASR_API int b200asr_norm_apply(const float *h, const float *ss, const void *weight, float eps,

@@ -392,6 +392,56 @@ def test_paged_decode_peaked_scores(kx, max_len):
     assert_attn_close(out, ref, f"decode peaked scores max_seqlen_k={max_len}")
 
 
+def test_paged_decode_newest_row_written_just_before_with_pdl(kx):
+    """The short-context kernel requests a sequence's stages before its PDL wait except
+    the last one, which holds the newest token: with PDL on, a store of each sequence's
+    newest K/V row immediately before it (in a graph) must be seen, as without PDL."""
+    rng = np.random.default_rng(21)
+    lens = [70, 128, 129, 200, 1, 64, 65, 250]
+    q, kc, vc, tables, cu_k = _decode_case(rng, lens, nblocks=32)
+    qd, kcd, vcd = bf16(q), bf16(kc), bf16(vc)
+    cu, tb = dev(cu_k, torch.int32), dev(tables, torch.int32)
+    newest = [int(tables[i, (n - 1) // 256]) * 256 + (n - 1) % 256 for i, n in enumerate(lens)]
+    slots = dev(np.asarray(newest, np.int32), torch.int32)
+    g = torch.Generator(device="cuda").manual_seed(5)
+    new_k = (torch.randn(len(lens), 8, 128, device="cuda", generator=g) * 0.3).bfloat16()
+    new_v = torch.randn(len(lens), 8, 128, device="cuda", generator=g).bfloat16()
+    ws = torch.zeros(1 << 20, dtype=torch.float32, device="cuda")
+    outs = []
+    for pdl in (False, True):
+        kx.set_pdl(pdl)
+        try:
+            k_run, v_run = kcd.clone(), vcd.clone()
+            out = torch.zeros_like(qd)
+
+            def step():
+                kx.store_kvcache(new_k, new_v, k_run, v_run, slots)
+                kx.paged_decode(qd, k_run, v_run, cu, tb, max_seqlen_k=512,
+                                scale=128 ** -0.5, out=out, workspace=ws)
+
+            step()
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                step()
+            for _ in range(3):  # the newest rows are rewritten each replay
+                k_run.copy_(kcd)
+                v_run.copy_(vcd)
+                graph.replay()
+            torch.cuda.synchronize()
+            outs.append(out.clone())
+            del graph
+        finally:
+            kx.set_pdl(False)
+    assert torch.equal(outs[0], outs[1])
+    kc2, vc2 = kc.copy(), vc.copy()
+    for i, s in enumerate(newest):
+        kc2.reshape(-1, 8, 128)[s] = new_k[i].float().cpu().numpy()
+        vc2.reshape(-1, 8, 128)[s] = new_v[i].float().cpu().numpy()
+    ref = K.paged_attention(q, kc2, vc2, np.arange(len(lens) + 1), cu_k, tables, 128 ** -0.5)
+    assert_attn_close(outs[1], ref, "decode after a PDL store of the newest rows")
+
+
 def test_paged_decode_config1(kx):
     """B=32, ctx ~ U[64, 1024], 4096-block pool, random tables."""
     rng = np.random.default_rng(0)
@@ -692,8 +742,13 @@ def test_linear_small_norm_qk_rope_matches_unfused(kx, m):
 
     table = rope_table(d, 4096, 1e6, "cuda")
     state = kx.rms_stats(y, kx.NormState(m, hidden, "cuda"))
+    # KV prefetch hint over ragged sequences, one with an out-of-pool block (skipped)
+    pf_lens = torch.tensor([0, 300, 1, 700, 255], dtype=torch.int32, device="cuda")
+    pf_cu = torch.cat([torch.zeros(1, dtype=torch.int32, device="cuda"), pf_lens.cumsum(0).int()])
+    pf_tables = torch.tensor([[0, 0, 0], [1, 2, 0], [3, 0, 0], [0, 1, 99], [2, 0, 0]],
+                             dtype=torch.int32, device="cuda")
     outs = []
-    for fused in (True, False):
+    for fused in (True, "prefetch", False):
         kc = torch.full((4, 256, hkv, d), 7.0, device="cuda").bfloat16()
         vc = kc.clone()
         q = torch.empty(m, hq, d, device="cuda", dtype=torch.bfloat16)
@@ -701,15 +756,16 @@ def test_linear_small_norm_qk_rope_matches_unfused(kx, m):
             kx.linear_small_norm_qk_rope(state, nw, 1e-6, w, positions, num_heads=hq,
                                          num_kv_heads=hkv, head_dim=d, q_weight=qw, k_weight=kw,
                                          qk_eps=1e-6, cos_sin_cache=table, q_out=q, k_cache=kc,
-                                         v_cache=vc, slot_mapping=slots)
+                                         v_cache=vc, slot_mapping=slots,
+                                         prefetch=(pf_cu, pf_tables) if fused == "prefetch" else None)
         else:
             qkv = kx.linear_small_norm(state, nw, 1e-6, w)
             kx.qk_norm_rope_store(qkv, positions, num_heads=hq, num_kv_heads=hkv, head_dim=d,
                                   q_weight=qw, k_weight=kw, eps=1e-6, cos_sin_cache=table,
                                   q_out=q, k_cache=kc, v_cache=vc, slot_mapping=slots)
         outs.append((q, kc, vc))
-    for a, b in zip(*outs):
-        assert torch.equal(a, b)
+    for a, b, c in zip(*outs):
+        assert torch.equal(a, c) and torch.equal(b, c)
     untouched = torch.ones(nslots, dtype=torch.bool, device="cuda")
     untouched[slots[slots >= 0].long()] = False
     assert bool((outs[0][1].view(nslots, -1)[untouched] == 7.0).all())

@@ -97,7 +97,40 @@ struct LinearFuse {
   __nv_bfloat16 *k_cache, *v_cache;
   const int32_t *slot_mapping;
   int64_t num_slots;
+  // optional (decode steps): L2 prefetch of this layer's cached K/V for the attention that
+  // follows. The block tables and lengths come from the step's packer, which finished
+  // before the first decoder kernel started, so they are read before the wait.
+  const int32_t *pf_cu_seqlens_k;  // null: no prefetch
+  const int32_t *pf_block_tables;
+  int pf_bt_stride, pf_batch, pf_block_size;
+  int64_t pf_num_blocks;
 };
+
+constexpr uint32_t kPfChunk = 16 * 1024;
+
+__device__ __forceinline__ void prefetch_l2_bulk(const void *p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// One warp: request sequence b's cached K and V rows (all KV heads, positions < len)
+// into L2, 16 KiB per prefetch, each block's rows being one contiguous range.
+__device__ __forceinline__ void prefetch_sequence_kv(const LinearFuse &f, int b, int lane) {
+  const int len = f.pf_cu_seqlens_k[b + 1] - f.pf_cu_seqlens_k[b];
+  const int bs = f.pf_block_size;
+  const int nblk = min((len + bs - 1) / bs, f.pf_bt_stride);
+  const int64_t row_bytes = static_cast<int64_t>(f.num_kv_heads) * kLnRows * 2;
+  for (int j = 0; j < nblk; ++j) {
+    const int blk = f.pf_block_tables[static_cast<int64_t>(b) * f.pf_bt_stride + j];
+    if (blk < 0 || blk >= f.pf_num_blocks) continue;  // a hint only: skip, never fault
+    const int64_t bytes = static_cast<int64_t>(min(bs, len - j * bs)) * row_bytes;
+    const int64_t off = static_cast<int64_t>(blk) * bs * row_bytes;
+    for (int64_t c = static_cast<int64_t>(lane) * kPfChunk; c < bytes; c += 32 * kPfChunk) {
+      const uint32_t sz = static_cast<uint32_t>(min(static_cast<int64_t>(kPfChunk), bytes - c));
+      prefetch_l2_bulk(reinterpret_cast<const uint8_t *>(f.k_cache) + off + c, sz);
+      prefetch_l2_bulk(reinterpret_cast<const uint8_t *>(f.v_cache) + off + c, sz);
+    }
+  }
+}
 
 __device__ __forceinline__ uint32_t cluster_rank() {
   uint32_t r;
@@ -382,6 +415,8 @@ __global__ void __launch_bounds__(kLnThreads)
 #pragma unroll
     for (int e = 0; e < 4; ++e) qk_nw[e] = bf2f(nw[e]);
   }
+  if (EPI == kEpiQkRope && f.pf_cu_seqlens_k != nullptr && warp == 2)
+    for (int b = blockIdx.x; b < f.pf_batch; b += gridDim.x) prefetch_sequence_kv(f, b, lane);
   if (NORM_IN) {
     uint4 wv[kLnStages][2];
     norm_in_weights(wv, a, f, k0);
@@ -827,8 +862,9 @@ extern "C" int b200asr_linear_small_norm_qk_rope(
     int32_t num_kv_heads, int32_t head_dim, const void *q_norm_weight, const void *k_norm_weight,
     float qk_eps, const int64_t *positions, const float *cos_sin_cache, int32_t max_position,
     void *q_out, int64_t q_out_row_stride, void *k_cache, void *v_cache,
-    const int32_t *slot_mapping, int64_t num_slots, int32_t *error_flag,
-    b200asr_stream_t stream) {
+    const int32_t *slot_mapping, int64_t num_slots, const int32_t *prefetch_cu_seqlens_k,
+    const int32_t *prefetch_block_tables, int32_t prefetch_bt_stride, int32_t prefetch_batch,
+    int32_t block_size, int32_t *error_flag, b200asr_stream_t stream) {
   B200_REQUIRE(m >= 0 && m <= 64, "linear_small_norm_qk_rope: %d rows (at most 64)", m);
   if (m == 0) return B200ASR_OK;
   B200_REQUIRE(head_dim == kLnRows, "linear_small_norm_qk_rope: head_dim %d (needs %d)", head_dim,
@@ -863,6 +899,17 @@ extern "C" int b200asr_linear_small_norm_qk_rope(
   f.v_cache = static_cast<__nv_bfloat16 *>(v_cache);
   f.slot_mapping = slot_mapping;
   f.num_slots = num_slots;
+  if (prefetch_cu_seqlens_k != nullptr) {
+    B200_REQUIRE(prefetch_block_tables && prefetch_bt_stride > 0 && prefetch_batch >= 0 &&
+                     block_size > 0 && num_slots % block_size == 0,
+                 "linear_small_norm_qk_rope: bad KV prefetch geometry");
+    f.pf_cu_seqlens_k = prefetch_cu_seqlens_k;
+    f.pf_block_tables = prefetch_block_tables;
+    f.pf_bt_stride = prefetch_bt_stride;
+    f.pf_batch = prefetch_batch;
+    f.pf_block_size = block_size;
+    f.pf_num_blocks = num_slots / block_size;
+  }
   const LinearArgs a = make_args(m, ks, 0, nullptr, 0, error_flag);
   return dispatch_linear<true, kEpiQkRope>(nullptr, 0, m, k, w, n, a, f, tiles,
                                            static_cast<cudaStream_t>(stream));

@@ -632,12 +632,22 @@ __global__ void __launch_bounds__(Short<G>::THREADS, 2)
     prefetch_tmap(&tm_k);
     prefetch_tmap(&tm_v);
   }
-  pdl_wait();  // q, the new token's K/V and the batch metadata come from earlier kernels
   __syncthreads();
 
   if (warp == kShortWarps) {
     // ------------------------------------------------------------------ producer
+    // With programmatic dependent launch this CTA may start while the kernel before it
+    // (the step's K/V store and q) still runs. The batch metadata and every cached row
+    // but each sequence's newest come from launches that finished before the step's
+    // decoder kernels began (the packer, earlier steps), so the first unit's stages
+    // except its last -- the one holding the newest token -- are requested before the
+    // wait; q and the last stage after it.
     uint32_t it_stage = 0;
+    bool waited = false;
+    auto wait_prev = [&]() {
+      if (!waited) pdl_wait();
+      waited = true;
+    };
     auto acquire = [&](int &st) -> bool {
       st = it_stage % kShortStages;
       const uint32_t ph = (it_stage / kShortStages) & 1;
@@ -646,10 +656,15 @@ __global__ void __launch_bounds__(Short<G>::THREADS, 2)
       return __shfl_sync(0xffffffffu, ok, 0) != 0;
     };
     for (int u = blockIdx.x; u < units; u += gridDim.x) {
+      const bool first_unit = u == static_cast<int>(blockIdx.x);
+      if (!first_unit) wait_prev();
       const int b = u / hkv, h = u - (u / hkv) * hkv;
       const int len = a.cu_seqlens_k[b + 1] - a.cu_seqlens_k[b];
       if (len <= 0) continue;  // zero rows: written by CTA 0's consumers
       const int nst = (len + kShortTok - 1) / kShortTok;
+      // stages [0, early) go out before the wait (a fresh ring: no acquire blocks)
+      const int early = waited ? 0 : min(nst - 1, kShortStages);
+      int q_stage = -1;  // ring slot whose barrier also counts q, when stage 0 went early
       for (int wb = 0; wb < nst; wb += 32) {
         // lane i: cache slot of stage wb + i (block-table reads in flight together)
         const int s = wb + lane;
@@ -675,8 +690,12 @@ __global__ void __launch_bounds__(Short<G>::THREADS, 2)
           const int slot = __shfl_sync(0xffffffffu, d_slot, i);
           const int n = min(kShortTok, len - j * kShortTok);
           const int fl = (j == 0 ? 1 : 0) | (j == nst - 1 ? 2 : 0);
+          if (j >= early) wait_prev();
           int st;
-          if (!acquire(st)) return;
+          if (!acquire(st)) {
+            wait_prev();
+            return;
+          }
           if (lane == 0) {
             info[st] = ShortStage{b, h, n, fl};
             mbar_arrive_expect_tx(&full[st], 2 * C::KV_BYTES + ((fl & 1) ? G * kDecD * 2 : 0));
@@ -684,13 +703,25 @@ __global__ void __launch_bounds__(Short<G>::THREADS, 2)
           __syncwarp();
           uint8_t *stage = stages + st * C::STAGE_BYTES;
           if (lane < 2) tma_load_4d(stage + lane * C::KV_BYTES, lane ? &tm_v : &tm_k, 0, slot, 0, h, &full[st]);
-          if ((fl & 1) && lane == 2)
-            bulk_g2s(stage + 2 * C::KV_BYTES, a.q + b * a.q_stride + h * G * kDecD,
-                     G * kDecD * 2, &full[st]);
+          if (fl & 1) {
+            if (j < early) {
+              q_stage = st;
+            } else if (lane == 2) {
+              bulk_g2s(stage + 2 * C::KV_BYTES, a.q + b * a.q_stride + h * G * kDecD,
+                       G * kDecD * 2, &full[st]);
+            }
+          }
           ++it_stage;
+          if (j == early - 1) {  // the early stages are out: wait, then q
+            wait_prev();
+            if (q_stage >= 0 && lane == 2)
+              bulk_g2s(stages + q_stage * C::STAGE_BYTES + 2 * C::KV_BYTES,
+                       a.q + b * a.q_stride + h * G * kDecD, G * kDecD * 2, &full[q_stage]);
+          }
         }
       }
     }
+    wait_prev();
     int st;  // terminal stage
     if (!acquire(st)) return;
     if (lane == 0) {
@@ -701,6 +732,7 @@ __global__ void __launch_bounds__(Short<G>::THREADS, 2)
   }
 
   // -------------------------------------------------------------------- consumers
+  pdl_wait();  // the output and the zero rows are written after the previous kernel
   const int w = warp;               // token slice [16w, 16w + 16) of every stage
   const int row = lane >> 2;        // MMA row = query head within the group (valid if < G)
   const int quad = lane & 3;

@@ -410,8 +410,12 @@ def linear_small_norm(state: NormState, norm_weight, eps: float, weight, *, silu
 def linear_small_norm_qk_rope(state: NormState, norm_weight, eps: float, weight, positions, *,
                               num_heads: int, num_kv_heads: int, head_dim: int, q_weight,
                               k_weight, qk_eps: float, cos_sin_cache, q_out, k_cache, v_cache,
-                              slot_mapping, error_flag=None) -> torch.Tensor:
-    """qkv_proj of RMSNorm(h), then q/k RMSNorm + RoPE and the K/V cache store per head."""
+                              slot_mapping, prefetch=None, error_flag=None) -> torch.Tensor:
+    """qkv_proj of RMSNorm(h), then q/k RMSNorm + RoPE and the K/V cache store per head.
+
+    ``prefetch = (cu_seqlens_k, block_tables)`` (decode steps) also requests the cached
+    K/V of those sequences into L2 for the attention that follows; both must come from a
+    launch that finished before the step's decoder kernels (the packer)."""
     _cuda(norm_weight, weight, positions, q_weight, k_weight, cos_sin_cache, q_out, k_cache,
           v_cache, slot_mapping)
     _need(positions.dtype == torch.int64 and slot_mapping.dtype == torch.int32,
@@ -420,13 +424,24 @@ def linear_small_norm_qk_rope(state: NormState, norm_weight, eps: float, weight,
     _need(weight.dtype == BF16 and weight.is_contiguous() and weight.shape[1] == state.hidden,
           "qkv weight [n, hidden] bf16")
     num_slots = k_cache.numel() // (num_kv_heads * head_dim)
+    pf_cu = pf_tables = None
+    pf_stride = pf_batch = 0
+    block_size = k_cache.shape[1] if k_cache.dim() == 4 else 0
+    if prefetch is not None:
+        pf_cu, pf_tables = prefetch
+        _cuda(pf_cu, pf_tables)
+        _need(pf_cu.dtype == torch.int32 and pf_tables.dtype == torch.int32
+              and pf_tables.dim() == 2 and pf_tables.stride(1) == 1 and k_cache.dim() == 4,
+              "prefetch: int32 cu_seqlens_k and [B, W] block tables, 4-D cache")
+        pf_stride, pf_batch = pf_tables.stride(0), pf_tables.shape[0]
     _count()
     check(lib.b200asr_linear_small_norm_qk_rope(
         _p(state.h), state.h.stride(0), _p(state.ss), state.tiles, _p(norm_weight), float(eps),
         state.rows, state.hidden, _p(weight), num_heads, num_kv_heads, head_dim, _p(q_weight),
         _p(k_weight), float(qk_eps), _p(positions), _p(cos_sin_cache), cos_sin_cache.shape[0],
         _p(q_out), q_out.stride(0), _p(k_cache), _p(v_cache), _p(slot_mapping), num_slots,
-        _p(error_flag), _stream()), "linear_small_norm_qk_rope")
+        _p(pf_cu), _p(pf_tables), pf_stride, pf_batch, block_size, _p(error_flag), _stream()),
+        "linear_small_norm_qk_rope")
     return q_out
 
 

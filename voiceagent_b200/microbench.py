@@ -361,7 +361,7 @@ class _DecodeRow:
         return self.length
 
 
-def decode_graph_step(fused: bool, iters: int = 64) -> dict:
+def decode_graph_step(fused: bool, iters: int = 64, kv_prefetch: bool = False) -> dict:
     """One whole decode step of Qwen3-ASR-0.6B (random init) as the engine replays it:
     the bucket-32 CUDA graph (28 layers of projections, norms, RoPE + KV store, paged
     attention, lm_head, argmax, descriptor advance) over 32 rows of contexts U[80, 250],
@@ -373,7 +373,7 @@ def decode_graph_step(fused: bool, iters: int = 64) -> dict:
 
     path = write_checkpoint(Path(tempfile.mkdtemp()) / "c06", "0.6b", weights=False)
     eng = AsrEngine(str(path), weights="random", seed=0, max_num_seqs=32, max_model_len=1024,
-                    num_kvcache_blocks=96, fused_decode=fused)
+                    num_kvcache_blocks=96, fused_decode=fused, kv_prefetch=kv_prefetch)
     gr = eng.model_runner.graph_runner
     rng = np.random.default_rng(3)
     lens = rng.integers(80, 251, size=32)
@@ -400,8 +400,10 @@ def decode_graph_step(fused: bool, iters: int = 64) -> dict:
     launches = gr.kernels_per_replay[(32, True)]
     del eng, gr, graph
     torch.cuda.empty_cache()
-    return _line("decode_step_graph", f"0.6B decode step, 32 rows ctx~U[80,250], "
-                 f"{'fused' if fused else 'unfused'} projections", us, weights + kv,
+    what = ("fused projections" + (", KV prefetch" if kv_prefetch else "")) if fused \
+        else "unfused projections"
+    return _line("decode_step_graph", f"0.6B decode step, 32 rows ctx~U[80,250], {what}",
+                 us, weights + kv,
                  bound="hbm (weights + KV, latency-bound)", launches_per_step=launches,
                  timing=f"{iters} replays of the bucket-32 graph back to back")
 
@@ -413,7 +415,8 @@ BENCHES = {
                        label="config3 decode-step shape B=32 ctx~U[80,250], short-context kernel"),
         decode_config1(lo=80, hi=250, sets=16, max_seqlen_k=4096,
                        label="config3 decode-step shape B=32 ctx~U[80,250], stream-K kernel")],
-    "step": lambda: [decode_graph_step(True), decode_graph_step(False)],
+    "step": lambda: [decode_graph_step(True), decode_graph_step(True, kv_prefetch=True),
+                     decode_graph_step(False)],
     "prefill": lambda: [prefill_config2()],
     "window": lambda: [window_config2()],
     "store": lambda: [store_rows(32), store_rows(8192)],

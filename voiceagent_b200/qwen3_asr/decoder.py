@@ -119,6 +119,7 @@ class Qwen3Model(nn.Module):
             [Qwen3DecoderLayer(config, self.rope) for _ in range(config.num_hidden_layers)])
         self.norm = RMSNorm(config.hidden_size, eps=config.rms_norm_eps)
         self.fused_decode = True  # decode-sized batches on the fused projections
+        self.kv_prefetch = False  # fused decode steps: L2 prefetch of each layer's K/V
         self._plain: bool | None = None  # projections without bias, bf16, contiguous
 
     def forward(self, input_ids, positions, inputs_embeds=None) -> torch.Tensor:
@@ -151,6 +152,9 @@ class Qwen3Model(nn.Module):
         ctx = get_attention_context()
         m, hidden = residual.shape
         state = kx.NormState(m, hidden, residual.device)
+        # decode steps: each qkv kernel also pulls its layer's cached K/V into L2
+        prefetch = ((ctx.cu_seqlens_k, ctx.block_tables)
+                    if ctx.decode_only and self.kv_prefetch else None)
         kx.rms_stats(residual, state)  # layer 0's input norm reads the embeddings
         for layer in self.layers:
             attn, mlp = layer.self_attn, layer.mlp
@@ -162,7 +166,7 @@ class Qwen3Model(nn.Module):
                 num_kv_heads=attn.num_kv_heads, head_dim=attn.head_dim,
                 q_weight=attn.q_norm.weight, k_weight=attn.k_norm.weight, qk_eps=attn.eps,
                 cos_sin_cache=attn.rope.table, q_out=q, k_cache=attn.attn.k_cache,
-                v_cache=attn.attn.v_cache, slot_mapping=ctx.slot_mapping,
+                v_cache=attn.attn.v_cache, slot_mapping=ctx.slot_mapping, prefetch=prefetch,
                 error_flag=ctx.error_flag)
             o = attn.attn(q)
             kx.linear_small_add(o.view(m, attn.q_size), attn.o_proj.weight, residual, state,
