@@ -392,10 +392,11 @@ def test_paged_decode_peaked_scores(kx, max_len):
     assert_attn_close(out, ref, f"decode peaked scores max_seqlen_k={max_len}")
 
 
-def test_paged_decode_newest_row_written_just_before_with_pdl(kx):
-    """The short-context kernel requests a sequence's stages before its PDL wait except
-    the last one, which holds the newest token: with PDL on, a store of each sequence's
-    newest K/V row immediately before it (in a graph) must be seen, as without PDL."""
+@pytest.mark.parametrize("max_len", [512, 4096])
+def test_paged_decode_newest_row_written_just_before_with_pdl(kx, max_len):
+    """Both decode kernels request stages before their PDL wait, except those holding a
+    sequence's newest token: with PDL on, a store of each sequence's newest K/V row
+    immediately before the decode (in a graph) must be seen, as without PDL."""
     rng = np.random.default_rng(21)
     lens = [70, 128, 129, 200, 1, 64, 65, 250]
     q, kc, vc, tables, cu_k = _decode_case(rng, lens, nblocks=32)
@@ -416,7 +417,7 @@ def test_paged_decode_newest_row_written_just_before_with_pdl(kx):
 
             def step():
                 kx.store_kvcache(new_k, new_v, k_run, v_run, slots)
-                kx.paged_decode(qd, k_run, v_run, cu, tb, max_seqlen_k=512,
+                kx.paged_decode(qd, k_run, v_run, cu, tb, max_seqlen_k=max_len,
                                 scale=128 ** -0.5, out=out, workspace=ws)
 
             step()

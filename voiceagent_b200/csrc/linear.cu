@@ -8,10 +8,12 @@
 // batch is the MMA's N (32 or 64 columns), so every CTA streams its own weight tile once.
 //
 //  * CTA = (128 weight rows, 1/ks of K). The ks CTAs sharing a tile form a thread-block
-//    cluster; each accumulates its K slice in TMEM, stages the 128 x MP fp32 partial in
-//    shared memory, and after a cluster barrier every CTA sums a share of the batch rows
-//    across the cluster through distributed shared memory (on-chip, no workspace, no
-//    second kernel) and writes bf16.
+//    cluster; each accumulates its K slice in TMEM. CTA r reduces batch columns
+//    [r * MP / ks, (r + 1) * MP / ks): every CTA pushes the columns its peers own from
+//    registers straight into their shared memory (st.async, completion counted in bytes
+//    on the receiver's mbarrier), so a receiver waits only for its own bytes, sums the ks
+//    partials in rank order and writes bf16 -- on chip, no workspace, no second kernel,
+//    and no cluster-wide barrier after the MMAs.
 //  * A 4-deep TMA ring (128-byte swizzle) per CTA: each weight tile arrives as two 64-row
 //    boxes, the activation tile as one box whose rows past M are zero-filled.
 //  * Fused SiLU*mul (layers/activation.py:11-14) for gate_up_proj: a tile's two boxes are
@@ -35,8 +37,9 @@
 //    A decode layer is then qkv (norm + rope + store) -> attention -> o_proj (+residual)
 //    -> gate_up (norm, SiLU*mul) -> down (+residual): five launches instead of eight.
 //
-// No TMA multicast is used. Every CTA arrives at both cluster barriers whatever happens
-// (a timed-out mbarrier wait only skips work), so no CTA waits for one that left.
+// No TMA multicast is used. Every CTA takes part in the one (split) cluster barrier and
+// pushes all its bytes whatever happens (a timed-out wait only skips work and raises the
+// flag), so no CTA waits for one that left.
 #include "common.cuh"
 
 namespace b200asr {
@@ -137,18 +140,25 @@ __device__ __forceinline__ uint32_t cluster_rank() {
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
   return r;
 }
-__device__ __forceinline__ void cluster_barrier() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
-                   : "memory");
+__device__ __forceinline__ void cluster_arrive() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
 }
-__device__ __forceinline__ float4 ld_dsmem_f4(uint32_t local_saddr, uint32_t rank) {
+__device__ __forceinline__ void cluster_wait() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t local_saddr, uint32_t rank) {
   uint32_t remote;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local_saddr), "r"(rank));
-  float4 v;  // ordered after the cluster barrier by the barrier's acquire
-  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
-               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-               : "r"(remote));
-  return v;
+  return remote;
+}
+// 16-byte store into another CTA's shared memory whose completion is counted (in bytes)
+// on that CTA's mbarrier.
+__device__ __forceinline__ void st_async_v4(uint32_t remote_saddr, float4 v, uint32_t remote_bar) {
+  asm volatile(
+      "st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];" ::
+          "r"(remote_saddr),
+      "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w), "r"(remote_bar)
+      : "memory");
 }
 
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int32_t c0,
@@ -357,12 +367,14 @@ __global__ void __launch_bounds__(kLnThreads)
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + kLnStages * C::STAGE + C::RED_BYTES);
   uint64_t *empty = full + kLnStages;
   uint64_t *done = empty + kLnStages;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done + 1);
+  uint64_t *recv_bar = done + 1;  // completes when every peer's columns have arrived
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(recv_bar + 1);
   __shared__ int abort_flag;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   pdl_trigger();
   const int ks = a.k_split;
+  const int cols = MP / ks;  // batch columns this CTA reduces (ks divides MP: powers of two)
   const int kz = static_cast<int>(cluster_rank());
   const int tile = blockIdx.x / ks;
   const int k0 = kz * a.steps * kLnBK;
@@ -382,7 +394,10 @@ __global__ void __launch_bounds__(kLnThreads)
       mbar_init(&empty[s], 1);
     }
     mbar_init(done, 1);
+    mbar_init(recv_bar, 1);
     fence_barrier_init();
+    // bytes the ks - 1 peers push: their 128 rows x this CTA's columns, fp32
+    mbar_arrive_expect_tx(recv_bar, static_cast<uint32_t>((ks - 1) * kLnRows * cols * 4));
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, C::TMEM_COLS);
@@ -392,6 +407,10 @@ __global__ void __launch_bounds__(kLnThreads)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // Peers push partials into this CTA's shared memory later: its receive barrier must be
+  // initialised first. Arrive now, wait just before the first push (split cluster barrier,
+  // so the weight loads and the prologue are not held up by it).
+  if (ks > 1) cluster_arrive();
 
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&tm_w);
@@ -468,49 +487,71 @@ __global__ void __launch_bounds__(kLnThreads)
     pdl_wait();
 #pragma unroll
     for (int i = 0; i < kEpiPre; ++i) {
-      const int c = kz + warp * ks + i * 4 * ks;
-      if (c < a.m) epi_fetch<EPI>(pre[i], f, a, c, tile, lane);
+      const int cl = warp + 4 * i, c = kz * cols + cl;
+      if (cl < cols && c < a.m) epi_fetch<EPI>(pre[i], f, a, c, tile, lane);
     }
   }
+  // Split-K reduction by push: CTA r of the cluster reduces batch columns
+  // [r * cols, (r + 1) * cols). The partial (thread = weight row, one TMEM lane, all MP
+  // columns) is first laid out column-major in this CTA's stage ring, free once the MMAs
+  // are done; then 16-byte pieces (4 rows of one column) go to the CTA owning the
+  // column: st.async into a peer's receive buffer (bytes counted on its barrier), a plain
+  // store into this CTA's own. Receive buffer: red[src][cl][128 rows] fp32.
   const int row = warp * 32 + lane;
   const bool have = __all_sync(0xffffffffu, mbar_wait(done, 0, a.error_flag, &abort_flag));
-  if (have) {
+  const uint32_t red_base = smem_addr(red), bar_base = smem_addr(recv_bar);
+  float *colmaj = reinterpret_cast<float *>(stages);  // [MP][128]
+  {
     tc_fence_after();
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
 #pragma unroll
     for (int cc = 0; cc < MP / 32; ++cc) {
       float v[32];
-      tmem_ld32(lane_base + cc * 32, v);
-      tmem_wait_ld();
+      if (have) {
+        tmem_ld32(lane_base + cc * 32, v);
+        tmem_wait_ld();
+      } else {
 #pragma unroll
-      for (int c = 0; c < 32; ++c) red[(cc * 32 + c) * kLnRows + row] = v[c];
+        for (int c = 0; c < 32; ++c) v[c] = 0.f;  // keeps the byte counts; the flag is raised
+      }
+#pragma unroll
+      for (int c = 0; c < 32; ++c) colmaj[(cc * 32 + c) * kLnRows + row] = v[c];
+    }
+  }
+  __syncthreads();
+  if (ks > 1) cluster_wait();  // every peer's receive barrier is initialised
+#pragma unroll
+  for (int i = 0; i < MP * (kLnRows / 4) / kLnThreads; ++i) {
+    const int id = i * kLnThreads + tid;  // (column, 4-row group): warps write 512 B runs
+    const int col = id / (kLnRows / 4), q = id % (kLnRows / 4);
+    const int r = col / cols, cl = col - r * cols;
+    const float4 v = *reinterpret_cast<const float4 *>(&colmaj[col * kLnRows + q * 4]);
+    const uint32_t off = static_cast<uint32_t>(((kz * cols + cl) * kLnRows + q * 4) * 4);
+    if (r == kz) {
+      *reinterpret_cast<float4 *>(&red[(kz * cols + cl) * kLnRows + q * 4]) = v;
+    } else {
+      st_async_v4(mapa_shared(red_base + off, static_cast<uint32_t>(r)), v,
+                  mapa_shared(bar_base, static_cast<uint32_t>(r)));
     }
   }
   tc_fence_before();
-  cluster_barrier();  // every partial of the cluster is in shared memory
+  __syncthreads();  // this CTA's own columns are in its buffer
+  const bool got = mbar_wait(recv_bar, 0, a.error_flag, &abort_flag);  // the peers' columns
 
   pdl_wait();  // (returns at once: the producer's wait has passed) orders the writes below
-  // This CTA reduces batch rows kz, kz + ks, ...; warp w takes every 4th of them and each
-  // lane 4 consecutive tile rows (128 rows = 32 lanes x 4).
-  const uint32_t red_base = smem_addr(red);
-  for (int c = kz + warp * ks, i = 0; c < a.m; c += 4 * ks, ++i) {
-    // all ks loads in flight before the first add (one DSMEM round trip, not ks)
-    const uint32_t at = red_base + (c * kLnRows + lane * 4) * 4;
-    float4 part[kLnMaxSplit];
-#pragma unroll
-    for (int j = 0; j < kLnMaxSplit; ++j)
-      if (j < ks) part[j] = ld_dsmem_f4(at, static_cast<uint32_t>(j));
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-    for (int j = 0; j < kLnMaxSplit; ++j) {
-      if (j < ks) {
-        acc.x += part[j].x;
-        acc.y += part[j].y;
-        acc.z += part[j].z;
-        acc.w += part[j].w;
-      }
+  // Warp w takes local columns w, w + 4, ...; each lane 4 consecutive tile rows.
+  for (int cl = warp, i = 0; cl < cols; cl += 4, ++i) {
+    const int c = kz * cols + cl;
+    if (c >= a.m) break;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);  // sources in rank order
+    for (int j = 0; j < ks; ++j) {
+      const float4 p = *reinterpret_cast<const float4 *>(&red[(j * cols + cl) * kLnRows + lane * 4]);
+      acc.x += p.x;
+      acc.y += p.y;
+      acc.z += p.z;
+      acc.w += p.w;
     }
-    if (!have) continue;
+    if (!have || !got) continue;
     if (EPI == kEpiSilu) {  // lanes 0-15: gate rows 0-63; lanes 16-31: the matching up rows
       const float ux = __shfl_down_sync(0xffffffffu, acc.x, 16);
       const float uy = __shfl_down_sync(0xffffffffu, acc.y, 16);
@@ -556,7 +597,8 @@ __global__ void __launch_bounds__(kLnThreads)
       *reinterpret_cast<uint2 *>(dst) = make_uint2(pack2(acc.x, acc.y), pack2(acc.z, acc.w));
     }
   }
-  cluster_barrier();  // peers finished reading this CTA's shared memory
+  // No closing cluster barrier: nothing reads another CTA's memory, and a CTA leaves only
+  // after every byte addressed to it has arrived.
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();

@@ -76,6 +76,7 @@ struct DecodeArgs {
   float *ws_o;    // [parts_cap][H][128]
   int parts_cap;
   int32_t *error_flag;
+  int early;  // launched with programmatic dependent launch: request stages before the wait
 };
 
 // What the producer tells the consumers about a stage (written before the stage's
@@ -264,7 +265,10 @@ __global__ void __launch_bounds__(Dec<HKV, G>::THREADS, 1)
     prefetch_tmap(&tm_k);
     prefetch_tmap(&tm_v);
   }
-  pdl_wait();  // q, the new token's K/V and the batch metadata come from earlier kernels
+  // The lengths, block tables and every cached row but each sequence's newest come from
+  // launches that finished before the step's decoder kernels (the packer, earlier
+  // steps): with programmatic dependent launch they are read, and the first ring of
+  // stages requested, before the wait on the kernel that wrote q and the newest K/V.
   for (int i = tid; i <= B; i += blockDim.x) s_cuk[i] = a.cu_seqlens_k[i];
   __syncthreads();
 
@@ -298,6 +302,21 @@ __global__ void __launch_bounds__(Dec<HKV, G>::THREADS, 1)
       if (lane == 0) ok = mbar_wait(&empty[st], ph ^ 1, a.error_flag, &abort_flag);
       return __shfl_sync(0xffffffffu, ok, 0) != 0;
     };
+    // Before the wait: stages up to the first one holding a sequence's newest token, at
+    // most one ring (no acquire blocks). Their q copies are issued after the wait, on the
+    // same stage barriers (which already count q's bytes).
+    bool waited = a.early == 0;  // without PDL the wait returns at once: no early phase
+    int n_early = 0, n_dq = 0;
+    int dq_st[kDecStages], dq_b[kDecStages];
+    auto wait_prev = [&]() {
+      if (waited) return;
+      pdl_wait();
+      waited = true;
+      if (lane == 2)
+        for (int i = 0; i < n_dq; ++i)
+          bulk_g2s(stages + dq_st[i] * C::STAGE_BYTES + 2 * C::KV_BYTES,
+                   a.q + dq_b[i] * a.q_stride, C::TX_Q, &full[dq_st[i]]);
+    };
     const int S = carry;
     const int geff = S < 1 ? 1 : (S < static_cast<int>(gridDim.x) ? S : static_cast<int>(gridDim.x));
     if (S > 0 && static_cast<int>(blockIdx.x) < geff) {
@@ -307,12 +326,13 @@ __global__ void __launch_bounds__(Dec<HKV, G>::THREADS, 1)
         // Lane i describes stage wb + i: sequence, token count, flags and cache slot
         // (the block-table reads of 32 stages are in flight together).
         const int j = wb + lane;
-        int d_b = 0, d_n = 0, d_fl = 0, d_slot = 0;
+        int d_b = 0, d_n = 0, d_fl = 0, d_slot = 0, d_end = 0;
         if (j < j1) {
           const int b = upper_index(s_sp, B + 1, j);  // s_sp[b] <= j < s_sp[b + 1]
           const int len = s_cuk[b + 1] - s_cuk[b];
           const int t0 = (j - s_sp[b]) * kDecStage;
           d_n = min(kDecStage, len - t0);
+          d_end = t0 + d_n == len;  // holds the sequence's newest token
           const bool first = t0 == 0 || j == j0, last = t0 + d_n == len || j == j1 - 1;
           const bool whole = s_sp[b] >= j0 && s_sp[b + 1] <= j1;
           const int col = t0 / a.block_size;
@@ -336,8 +356,12 @@ __global__ void __launch_bounds__(Dec<HKV, G>::THREADS, 1)
           const int n = __shfl_sync(0xffffffffu, d_n, i);
           const int fl = __shfl_sync(0xffffffffu, d_fl, i);
           const int slot = __shfl_sync(0xffffffffu, d_slot, i);
+          if (__shfl_sync(0xffffffffu, d_end, i) || n_early == kDecStages) wait_prev();
           int st;
-          if (!acquire(st)) return;
+          if (!acquire(st)) {
+            wait_prev();
+            return;
+          }
           if (lane == 0) {
             info[st] = StageInfo{b, n, fl};
             mbar_arrive_expect_tx(&full[st], C::TX_KV + ((fl & 1) ? C::TX_Q : 0));
@@ -346,12 +370,21 @@ __global__ void __launch_bounds__(Dec<HKV, G>::THREADS, 1)
           uint8_t *stage = stages + st * C::STAGE_BYTES;
           // One box per operand: 16 tokens x every KV head x both 64-dim halves (32 KiB).
           if (lane < 2) tma_load_4d(stage + lane * C::KV_BYTES, lane ? &tm_v : &tm_k, 0, slot, 0, 0, &full[st]);
-          if ((fl & 1) && lane == 2)
-            bulk_g2s(stage + 2 * C::KV_BYTES, a.q + b * a.q_stride, C::TX_Q, &full[st]);
+          if (fl & 1) {
+            if (!waited) {
+              dq_st[n_dq] = st;
+              dq_b[n_dq] = b;
+              ++n_dq;
+            } else if (lane == 2) {
+              bulk_g2s(stage + 2 * C::KV_BYTES, a.q + b * a.q_stride, C::TX_Q, &full[st]);
+            }
+          }
+          if (!waited) ++n_early;
           ++it_stage;
         }
       }
     }
+    wait_prev();
     int st;  // terminal stage: tells the consumers to stop
     if (!acquire(st)) return;
     if (lane == 0) {
@@ -362,6 +395,7 @@ __global__ void __launch_bounds__(Dec<HKV, G>::THREADS, 1)
   }
 
   // -------------------------------------------------------------------- consumers
+  pdl_wait();  // partials, counters and outputs are written after the previous kernel
   asm volatile("bar.sync 2, %0;" ::"r"(C::THREADS) : "memory");  // stage prefix ready
   const int S = s_sp[B];
   const int geff = S < 1 ? 1 : (S < static_cast<int>(gridDim.x) ? S : static_cast<int>(gridDim.x));
@@ -643,7 +677,7 @@ __global__ void __launch_bounds__(Short<G>::THREADS, 2)
     // except its last -- the one holding the newest token -- are requested before the
     // wait; q and the last stage after it.
     uint32_t it_stage = 0;
-    bool waited = false;
+    bool waited = a.early == 0;  // without PDL the wait returns at once: no early phase
     auto wait_prev = [&]() {
       if (!waited) pdl_wait();
       waited = true;
@@ -1009,6 +1043,7 @@ extern "C" int b200asr_paged_decode(const void *q, int64_t q_row_stride, const v
   a.ws_ml = reinterpret_cast<float *>(static_cast<uint8_t *>(workspace) + kDecHeaderBytes);
   a.ws_o = a.ws_ml + static_cast<size_t>(a.parts_cap) * num_heads * 2;
   a.error_flag = error_flag;
+  a.early = pdl_enabled() ? 1 : 0;
   const int64_t slots = static_cast<int64_t>(num_blocks) * block_size;
   // Contexts of at most kShortMaxCtx tokens: one CTA per (sequence, KV head).
   if (max_seqlen_k <= kShortMaxCtx && block_size % kShortTok == 0 &&

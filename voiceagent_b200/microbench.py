@@ -83,7 +83,7 @@ def _sets(per_set_bytes: int) -> int:
 
 def decode_config1(iters: int = 64, sets: int = 4, lo: int = 64, hi: int = 1024,
                    label: str = "config1 B=32 ctx~U[64,1024] Hq16/Hkv8 d128",
-                   max_seqlen_k: int = 4096) -> dict:
+                   max_seqlen_k: int = 4096, pdl: bool = False) -> dict:
     """Paged decode, config 1: B = 32, ctx ~ U[lo, hi] (64-1024), 4096-block pool (2 GiB per
     K/V), block tables = slices of a random permutation; ``sets`` disjoint table sets rotate."""
     dev = torch.device("cuda")
@@ -114,14 +114,21 @@ def decode_config1(iters: int = 64, sets: int = 4, lo: int = 64, hi: int = 1024,
         return lambda: kx.paged_decode(q, kc, vc, cu, tables[i % sets], max_seqlen_k=max_seqlen_k,
                                        scale=d ** -0.5, out=out, workspace=ws)
 
-    us = graph_time_us([op(i) for i in range(iters)])
+    was = kx.pdl_enabled()
+    kx.set_pdl(pdl)  # PDL: each launch's metadata reads and first ring overlap the last
+    try:
+        us = graph_time_us([op(i) for i in range(iters)])
+    finally:
+        kx.set_pdl(was)
     sumctx = int(lens.sum())
     algo = sumctx * hkv * d * 2 * 2 + 2 * b * h * d * 2 + 4 * need + 4 * b
     del kc, vc
     torch.cuda.empty_cache()
-    return _line("paged_decode", label, us, algo,
+    return _line("paged_decode", label + (", PDL chain" if pdl else ""), us, algo,
                  sum_ctx=sumctx, timing=f"graph of {iters} launches over {sets} rotating KV sets "
-                                           f"of {algo / 1e6:.0f} MB each (together > L2)")
+                                           f"of {algo / 1e6:.0f} MB each (together > L2)"
+                                           + (", programmatic dependent launch between them"
+                                              if pdl else ""))
 
 
 # ------------------------------------------------------------------ config 2
@@ -409,7 +416,7 @@ def decode_graph_step(fused: bool, iters: int = 64, kv_prefetch: bool = False) -
 
 
 BENCHES = {
-    "decode": lambda: [decode_config1()],
+    "decode": lambda: [decode_config1(), decode_config1(pdl=True)],
     "decode_step": lambda: [
         decode_config1(lo=80, hi=250, sets=16, max_seqlen_k=512,
                        label="config3 decode-step shape B=32 ctx~U[80,250], short-context kernel"),
