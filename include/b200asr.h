@@ -63,8 +63,8 @@ B200ASR_API const char *b200asr_last_error(void);
  * overlap. Process-wide; set it before capturing graphs.
  * Two reads happen before that wait, on data a decode step fixes before its decoder
  * kernels run: paged_decode with max_seqlen_k <= 512 reads cu_seqlens_k, block_tables
- * and the cached K/V rows of every position but each sequence's newest, and
- * linear_small_norm_qk_rope's optional KV prefetch reads cu_seqlens_k / block_tables.
+ * and the cached K/V rows of every position but each sequence's newest, and a
+ * b200asr_l2_prefetch's K/V part reads cu_seqlens_k / block_tables.
  * With PDL on, those must have been written before the nearest preceding launch in the
  * stream that is not itself a PDL launch (the engine's embedding kernel follows the
  * step's packer); the newest row may be written by the kernel right before.          */
@@ -294,33 +294,46 @@ B200ASR_API int b200asr_linear_small(const void *x, int64_t x_row_stride, int32_
  *   models/qwen3.py:43-48, + the KV store of PagedAttention.forward, attention.py:90):
  *   the projection of RMSNorm(h), then per head exactly what b200asr_qk_norm_rope_store
  *   does (q heads to q_out, K and V into the cache at slot_mapping; slot -1 skipped);
- *   head_dim 128. Optional (prefetch_cu_seqlens_k non-NULL, decode steps): the cached
- *   K/V rows of the prefetch_batch sequences described by prefetch_cu_seqlens_k /
- *   prefetch_block_tables (row stride prefetch_bt_stride, block_size tokens per block)
- *   are requested into L2 for the attention that follows; they are read before the
- *   wait on the previous kernel, so they must have been written by an earlier
- *   non-overlapping launch (the step's packer). Out-of-pool block ids are skipped.
+ *   head_dim 128.
+ * The three projections take an optional b200asr_l2_prefetch (NULL: none).
  * rms_stats: h and ss of x (+ residual, updated in place to bf16(x + residual)) -- the
  *   layer-0 input norm, whose input is the embedding.
  * norm_apply: out = RMSNorm of (h, ss) -- the model's final norm before lm_head.     */
+/* Optional L2 prefetch issued by a fused projection before it waits on the previous
+ * kernel (no reference counterpart; pure performance hint, results are unchanged):
+ * the cached K/V rows (positions < length) of `batch` sequences of one layer, described
+ * like b200asr_paged_decode's inputs (cu_seqlens_k NULL: none), and up to two
+ * contiguous ranges (16-byte aligned, multiples of 16 bytes; NULL: none), e.g. the
+ * next layer's weights. Out-of-pool block ids are skipped. The lengths and tables are
+ * read before the wait: with PDL on they follow the contract of b200asr_set_pdl.     */
+typedef struct {
+  const int32_t *cu_seqlens_k;
+  const int32_t *block_tables;
+  int32_t bt_stride, batch, block_size, num_kv_heads, head_dim;
+  const void *k_cache, *v_cache;
+  int64_t num_slots;
+  const void *range[2];
+  int64_t range_bytes[2];
+} b200asr_l2_prefetch;
+
 B200ASR_API int b200asr_linear_small_add(const void *x, int64_t x_row_stride, int32_t m, int32_t k,
                              const void *w, int32_t n, void *residual,
                              int64_t residual_row_stride, float *h_out, int64_t h_row_stride,
-                             float *ss_out, int32_t *error_flag, b200asr_stream_t stream);
+                             float *ss_out, const b200asr_l2_prefetch *prefetch,
+                             int32_t *error_flag, b200asr_stream_t stream);
 B200ASR_API int b200asr_linear_small_norm(const float *h, int64_t h_row_stride, const float *ss,
                               int32_t ss_tiles, const void *norm_weight, float eps, int32_t m,
                               int32_t k, const void *w, int32_t n, int32_t silu_inner, void *y,
-                              int64_t y_row_stride, int32_t *error_flag,
-                              b200asr_stream_t stream);
+                              int64_t y_row_stride, const b200asr_l2_prefetch *prefetch,
+                              int32_t *error_flag, b200asr_stream_t stream);
 B200ASR_API int b200asr_linear_small_norm_qk_rope(
     const float *h, int64_t h_row_stride, const float *ss, int32_t ss_tiles,
     const void *norm_weight, float eps, int32_t m, int32_t k, const void *w, int32_t num_heads,
     int32_t num_kv_heads, int32_t head_dim, const void *q_norm_weight, const void *k_norm_weight,
     float qk_eps, const int64_t *positions, const float *cos_sin_cache, int32_t max_position,
     void *q_out, int64_t q_out_row_stride, void *k_cache, void *v_cache,
-    const int32_t *slot_mapping, int64_t num_slots, const int32_t *prefetch_cu_seqlens_k,
-    const int32_t *prefetch_block_tables, int32_t prefetch_bt_stride, int32_t prefetch_batch,
-    int32_t block_size, int32_t *error_flag, b200asr_stream_t stream);
+    const int32_t *slot_mapping, int64_t num_slots, const b200asr_l2_prefetch *prefetch,
+    int32_t *error_flag, b200asr_stream_t stream);
 B200ASR_API int b200asr_rms_stats(const void *x, void *residual, int32_t rows, int32_t hidden,
                       float *h_out, float *ss_out, b200asr_stream_t stream);
 B200ASR_API int b200asr_norm_apply(const float *h, const float *ss, const void *weight, float eps,

@@ -712,6 +712,10 @@ def test_linear_small_norm_matches_unfused(kx, m, silu):
     w = (torch.randn(n, hidden, device="cuda", generator=g) * hidden ** -0.5).bfloat16()
     state = kx.rms_stats(y, kx.NormState(m, hidden, "cuda"), residual=res.clone())
     fused = kx.linear_small_norm(state, nw, 1e-6, w, silu=silu)
+    # an L2 prefetch hint of two ranges changes nothing
+    hinted = kx.linear_small_norm(state, nw, 1e-6, w, silu=silu,
+                                  prefetch=kx.l2_prefetch(ranges=(w, nw)))
+    assert torch.equal(fused, hinted)
     normed = kx.rmsnorm(y, nw, 1e-6, residual=res.clone())
     # the normalised activation itself, as the prologue builds it
     ok, same = _within_one_ulp(kx.norm_apply(state, nw, 1e-6), normed, 0.995)
@@ -743,11 +747,13 @@ def test_linear_small_norm_qk_rope_matches_unfused(kx, m):
 
     table = rope_table(d, 4096, 1e6, "cuda")
     state = kx.rms_stats(y, kx.NormState(m, hidden, "cuda"))
-    # KV prefetch hint over ragged sequences, one with an out-of-pool block (skipped)
+    # an L2 prefetch hint (K/V over ragged sequences, one with an out-of-pool block that is
+    # skipped, and two ranges) changes nothing
     pf_lens = torch.tensor([0, 300, 1, 700, 255], dtype=torch.int32, device="cuda")
     pf_cu = torch.cat([torch.zeros(1, dtype=torch.int32, device="cuda"), pf_lens.cumsum(0).int()])
     pf_tables = torch.tensor([[0, 0, 0], [1, 2, 0], [3, 0, 0], [0, 1, 99], [2, 0, 0]],
                              dtype=torch.int32, device="cuda")
+    pf_k = torch.zeros(4, 256, hkv, d, device="cuda", dtype=torch.bfloat16)
     outs = []
     for fused in (True, "prefetch", False):
         kc = torch.full((4, 256, hkv, d), 7.0, device="cuda").bfloat16()
@@ -758,7 +764,9 @@ def test_linear_small_norm_qk_rope_matches_unfused(kx, m):
                                          num_kv_heads=hkv, head_dim=d, q_weight=qw, k_weight=kw,
                                          qk_eps=1e-6, cos_sin_cache=table, q_out=q, k_cache=kc,
                                          v_cache=vc, slot_mapping=slots,
-                                         prefetch=(pf_cu, pf_tables) if fused == "prefetch" else None)
+                                         prefetch=kx.l2_prefetch(
+                                             kv=(pf_cu, pf_tables, pf_k, pf_k), ranges=(w, table))
+                                         if fused == "prefetch" else None)
         else:
             qkv = kx.linear_small_norm(state, nw, 1e-6, w)
             kx.qk_norm_rope_store(qkv, positions, num_heads=hq, num_kv_heads=hkv, head_dim=d,

@@ -45,14 +45,13 @@ SIGNATURES: dict[str, tuple] = {
     "b200asr_linear_small": (c_int32, [P, c_int64, c_int32, c_int32, P, c_int32, c_int32, P,
                                        c_int64, P, P]),
     "b200asr_linear_small_add": (c_int32, [P, c_int64, c_int32, c_int32, P, c_int32, P, c_int64,
-                                           P, c_int64, P, P, P]),
+                                           P, c_int64, P, P, P, P]),
     "b200asr_linear_small_norm": (c_int32, [P, c_int64, P, c_int32, P, c_float, c_int32, c_int32,
-                                            P, c_int32, c_int32, P, c_int64, P, P]),
+                                            P, c_int32, c_int32, P, c_int64, P, P, P]),
     "b200asr_linear_small_norm_qk_rope": (c_int32, [P, c_int64, P, c_int32, P, c_float, c_int32,
                                                     c_int32, P, c_int32, c_int32, c_int32, P, P,
                                                     c_float, P, P, c_int32, P, c_int64, P, P, P,
-                                                    c_int64, P, P, c_int32, c_int32, c_int32, P,
-                                                    P]),
+                                                    c_int64, P, P, P]),
     "b200asr_rms_stats": (c_int32, [P, P, c_int32, c_int32, P, P, P]),
     "b200asr_norm_apply": (c_int32, [P, P, P, c_float, c_int32, c_int32, P, P]),
     "b200asr_log_mel_workspace_size": (c_size_t, [c_int32, c_int32]),
@@ -73,6 +72,15 @@ SIGNATURES: dict[str, tuple] = {
                                            c_int64, P, P]),
     "b200asr_greedy_argmax": (c_int32, [P, c_int64, c_int32, c_int32, P, P]),
 }
+
+
+class L2Prefetch(ctypes.Structure):
+    """``b200asr_l2_prefetch`` (include/b200asr.h), passed by pointer."""
+
+    _fields_ = [("cu_seqlens_k", c_void_p), ("block_tables", c_void_p), ("bt_stride", c_int32),
+                ("batch", c_int32), ("block_size", c_int32), ("num_kv_heads", c_int32),
+                ("head_dim", c_int32), ("k_cache", c_void_p), ("v_cache", c_void_p),
+                ("num_slots", c_int64), ("range", c_void_p * 2), ("range_bytes", c_int64 * 2)]
 
 
 class B200AsrError(RuntimeError):

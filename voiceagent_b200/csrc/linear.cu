@@ -100,13 +100,15 @@ struct LinearFuse {
   __nv_bfloat16 *k_cache, *v_cache;
   const int32_t *slot_mapping;
   int64_t num_slots;
-  // optional (decode steps): L2 prefetch of this layer's cached K/V for the attention that
-  // follows. The block tables and lengths come from the step's packer, which finished
-  // before the first decoder kernel started, so they are read before the wait.
-  const int32_t *pf_cu_seqlens_k;  // null: no prefetch
+  // optional L2 prefetch, issued before the wait (b200asr_l2_prefetch): a layer's cached
+  // K/V rows of the listed sequences, and up to two contiguous byte ranges
+  const int32_t *pf_cu_seqlens_k;  // null: no K/V prefetch
   const int32_t *pf_block_tables;
-  int pf_bt_stride, pf_batch, pf_block_size;
+  int pf_bt_stride, pf_batch, pf_block_size, pf_row_bytes;
   int64_t pf_num_blocks;
+  const uint8_t *pf_k_cache, *pf_v_cache;
+  const uint8_t *pf_range[2];
+  int64_t pf_range_bytes[2];
 };
 
 constexpr uint32_t kPfChunk = 16 * 1024;
@@ -121,7 +123,7 @@ __device__ __forceinline__ void prefetch_sequence_kv(const LinearFuse &f, int b,
   const int len = f.pf_cu_seqlens_k[b + 1] - f.pf_cu_seqlens_k[b];
   const int bs = f.pf_block_size;
   const int nblk = min((len + bs - 1) / bs, f.pf_bt_stride);
-  const int64_t row_bytes = static_cast<int64_t>(f.num_kv_heads) * kLnRows * 2;
+  const int64_t row_bytes = f.pf_row_bytes;
   for (int j = 0; j < nblk; ++j) {
     const int blk = f.pf_block_tables[static_cast<int64_t>(b) * f.pf_bt_stride + j];
     if (blk < 0 || blk >= f.pf_num_blocks) continue;  // a hint only: skip, never fault
@@ -129,10 +131,19 @@ __device__ __forceinline__ void prefetch_sequence_kv(const LinearFuse &f, int b,
     const int64_t off = static_cast<int64_t>(blk) * bs * row_bytes;
     for (int64_t c = static_cast<int64_t>(lane) * kPfChunk; c < bytes; c += 32 * kPfChunk) {
       const uint32_t sz = static_cast<uint32_t>(min(static_cast<int64_t>(kPfChunk), bytes - c));
-      prefetch_l2_bulk(reinterpret_cast<const uint8_t *>(f.k_cache) + off + c, sz);
-      prefetch_l2_bulk(reinterpret_cast<const uint8_t *>(f.v_cache) + off + c, sz);
+      prefetch_l2_bulk(f.pf_k_cache + off + c, sz);
+      prefetch_l2_bulk(f.pf_v_cache + off + c, sz);
     }
   }
+}
+
+// One warp of each CTA: this CTA's share of a contiguous range (16-byte multiples).
+__device__ __forceinline__ void prefetch_range_share(const uint8_t *base, int64_t bytes, int lane) {
+  const int64_t per = ((bytes + gridDim.x - 1) / gridDim.x + 15) / 16 * 16;
+  const int64_t start = static_cast<int64_t>(blockIdx.x) * per;
+  const int64_t end = min(bytes, start + per);
+  for (int64_t c = start + static_cast<int64_t>(lane) * kPfChunk; c < end; c += 32 * kPfChunk)
+    prefetch_l2_bulk(base + c, static_cast<uint32_t>(min(static_cast<int64_t>(kPfChunk), end - c)));
 }
 
 __device__ __forceinline__ uint32_t cluster_rank() {
@@ -434,8 +445,12 @@ __global__ void __launch_bounds__(kLnThreads)
 #pragma unroll
     for (int e = 0; e < 4; ++e) qk_nw[e] = bf2f(nw[e]);
   }
-  if (EPI == kEpiQkRope && f.pf_cu_seqlens_k != nullptr && warp == 2)
+  // L2 prefetch hints (data of later kernels; read-only, fixed before this step began)
+  if (f.pf_cu_seqlens_k != nullptr && warp == 2)
     for (int b = blockIdx.x; b < f.pf_batch; b += gridDim.x) prefetch_sequence_kv(f, b, lane);
+  if (warp == 3)
+    for (int i = 0; i < 2; ++i)
+      if (f.pf_range[i] != nullptr) prefetch_range_share(f.pf_range[i], f.pf_range_bytes[i], lane);
   if (NORM_IN) {
     uint4 wv[kLnStages][2];
     norm_in_weights(wv, a, f, k0);
@@ -818,6 +833,36 @@ int norm_in_args(const float *h, int64_t h_stride, const float *ss, int32_t ss_t
   return B200ASR_OK;
 }
 
+// Validates a b200asr_l2_prefetch and fills the prefetch part of f (NULL: none).
+int prefetch_args(const b200asr_l2_prefetch *p, LinearFuse *f) {
+  if (p == nullptr) return B200ASR_OK;
+  if (p->cu_seqlens_k != nullptr) {
+    B200_REQUIRE(p->block_tables && p->bt_stride > 0 && p->batch >= 0 && p->block_size > 0 &&
+                     p->num_kv_heads > 0 && p->head_dim > 0 && p->k_cache && p->v_cache &&
+                     p->num_slots > 0 && p->num_slots % p->block_size == 0 &&
+                     aligned16(p->k_cache) && aligned16(p->v_cache) &&
+                     (p->num_kv_heads * p->head_dim * 2) % 16 == 0,
+                 "l2_prefetch: bad K/V geometry");
+    f->pf_cu_seqlens_k = p->cu_seqlens_k;
+    f->pf_block_tables = p->block_tables;
+    f->pf_bt_stride = p->bt_stride;
+    f->pf_batch = p->batch;
+    f->pf_block_size = p->block_size;
+    f->pf_row_bytes = p->num_kv_heads * p->head_dim * 2;
+    f->pf_num_blocks = p->num_slots / p->block_size;
+    f->pf_k_cache = static_cast<const uint8_t *>(p->k_cache);
+    f->pf_v_cache = static_cast<const uint8_t *>(p->v_cache);
+  }
+  for (int i = 0; i < 2; ++i) {
+    if (p->range[i] == nullptr) continue;
+    B200_REQUIRE(aligned16(p->range[i]) && p->range_bytes[i] > 0 && p->range_bytes[i] % 16 == 0,
+                 "l2_prefetch: range %d must be 16-byte aligned and a multiple of 16 bytes", i);
+    f->pf_range[i] = static_cast<const uint8_t *>(p->range[i]);
+    f->pf_range_bytes[i] = p->range_bytes[i];
+  }
+  return B200ASR_OK;
+}
+
 }  // namespace
 
 extern "C" int b200asr_linear_small(const void *x, int64_t x_row_stride, int32_t m, int32_t k,
@@ -849,6 +894,7 @@ extern "C" int b200asr_linear_small_add(const void *x, int64_t x_row_stride, int
                                         const void *w, int32_t n, void *residual,
                                         int64_t residual_row_stride, float *h_out,
                                         int64_t h_row_stride, float *ss_out,
+                                        const b200asr_l2_prefetch *prefetch,
                                         int32_t *error_flag, b200asr_stream_t stream) {
   B200_REQUIRE(m >= 0 && m <= 64, "linear_small_add: %d rows (at most 64)", m);
   if (m == 0) return B200ASR_OK;
@@ -868,6 +914,8 @@ extern "C" int b200asr_linear_small_add(const void *x, int64_t x_row_stride, int
   f.h_out = h_out;
   f.h_out_stride = h_row_stride;
   f.ss_out = ss_out;
+  const int prc = prefetch_args(prefetch, &f);
+  if (prc != B200ASR_OK) return prc;
   return dispatch_linear<false, kEpiAdd>(x, x_row_stride, m, k, w, n, a, f, tiles,
                                          static_cast<cudaStream_t>(stream));
 }
@@ -876,6 +924,7 @@ extern "C" int b200asr_linear_small_norm(const float *h, int64_t h_row_stride, c
                                          int32_t ss_tiles, const void *norm_weight, float eps,
                                          int32_t m, int32_t k, const void *w, int32_t n,
                                          int32_t silu_inner, void *y, int64_t y_row_stride,
+                                         const b200asr_l2_prefetch *prefetch,
                                          int32_t *error_flag, b200asr_stream_t stream) {
   B200_REQUIRE(m >= 0 && m <= 64, "linear_small_norm: %d rows (at most 64)", m);
   if (m == 0) return B200ASR_OK;
@@ -885,6 +934,8 @@ extern "C" int b200asr_linear_small_norm(const float *h, int64_t h_row_stride, c
   LinearFuse f = {};
   const int rc = norm_in_args(h, h_row_stride, ss, ss_tiles, norm_weight, eps, m, k, &f);
   if (rc != B200ASR_OK) return rc;
+  const int prc = prefetch_args(prefetch, &f);
+  if (prc != B200ASR_OK) return prc;
   int tiles = 0;
   B200_REQUIRE(valid_weight_rows(n, silu_inner, &tiles),
                "linear_small_norm: N %d / SiLU inner %d unsupported", n, silu_inner);
@@ -904,9 +955,8 @@ extern "C" int b200asr_linear_small_norm_qk_rope(
     int32_t num_kv_heads, int32_t head_dim, const void *q_norm_weight, const void *k_norm_weight,
     float qk_eps, const int64_t *positions, const float *cos_sin_cache, int32_t max_position,
     void *q_out, int64_t q_out_row_stride, void *k_cache, void *v_cache,
-    const int32_t *slot_mapping, int64_t num_slots, const int32_t *prefetch_cu_seqlens_k,
-    const int32_t *prefetch_block_tables, int32_t prefetch_bt_stride, int32_t prefetch_batch,
-    int32_t block_size, int32_t *error_flag, b200asr_stream_t stream) {
+    const int32_t *slot_mapping, int64_t num_slots, const b200asr_l2_prefetch *prefetch,
+    int32_t *error_flag, b200asr_stream_t stream) {
   B200_REQUIRE(m >= 0 && m <= 64, "linear_small_norm_qk_rope: %d rows (at most 64)", m);
   if (m == 0) return B200ASR_OK;
   B200_REQUIRE(head_dim == kLnRows, "linear_small_norm_qk_rope: head_dim %d (needs %d)", head_dim,
@@ -941,17 +991,8 @@ extern "C" int b200asr_linear_small_norm_qk_rope(
   f.v_cache = static_cast<__nv_bfloat16 *>(v_cache);
   f.slot_mapping = slot_mapping;
   f.num_slots = num_slots;
-  if (prefetch_cu_seqlens_k != nullptr) {
-    B200_REQUIRE(prefetch_block_tables && prefetch_bt_stride > 0 && prefetch_batch >= 0 &&
-                     block_size > 0 && num_slots % block_size == 0,
-                 "linear_small_norm_qk_rope: bad KV prefetch geometry");
-    f.pf_cu_seqlens_k = prefetch_cu_seqlens_k;
-    f.pf_block_tables = prefetch_block_tables;
-    f.pf_bt_stride = prefetch_bt_stride;
-    f.pf_batch = prefetch_batch;
-    f.pf_block_size = block_size;
-    f.pf_num_blocks = num_slots / block_size;
-  }
+  const int prc = prefetch_args(prefetch, &f);
+  if (prc != B200ASR_OK) return prc;
   const LinearArgs a = make_args(m, ks, 0, nullptr, 0, error_flag);
   return dispatch_linear<true, kEpiQkRope>(nullptr, 0, m, k, w, n, a, f, tiles,
                                            static_cast<cudaStream_t>(stream));

@@ -81,7 +81,7 @@ class AsrEngine:
                                             or (151643, 151645))
         self.model = self._build_model(weights, seed)
         self.model.model.fused_decode = self.config.fused_decode
-        self.model.model.kv_prefetch = self.config.kv_prefetch
+        self.model.model.l2_prefetch = self.config.l2_prefetch
         self.model_runner = ModelRunner(self.model, self.config)
         num_blocks = self.model_runner.determine_num_blocks()
         self.model_runner.allocate_kv_cache(num_blocks)

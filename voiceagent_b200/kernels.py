@@ -8,6 +8,8 @@ CUDA stream. Nothing here allocates inside a captured region when the caller pas
 
 from __future__ import annotations
 
+import ctypes
+
 import torch
 
 from voiceagent_b200._lib import check, lib
@@ -330,6 +332,39 @@ def linear_small(x, weight, *, silu: bool = False, out=None, error_flag=None) ->
 # 128-column partial sums of h^2); the RMSNorm is applied by the next projection.
 
 
+def l2_prefetch(kv=None, ranges=()):
+    """A ``b200asr_l2_prefetch`` for the fused projections: ``kv = (cu_seqlens_k,
+    block_tables, k_cache, v_cache)`` of one layer (4-D caches) and up to two tensors
+    whose bytes to request (e.g. the next layer's weights). None when empty."""
+    from voiceagent_b200._lib import L2Prefetch
+
+    if kv is None and not ranges:
+        return None
+    p = L2Prefetch()
+    if kv is not None:
+        cu, tables, kc, vc = kv
+        _cuda(cu, tables, kc, vc)
+        _need(cu.dtype == torch.int32 and tables.dtype == torch.int32 and tables.dim() == 2
+              and tables.stride(1) == 1 and kc.dim() == 4 and kc.is_contiguous()
+              and vc.is_contiguous(), "l2_prefetch: int32 metadata, 4-D contiguous caches")
+        p.cu_seqlens_k, p.block_tables = cu.data_ptr(), tables.data_ptr()
+        p.bt_stride, p.batch = tables.stride(0), tables.shape[0]
+        p.block_size, p.num_kv_heads, p.head_dim = kc.shape[1], kc.shape[2], kc.shape[3]
+        p.k_cache, p.v_cache = kc.data_ptr(), vc.data_ptr()
+        p.num_slots = kc.shape[0] * kc.shape[1]
+    _need(len(ranges) <= 2, "l2_prefetch: at most two ranges")
+    for i, t in enumerate(ranges):
+        _cuda(t)
+        _need(t.is_contiguous(), "l2_prefetch: contiguous ranges")
+        p.range[i] = t.data_ptr()
+        p.range_bytes[i] = t.numel() * t.element_size()
+    return p
+
+
+def _pf(p):
+    return None if p is None else ctypes.byref(p)
+
+
 class NormState:
     """``h`` and ``ss`` buffers of a decode step (rows <= 64)."""
 
@@ -371,7 +406,8 @@ def norm_apply(state: NormState, weight, eps: float, out=None) -> torch.Tensor:
     return out
 
 
-def linear_small_add(x, weight, residual, state: NormState, error_flag=None) -> NormState:
+def linear_small_add(x, weight, residual, state: NormState, prefetch=None,
+                     error_flag=None) -> NormState:
     """``x @ weight.T`` + the residual add of the following RMSNorm: residual <- bf16(h),
     state <- (h, tile sums of h^2)."""
     _cuda(x, weight, residual)
@@ -383,13 +419,13 @@ def linear_small_add(x, weight, residual, state: NormState, error_flag=None) -> 
     _count()
     check(lib.b200asr_linear_small_add(_p(x), x.stride(0), m, k, _p(weight), n, _p(residual),
                                        residual.stride(0), _p(state.h), state.h.stride(0),
-                                       _p(state.ss), _p(error_flag), _stream()),
+                                       _p(state.ss), _pf(prefetch), _p(error_flag), _stream()),
           "linear_small_add")
     return state
 
 
 def linear_small_norm(state: NormState, norm_weight, eps: float, weight, *, silu: bool = False,
-                      out=None, error_flag=None) -> torch.Tensor:
+                      out=None, prefetch=None, error_flag=None) -> torch.Tensor:
     """``RMSNorm(h) @ weight.T`` (fused SiLU*mul when ``silu``)."""
     _cuda(norm_weight, weight)
     m, k = state.rows, state.hidden
@@ -403,7 +439,8 @@ def linear_small_norm(state: NormState, norm_weight, eps: float, weight, *, silu
     check(lib.b200asr_linear_small_norm(_p(state.h), state.h.stride(0), _p(state.ss), state.tiles,
                                         _p(norm_weight), float(eps), m, k, _p(weight), n,
                                         cols if silu else 0, _p(out), out.stride(0),
-                                        _p(error_flag), _stream()), "linear_small_norm")
+                                        _pf(prefetch), _p(error_flag), _stream()),
+          "linear_small_norm")
     return out
 
 
@@ -411,11 +448,8 @@ def linear_small_norm_qk_rope(state: NormState, norm_weight, eps: float, weight,
                               num_heads: int, num_kv_heads: int, head_dim: int, q_weight,
                               k_weight, qk_eps: float, cos_sin_cache, q_out, k_cache, v_cache,
                               slot_mapping, prefetch=None, error_flag=None) -> torch.Tensor:
-    """qkv_proj of RMSNorm(h), then q/k RMSNorm + RoPE and the K/V cache store per head.
-
-    ``prefetch = (cu_seqlens_k, block_tables)`` (decode steps) also requests the cached
-    K/V of those sequences into L2 for the attention that follows; both must come from a
-    launch that finished before the step's decoder kernels (the packer)."""
+    """qkv_proj of RMSNorm(h), then q/k RMSNorm + RoPE and the K/V cache store per head
+    (``prefetch``: an ``l2_prefetch`` hint or None)."""
     _cuda(norm_weight, weight, positions, q_weight, k_weight, cos_sin_cache, q_out, k_cache,
           v_cache, slot_mapping)
     _need(positions.dtype == torch.int64 and slot_mapping.dtype == torch.int32,
@@ -424,23 +458,13 @@ def linear_small_norm_qk_rope(state: NormState, norm_weight, eps: float, weight,
     _need(weight.dtype == BF16 and weight.is_contiguous() and weight.shape[1] == state.hidden,
           "qkv weight [n, hidden] bf16")
     num_slots = k_cache.numel() // (num_kv_heads * head_dim)
-    pf_cu = pf_tables = None
-    pf_stride = pf_batch = 0
-    block_size = k_cache.shape[1] if k_cache.dim() == 4 else 0
-    if prefetch is not None:
-        pf_cu, pf_tables = prefetch
-        _cuda(pf_cu, pf_tables)
-        _need(pf_cu.dtype == torch.int32 and pf_tables.dtype == torch.int32
-              and pf_tables.dim() == 2 and pf_tables.stride(1) == 1 and k_cache.dim() == 4,
-              "prefetch: int32 cu_seqlens_k and [B, W] block tables, 4-D cache")
-        pf_stride, pf_batch = pf_tables.stride(0), pf_tables.shape[0]
     _count()
     check(lib.b200asr_linear_small_norm_qk_rope(
         _p(state.h), state.h.stride(0), _p(state.ss), state.tiles, _p(norm_weight), float(eps),
         state.rows, state.hidden, _p(weight), num_heads, num_kv_heads, head_dim, _p(q_weight),
         _p(k_weight), float(qk_eps), _p(positions), _p(cos_sin_cache), cos_sin_cache.shape[0],
         _p(q_out), q_out.stride(0), _p(k_cache), _p(v_cache), _p(slot_mapping), num_slots,
-        _p(pf_cu), _p(pf_tables), pf_stride, pf_batch, block_size, _p(error_flag), _stream()),
+        _pf(prefetch), _p(error_flag), _stream()),
         "linear_small_norm_qk_rope")
     return q_out
 

@@ -368,7 +368,8 @@ class _DecodeRow:
         return self.length
 
 
-def decode_graph_step(fused: bool, iters: int = 64, kv_prefetch: bool = False) -> dict:
+def decode_graph_step(fused: bool, iters: int = 64, l2_prefetch: bool = False,
+                      profile_one: bool = False) -> dict:
     """One whole decode step of Qwen3-ASR-0.6B (random init) as the engine replays it:
     the bucket-32 CUDA graph (28 layers of projections, norms, RoPE + KV store, paged
     attention, lm_head, argmax, descriptor advance) over 32 rows of contexts U[80, 250],
@@ -380,7 +381,7 @@ def decode_graph_step(fused: bool, iters: int = 64, kv_prefetch: bool = False) -
 
     path = write_checkpoint(Path(tempfile.mkdtemp()) / "c06", "0.6b", weights=False)
     eng = AsrEngine(str(path), weights="random", seed=0, max_num_seqs=32, max_model_len=1024,
-                    num_kvcache_blocks=96, fused_decode=fused, kv_prefetch=kv_prefetch)
+                    num_kvcache_blocks=96, fused_decode=fused, l2_prefetch=l2_prefetch)
     gr = eng.model_runner.graph_runner
     rng = np.random.default_rng(3)
     lens = rng.integers(80, 251, size=32)
@@ -397,6 +398,11 @@ def decode_graph_step(fused: bool, iters: int = 64, kv_prefetch: bool = False) -
     e.record()
     e.synchronize()
     us = s.elapsed_time(e) * 1000.0 / iters
+    if profile_one:  # one more replay between profiler start/stop (ncu --profile-from-start off)
+        torch.cuda.profiler.start()
+        graph.replay()
+        torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
     t = eng.config.model_config.text
     hd = t.head_dim or t.hidden_size // t.num_attention_heads
     per_layer = (t.hidden_size * (t.num_attention_heads + 2 * t.num_key_value_heads) * hd
@@ -407,7 +413,7 @@ def decode_graph_step(fused: bool, iters: int = 64, kv_prefetch: bool = False) -
     launches = gr.kernels_per_replay[(32, True)]
     del eng, gr, graph
     torch.cuda.empty_cache()
-    what = ("fused projections" + (", KV prefetch" if kv_prefetch else "")) if fused \
+    what = ("fused projections" + (", next-layer L2 prefetch" if l2_prefetch else "")) if fused \
         else "unfused projections"
     return _line("decode_step_graph", f"0.6B decode step, 32 rows ctx~U[80,250], {what}",
                  us, weights + kv,
@@ -422,8 +428,10 @@ BENCHES = {
                        label="config3 decode-step shape B=32 ctx~U[80,250], short-context kernel"),
         decode_config1(lo=80, hi=250, sets=16, max_seqlen_k=4096,
                        label="config3 decode-step shape B=32 ctx~U[80,250], stream-K kernel")],
-    "step": lambda: [decode_graph_step(True), decode_graph_step(True, kv_prefetch=True),
+    "step": lambda: [decode_graph_step(True), decode_graph_step(True, l2_prefetch=True),
                      decode_graph_step(False)],
+    # one fused decode step bracketed for a profiler: its launch list is the step's kernels
+    "step_profile": lambda: [decode_graph_step(True, iters=8, profile_one=True)],
     "prefill": lambda: [prefill_config2()],
     "window": lambda: [window_config2()],
     "store": lambda: [store_rows(32), store_rows(8192)],

@@ -119,7 +119,7 @@ class Qwen3Model(nn.Module):
             [Qwen3DecoderLayer(config, self.rope) for _ in range(config.num_hidden_layers)])
         self.norm = RMSNorm(config.hidden_size, eps=config.rms_norm_eps)
         self.fused_decode = True  # decode-sized batches on the fused projections
-        self.kv_prefetch = False  # fused decode steps: L2 prefetch of each layer's K/V
+        self.l2_prefetch = False  # fused decode steps: next layer's K/V + weights into L2
         self._plain: bool | None = None  # projections without bias, bf16, contiguous
 
     def forward(self, input_ids, positions, inputs_embeds=None) -> torch.Tensor:
@@ -152,12 +152,17 @@ class Qwen3Model(nn.Module):
         ctx = get_attention_context()
         m, hidden = residual.shape
         state = kx.NormState(m, hidden, residual.device)
-        # decode steps: each qkv kernel also pulls its layer's cached K/V into L2
-        prefetch = ((ctx.cu_seqlens_k, ctx.block_tables)
-                    if ctx.decode_only and self.kv_prefetch else None)
         kx.rms_stats(residual, state)  # layer 0's input norm reads the embeddings
-        for layer in self.layers:
+        for i, layer in enumerate(self.layers):
             attn, mlp = layer.self_attn, layer.mlp
+            # optional (EngineConfig.l2_prefetch): while this layer's MLP runs, gate_up
+            # requests the next layer's cached K/V and its qkv / o_proj weights into L2
+            prefetch = None
+            if ctx.decode_only and self.l2_prefetch and i + 1 < len(self.layers):
+                nxt = self.layers[i + 1].self_attn
+                prefetch = kx.l2_prefetch(
+                    kv=(ctx.cu_seqlens_k, ctx.block_tables, nxt.attn.k_cache, nxt.attn.v_cache),
+                    ranges=(nxt.qkv_proj.weight, nxt.o_proj.weight))
             q = torch.empty(m, attn.num_heads, attn.head_dim, dtype=residual.dtype,
                             device=residual.device)
             kx.linear_small_norm_qk_rope(
@@ -166,14 +171,14 @@ class Qwen3Model(nn.Module):
                 num_kv_heads=attn.num_kv_heads, head_dim=attn.head_dim,
                 q_weight=attn.q_norm.weight, k_weight=attn.k_norm.weight, qk_eps=attn.eps,
                 cos_sin_cache=attn.rope.table, q_out=q, k_cache=attn.attn.k_cache,
-                v_cache=attn.attn.v_cache, slot_mapping=ctx.slot_mapping, prefetch=prefetch,
+                v_cache=attn.attn.v_cache, slot_mapping=ctx.slot_mapping,
                 error_flag=ctx.error_flag)
             o = attn.attn(q)
             kx.linear_small_add(o.view(m, attn.q_size), attn.o_proj.weight, residual, state,
                                 error_flag=ctx.error_flag)
             act = kx.linear_small_norm(state, layer.post_attention_layernorm.weight,
                                        layer.post_attention_layernorm.eps,
-                                       mlp.gate_up_proj.weight, silu=True,
+                                       mlp.gate_up_proj.weight, silu=True, prefetch=prefetch,
                                        error_flag=ctx.error_flag)
             kx.linear_small_add(act, mlp.down_proj.weight, residual, state,
                                 error_flag=ctx.error_flag)
