@@ -158,6 +158,15 @@ __device__ __forceinline__ void tma_load_4d(void *dst, const CUtensorMap *map, i
       : "memory");
 }
 
+// The same box, into L2 only (no shared memory, no barrier).
+__device__ __forceinline__ void tma_prefetch_4d(const CUtensorMap *map, int32_t c0, int32_t c1,
+                                                int32_t c2, int32_t c3) {
+  asm volatile("cp.async.bulk.prefetch.tensor.4d.L2.global.tile [%0, {%1, %2, %3, %4}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+               : "memory");
+}
+
 // Merge the n_parts split-K partials of sequence b (workspace slots first..first+n_parts-1)
 // for the G query heads of KV head w (one warp each). Runs after this CTA's last stage,
 // when the stage buffers are free: all consumer threads stage a chunk of partials --
@@ -717,6 +726,13 @@ __global__ void __launch_bounds__(Short<G>::THREADS, 2)
             }
           }
           d_slot = blk * a.block_size + t0 % a.block_size;
+        }
+        // Before the wait, the stages the ring cannot take yet -- and the one holding the
+        // newest token, which the previous kernel writes through L2 -- are requested into
+        // L2, so their loads after the wait are L2 hits.
+        if (!waited && s < nst && s >= early) {
+          tma_prefetch_4d(&tm_k, 0, d_slot, 0, h);
+          tma_prefetch_4d(&tm_v, 0, d_slot, 0, h);
         }
         const int nw = min(32, nst - wb);
         for (int i = 0; i < nw; ++i) {
