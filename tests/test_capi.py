@@ -46,6 +46,21 @@ def test_binding_signatures_cover_the_header():
     assert sorted(SIGNATURES) == declared_symbols()
 
 
+def test_integration_stub_matches_the_binding():
+    """The ctypes stub a reference maintainer would paste declares the
+    same argument types as the binding the tests exercise."""
+    from voiceagent_b200._lib import SIGNATURES
+
+    text = (REPO / "INTEGRATION.md").read_text()
+    types = {"P": ctypes.c_void_p, "I32": ctypes.c_int32, "I64": ctypes.c_int64,
+             "F32": ctypes.c_float, "SZ": ctypes.c_size_t}
+    stubs = re.findall(r"_lib\.(b200asr_\w+)\.argtypes = \[([^\]]*)\]", text, re.S)
+    assert len(stubs) >= 10
+    for name, args in stubs:
+        got = [types[a.strip()] for a in args.replace("\n", " ").split(",") if a.strip()]
+        assert got == SIGNATURES[name][1], name
+
+
 def test_only_the_c_abi_is_exported():
     import subprocess
 
