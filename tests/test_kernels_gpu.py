@@ -377,6 +377,21 @@ def test_paged_decode_step_shape_both_kernels(kx, max_len):
     assert_attn_close(out, ref, f"decode step shape max_seqlen_k={max_len}")
 
 
+@pytest.mark.parametrize("hq,hkv", [(8, 8), (16, 4), (16, 8)])
+@pytest.mark.parametrize("max_len", [512, 4096])
+def test_paged_decode_query_groups(kx, hq, hkv, max_len):
+    """Query heads per KV head G = 1, 4 and 2 through both kernels (peaked scores, lengths
+    across stage and block boundaries)."""
+    rng = np.random.default_rng(hq * 10 + hkv)
+    lens = [1, 17, 64, 65, 200, 256, 300, 511]
+    q, kc, vc, tables, cu_k = _decode_case(rng, lens, nblocks=64, hq=hq, hkv=hkv)
+    q, kc = K.bf16_round(q * 2 * np.sqrt(128)), K.bf16_round(kc * 2 * np.sqrt(128))
+    vc = vc * 8
+    out = _run_decode(kx, q, kc, vc, tables, cu_k, max_len)
+    ref = K.paged_attention(q, kc, vc, np.arange(len(lens) + 1), cu_k, tables, 128 ** -0.5)
+    assert_attn_close(out, ref, f"decode G={hq // hkv} max_seqlen_k={max_len}")
+
+
 @pytest.mark.parametrize("max_len", [512, 4096])
 def test_paged_decode_peaked_scores(kx, max_len):
     """Scores with a spread of ~9 (q, k ~ 3 N(0, 1) after the 1/sqrt(d) scale): the

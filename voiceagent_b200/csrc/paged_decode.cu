@@ -125,6 +125,22 @@ __device__ __forceinline__ void mma16816(float *d, uint32_t a0, uint32_t a1, uin
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// The same MMA as a plain (reorderable) asm: a pure register operation.
+__device__ __forceinline__ void mma16816_nv(float *d, uint32_t a0, uint32_t a1, uint32_t a2,
+                                            uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Transpose of an 8x8 bf16 matrix held one fragment register per lane.
+__device__ __forceinline__ uint32_t movmatrix_t(uint32_t x) {
+  uint32_t y;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
+}
+
 // Byte offset of (row, 16-byte chunk) inside a 128-byte-swizzled tile (1024-aligned).
 __device__ __forceinline__ uint32_t swz(int row, int chunk) {
   return static_cast<uint32_t>(row * 128 + ((chunk ^ (row & 7)) << 4));
@@ -800,9 +816,15 @@ __global__ void __launch_bounds__(Short<G>::THREADS, 2)
     }
   }
 
-  uint32_t qa[8][2];
-  float o[16][4];
-  float m_run = -INFINITY, l_run = 0.f;
+  // Token-major MMAs: with G = 1-4 query rows per unit, putting the 16 tokens of a
+  // warp's slice on the MMA's M side (S^T = K Q^T, O^T += V^T P^T) halves the MMAs of
+  // the row-major form (where 12-15 of every 16 query rows are padding), halves the
+  // accumulator registers, and the QK^T sum runs as two independent chains. Lane
+  // (g = lane / 4, c = lane % 4) holds S^T for tokens g and g + 8 and queries 2c, 2c + 1
+  // (valid when < G), and O^T for dims 16 mt + g (+ 8) of the same queries.
+  uint32_t qa[8][2];  // Q as the B operand: Q[g][16 kk + 2c ..], Q[g][16 kk + 8 + 2c ..]
+  float o[8][4];
+  float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
   for (uint32_t it_stage = 0;; ++it_stage) {
     const int st = it_stage % kShortStages;
     const uint32_t ph = (it_stage / kShortStages) & 1;
@@ -815,9 +837,9 @@ __global__ void __launch_bounds__(Short<G>::THREADS, 2)
 
     if (si.flags & 1) {  // first stage of a unit: fresh state + the unit's query rows
 #pragma unroll
-      for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
-      m_run = -INFINITY;
-      l_run = 0.f;
+      for (int j = 0; j < 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+      m_run[0] = m_run[1] = -INFINITY;
+      l_run[0] = l_run[1] = 0.f;
       const uint8_t *qs = stages + st * C::STAGE_BYTES + 2 * C::KV_BYTES + (row_valid ? row : 0) * kDecD * 2;
 #pragma unroll
       for (int kk = 0; kk < 8; ++kk) {
@@ -836,59 +858,61 @@ __global__ void __launch_bounds__(Short<G>::THREADS, 2)
         }
         __syncwarp();
       }
-      float s[2][4];
+      // S^T[16 tokens][8 queries] = K (A, 16 x 16 per step) x Q^T (B): even / odd steps
+      // accumulate separately
+      float sa[4] = {0.f, 0.f, 0.f, 0.f}, sb[4] = {0.f, 0.f, 0.f, 0.f};
+      const int kt = (lm_mat & 1) * 8 + lm_row;  // ldmatrix row: token
 #pragma unroll
-      for (int nt = 0; nt < 2; ++nt) {
-        s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
-#pragma unroll
-        for (int kp = 0; kp < 4; ++kp) {
-          const int chunk = 4 * kp + lm_mat;
-          uint32_t b0, b1, b2, b3;
-          ldsm_x4(k_tile + (chunk >> 3) * C::HALF + swz(nt * 8 + lm_row, chunk & 7), b0, b1, b2, b3);
-          mma16816(s[nt], qa[2 * kp][0], 0u, qa[2 * kp][1], 0u, b0, b1);
-          mma16816(s[nt], qa[2 * kp + 1][0], 0u, qa[2 * kp + 1][1], 0u, b2, b3);
-        }
+      for (int kk = 0; kk < 8; ++kk) {
+        const int chunk = 2 * kk + (lm_mat >> 1);
+        uint32_t a0, a1, a2, a3;
+        ldsm_x4(k_tile + (chunk >> 3) * C::HALF + swz(kt, chunk & 7), a0, a1, a2, a3);
+        mma16816_nv((kk & 1) ? sb : sa, a0, a1, a2, a3, qa[kk][0], qa[kk][1]);
       }
-      float mx = -INFINITY;
+      // lane: tokens t0 = g, t1 = g + 8; queries 2c + e
+      float sv[2][2];  // [token][e]
+      const int t0 = row, t1 = row + 8;
 #pragma unroll
-      for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int t = nt * 8 + quad * 2 + e;
-          s[nt][e] = t < ntok ? s[nt][e] * a.scale_log2 : -INFINITY;
-          mx = fmaxf(mx, s[nt][e]);
-        }
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-      const float m_new = fmaxf(m_run, mx);  // token 0 of the slice is valid: finite
-      const float alpha = exp2f(m_run - m_new);
-      float p[2][2], sum = 0.f;
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          p[nt][e] = exp2f(s[nt][e] - m_new);
-          sum += p[nt][e];
-        }
-      sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-      sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-      l_run = l_run * alpha + sum;
-      m_run = m_new;
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        o[j][0] *= alpha;
-        o[j][1] *= alpha;
+      for (int e = 0; e < 2; ++e) {
+        sv[0][e] = t0 < ntok ? (sa[e] + sb[e]) * a.scale_log2 : -INFINITY;
+        sv[1][e] = t1 < ntok ? (sa[2 + e] + sb[2 + e]) * a.scale_log2 : -INFINITY;
       }
-      const uint32_t pa0 = row_valid ? pack2(p[0][0], p[0][1]) : 0u;
-      const uint32_t pa2 = row_valid ? pack2(p[1][0], p[1][1]) : 0u;
+      float alpha[2], pr[2][2];
 #pragma unroll
-      for (int nd = 0; nd < 8; ++nd) {
-        const int chunk = 2 * nd + (lm_mat >> 1);
-        const int trow = (lm_mat & 1) * 8 + lm_row;
-        uint32_t b0, b1, b2, b3;
-        ldsm_x4_t(v_tile + (chunk >> 3) * C::HALF + swz(trow, chunk & 7), b0, b1, b2, b3);
-        mma16816(o[2 * nd], pa0, 0u, pa2, 0u, b0, b1);
-        mma16816(o[2 * nd + 1], pa0, 0u, pa2, 0u, b2, b3);
+      for (int e = 0; e < 2; ++e) {
+        float mx = fmaxf(sv[0][e], sv[1][e]);  // over the 16 tokens: lanes of equal c
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+        const float m_new = fmaxf(m_run[e], mx);  // token 0 of the slice is valid: finite
+        alpha[e] = exp2f(m_run[e] - m_new);
+        pr[0][e] = exp2f(sv[0][e] - m_new);
+        pr[1][e] = exp2f(sv[1][e] - m_new);
+        float sum = pr[0][e] + pr[1][e];
+        sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 8);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 16);
+        l_run[e] = l_run[e] * alpha[e] + sum;
+        m_run[e] = m_new;
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        o[j][0] *= alpha[0];
+        o[j][1] *= alpha[1];
+        o[j][2] *= alpha[0];
+        o[j][3] *= alpha[1];
+      }
+      // P^T (tokens x queries) as two 8x8 blocks in accumulator layout -> transposed into
+      // the B fragments of O^T += V^T P^T (k = token, n = query)
+      const uint32_t pb0 = movmatrix_t(pack2(pr[0][0], pr[0][1]));  // tokens 0-7
+      const uint32_t pb1 = movmatrix_t(pack2(pr[1][0], pr[1][1]));  // tokens 8-15
+      const int vt_row = (lm_mat >> 1) * 8 + lm_row;  // ldmatrix row: token
+#pragma unroll
+      for (int mt = 0; mt < 8; ++mt) {
+        const int chunk = 2 * mt + (lm_mat & 1);
+        uint32_t a0, a1, a2, a3;
+        ldsm_x4_t(v_tile + (chunk >> 3) * C::HALF + swz(vt_row, chunk & 7), a0, a1, a2, a3);
+        mma16816_nv(o[mt], a0, a1, a2, a3, pb0, pb1);
       }
     }
     __syncwarp();
@@ -897,15 +921,18 @@ __global__ void __launch_bounds__(Short<G>::THREADS, 2)
 
     // ----------------------------------------------- unit end: combine the 4 warps
     float *sm = scratch + w * H * (kDecD + 2);  // [H][2] (m, l) then [H][128] o
-    if (row_valid) {
-      if (quad == 0) {
-        sm[row * 2] = m_run;
-        sm[row * 2 + 1] = l_run;
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int q = 2 * quad + e;
+      if (q >= H) continue;
+      if (row == 0) {
+        sm[q * 2] = m_run[e];
+        sm[q * 2 + 1] = l_run[e];
       }
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        sm[2 * H + row * kDecD + j * 8 + quad * 2] = o[j][0];
-        sm[2 * H + row * kDecD + j * 8 + quad * 2 + 1] = o[j][1];
+      for (int j = 0; j < 8; ++j) {
+        sm[2 * H + q * kDecD + j * 16 + row] = o[j][e];
+        sm[2 * H + q * kDecD + j * 16 + row + 8] = o[j][2 + e];
       }
     }
     consumer_sync(C::CONSUMERS);
