@@ -116,6 +116,14 @@ __device__ __forceinline__ uint32_t pack2(float a, float b) {
   return *reinterpret_cast<uint32_t *>(&h);
 }
 
+// The two bf16 halves of a packed pair as floats (low element first).
+__device__ __forceinline__ float2 unpack2(uint32_t v) {
+  return make_float2(__uint_as_float(v << 16), __uint_as_float(v & 0xffff0000u));
+}
+
+// bf16(a), bf16(b) as floats: one paired conversion instead of two.
+__device__ __forceinline__ float2 round2_bf16(float a, float b) { return unpack2(pack2(a, b)); }
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

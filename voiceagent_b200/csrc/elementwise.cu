@@ -131,11 +131,13 @@ __global__ void qk_norm_rope_store_kernel(
     for (int e = 0; e < EPL; ++e) ss += x[i][e] * x[i][e];
     ss = warp_sum(ss);
     const float r = rsqrtf(ss / static_cast<float>(D) + eps);
-    float y[EPL];
+    float y[EPL];  // x.to(bf16), then .mul_(weight) rounded: paired conversions
 #pragma unroll
-    for (int e = 0; e < EPL; ++e) {
-      const float n = bf2f(f2bf(x[i][e] * r));                   // x.to(bf16)
-      y[e] = bf2f(f2bf(n * (is_q ? wq[e] : wk[e])));             // .mul_(weight)
+    for (int e = 0; e < EPL; e += 2) {
+      const float2 n = round2_bf16(x[i][e] * r, x[i][e + 1] * r);
+      const float2 m = round2_bf16(n.x * (is_q ? wq[e] : wk[e]), n.y * (is_q ? wq[e + 1] : wk[e + 1]));
+      y[e] = m.x;
+      y[e + 1] = m.y;
     }
     int64_t p = pos[i];
     if (p < 0 || p >= max_position) {
@@ -209,11 +211,13 @@ __global__ void rmsnorm_kernel(const __nv_bfloat16 *__restrict__ x, __nv_bfloat1
   __syncthreads();
   const float r = rsqrtf(red[0] / static_cast<float>(hidden) + eps);
   if (!active) return;
-  float y[8];
+  uint32_t y[4];  // bf16(bf16(v * r) * w), paired conversions; the second is the output
 #pragma unroll
-  for (int e = 0; e < 8; ++e) y[e] = bf2f(f2bf(bf2f(f2bf(v[e] * r)) * w[e]));
-  *reinterpret_cast<uint4 *>(out + row * hidden + i8 * 8) =
-      make_uint4(pack2(y[0], y[1]), pack2(y[2], y[3]), pack2(y[4], y[5]), pack2(y[6], y[7]));
+  for (int e = 0; e < 4; ++e) {
+    const float2 n = round2_bf16(v[2 * e] * r, v[2 * e + 1] * r);
+    y[e] = pack2(n.x * w[2 * e], n.y * w[2 * e + 1]);
+  }
+  *reinterpret_cast<uint4 *>(out + row * hidden + i8 * 8) = make_uint4(y[0], y[1], y[2], y[3]);
 }
 
 // ------------------------------------------------------------------- SiLU*mul

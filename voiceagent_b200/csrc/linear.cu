@@ -270,11 +270,15 @@ __device__ __forceinline__ void norm_in_fill(uint8_t *stages, const LinearArgs &
         unpack8(wv[s][jj], w);
         const float h[8] = {hv[s][jj][0].x, hv[s][jj][0].y, hv[s][jj][0].z, hv[s][jj][0].w,
                             hv[s][jj][1].x, hv[s][jj][1].y, hv[s][jj][1].z, hv[s][jj][1].w};
-        float y[8];
+        // bf16(bf16(h * rs) * w), converted in pairs; the second rounding is the output
+        uint32_t y[4];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) y[e] = bf2f(f2bf(bf2f(f2bf(h[e] * rs)) * w[e]));
+        for (int e = 0; e < 4; ++e) {
+          const float2 n = round2_bf16(h[2 * e] * rs, h[2 * e + 1] * rs);
+          y[e] = pack2(n.x * w[2 * e], n.y * w[2 * e + 1]);
+        }
         *reinterpret_cast<uint4 *>(xrow + s * C::STAGE + ((j ^ (r & 7)) << 4)) =
-            make_uint4(pack2(y[0], y[1]), pack2(y[2], y[3]), pack2(y[4], y[5]), pack2(y[6], y[7]));
+            make_uint4(y[0], y[1], y[2], y[3]);
       }
   }
 }
@@ -315,9 +319,10 @@ __device__ __forceinline__ void qk_rope_store4(const LinearFuse &f, const Linear
                                                int head, int lane, const float *acc,
                                                const EpiRow &pre, const float *nw) {
   constexpr int D = kLnRows;
-  float x[4];
-#pragma unroll
-  for (int e = 0; e < 4; ++e) x[e] = bf2f(f2bf(acc[e]));  // the bf16 projection output
+  // the bf16 projection output (paired conversions)
+  const uint32_t xp[2] = {pack2(acc[0], acc[1]), pack2(acc[2], acc[3])};
+  const float2 x01 = unpack2(xp[0]), x23 = unpack2(xp[1]);
+  const float x[4] = {x01.x, x01.y, x23.x, x23.y};
   const int kv_hidden = f.num_kv_heads * D;
   const int64_t slot = pre.slot;
   const bool slot_bad = slot != -1 && (slot < 0 || slot >= f.num_slots);
@@ -329,7 +334,7 @@ __device__ __forceinline__ void qk_rope_store4(const LinearFuse &f, const Linear
     }
     const int hv = head - f.num_heads - f.num_kv_heads;
     *reinterpret_cast<uint2 *>(f.v_cache + slot * kv_hidden + hv * D + lane * 4) =
-        make_uint2(pack2(x[0], x[1]), pack2(x[2], x[3]));
+        make_uint2(xp[0], xp[1]);
     return;
   }
   const bool is_q = head < f.num_heads;
@@ -338,9 +343,14 @@ __device__ __forceinline__ void qk_rope_store4(const LinearFuse &f, const Linear
   for (int e = 0; e < 4; ++e) ss += x[e] * x[e];
   ss = warp_sum(ss);
   const float r = rsqrtf(ss / static_cast<float>(D) + f.qk_eps);
-  float y[4];
+  float y[4];  // bf16(bf16(x * r) * w), paired conversions
 #pragma unroll
-  for (int e = 0; e < 4; ++e) y[e] = bf2f(f2bf(bf2f(f2bf(x[e] * r)) * nw[e]));
+  for (int e = 0; e < 2; ++e) {
+    const float2 n = round2_bf16(x[2 * e] * r, x[2 * e + 1] * r);
+    const float2 m = round2_bf16(n.x * nw[2 * e], n.y * nw[2 * e + 1]);
+    y[2 * e] = m.x;
+    y[2 * e + 1] = m.y;
+  }
   const bool first_half = lane < 16;
   float o[4];
 #pragma unroll
@@ -589,10 +599,12 @@ __global__ void __launch_bounds__(kLnThreads)
       const float y[4] = {acc.x, acc.y, acc.z, acc.w};
       const float rr[4] = {__uint_as_float(rv.x << 16), __uint_as_float(rv.x & 0xffff0000u),
                            __uint_as_float(rv.y << 16), __uint_as_float(rv.y & 0xffff0000u)};
+      const float2 y01 = round2_bf16(y[0], y[1]), y23 = round2_bf16(y[2], y[3]);
+      const float yb[4] = {y01.x, y01.y, y23.x, y23.y};  // the bf16 projection output
       float h[4], ss = 0.f;
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        h[e] = bf2f(f2bf(y[e])) + rr[e];  // bf16 projection output + residual, in fp32
+        h[e] = yb[e] + rr[e];  // + residual, in fp32
         ss += h[e] * h[e];
       }
       *reinterpret_cast<uint2 *>(rp) = make_uint2(pack2(h[0], h[1]), pack2(h[2], h[3]));
