@@ -230,16 +230,17 @@ __global__ void silu_mul_kernel(const __nv_bfloat16 *__restrict__ x, int64_t row
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int64_t row = i / (inner / 8);
     const int c = static_cast<int>(i - row * (inner / 8)) * 8;
-    float g[8], u[8], y[8];
+    float g[8], u[8];
     unpack8(*reinterpret_cast<const uint4 *>(x + row * 2 * inner + c), g);
     unpack8(*reinterpret_cast<const uint4 *>(x + row * 2 * inner + inner + c), u);
+    uint32_t y[4];  // F.silu -> bf16, times u -> bf16 (paired conversions)
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const float s = bf2f(f2bf(g[e] / (1.0f + expf(-g[e]))));  // F.silu -> bf16
-      y[e] = s * u[e];
+    for (int e = 0; e < 4; ++e) {
+      const float2 sb = round2_bf16(g[2 * e] / (1.0f + expf(-g[2 * e])),
+                                    g[2 * e + 1] / (1.0f + expf(-g[2 * e + 1])));
+      y[e] = pack2(sb.x * u[2 * e], sb.y * u[2 * e + 1]);
     }
-    *reinterpret_cast<uint4 *>(out + row * inner + c) =
-        make_uint4(pack2(y[0], y[1]), pack2(y[2], y[3]), pack2(y[4], y[5]), pack2(y[6], y[7]));
+    *reinterpret_cast<uint4 *>(out + row * inner + c) = make_uint4(y[0], y[1], y[2], y[3]);
   }
 }
 

@@ -181,11 +181,13 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, i
       : "memory");
 }
 
-// silu(g) * u with the unfused path's roundings: g, u are bf16 projections, F.silu
-// returns bf16, the product is rounded once more by the caller's pack.
-__device__ __forceinline__ float silu_mul1(float g, float u) {
-  const float gb = bf2f(f2bf(g)), ub = bf2f(f2bf(u));
-  return bf2f(f2bf(gb / (1.0f + expf(-gb)))) * ub;
+// silu(g) * u for two columns, with the unfused path's roundings: g, u are bf16
+// projections, F.silu returns bf16, the product is rounded to bf16 (the packed result).
+// Conversions in pairs: one paired conversion per two values.
+__device__ __forceinline__ uint32_t silu_mul2(float g0, float g1, float u0, float u1) {
+  const float2 gb = round2_bf16(g0, g1), ub = round2_bf16(u0, u1);
+  const float2 sb = round2_bf16(gb.x / (1.0f + expf(-gb.x)), gb.y / (1.0f + expf(-gb.y)));
+  return pack2(sb.x * ub.x, sb.y * ub.y);
 }
 
 constexpr int kNormMaxTiles = 32;  // RMSNorm prologue: hidden <= 32 x 128
@@ -585,8 +587,7 @@ __global__ void __launch_bounds__(kLnThreads)
       if (lane < 16) {
         __nv_bfloat16 *dst = a.y + c * a.y_stride + tile * 64 + lane * 4;
         *reinterpret_cast<uint2 *>(dst) =
-            make_uint2(pack2(silu_mul1(acc.x, ux), silu_mul1(acc.y, uy)),
-                       pack2(silu_mul1(acc.z, uz), silu_mul1(acc.w, uw)));
+            make_uint2(silu_mul2(acc.x, acc.y, ux, uy), silu_mul2(acc.z, acc.w, uz, uw));
       }
     } else if (EPI == kEpiAdd) {
       const int col = tile * kLnRows + lane * 4;
@@ -687,11 +688,13 @@ __global__ void norm_apply_kernel(const float *__restrict__ h, const float *__re
   const float w[4] = {__uint_as_float(wv.x << 16), __uint_as_float(wv.x & 0xffff0000u),
                       __uint_as_float(wv.y << 16), __uint_as_float(wv.y & 0xffff0000u)};
   const float hh[4] = {hv.x, hv.y, hv.z, hv.w};
-  float y[4];
+  uint32_t y[2];  // bf16(bf16(h * rs) * w), paired conversions
 #pragma unroll
-  for (int e = 0; e < 4; ++e) y[e] = bf2f(f2bf(bf2f(f2bf(hh[e] * rs)) * w[e]));
-  *reinterpret_cast<uint2 *>(out + static_cast<int64_t>(r) * hidden + col) =
-      make_uint2(pack2(y[0], y[1]), pack2(y[2], y[3]));
+  for (int e = 0; e < 2; ++e) {
+    const float2 n = round2_bf16(hh[2 * e] * rs, hh[2 * e + 1] * rs);
+    y[e] = pack2(n.x * w[2 * e], n.y * w[2 * e + 1]);
+  }
+  *reinterpret_cast<uint2 *>(out + static_cast<int64_t>(r) * hidden + col) = make_uint2(y[0], y[1]);
 }
 
 // Smallest split (power of two dividing the K stages, <= 16) that puts >= 120 CTAs on
