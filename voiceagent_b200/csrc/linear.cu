@@ -398,6 +398,7 @@ __global__ void __launch_bounds__(kLnThreads)
   pdl_trigger();
   const int ks = a.k_split;
   const int cols = MP / ks;  // batch columns this CTA reduces (ks divides MP: powers of two)
+  const int cols_log2 = __ffs(cols) - 1;
   const int kz = static_cast<int>(cluster_rank());
   const int tile = blockIdx.x / ks;
   const int k0 = kz * a.steps * kLnBK;
@@ -551,7 +552,7 @@ __global__ void __launch_bounds__(kLnThreads)
   for (int i = 0; i < MP * (kLnRows / 4) / kLnThreads; ++i) {
     const int id = i * kLnThreads + tid;  // (column, 4-row group): warps write 512 B runs
     const int col = id / (kLnRows / 4), q = id % (kLnRows / 4);
-    const int r = col / cols, cl = col - r * cols;
+    const int r = col >> cols_log2, cl = col & (cols - 1);  // cols: a power of two
     const float4 v = *reinterpret_cast<const float4 *>(&colmaj[col * kLnRows + q * 4]);
     const uint32_t off = static_cast<uint32_t>(((kz * cols + cl) * kLnRows + q * 4) * 4);
     if (r == kz) {
