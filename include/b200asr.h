@@ -257,6 +257,55 @@ B200ASR_API int b200asr_varlen_attention(const void *q, int64_t q_row_stride, co
                              int32_t head_dim, float scale, void *out, int64_t out_row_stride,
                              int32_t *error_flag, b200asr_stream_t stream);
 
+/* Element types of b200asr_pool_paged_decode. */
+enum { B200ASR_DTYPE_BF16 = 0, B200ASR_DTYPE_F16 = 1, B200ASR_DTYPE_F32 = 2 };
+
+/* One-token decode attention over a page pool in the TTS talker's layout, with the
+ * current token's K/V written by the same launch. Replaces paged_attention_decode and
+ * its Triton kernel (agent/qwen_tts_paged_attention.py:130-287, 383-516; the write of
+ * its torch path, 519-532), as called by QwenPagedCache.paged_attention_decode
+ * (agent/qwen_tts_outer_varlen.py:392-436).
+ *   query       [batch, num_heads, 1, head_dim], strides q_stride_b / q_stride_h
+ *   key_pool,
+ *   value_pool  [num_pages, num_kv_heads, page_size, head_dim], strides kv_stride_p /
+ *               kv_stride_h / kv_stride_s (shared by both pools)
+ *   page_table  int64 [batch, table_stride]: row b's logical page p is physical page
+ *               page_table[b][p], p < table_width (the padded width, the reference's
+ *               kernel_page_count)
+ *   seq_lens    int64 [batch], positive
+ *   key_valid_mask  NULL or bool/uint8 [batch, valid_stride]: positions t < valid_len
+ *               with a zero byte are not attended; positions >= valid_len are
+ *   new_key,
+ *   new_value   NULL, or [batch, num_kv_heads, 1, head_dim] with strides new_stride_b /
+ *               new_stride_h (shared by both): stored at position seq_lens[b] - 1 of
+ *               row b's pages and attended in the same pass
+ *   out         [batch, num_heads, 1, head_dim], strides out_stride_b / out_stride_h
+ * All strides in elements; head_dim is the unit stride. dtype B200ASR_DTYPE_* for
+ * query, pools, new K/V and out alike; softmax and accumulation in fp32. Row b attends
+ * positions < min(seq_lens[b], max_seq_len) (the reference's kernel_seq_len bound); a
+ * row whose positions are all masked yields zeros. Supported: num_heads / num_kv_heads
+ * in {1, 2, 4, 8}, head_dim * element size a multiple of 16 bytes and at most 1024,
+ * 16-byte aligned query, pools and new K/V. tokens_per_cta: positions per CTA (0 =
+ * chosen from the batch; else >= 64). workspace: at least
+ * b200asr_pool_paged_decode_workspace_size(batch, num_heads, head_dim, max_seq_len)
+ * bytes whose first bytes (merge counters) are zero before the first call; every call
+ * leaves them zero, and calls sharing a workspace must not overlap on the GPU.
+ * Device-side checks: a page outside the table or the pool raises
+ * B200ASR_DEVERR_BLOCK (the position is skipped); seq_lens[b] <= 0 or > max_seq_len
+ * raises B200ASR_DEVERR_LENGTH.                                                    */
+B200ASR_API size_t b200asr_pool_paged_decode_workspace_size(int32_t batch, int32_t num_heads,
+                                                int32_t head_dim, int32_t max_seq_len);
+B200ASR_API int b200asr_pool_paged_decode(
+    int32_t dtype, int32_t batch, int32_t num_heads, int32_t num_kv_heads, int32_t head_dim,
+    const void *query, int64_t q_stride_b, int64_t q_stride_h, void *key_pool, void *value_pool,
+    int32_t num_pages, int32_t page_size, int64_t kv_stride_p, int64_t kv_stride_h,
+    int64_t kv_stride_s, const int64_t *page_table, int64_t table_stride, int32_t table_width,
+    const int64_t *seq_lens, const uint8_t *key_valid_mask, int64_t valid_stride,
+    int32_t valid_len, const void *new_key, const void *new_value, int64_t new_stride_b,
+    int64_t new_stride_h, void *out, int64_t out_stride_b, int64_t out_stride_h,
+    int32_t max_seq_len, int32_t tokens_per_cta, float scale, void *workspace,
+    size_t workspace_bytes, int32_t *error_flag, b200asr_stream_t stream);
+
 /* ------------------------------------------------------------------ sampler ----
  * Replaces the greedy branch of Sampler.forward (layers/sampler.py:16-20):
  * out_ids[b] = argmax over logits[b, :vocab] (bf16, row stride in elements) in

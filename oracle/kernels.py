@@ -258,6 +258,66 @@ def paged_attention(q, k_cache, v_cache, cu_seqlens_q, cu_seqlens_k, block_table
     return out
 
 
+def write_current_kv(key_pool, value_pool, page_table, seq_lens, new_key, new_value) -> None:
+    """``agent/qwen_tts_paged_attention.py:519-532`` (``_write_current_kv``): row b's new
+    key/value (``[B, H_kv, 1, D]``) land at position ``seq_lens[b] - 1`` of its pages in
+    the pool ``[pages, H_kv, page_size, D]`` (in place)."""
+    ps = key_pool.shape[2]
+    for b in range(new_key.shape[0]):
+        pos = int(seq_lens[b]) - 1
+        page = int(page_table[b, pos // ps])
+        key_pool[page, :, pos % ps, :] = new_key[b, :, 0, :]
+        value_pool[page, :, pos % ps, :] = new_value[b, :, 0, :]
+
+
+def pool_paged_attention(query, key_pool, value_pool, page_table, seq_lens, scale,
+                         key_valid_mask=None, new_key=None, new_value=None,
+                         kernel_seq_len=None) -> np.ndarray:
+    """One-token GQA attention over a page pool in the TTS talker layout.
+
+    Restates ``paged_attention_decode`` (agent/qwen_tts_paged_attention.py:383-516) with
+    the semantics of its CUDA kernel (130-287) and torch path (353-380):
+
+    * query ``[B, H, 1, D]``; pools ``[pages, H_kv, page_size, D]``; ``page_table``
+      ``[B, W]`` maps logical page ``p // page_size`` of row b to a physical page;
+    * with ``new_key``/``new_value`` the current token is written first
+      (:func:`write_current_kv`, in place) and attended like any cached token;
+    * row b attends positions ``0 .. min(seq_lens[b], kernel_seq_len) - 1`` (the kernel's
+      loop bound, 226-232), minus those whose ``key_valid_mask[b, t]`` is False; mask
+      columns beyond the mask's width count as valid (the launcher pads with True,
+      466-475);
+    * a row with no valid key returns zeros (the kernel's ``max(sum, 1e-20)`` guard with
+      zero-filled masked values; the torch path would average the masked values instead).
+
+    Float64 arithmetic; returns ``[B, H, 1, D]``.
+    """
+    if new_key is not None:
+        write_current_kv(key_pool, value_pool, page_table, seq_lens, new_key, new_value)
+    bsz, hq, _, d = query.shape
+    hkv, ps = key_pool.shape[1], key_pool.shape[2]
+    group = hq // hkv
+    out = np.zeros((bsz, hq, 1, d), dtype=np.float64)
+    for b in range(bsz):
+        length = int(seq_lens[b])
+        if kernel_seq_len is not None:
+            length = min(length, int(kernel_seq_len))
+        pos = np.arange(length)
+        valid = np.ones(length, dtype=bool)
+        if key_valid_mask is not None:
+            w = min(length, key_valid_mask.shape[1])
+            valid[:w] = key_valid_mask[b, :w]
+        pos = pos[valid]
+        if pos.size == 0:
+            continue
+        pages = np.asarray(page_table[b], dtype=np.int64)[pos // ps]
+        keys = key_pool[pages, :, pos % ps, :]    # (n, H_kv, D)
+        vals = value_pool[pages, :, pos % ps, :]
+        for h in range(hq):
+            out[b, h, 0] = _softmax_attend(query[b, h], keys[:, h // group], vals[:, h // group],
+                                           scale)
+    return out
+
+
 def varlen_attention(q, k, v, cu_seqlens, scale) -> np.ndarray:
     """``layers/attention.py:121-139``: non-causal attention inside each segment."""
     out = np.zeros(q.shape, dtype=np.float64)

@@ -17,6 +17,9 @@ the TTS paged decode) on the CPU interpreter. What each fixture pins:
 * ``store.npz``         -- ``store_kvcache`` Triton kernel (attention.py:31-67)
 * ``paged_decode.npz``  -- TTS paged decode, its torch reference path
   (the Triton launcher refuses CPU tensors)
+* ``tts_pool_decode.npz`` -- the same function in its own pool layout
+  ``[pages, kv_heads, page_size, head_dim]``: the reference test's inputs, the fused
+  current-token write, and talker-shaped cases with key-valid masks
 * ``norm_rope.npz``     -- RMSNorm + RotaryEmbedding as used in qwen3.py:42-48
 * ``elementwise.npz``   -- fused add-RMSNorm and SiluAndMul (layernorm.py, activation.py)
 * ``sampler.npz``       -- greedy ``Sampler`` (sampler.py:16-27)
@@ -319,6 +322,85 @@ def gen_paged_decode(out: Path):
                         out_reference=_f32(ref.squeeze(2)))
 
 
+def gen_tts_pool_decode(out: Path):
+    """``paged_attention_decode`` (agent/qwen_tts_paged_attention.py:383-516) through its
+    torch path, on the layout the TTS talker's page pool uses.
+
+    Case ``ref``: the reference test's own inputs (tests/test_qwen_tts_paged_attention_
+    kernel.py:16-35; fp32, head_dim 4, page 2, left-padded mask), once without and once
+    with the fused current-token write (its 144-177). Cases ``talker_*``: bf16 values
+    (stored as bits, promoted to fp32 for the call), head_dim 128, GQA 2 and 4, pages of
+    16 and 24 tokens, page tables padded with -1 as ``QwenPagedCache`` pads them
+    (qwen_tts_outer_varlen.py:343-361), lengths on and around page boundaries, masks
+    with left padding, and the current-token write.
+    """
+    import torch
+    from qwen_asr_vllm.agent.qwen_tts_paged_attention import paged_attention_decode
+
+    arrays = {}
+    # -- the reference test's inputs, rebuilt exactly as its _inputs() does
+    page_table = torch.tensor([[3, 5, 0], [1, 7, 2]], dtype=torch.long)
+    seq_lens = torch.tensor([3, 5], dtype=torch.long)
+    valid = torch.tensor([[True, True, True, False, False], [False, True, True, True, True]])
+    k_pool = torch.zeros((8, 2, 2, 4), dtype=torch.float32)
+    v_pool = torch.zeros_like(k_pool)
+    torch.manual_seed(17)
+    for page in (3, 5, 1, 7, 2):
+        k_pool[page].normal_()
+        v_pool[page].normal_()
+    q = torch.ones((2, 4, 1, 4), dtype=torch.float32)
+    g = torch.Generator().manual_seed(18)
+    new_k = torch.randn((2, 2, 1, 4), generator=g)
+    new_v = torch.randn((2, 2, 1, 4), generator=g)
+    plain = paged_attention_decode(q, k_pool, v_pool, page_table, seq_lens, valid,
+                                   use_triton=False)
+    kw, vw = k_pool.clone(), v_pool.clone()
+    fused = paged_attention_decode(q, kw, vw, page_table, seq_lens, valid, new_key=new_k,
+                                   new_value=new_v, use_triton=False)
+    arrays.update(ref_q=q.numpy(), ref_k_pool=k_pool.numpy(), ref_v_pool=v_pool.numpy(),
+                  ref_page_table=page_table.numpy(), ref_seq_lens=seq_lens.numpy(),
+                  ref_valid=valid.numpy(), ref_new_k=new_k.numpy(), ref_new_v=new_v.numpy(),
+                  ref_out=plain.numpy(), ref_out_fused=fused.numpy(),
+                  ref_k_pool_after=kw.numpy(), ref_v_pool_after=vw.numpy())
+
+    # -- talker-shaped cases
+    cases = {
+        "talker_g2": dict(hq=16, hkv=8, ps=16, lens=[1, 15, 16, 17, 40, 70], seed=31),
+        "talker_g4": dict(hq=8, hkv=2, ps=24, lens=[3, 24, 25, 200], seed=32),
+    }
+    for name, c in cases.items():
+        g = torch.Generator().manual_seed(c["seed"])
+        lens = torch.tensor(c["lens"], dtype=torch.long)
+        b, hq, hkv, ps, d = len(c["lens"]), c["hq"], c["hkv"], c["ps"], 128
+        need = [(n + ps - 1) // ps for n in c["lens"]]
+        pages = sum(need) + 1
+        kp = (torch.randn(pages, hkv, ps, d, generator=g) / d**0.5).bfloat16()
+        vp = (torch.randn(pages, hkv, ps, d, generator=g) / d**0.5).bfloat16()
+        q = (torch.randn(b, hq, 1, d, generator=g)).bfloat16()
+        nk = (torch.randn(b, hkv, 1, d, generator=g) / d**0.5).bfloat16()
+        nv = (torch.randn(b, hkv, 1, d, generator=g) / d**0.5).bfloat16()
+        perm = torch.randperm(pages, generator=g)
+        width = max(need) + 1
+        table = torch.full((b, width), -1, dtype=torch.long)
+        cursor = 0
+        for row, n in enumerate(need):
+            table[row, :n] = perm[cursor:cursor + n]
+            cursor += n
+        mask = torch.ones(b, max(c["lens"]), dtype=torch.bool)
+        mask[1, :2] = False          # left padding
+        mask[-1, :9] = False
+        mask[-1, 20] = False
+        kw, vw = kp.float(), vp.float()
+        res = paged_attention_decode(q.float(), kw, vw, table, lens, mask, new_key=nk.float(),
+                                     new_value=nv.float(), use_triton=False)
+        arrays.update({f"{name}_q": _bf16_bits(q), f"{name}_k_pool": _bf16_bits(kp),
+                       f"{name}_v_pool": _bf16_bits(vp), f"{name}_new_k": _bf16_bits(nk),
+                       f"{name}_new_v": _bf16_bits(nv), f"{name}_page_table": table.numpy(),
+                       f"{name}_seq_lens": lens.numpy(), f"{name}_valid": mask.numpy(),
+                       f"{name}_out": _f32(res)})
+    np.savez_compressed(out / "tts_pool_decode.npz", **arrays)
+
+
 def gen_norm_rope(out: Path):
     import torch
     from qwen_asr_vllm.layers.layernorm import RMSNorm
@@ -548,6 +630,7 @@ GENERATORS = {
     "block_manager": gen_block_manager,
     "store": gen_store,
     "paged_decode": gen_paged_decode,
+    "tts_pool_decode": gen_tts_pool_decode,
     "norm_rope": gen_norm_rope,
     "elementwise": gen_elementwise,
     "sampler": gen_sampler,

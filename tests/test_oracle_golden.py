@@ -128,6 +128,56 @@ def test_paged_decode_matches_reference_torch_path():
     np.testing.assert_allclose(got, g["out_reference"], atol=2e-5, rtol=1e-4)
 
 
+def test_pool_decode_matches_reference_test_inputs():
+    """The reference test's own case (fp32, head_dim 4, page 2, left-padded mask), with
+    and without the fused current-token write."""
+    g = load_npz("tts_pool_decode.npz")
+    args = (g["ref_q"], g["ref_k_pool"].copy(), g["ref_v_pool"].copy(), g["ref_page_table"],
+            g["ref_seq_lens"], 0.5)
+    got = K.pool_paged_attention(*args, key_valid_mask=g["ref_valid"])
+    np.testing.assert_allclose(got, g["ref_out"], atol=1e-6, rtol=1e-5)
+    kp, vp = g["ref_k_pool"].copy(), g["ref_v_pool"].copy()
+    got = K.pool_paged_attention(g["ref_q"], kp, vp, g["ref_page_table"], g["ref_seq_lens"], 0.5,
+                                 key_valid_mask=g["ref_valid"], new_key=g["ref_new_k"],
+                                 new_value=g["ref_new_v"])
+    np.testing.assert_allclose(got, g["ref_out_fused"], atol=1e-6, rtol=1e-5)
+    np.testing.assert_array_equal(kp, g["ref_k_pool_after"])
+    np.testing.assert_array_equal(vp, g["ref_v_pool_after"])
+
+
+@pytest.mark.parametrize("case", ["talker_g2", "talker_g4"])
+def test_pool_decode_matches_reference_talker_cases(case):
+    g = load_npz("tts_pool_decode.npz")
+    f = {k[len(case) + 1:]: v for k, v in g.items() if k.startswith(case + "_")}
+    bf = {k: bf16_bits_to_f32(f[k]) for k in ("q", "k_pool", "v_pool", "new_k", "new_v")}
+    got = K.pool_paged_attention(bf["q"], bf["k_pool"].copy(), bf["v_pool"].copy(),
+                                 f["page_table"], f["seq_lens"], 128 ** -0.5,
+                                 key_valid_mask=f["valid"], new_key=bf["new_k"],
+                                 new_value=bf["new_v"])
+    np.testing.assert_allclose(got, f["out"], atol=2e-5, rtol=1e-4)
+
+
+def test_pool_decode_edge_semantics():
+    """Fully masked rows give zeros (the reference kernel's guard); kernel_seq_len bounds
+    the attended positions as the reference kernel's loop does; mask columns beyond the
+    mask's width are valid."""
+    rng = np.random.default_rng(3)
+    kp = rng.standard_normal((4, 1, 2, 8)).astype(np.float32)
+    vp = rng.standard_normal((4, 1, 2, 8)).astype(np.float32)
+    q = rng.standard_normal((1, 2, 1, 8)).astype(np.float32)
+    table = np.array([[2, 0, 3]])
+    mask = np.zeros((1, 6), dtype=bool)
+    assert not K.pool_paged_attention(q, kp, vp, table, [5], 0.3, key_valid_mask=mask).any()
+    short = K.pool_paged_attention(q, kp, vp, table, [5], 0.3, kernel_seq_len=3)
+    np.testing.assert_allclose(short, K.pool_paged_attention(q, kp, vp, table, [3], 0.3))
+    narrow = np.array([[False, True]])
+    full = np.array([[False, True, True, True, True]])
+    np.testing.assert_allclose(K.pool_paged_attention(q, kp, vp, table, [5], 0.3,
+                                                      key_valid_mask=narrow),
+                               K.pool_paged_attention(q, kp, vp, table, [5], 0.3,
+                                                      key_valid_mask=full))
+
+
 def test_paged_prefill_is_bottom_right_causal():
     """A request prefilled in one pass equals the same request decoded one token at a
     time -- the property FlashAttention's bottom-right alignment provides."""

@@ -70,6 +70,13 @@ SIGNATURES: dict[str, tuple] = {
     "b200asr_varlen_attention": (c_int32, [P, c_int64, P, c_int64, P, c_int64, P, c_int32,
                                            c_int32, c_int32, c_int32, c_int32, c_float, P,
                                            c_int64, P, P]),
+    "b200asr_pool_paged_decode_workspace_size": (c_size_t, [c_int32, c_int32, c_int32, c_int32]),
+    "b200asr_pool_paged_decode": (c_int32, [c_int32, c_int32, c_int32, c_int32, c_int32,
+                                            P, c_int64, c_int64, P, P, c_int32, c_int32,
+                                            c_int64, c_int64, c_int64, P, c_int64, c_int32,
+                                            P, P, c_int64, c_int32, P, P, c_int64, c_int64,
+                                            P, c_int64, c_int64, c_int32, c_int32, c_float,
+                                            P, c_size_t, P, P]),
     "b200asr_greedy_argmax": (c_int32, [P, c_int64, c_int32, c_int32, P, P]),
 }
 

@@ -517,7 +517,7 @@ extern "C" int b200asr_paged_prefill(const void *q, int64_t q_row_stride, const 
     if (rc) return rc;
     configured = true;
   }
-  PrefillArgs a;
+  PrefillArgs a{};
   a.cu_seqlens_q = cu_seqlens_q;
   a.cu_seqlens_k = cu_seqlens_k;
   a.block_tables = block_tables;
@@ -567,7 +567,7 @@ extern "C" int b200asr_varlen_attention(const void *q, int64_t q_row_stride, con
     if (rc) return rc;
     configured = true;
   }
-  WindowArgs a;
+  WindowArgs a{};
   a.cu_seqlens = cu_seqlens;
   a.num_segments = num_segments;
   a.scale_log2 = scale * kTcLog2e;

@@ -193,7 +193,7 @@ extern "C" int b200asr_log_mel(const float *waveform, const int64_t *cu_samples,
   }
   B200_REQUIRE((reinterpret_cast<uintptr_t>(workspace) & (kMelMaxAlign - 1)) == 0,
                "log_mel: workspace must be 256-byte aligned");
-  MelArgs a;
+  MelArgs a{};
   a.wave = waveform;
   a.cu_samples = cu_samples;
   a.frame_start = frame_start;

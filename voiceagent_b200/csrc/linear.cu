@@ -818,7 +818,7 @@ bool valid_weight_rows(int n, int silu_inner, int *tiles) {
 
 LinearArgs make_args(int m, int k_split, int silu_inner, void *y, int64_t y_stride,
                      int32_t *error_flag) {
-  LinearArgs a;
+  LinearArgs a{};
   a.m = m;
   a.steps = 0;
   a.k_split = k_split;

@@ -1069,7 +1069,7 @@ extern "C" int b200asr_paged_decode(const void *q, int64_t q_row_stride, const v
     set_error("paged_decode: workspace %zu bytes < %zu needed", workspace_bytes, need);
     return B200ASR_ERR_WORKSPACE;
   }
-  DecodeArgs a;
+  DecodeArgs a{};
   a.q = static_cast<const __nv_bfloat16 *>(q);
   a.q_stride = q_row_stride;
   a.num_blocks = num_blocks;

@@ -223,6 +223,75 @@ def paged_decode(q, k_cache, v_cache, cu_seqlens_k, block_tables, *, max_seqlen_
     return out
 
 
+_POOL_DTYPES = {torch.bfloat16: 0, torch.float16: 1, torch.float32: 2}
+_POOL_WORKSPACE: dict[int, torch.Tensor] = {}
+
+
+def pool_decode_workspace(batch: int, num_heads: int, head_dim: int, max_seq_len: int,
+                          device) -> torch.Tensor:
+    """A zero-filled workspace for :func:`pool_paged_decode`, cached per device and grown
+    on demand (allocate it before capturing a CUDA graph that uses it)."""
+    need = lib.b200asr_pool_paged_decode_workspace_size(batch, num_heads, head_dim, max_seq_len)
+    dev = torch.device(device).index or 0
+    ws = _POOL_WORKSPACE.get(dev)
+    if ws is None or ws.numel() < need:
+        ws = torch.zeros(max(need, 1 << 20), dtype=torch.uint8, device=device)
+        _POOL_WORKSPACE[dev] = ws
+    return ws
+
+
+def pool_paged_decode(query, key_pool, value_pool, page_table, seq_lens, *, max_seq_len: int,
+                      scale: float, out=None, key_valid_mask=None, new_key=None, new_value=None,
+                      tokens_per_cta: int = 0, workspace=None, error_flag=None) -> torch.Tensor:
+    """One-token decode over a page pool ``[pages, H_kv, page_size, D]`` with the fused
+    current-token write (agent/qwen_tts_paged_attention.py:130-287, 383-532).
+
+    query/out ``[B, H, 1, D]`` (any strides with a unit last one), page_table/seq_lens
+    int64, key_valid_mask bool ``[B, >= 0]``, new_key/new_value ``[B, H_kv, 1, D]`` or
+    None. The pools are updated in place when new K/V are given."""
+    _cuda(query, key_pool, value_pool, page_table, seq_lens, key_valid_mask, new_key, new_value)
+    batch, num_heads, _, head_dim = query.shape
+    num_pages, num_kv_heads, page_size, _ = key_pool.shape
+    dtype = _POOL_DTYPES.get(query.dtype)
+    _need(dtype is not None, "pool_paged_decode: bf16, fp16 or fp32 tensors")
+    _need(key_pool.dtype == query.dtype and value_pool.dtype == query.dtype,
+          "pool_paged_decode: query and pools must share a dtype")
+    _need(key_pool.stride() == value_pool.stride(), "pool_paged_decode: pools must share strides")
+    _need(query.stride(-1) == 1 and key_pool.stride(-1) == 1, "pool_paged_decode: unit head_dim stride")
+    _need(page_table.dtype == torch.int64 and seq_lens.dtype == torch.int64,
+          "pool_paged_decode: int64 page table and lengths")
+    if page_table.stride(-1) != 1:
+        page_table = page_table.contiguous()
+    if out is None:
+        out = torch.empty_like(query)
+    valid_stride = valid_len = 0
+    if key_valid_mask is not None:
+        _need(key_valid_mask.dtype in (torch.bool, torch.uint8) and key_valid_mask.dim() == 2,
+              "pool_paged_decode: key_valid_mask [B, L] bool")
+        if key_valid_mask.stride(-1) != 1:
+            key_valid_mask = key_valid_mask.contiguous()
+        valid_stride, valid_len = key_valid_mask.stride(0), key_valid_mask.shape[1]
+    new_sb = new_sh = 0
+    if new_key is not None:
+        _need(new_value is not None and new_key.stride() == new_value.stride()
+              and new_key.dtype == query.dtype and new_key.stride(-1) == 1,
+              "pool_paged_decode: new_key/new_value must match (dtype, strides)")
+        new_sb, new_sh = new_key.stride(0), new_key.stride(1)
+    if workspace is None:
+        workspace = pool_decode_workspace(batch, num_heads, head_dim, max_seq_len, query.device)
+    _count()
+    check(lib.b200asr_pool_paged_decode(
+        dtype, batch, num_heads, num_kv_heads, head_dim, _p(query), query.stride(0),
+        query.stride(1), _p(key_pool), _p(value_pool), num_pages, page_size, key_pool.stride(0),
+        key_pool.stride(1), key_pool.stride(2), _p(page_table), page_table.stride(0),
+        page_table.shape[1], _p(seq_lens), _p(key_valid_mask), valid_stride, valid_len,
+        _p(new_key), _p(new_value), new_sb, new_sh, _p(out), out.stride(0), out.stride(1),
+        int(max_seq_len), int(tokens_per_cta), float(scale), _p(workspace),
+        workspace.numel() * workspace.element_size(), _p(error_flag), _stream()),
+        "pool_paged_decode")
+    return out
+
+
 def paged_prefill(q, k_cache, v_cache, cu_seqlens_q, cu_seqlens_k, block_tables, *,
                   max_seqlen_q: int, scale: float, out, error_flag=None) -> torch.Tensor:
     """Varlen causal GQA over the paged cache on tcgen05 (layers/attention.py:96-107)."""

@@ -131,6 +131,90 @@ def decode_config1(iters: int = 64, sets: int = 4, lo: int = 64, hi: int = 1024,
                                               if pdl else ""))
 
 
+def _reference_tts_module():
+    """The reference's TTS paged attention module from its installed copy (baseline/_ref),
+    or None when it or Triton is unavailable."""
+    import sys
+
+    ref = REPO / "baseline" / "_ref"
+    if not (ref / "qwen_asr_vllm").is_dir():
+        return None
+    sys.path.insert(0, str(ref))
+    try:
+        from qwen_asr_vllm.agent import qwen_tts_paged_attention as m
+    except Exception:  # noqa: BLE001 - the comparison arm is optional
+        return None
+    finally:
+        sys.path.remove(str(ref))
+    return m if getattr(m, "HAS_TRITON", False) else None
+
+
+def tts_pool_decode(iters: int = 64, sets: int = 4, lo: int = 64, hi: int = 1024,
+                    page: int = 16) -> list[dict]:
+    """TTS talker decode over a page pool [pages, H_kv, page, D] (the reference's default
+    page of 16 tokens), config-1 geometry and lengths: B = 32, H 16 / H_kv 8, d 128, ctx ~
+    U[64, 1024], a 2 GiB pool per K/V, page tables slices of a random permutation, with
+    the fused current-token write and an all-true key-valid mask as QwenPagedCache passes
+    them (agent/qwen_tts_outer_varlen.py:392-436). Both this library's kernel and, when
+    its installed copy imports, the reference's Triton kernel on the same inputs."""
+    dev = torch.device("cuda")
+    rng = np.random.default_rng(0)
+    b, h, hkv, d = 32, 16, 8, 128
+    pages = 4096 * 256 // page
+    lens = rng.integers(lo, hi + 1, size=b)
+    need = (lens + page - 1) // page
+    gen = torch.Generator(device=dev).manual_seed(0)
+    kp = (torch.randn(pages, hkv, page, d, device=dev, generator=gen) / d ** 0.5).bfloat16()
+    vp = (torch.randn(pages, hkv, page, d, device=dev, generator=gen) / d ** 0.5).bfloat16()
+    q = (torch.randn(b, h, 1, d, device=dev, generator=gen) / d ** 0.5).bfloat16()
+    nk = (torch.randn(b, hkv, 1, d, device=dev, generator=gen) / d ** 0.5).bfloat16()
+    nv = (torch.randn(b, hkv, 1, d, device=dev, generator=gen) / d ** 0.5).bfloat16()
+    perm = rng.permutation(pages)
+    width = -(-hi // page)
+    tables = []
+    for k in range(sets):
+        t = np.full((b, width), -1, np.int64)
+        c = k * int(need.sum())
+        for i, n in enumerate(need):
+            t[i, :n] = perm[c:c + n]
+            c += int(n)
+        tables.append(torch.from_numpy(t).to(dev))
+    seq = torch.from_numpy(lens.astype(np.int64)).to(dev)
+    max_len = -(-hi // 128) * 128
+    valid = torch.ones(b, max_len, dtype=torch.bool, device=dev)
+    out = torch.empty_like(q)
+    ws = kx.pool_decode_workspace(b, h, d, max_len, dev)
+    sumctx = int(lens.sum())
+    algo = (sumctx * hkv * d * 2 * 2 + 2 * b * h * d * 2 + 2 * b * hkv * d * 2
+            + 8 * int(need.sum()) + 8 * b + b * max_len)
+    cfg = f"talker B=32 ctx~U[{lo},{hi}] Hq16/Hkv8 d128 page {page} (+ current-token write)"
+    timing = (f"graph of {iters} launches over {sets} rotating page-table sets of "
+              f"{algo / 1e6:.0f} MB each (together > L2)")
+
+    def mine(i):
+        return lambda: kx.pool_paged_decode(q, kp, vp, tables[i % sets], seq, max_seq_len=max_len,
+                                            scale=d ** -0.5, out=out, key_valid_mask=valid,
+                                            new_key=nk, new_value=nv, workspace=ws)
+
+    lines = [_line("pool_paged_decode", cfg, graph_time_us([mine(i) for i in range(iters)]), algo,
+                   sum_ctx=sumctx, timing=timing)]
+    m = _reference_tts_module()
+    if m is not None:
+        def theirs(i):
+            return lambda: m.paged_attention_decode(
+                q, kp, vp, tables[i % sets], seq, valid, new_key=nk, new_value=nv,
+                kernel_seq_len=max_len, kernel_page_count=width, scale=d ** -0.5,
+                use_triton=True, validate=False)
+
+        lines.append(_line("reference _paged_decode_attention_kernel (Triton)", cfg,
+                           graph_time_us([theirs(i) for i in range(iters)]), algo,
+                           sum_ctx=sumctx, timing=timing + "; block_n 128, num_warps 4 "
+                                                           "(QwenPagedCache defaults)"))
+    del kp, vp
+    torch.cuda.empty_cache()
+    return lines
+
+
 # ------------------------------------------------------------------ config 2
 
 
@@ -440,6 +524,7 @@ BENCHES = {
     "linear": lambda: linear_decode(32),
     "argmax": lambda: [argmax_rows(32)],
     "log_mel": lambda: [log_mel_config3()],
+    "tts_decode": lambda: tts_pool_decode(),
 }
 
 
