@@ -50,6 +50,7 @@ struct PoolArgs {
   int64_t o_sb, o_sh;
   int32_t num_kv_heads, head_dim, nvr, lpt_log2;
   int32_t max_seq_len, chunk, max_splits;
+  int32_t pages_cap;  // page-offset slots staged per CTA (chunk / page_size + 2)
   float scale_log2;
   int *counters;
   float *ws;
@@ -125,7 +126,8 @@ __global__ void __launch_bounds__(kPoolThreads) pool_decode_kernel(const PoolArg
   constexpr int E = V::E;
   // tokens in flight per lane group and step (fewer where the accumulators are large)
   constexpr int U = G * NPL <= 2 ? 4 : (G * NPL <= 8 ? 2 : 1);
-  extern __shared__ float s_red[];   // [kPoolWarps][G][head_dim + 2]
+  // [kPoolWarps][G][head_dim + 2] merge rows | int64 [pages_cap] page offsets | u8 [chunk]
+  extern __shared__ float s_red[];
   __shared__ int s_last;
 
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
@@ -201,37 +203,71 @@ __global__ void __launch_bounds__(kPoolThreads) pool_decode_kernel(const PoolArg
 
   const int t0 = split * a.chunk;
   const int t1 = min(L, t0 + a.chunk);
+
+  // Stage this chunk's page offsets (element offset of the page plus the KV head, or -1
+  // for a page outside the table or the pool) and per-position attend bytes in shared
+  // memory, so the per-token addresses below need no global round trip and a step's
+  // loads can all be in flight at once.
+  int64_t *s_off = reinterpret_cast<int64_t *>(s_red + kPoolWarps * G * rowf);
+  uint8_t *s_ok = reinterpret_cast<uint8_t *>(s_off + a.pages_cap);
+  const int p0 = a.page_shift >= 0 ? (t0 >> a.page_shift) : t0 / a.page_size;
+  if (t1 > t0) {
+    const int p_last = a.page_shift >= 0 ? ((t1 - 1) >> a.page_shift) : (t1 - 1) / a.page_size;
+    for (int i = tid; i <= p_last - p0; i += kPoolThreads) {
+      const int pi = p0 + i;
+      int64_t off = -1;
+      if (pi < a.table_width) {
+        const int64_t page = __ldg(a.table + b * a.table_stride + pi);
+        if (page >= 0 && page < a.num_pages) off = page * a.sp + head_off;
+      }
+      s_off[i] = off;
+    }
+    for (int i = tid; i < t1 - t0; i += kPoolThreads) {
+      const int t = t0 + i;
+      s_ok[i] = (a.valid != nullptr && t < a.valid_len)
+                    ? static_cast<uint8_t>(__ldg(a.valid + b * a.valid_stride + t) != 0)
+                    : static_cast<uint8_t>(1);
+    }
+  }
+  __syncthreads();
+
   const int step = kPoolWarps * tpw;
   for (int base = t0 + warp * tpw; base < t1; base += U * step) {  // warp-uniform bound
-    uint4 kr[U][NPL], vr[U][NPL];
+    // addresses of this step's U tokens (shared-memory lookups only) ...
+    const T *kptr[U], *vptr[U];
     bool ok[U];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const int t = base + u * step + slot;
-      ok[u] = t < t1;
-      if (ok[u] && a.valid != nullptr && t < a.valid_len)
-        ok[u] = __ldg(a.valid + b * a.valid_stride + t) != 0;
-      const T *ks = nullptr, *vs = nullptr;
-      if (ok[u]) {
-        if (has_new && t == pos_new) {
-          ks = nk + new_off;
-          vs = nv + new_off;
+      ok[u] = t < t1 && s_ok[t - t0] != 0;
+      kptr[u] = nk;
+      vptr[u] = nv;
+      if (ok[u] && !(has_new && t == pos_new)) {
+        const int pi = a.page_shift >= 0 ? (t >> a.page_shift) : t / a.page_size;
+        const int64_t off = s_off[pi - p0];
+        if (off < 0) {
+          raise_flag(a.error_flag, B200ASR_DEVERR_BLOCK);
+          ok[u] = false;
         } else {
-          const int64_t off = pool_offset(a, b, t);
-          if (off >= 0) {
-            ks = kp + off + head_off;
-            vs = vp + off + head_off;
-          } else {
-            ok[u] = false;
-          }
+          const int64_t row = off + static_cast<int64_t>(t - pi * a.page_size) * a.ss;
+          kptr[u] = kp + row;
+          vptr[u] = vp + row;
         }
+      } else if (ok[u]) {
+        kptr[u] = nk + new_off;
+        vptr[u] = nv + new_off;
       }
+    }
+    // ... then all of their loads back to back
+    uint4 kr[U][NPL], vr[U][NPL];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
 #pragma unroll
       for (int j = 0; j < NPL; ++j) {
         const int v = sub + j * lpt;
         if (ok[u] && v < a.nvr) {
-          kr[u][j] = ld_stream16(ks + v * E);
-          vr[u][j] = ld_stream16(vs + v * E);
+          kr[u][j] = ld_stream16(kptr[u] + v * E);
+          vr[u][j] = ld_stream16(vptr[u] + v * E);
         } else {
           kr[u][j] = make_uint4(0, 0, 0, 0);
           vr[u][j] = make_uint4(0, 0, 0, 0);
@@ -413,6 +449,13 @@ int num_sms_pool() {
 
 size_t header_bytes(int64_t pairs) { return static_cast<size_t>((pairs * 4 + 255) / 256 * 256); }
 
+constexpr size_t kPoolSmemLimit = 48 * 1024;
+
+// Shared memory a CTA stages for `chunk` positions: page offsets and attend bytes.
+size_t pool_stage_bytes(int64_t chunk, int page_size) {
+  return static_cast<size_t>((chunk / page_size + 2) * 8 + (chunk + 15) / 16 * 16);
+}
+
 template <typename T, int G, int NPL>
 int launch_pool(const PoolArgs &a, int batch, size_t smem, cudaStream_t stream) {
   auto kernel = pool_decode_kernel<T, G, NPL>;
@@ -482,8 +525,8 @@ extern "C" int b200asr_pool_paged_decode(
               head_dim, esz);
     return B200ASR_ERR_UNSUPPORTED;
   }
-  const size_t smem = static_cast<size_t>(kPoolWarps) * g * (head_dim + 2) * sizeof(float);
-  if (smem > 48 * 1024) {
+  const size_t red_bytes = static_cast<size_t>(kPoolWarps) * g * (head_dim + 2) * sizeof(float);
+  if (red_bytes + pool_stage_bytes(kPoolMinChunk, page_size) > kPoolSmemLimit) {
     set_error("pool_paged_decode: group %d x head_dim %d too large", g, head_dim);
     return B200ASR_ERR_UNSUPPORTED;
   }
@@ -551,15 +594,21 @@ extern "C" int b200asr_pool_paged_decode(
   const int step = kPoolWarps * (32 >> lg);
   int64_t chunk = tokens_per_cta;
   if (chunk == 0) {
-    // Enough chunks for ~8 CTAs per SM at the longest row, at least kPoolMinChunk tokens.
-    const int64_t target = static_cast<int64_t>(num_sms_pool()) * 8;
+    // ~6 CTAs per SM at the longest row (the talker shape, B = 32 x 8 KV heads at 1024
+    // positions, measured fastest at 256-384 positions per CTA), at least kPoolMinChunk.
+    const int64_t target = static_cast<int64_t>(num_sms_pool()) * 6;
     const int64_t work = static_cast<int64_t>(batch) * num_kv_heads * max_seq_len;
     chunk = (work + target - 1) / target;
     if (chunk < kPoolMinChunk) chunk = kPoolMinChunk;
     chunk = (chunk + step - 1) / step * step;
   }
   if (chunk > max_seq_len) chunk = max_seq_len;
+  // the staged page offsets and attend bytes must fit next to the merge rows
+  while (chunk > kPoolMinChunk && red_bytes + pool_stage_bytes(chunk, page_size) > kPoolSmemLimit)
+    chunk = chunk / 2 > kPoolMinChunk ? chunk / 2 : kPoolMinChunk;
   a.chunk = static_cast<int32_t>(chunk);
+  a.pages_cap = static_cast<int32_t>(chunk / page_size + 2);
+  const size_t smem = red_bytes + pool_stage_bytes(chunk, page_size);
   a.max_splits = static_cast<int32_t>((max_seq_len + chunk - 1) / chunk);
   a.scale_log2 = scale * 1.4426950408889634f;
   a.counters = static_cast<int *>(workspace);
