@@ -331,9 +331,11 @@ def run_reference_engine(args) -> None:
             "ms_per_step": 1000.0 * sec_max / args.steps, "higher_is_better": True,
             "scaling": "weak", "dtype": "bf16",
             "data": "synthetic (seeded noise + sines; random-init weights, seed 0)",
-            "config": {"workload": "config3 through qwen_asr_vllm.AsrEngine.transcribe "
-                                   "(flash-attn + Triton, CUDA-graph decode), wall clock, "
-                                   "max over ranks", "clips_per_step": args.clips_per_step,
+            "config": {"workload": f"{'config3' if args.preset == '0.6b' else 'config4'} "
+                                   f"(Qwen3-ASR-{args.preset.upper()}) through "
+                                   "qwen_asr_vllm.AsrEngine.transcribe (flash-attn + Triton, "
+                                   "CUDA-graph decode), wall clock, max over ranks",
+                       "preset": args.preset, "clips_per_step": args.clips_per_step,
                        "concurrency": args.concurrency, "output_tokens": toks},
         }), flush=True)
     dist.close()
@@ -462,14 +464,18 @@ def run_ours(args) -> None:
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded noise + sines; random-init weights, seed 0)",
             "config": {
-                "workload": "config3: Qwen3-ASR-0.6B bf16 random-init, max_num_seqs=32, "
+                "workload": f"{'config3' if args.preset == '0.6b' else 'config4'}: "
+                            f"Qwen3-ASR-{args.preset.upper()} bf16 random-init, "
+                            f"max_num_seqs={args.concurrency}, "
                             f"{args.clips} clips/GPU lognormal(7 s, 0.6) in [1, 35] s, "
                             f"{args.decode_tokens} greedy tokens, CUDA-graph decode",
+                "preset": args.preset,
                 "clips_per_step": args.clips_per_step, "concurrency": args.concurrency,
                 "audio_seconds_per_gpu": float(sum(durations[j] for i in range(args.steps)
                                                    for j in step_slice(i))),
                 "parallelism": f"dp{world} (independent replicas)",
-                "l2": "inputs larger than L2 (1.2 GB of weights streamed per decode step)",
+                "l2": "inputs larger than L2 (the decoder's weights, 1.2 GB for 0.6B and "
+                      "3.4 GB for 1.7B, stream through every decode step)",
                 "timing": "CUDA events on the engine stream, max over ranks",
             },
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"],

@@ -232,10 +232,11 @@ def pool_decode_workspace(batch: int, num_heads: int, head_dim: int, max_seq_len
     """A zero-filled workspace for :func:`pool_paged_decode`, cached per device and grown
     on demand (allocate it before capturing a CUDA graph that uses it)."""
     need = lib.b200asr_pool_paged_decode_workspace_size(batch, num_heads, head_dim, max_seq_len)
-    dev = torch.device(device).index or 0
+    device = torch.device(device)
+    dev = device.index if device.index is not None else torch.cuda.current_device()
     ws = _POOL_WORKSPACE.get(dev)
     if ws is None or ws.numel() < need:
-        ws = torch.zeros(max(need, 1 << 20), dtype=torch.uint8, device=device)
+        ws = torch.zeros(max(need, 1 << 20), dtype=torch.uint8, device=torch.device("cuda", dev))
         _POOL_WORKSPACE[dev] = ws
     return ws
 
