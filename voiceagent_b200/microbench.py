@@ -150,7 +150,8 @@ def _reference_tts_module():
 
 
 def tts_pool_decode(iters: int = 64, sets: int = 4, lo: int = 64, hi: int = 1024,
-                    page: int = 16) -> list[dict]:
+                    page: int = 16, pool_tokens: int = 4096 * 256,
+                    reference: bool = True) -> list[dict]:
     """TTS talker decode over a page pool [pages, H_kv, page, D] (the reference's default
     page of 16 tokens), config-1 geometry and lengths: B = 32, H 16 / H_kv 8, d 128, ctx ~
     U[64, 1024], a 2 GiB pool per K/V, page tables slices of a random permutation, with
@@ -160,7 +161,7 @@ def tts_pool_decode(iters: int = 64, sets: int = 4, lo: int = 64, hi: int = 1024
     dev = torch.device("cuda")
     rng = np.random.default_rng(0)
     b, h, hkv, d = 32, 16, 8, 128
-    pages = 4096 * 256 // page
+    pages = pool_tokens // page
     lens = rng.integers(lo, hi + 1, size=b)
     need = (lens + page - 1) // page
     gen = torch.Generator(device=dev).manual_seed(0)
@@ -198,7 +199,7 @@ def tts_pool_decode(iters: int = 64, sets: int = 4, lo: int = 64, hi: int = 1024
 
     lines = [_line("pool_paged_decode", cfg, graph_time_us([mine(i) for i in range(iters)]), algo,
                    sum_ctx=sumctx, timing=timing)]
-    m = _reference_tts_module()
+    m = _reference_tts_module() if reference else None
     if m is not None:
         def theirs(i):
             return lambda: m.paged_attention_decode(
@@ -525,6 +526,9 @@ BENCHES = {
     "argmax": lambda: [argmax_rows(32)],
     "log_mel": lambda: [log_mel_config3()],
     "tts_decode": lambda: tts_pool_decode(),
+    # a 256 MB pool and four launches: the size for an ncu capture of one launch
+    "tts_decode_profile": lambda: tts_pool_decode(iters=4, sets=1, pool_tokens=131072,
+                                                  reference=False),
 }
 
 
