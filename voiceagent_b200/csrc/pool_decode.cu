@@ -594,9 +594,10 @@ extern "C" int b200asr_pool_paged_decode(
   const int step = kPoolWarps * (32 >> lg);
   int64_t chunk = tokens_per_cta;
   if (chunk == 0) {
-    // ~6 CTAs per SM at the longest row (the talker shape, B = 32 x 8 KV heads at 1024
-    // positions, measured fastest at 256-384 positions per CTA), at least kPoolMinChunk.
-    const int64_t target = static_cast<int64_t>(num_sms_pool()) * 6;
+    // ~7 CTAs per SM at the longest row: 256 positions per CTA for the talker shape
+    // (B = 32 x 8 KV heads at 1024 positions), the fastest measured there; at least
+    // kPoolMinChunk.
+    const int64_t target = static_cast<int64_t>(num_sms_pool()) * 7;
     const int64_t work = static_cast<int64_t>(batch) * num_kv_heads * max_seq_len;
     chunk = (work + target - 1) / target;
     if (chunk < kPoolMinChunk) chunk = kPoolMinChunk;
