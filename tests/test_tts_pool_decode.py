@@ -252,6 +252,26 @@ def test_sweep_against_oracle(dtype, hq, hkv, d, ps, lens, mask, tpc):
 
 
 @pytest.mark.gpu
+def test_strided_lengths_and_table_views():
+    """Lengths and page tables handed over as strided views (as sliced metadata would be)."""
+    from voiceagent_b200 import kernels as kx
+
+    rng = np.random.default_rng(7)
+    c = _random_case(rng, batch=3, hq=16, hkv=8, d=128, ps=16, lens=[5, 300, 77],
+                     dtype=torch.bfloat16)
+    t = {k: torch.from_numpy(c[k]).bfloat16().cuda() for k in ("q", "kp", "vp")}
+    lens2 = torch.from_numpy(np.stack([c["lens"], c["lens"] * 0 + 9], 1)).cuda()[:, 0]
+    wide = np.full((3, c["table"].shape[1] * 2), -1, np.int64)
+    wide[:, ::2] = c["table"]
+    table2 = torch.from_numpy(wide).cuda()[:, ::2]
+    assert lens2.stride(0) != 1 and table2.stride(-1) != 1
+    out = kx.pool_paged_decode(t["q"], t["kp"], t["vp"], table2, lens2, max_seq_len=300,
+                               scale=0.1)
+    want = K.pool_paged_attention(c["q"], c["kp"], c["vp"], c["table"], c["lens"], 0.1)
+    _assert_close(out.float().cpu().numpy(), want, "strided views")
+
+
+@pytest.mark.gpu
 def test_truncation_flags_and_bad_pages():
     """kernel_seq_len below a length attends the first kernel_seq_len positions (the
     reference kernel's loop bound) and raises LENGTH; a page outside the pool is skipped

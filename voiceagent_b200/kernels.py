@@ -263,6 +263,8 @@ def pool_paged_decode(query, key_pool, value_pool, page_table, seq_lens, *, max_
           "pool_paged_decode: int64 page table and lengths")
     if page_table.stride(-1) != 1:
         page_table = page_table.contiguous()
+    if seq_lens.stride(0) != 1:  # the kernel reads lengths as a dense vector
+        seq_lens = seq_lens.contiguous()
     if out is None:
         out = torch.empty_like(query)
     valid_stride = valid_len = 0
