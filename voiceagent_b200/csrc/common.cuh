@@ -54,6 +54,7 @@ inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 
 // memory, tensor maps, TMEM and loads of static data (weights). Without the attribute
 // both instructions are no-ops.
 bool pdl_enabled();  // defined in capi.cu
+int num_sms();       // SMs of the current device (defined in paged_decode.cu)
 
 template <typename... KArgs, typename... Args>
 cudaError_t launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,

@@ -436,16 +436,6 @@ __global__ void __launch_bounds__(kPoolThreads) pool_decode_kernel(const PoolArg
   }
 }
 
-int num_sms_pool() {
-  static int sms = 0;
-  if (sms == 0) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if (sms <= 0) sms = 148;
-  }
-  return sms;
-}
 
 size_t header_bytes(int64_t pairs) { return static_cast<size_t>((pairs * 4 + 255) / 256 * 256); }
 
@@ -597,7 +587,7 @@ extern "C" int b200asr_pool_paged_decode(
     // ~7 CTAs per SM at the longest row: 256 positions per CTA for the talker shape
     // (B = 32 x 8 KV heads at 1024 positions), the fastest measured there; at least
     // kPoolMinChunk.
-    const int64_t target = static_cast<int64_t>(num_sms_pool()) * 7;
+    const int64_t target = static_cast<int64_t>(num_sms()) * 7;
     const int64_t work = static_cast<int64_t>(batch) * num_kv_heads * max_seq_len;
     chunk = (work + target - 1) / target;
     if (chunk < kPoolMinChunk) chunk = kPoolMinChunk;
