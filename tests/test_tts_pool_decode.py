@@ -88,6 +88,39 @@ def test_new_kv_contract_and_no_cpu_path():
         paged_attention_decode(q, kp, vp, table, lens, valid, use_triton=False)
 
 
+def test_oracle_is_independent_of_page_placement():
+    """Moving a row's pages to other physical slots (table updated to match) leaves the
+    attention unchanged: only the logical order of positions matters."""
+    rng = np.random.default_rng(11)
+    c = _random_case(rng, batch=3, hq=8, hkv=4, d=16, ps=4, lens=[3, 9, 14], dtype=torch.float32,
+                     mask=True)
+    want = K.pool_paged_attention(c["q"], c["kp"].copy(), c["vp"].copy(), c["table"], c["lens"],
+                                  0.25, key_valid_mask=c["valid"])
+    perm = rng.permutation(c["kp"].shape[0])
+    inv = np.argsort(perm)
+    kp2, vp2 = c["kp"][perm], c["vp"][perm]  # physical page p moves to slot inv[p]
+    table2 = np.where(c["table"] >= 0, inv[np.maximum(c["table"], 0)], -1)
+    got = K.pool_paged_attention(c["q"], kp2, vp2, table2, c["lens"], 0.25,
+                                 key_valid_mask=c["valid"])
+    np.testing.assert_allclose(got, want, rtol=1e-12, atol=1e-12)
+
+
+def test_oracle_fused_write_equals_prewritten_pool():
+    """Attending with new_key/new_value equals attending over a pool that already holds
+    the current token's row (the reference's fused-write contract)."""
+    rng = np.random.default_rng(12)
+    c = _random_case(rng, batch=2, hq=4, hkv=2, d=8, ps=4, lens=[6, 13], dtype=torch.float32)
+    kw, vw = c["kp"].copy(), c["vp"].copy()
+    fused = K.pool_paged_attention(c["q"], kw, vw, c["table"], c["lens"], 0.3, new_key=c["nk"],
+                                   new_value=c["nv"])
+    kp, vp = c["kp"].copy(), c["vp"].copy()
+    K.write_current_kv(kp, vp, c["table"], c["lens"], c["nk"], c["nv"])
+    np.testing.assert_array_equal(kp, kw)
+    np.testing.assert_array_equal(vp, vw)
+    np.testing.assert_allclose(fused, K.pool_paged_attention(c["q"], kp, vp, c["table"],
+                                                             c["lens"], 0.3), rtol=0, atol=0)
+
+
 def _capi_call(lib, **over):
     dummy = ctypes.c_void_p(256)
     args = dict(dtype=0, batch=2, num_heads=16, num_kv_heads=8, head_dim=128, query=dummy,
