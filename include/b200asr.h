@@ -193,8 +193,9 @@ B200ASR_API int b200asr_silu_mul(const void *x, int32_t rows, int32_t inner, voi
  * bounds select the stream-K split over the whole batch.
  * Its first 4096 bytes hold per-sequence merge counters that must be zero
  * before the first call with that workspace; every completed call leaves them zero
- * (allocate it zero-filled once). Calls sharing a workspace must not overlap on the
- * GPU.                                                                             */
+ * (allocate it zero-filled once). A call that set an error bit in error_flag may
+ * leave them non-zero: clear them before the workspace is used again. Calls sharing
+ * a workspace must not overlap on the GPU.                                         */
 B200ASR_API size_t b200asr_paged_decode_workspace_size(int32_t batch, int32_t max_seqlen_k,
                                            int32_t num_heads, int32_t head_dim);
 B200ASR_API int b200asr_paged_decode(const void *q, int64_t q_row_stride, const void *k_cache,
@@ -214,8 +215,11 @@ B200ASR_API int b200asr_paged_decode(const void *q, int64_t q_row_stride, const 
  * Requests whose b200asr_paged_decode_workspace_size exceeds that limit are rejected
  * with B200ASR_ERR_WORKSPACE. The first call on each device resolves the array's address
  * (cudaGetSymbolAddress, with that device current): make it before any stream capture.
- * Every call shares the array, so calls whose kernels overlap on the GPU race on it;
- * serialise them (one stream, or one replay at a time). Allocates nothing.           */
+ * Every call clears the array's merge counters with cudaMemsetAsync on `stream` before
+ * its kernel, so the clear is ordered with the launch on any stream and nothing a
+ * failed call left behind reaches the next one. Every call shares the array, so calls
+ * whose kernels overlap on the GPU race on it; serialise them (one stream, or one
+ * replay at a time). Allocates nothing.                                             */
 #define B200ASR_NOALLOC_SCRATCH_BYTES (12u << 20)
 B200ASR_API int b200asr_paged_decode_noalloc(const void *q, int64_t q_row_stride,
                                  const void *k_cache, const void *v_cache, int32_t num_blocks,

@@ -46,19 +46,46 @@ def test_binding_signatures_cover_the_header():
     assert sorted(SIGNATURES) == declared_symbols()
 
 
-def test_integration_stub_matches_the_binding():
-    """The ctypes stub a reference maintainer would paste declares the
-    same argument types as the binding the tests exercise."""
+def _header_prototypes() -> dict[str, tuple[str, list[str]]]:
+    """name -> (return type, [parameter types]) of every B200ASR_API declaration."""
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    protos = {}
+    for ret, name, params in re.findall(
+            r"B200ASR_API\s+([\w\s\*]+?)\s*\b(b200asr_\w+)\s*\(([^)]*)\)\s*;", text):
+        kinds = []
+        for param in params.split(","):
+            param = " ".join(param.split())
+            if not param or param == "void":
+                continue
+            # drop the parameter name: the last identifier after the type
+            kinds.append(re.sub(r"\s*\b\w+$", "", param) if not param.endswith("*") else param)
+        protos[name] = (" ".join(ret.split()), kinds)
+    return protos
+
+
+def _ctype_of(decl: str):
+    if "*" in decl or decl == "b200asr_stream_t":
+        return ctypes.c_void_p
+    return {"int32_t": ctypes.c_int32, "int": ctypes.c_int32, "int64_t": ctypes.c_int64,
+            "float": ctypes.c_float, "size_t": ctypes.c_size_t}[decl.replace("const ", "")]
+
+
+def test_binding_matches_the_header_prototypes():
+    """Every ctypes signature in the binding has the parameter and return types the C
+    header declares (pointers and the stream cross as void*)."""
     from voiceagent_b200._lib import SIGNATURES
 
-    text = (REPO / "INTEGRATION.md").read_text()
-    types = {"P": ctypes.c_void_p, "I32": ctypes.c_int32, "I64": ctypes.c_int64,
-             "F32": ctypes.c_float, "SZ": ctypes.c_size_t}
-    stubs = re.findall(r"_lib\.(b200asr_\w+)\.argtypes = \[([^\]]*)\]", text, re.S)
-    assert len(stubs) >= 10
-    for name, args in stubs:
-        got = [types[a.strip()] for a in args.replace("\n", " ").split(",") if a.strip()]
-        assert got == SIGNATURES[name][1], name
+    protos = _header_prototypes()
+    assert sorted(protos) == sorted(SIGNATURES)
+    for name, (ret, params) in protos.items():
+        restype, argtypes = SIGNATURES[name]
+        assert [_ctype_of(p) for p in params] == list(argtypes), name
+        if ret == "void":
+            assert restype is None, name
+        elif ret == "const char *":
+            assert restype is ctypes.c_char_p, name
+        else:
+            assert restype is _ctype_of(ret), name
 
 
 def test_only_the_c_abi_is_exported():

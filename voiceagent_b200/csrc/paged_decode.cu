@@ -1116,12 +1116,16 @@ extern "C" int b200asr_paged_decode(const void *q, int64_t q_row_stride, const v
 //
 // The array is a file-scope __device__ symbol of B200ASR_NOALLOC_SCRATCH_BYTES; every GPU
 // that loads the library holds that much memory until the process exits. Host code cannot
-// use the symbol's name as a device address, so on the first call on each device (with
-// that device current) cudaGetSymbolAddress resolves it once, the per-sequence merge
-// counters at its head are cleared (they must start at zero; the kernel leaves them at
-// zero), and the pointer is cached. That first call may trigger module loading and
-// synchronises the device, so it must come before any stream capture. All calls share the
-// one array, so two calls whose kernels overlap on the GPU -- different streams, or graphs
+// use the symbol's name as a device address, so the first call on each device (with that
+// device current) resolves it once with cudaGetSymbolAddress and caches the pointer. That
+// first call may load the module, so it should come before any stream capture.
+//
+// The per-sequence merge counters at the head of the array must be zero when a launch
+// starts. Every call therefore clears them with cudaMemsetAsync on the caller's stream,
+// right before its kernel: the clear is ordered with the launch on any stream (a
+// non-blocking one included), and counters that a call whose waits timed out left
+// behind do not leak into the next call. No call allocates. All calls share the one
+// array, so two calls whose kernels overlap on the GPU -- different streams, or graphs
 // replayed concurrently -- race on it and must be serialised by the caller.
 
 static __device__ __align__(256) unsigned char g_decode_noalloc_scratch[B200ASR_NOALLOC_SCRATCH_BYTES];
@@ -1143,7 +1147,6 @@ static void *noalloc_scratch(int *status) {
   if (resolved[dev] == nullptr) {
     void *p = nullptr;
     e = cudaGetSymbolAddress(&p, g_decode_noalloc_scratch);
-    if (e == cudaSuccess && p != nullptr) e = cudaMemset(p, 0, kDecHeaderBytes);
     if (e != cudaSuccess || p == nullptr) {
       set_error("paged_decode_noalloc: set-up of the static scratch failed on device %d: %s", dev,
                 cudaGetErrorString(e));
@@ -1179,6 +1182,12 @@ extern "C" int b200asr_paged_decode_noalloc(const void *q, int64_t q_row_stride,
   int status = B200ASR_OK;
   void *scratch = noalloc_scratch(&status);
   if (scratch == nullptr) return status;
+  // Merge counters to zero on the caller's stream, ordered before this call's kernel.
+  const cudaError_t e = cudaMemsetAsync(scratch, 0, kDecHeaderBytes, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) {
+    set_error("paged_decode_noalloc: clearing the merge counters failed: %s", cudaGetErrorString(e));
+    return B200ASR_ERR_CUDA;
+  }
   return b200asr_paged_decode(q, q_row_stride, k_cache, v_cache, num_blocks, block_size,
                               num_heads, num_kv_heads, head_dim, cu_seqlens_k, block_tables,
                               bt_stride, batch, max_seqlen_k, scale, out, out_row_stride, scratch,

@@ -224,21 +224,23 @@ def paged_decode(q, k_cache, v_cache, cu_seqlens_k, block_tables, *, max_seqlen_
 
 
 _POOL_DTYPES = {torch.bfloat16: 0, torch.float16: 1, torch.float32: 2}
-_POOL_WORKSPACE: dict[int, torch.Tensor] = {}
+_POOL_WORKSPACE: dict[int, list[torch.Tensor]] = {}
 
 
 def pool_decode_workspace(batch: int, num_heads: int, head_dim: int, max_seq_len: int,
                           device) -> torch.Tensor:
     """A zero-filled workspace for :func:`pool_paged_decode`, cached per device and grown
-    on demand (allocate it before capturing a CUDA graph that uses it)."""
+    on demand. Growing allocates a new, larger buffer but keeps every buffer handed out
+    before alive for the life of the process, so a CUDA graph captured earlier with a
+    smaller one still replays into memory it owns (allocate before capturing)."""
     need = lib.b200asr_pool_paged_decode_workspace_size(batch, num_heads, head_dim, max_seq_len)
     device = torch.device(device)
     dev = device.index if device.index is not None else torch.cuda.current_device()
-    ws = _POOL_WORKSPACE.get(dev)
-    if ws is None or ws.numel() < need:
-        ws = torch.zeros(max(need, 1 << 20), dtype=torch.uint8, device=torch.device("cuda", dev))
-        _POOL_WORKSPACE[dev] = ws
-    return ws
+    held = _POOL_WORKSPACE.setdefault(dev, [])
+    if not held or held[-1].numel() < need:
+        held.append(torch.zeros(max(need, 1 << 20), dtype=torch.uint8,
+                                device=torch.device("cuda", dev)))
+    return held[-1]
 
 
 def pool_paged_decode(query, key_pool, value_pool, page_table, seq_lens, *, max_seq_len: int,
