@@ -4,16 +4,25 @@
     python bench.py [--gpus N --steps K --warmup W] [--impl reference]
     torchrun --nproc-per-node N bench.py --gpus N ...   (one process per GPU)
 
-Workload (per GPU): 512 synthetic 16 kHz clips, durations
-lognormal(median 7 s, sigma 0.6) clipped to 1-35 s, Qwen3-ASR-0.6B architecture with
+Default workload: a job of 512 synthetic 16 kHz clips per GPU,
+durations lognormal(median 7 s, sigma 0.6) clipped to 1-35 s, Qwen3-ASR-0.6B with
 seeded random-init bf16 weights, max_num_seqs = 32, exactly 64 greedy tokens per
-request (EOS ignored), CUDA-graph decode on. A step transcribes one slice of
-``--clips-per-step`` clips through ``AsrEngine.transcribe``; K steps cover the 512.
+request (EOS ignored), CUDA-graph decode on. The job is ONE request list that the host
+router (``replicas.route_by_duration``) splits over the ranks; each rank synthesises
+only its own requests and transcribes them in steps of ``--clips-per-step`` through
+``AsrEngine.transcribe``. ``--workload config4`` runs BASELINE config 4 instead: the
+1.7B architecture at 64 concurrent requests, 4096 clips plus one 20-minute recording
+cut into 30 s chunks, 96 greedy tokens each, the whole job split over the ranks
+(strong scaling).
 
 * ``value``    audio-s/s with each clip's mel features already resident in HBM
                (device-timed with CUDA events, max over ranks, all ranks summed);
 * ``e2e``      the same through the public API from host waveforms: waveform copies,
                GPU log-mel frontend and token read-back inside the timing;
+* ``reference_engine`` (N = 1) the reference's own GPU engine (``qwen_asr_vllm.AsrEngine``
+               under baseline/_ref: flash-attn, Triton store, CUDA-graph decode) on the
+               same job, weights and settings, run in a child process after ours, and the
+               ratio of our ``e2e`` to it (or why it could not run);
 * ``roofline`` the paged decode attention kernel (stream-K split with fused merge) on config 1
                (B = 32, ctx ~ U[64, 1024], 4096-block pool), timed live here with CUDA
                events around a graph of back-to-back launches over rotating KV sets that
@@ -21,12 +30,11 @@ request (EOS ignored), CUDA-graph decode on. A step transcribes one slice of
 * ``cpu_baseline`` the CPU fp32 restatement of the upstream model (oracle/model.py)
                transcribing a bounded sample of the same workload on the host cores.
 
-Multi-GPU: independent engine replicas (weak scaling), no collective on the data
-path; torch.distributed (NCCL) is used only for barriers and the max-over-ranks
-timing. ``--impl reference`` times the CPU restatement of the reference's path on
-rank 0 with all host threads (other ranks exit 0). ``--impl reference-engine`` runs
-the reference's own GPU engine (``qwen_asr_vllm.AsrEngine``, installed under
-baseline/_ref) on the same workload for a like-for-like e2e comparison.
+Multi-GPU: independent engine replicas, no collective on the data path;
+torch.distributed (NCCL) is used only for barriers and the max-over-ranks timing.
+Each rank is pinned to its own slice of the host cores. ``--impl reference`` times the
+CPU restatement of the reference's path on rank 0 with all host threads (other ranks
+exit 0). ``--impl reference-engine`` runs only the reference's own GPU engine.
 """
 
 from __future__ import annotations
@@ -63,13 +71,25 @@ def parse_args():
     p.add_argument("--decode-tokens", type=int, default=64)
     p.add_argument("--decode-steps", type=int, default=4,
                    help="decode steps per CUDA-graph call (EngineConfig.decode_steps)")
-    p.add_argument("--preset", default="0.6b")
+    p.add_argument("--preset", default=None, help="model preset (default: 0.6b; config4: 1.7b)")
+    p.add_argument("--workload", choices=["config3", "config4"], default="config3")
+    p.add_argument("--no-reference-engine", action="store_true",
+                   help="skip the reference GPU engine run that follows ours at N = 1")
     p.add_argument("--cpu-sample-clips", type=int, default=2)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--roofline-only", action="store_true",
                    help="only the config-1 paged decode op (e.g. for an ncu capture)")
-    return p.parse_args()
+    args = p.parse_args()
+    if args.workload == "config4":
+        # 1.7B at 64 concurrent requests, 96 greedy tokens per chunk
+        args.preset = args.preset or "1.7b"
+        if args.concurrency == 32:
+            args.concurrency = 64
+        if args.decode_tokens == 64:
+            args.decode_tokens = 96
+    args.preset = args.preset or "0.6b"
+    return args
 
 
 # ------------------------------------------------------------------ plumbing
@@ -211,21 +231,46 @@ def cpu_oracle_rate(clips, preset: str, decode_tokens: int, threads: int) -> dic
 # ----------------------------------------------------------------------- arms
 
 
+def make_job(args, world: int):
+    """The whole job (one request list for all ranks) of the chosen workload."""
+    from voiceagent_b200.workload import Job
+
+    if args.workload == "config4":
+        return Job("config4", seed=0)
+    return Job("config3", count=args.clips * world, seed=0)
+
+
+def workload_label(args, world: int) -> str:
+    if args.workload == "config4":
+        return (f"config4: Qwen3-ASR-{args.preset.upper()} bf16 random-init, "
+                f"max_num_seqs={args.concurrency}, 4096 clips lognormal(7 s, 0.6) in [1, 35] s "
+                f"+ one 20-min recording in 40 x 30 s chunks, {args.decode_tokens} greedy tokens, "
+                f"CUDA-graph decode, whole job routed over {world} GPU(s)")
+    return (f"{'config3' if args.preset == '0.6b' else 'config3-shaped'}: "
+            f"Qwen3-ASR-{args.preset.upper()} bf16 random-init, max_num_seqs={args.concurrency}, "
+            f"{args.clips} clips/GPU lognormal(7 s, 0.6) in [1, 35] s, {args.decode_tokens} "
+            "greedy tokens, CUDA-graph decode, one job routed over the GPUs by duration")
+
+
+def step_slices(n_requests: int, per_step: int) -> list[list[int]]:
+    """Positions (into a rank's share) of each step's requests: consecutive slices,
+    the last one shorter when the share does not divide evenly."""
+    return [list(range(i, min(i + per_step, n_requests))) for i in range(0, n_requests, per_step)]
+
+
 def run_reference_arm(args) -> None:
     rank, world, _ = dist_env()
     if rank != 0:
         return
-    from voiceagent_b200.workload import config3_clips
-
     threads = os.cpu_count() or 1
-    clips = config3_clips(args.clips, seed=0)
+    job = make_job(args, 1)
     order = list(range(args.warmup + args.steps))
     for i in order[:args.warmup]:
-        cpu_oracle_rate([clips[i]], args.preset, args.decode_tokens, threads)
-    timed = cpu_oracle_rate([clips[args.warmup + i] for i in range(args.steps)], args.preset,
-                            args.decode_tokens, threads)
+        cpu_oracle_rate([job.waveform(i)], args.preset, args.decode_tokens, threads)
+    timed = cpu_oracle_rate(job.waveforms(range(args.warmup, args.warmup + args.steps)),
+                            args.preset, args.decode_tokens, threads)
     value = timed["value"]
-    sample = (f"{args.steps} clips ({timed['audio_s']:.1f} s of audio) of the config-3 workload, one "
+    sample = (f"{args.steps} clips ({timed['audio_s']:.1f} s of audio) of the {args.workload} job, one "
               f"per step, {args.decode_tokens} greedy tokens each, fp32 CPU restatement of the "
               "upstream Qwen3-ASR thinker (oracle/model.py), mel frontend included")
     line = {
@@ -233,7 +278,7 @@ def run_reference_arm(args) -> None:
         "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 1000.0 * timed["seconds"] / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "config3 sample on host cores", "preset": args.preset,
+        "config": {"workload": f"{args.workload} sample on host cores", "preset": args.preset,
                    "decode_tokens": args.decode_tokens},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
                          "sample": sample},
@@ -242,97 +287,64 @@ def run_reference_arm(args) -> None:
     print(json.dumps(line), flush=True)
 
 
-class _TemplateTokenizer:
-    """Stands in for the checkpoint tokenizer, which does not exist offline.
-
-    The reference engine only asks its tokenizer to encode the chat template (once per
-    context/language pair), for the EOS id, and to decode output text. This returns the
-    same template ids as ``voiceagent_b200.prompt`` (pinned by the reference's
-    tests/test_prompt.py) so both engines see prompts of identical length; text output
-    is empty. Everything after the prompt -- frontend, scheduler, model, flash-attn,
-    Triton store, CUDA graphs -- is the reference's own, unmodified code.
-    """
-
-    eos_token_id = 151645
-
-    @classmethod
-    def from_pretrained(cls, *args, **kwargs):
-        return cls()
-
-    def encode(self, text: str) -> list[int]:
-        from voiceagent_b200.prompt import PromptBuilder
-
-        head, sep, tail = text.partition("<|im_start|>assistant\n")
-        if not sep or "<|im_start|>system\n<|im_end|>" not in head:
-            raise ValueError("template tokenizer: only the empty-context ASR template is known")
-        language = tail[len("language "):].replace("<asr_text>", "") if tail else None
-        return PromptBuilder().template(None, language or None)[0]
-
-    def decode(self, ids, skip_special_tokens: bool = True) -> str:
-        return ""
-
-
 def run_reference_engine(args) -> None:
     """The reference's own GPU engine (``qwen_asr_vllm.AsrEngine`` from baseline/_ref) on
-    the config-3 workload, for comparison with our e2e number: same seeded random
-    weights (written as a safetensors checkpoint), clips, concurrency and sampling."""
-    ref = Path(__file__).resolve().parent / "baseline" / "_ref"
-    if not (ref / "qwen_asr_vllm").is_dir():
-        print(json.dumps({"impl": "reference-engine", "unavailable":
-                          "baseline/_ref is not installed (pip install --target baseline/_ref)"}))
+    the same job as ours: same seeded random weights (written as a safetensors
+    checkpoint), clips, routing, concurrency and sampling; wall clock around the same
+    steps, max over ranks."""
+    from baseline import ref_engine
+
+    ok, why = ref_engine.available()
+    if not ok:
+        print(json.dumps({"impl": "reference-engine", "unavailable": why}), flush=True)
         return
-    sys.path.insert(0, str(ref))
     import torch
 
-    import qwen_asr_vllm.prompt as ref_prompt
-    from qwen_asr_vllm import AsrEngine as RefEngine
-    from qwen_asr_vllm.engine.request import SamplingParams as RefSampling
-
     from voiceagent_b200.checkpoint import write_checkpoint
-    from voiceagent_b200.workload import config3_clips, lognormal_durations
+    from voiceagent_b200.replicas import pin_host_cores, share_of
 
-    ref_prompt.AutoTokenizer = _TemplateTokenizer
     dist = Dist()
     rank, world, local = dist.rank, dist.world, dist.local
+    pin_host_cores(local, int(os.environ.get("LOCAL_WORLD_SIZE", world)))
     torch.cuda.set_device(local)
     ckpt = write_checkpoint(Path(tempfile.mkdtemp(prefix="b200asr_ref_")) / "ckpt", args.preset,
                             seed=0, weights=True)
-    engine = RefEngine(model=str(ckpt), max_num_seqs=args.concurrency, max_model_len=4096,
-                       max_num_batched_tokens=8192, max_audio_batch_size=args.concurrency,
-                       num_kvcache_blocks=1024, device=f"cuda:{local}")
-    sampling = RefSampling(max_new_tokens=args.decode_tokens, ignore_eos=True)
-    clips = config3_clips(args.clips, seed=rank)
-    durations = lognormal_durations(args.clips, seed=rank)
-    n_slices = max(1, args.clips // args.clips_per_step)
-    slices = [list(range(i * args.clips_per_step, (i + 1) * args.clips_per_step))
-              for i in range(n_slices)]
+    engine = ref_engine.build_engine(ckpt, max_num_seqs=args.concurrency, max_model_len=4096,
+                                     max_num_batched_tokens=8192,
+                                     max_audio_batch_size=args.concurrency,
+                                     num_kvcache_blocks=1024, device=f"cuda:{local}")
+    sampling = ref_engine.sampling_params(args.decode_tokens)
+    job = make_job(args, world)
+    mine = share_of(job.durations, dist)
+    slices = step_slices(len(mine), args.clips_per_step)
+    clips = job.waveforms(mine)
 
     def run(i):
-        return engine.transcribe([clips[j] for j in slices[i % n_slices]], language="en",
+        return engine.transcribe([clips[j] for j in slices[i % len(slices)]], language="en",
                                  sampling=sampling)
 
+    steps = len(slices) if args.workload == "config4" else args.steps
     for i in range(args.warmup):
         run(i)
     dist.barrier()
     torch.cuda.synchronize()
     t0 = time.perf_counter()
-    outs = [run(i) for i in range(args.steps)]
+    outs = [run(i) for i in range(steps)]
     torch.cuda.synchronize()
     sec = time.perf_counter() - t0
     dist.barrier()
     toks = sum(len(o.output_token_ids) for batch in outs for o in batch)
-    audio = float(sum(durations[j] for i in range(args.steps) for j in slices[i % n_slices]))
+    audio = float(sum(job.durations[mine[j]] for i in range(steps) for j in slices[i % len(slices)]))
     sec_max = dist.max(sec)
     value = dist.sum(audio) / sec_max
     if rank == 0:
         print(json.dumps({
             "impl": "reference-engine", "metric": METRIC, "value": value, "unit": UNIT,
-            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": 1000.0 * sec_max / args.steps, "higher_is_better": True,
-            "scaling": "weak", "dtype": "bf16",
+            "n_gpus": world, "steps": steps, "warmup": args.warmup,
+            "ms_per_step": 1000.0 * sec_max / steps, "higher_is_better": True,
+            "scaling": "strong" if args.workload == "config4" else "weak", "dtype": "bf16",
             "data": "synthetic (seeded noise + sines; random-init weights, seed 0)",
-            "config": {"workload": f"{'config3' if args.preset == '0.6b' else 'config4'} "
-                                   f"(Qwen3-ASR-{args.preset.upper()}) through "
+            "config": {"workload": workload_label(args, world) + " -- through "
                                    "qwen_asr_vllm.AsrEngine.transcribe (flash-attn + Triton, "
                                    "CUDA-graph decode), wall clock, max over ranks",
                        "preset": args.preset, "clips_per_step": args.clips_per_step,
@@ -341,18 +353,51 @@ def run_reference_engine(args) -> None:
     dist.close()
 
 
+def reference_engine_child(args) -> dict:
+    """Run ``--impl reference-engine`` with the same settings in a child process (its
+    own CUDA context and module state) and return its JSON line, or why it is missing."""
+    from baseline import ref_engine
+
+    ok, why = ref_engine.available()
+    if not ok:
+        return {"unavailable": why}
+    cmd = [sys.executable, str(REPO / "bench.py"), "--impl", "reference-engine",
+           "--steps", str(args.steps), "--warmup", str(args.warmup), "--clips", str(args.clips),
+           "--clips-per-step", str(args.clips_per_step), "--concurrency", str(args.concurrency),
+           "--decode-tokens", str(args.decode_tokens), "--preset", args.preset,
+           "--workload", args.workload]
+    env = {k: v for k, v in os.environ.items()
+           if k not in ("RANK", "WORLD_SIZE", "LOCAL_RANK", "LOCAL_WORLD_SIZE", "MASTER_ADDR",
+                        "MASTER_PORT", "GROUP_RANK", "ROLE_RANK", "TORCHELASTIC_RUN_ID")}
+    try:
+        proc = subprocess.run(cmd, capture_output=True, text=True, timeout=1200, env=env,
+                              cwd=str(REPO))
+    except subprocess.TimeoutExpired:
+        return {"unavailable": "the reference engine run exceeded 20 minutes"}
+    for line in reversed(proc.stdout.strip().splitlines()):
+        if line.startswith("{"):
+            try:
+                return json.loads(line)
+            except json.JSONDecodeError:
+                break
+    tail = (proc.stderr or proc.stdout or "").strip().splitlines()[-1:] or ["no output"]
+    return {"unavailable": f"reference engine exited {proc.returncode}: {tail[0][:300]}"}
+
+
 def run_ours(args) -> None:
     import torch
 
     from voiceagent_b200 import kernels as kx
+    from voiceagent_b200.audio.frontend import AudioFrontend
     from voiceagent_b200.checkpoint import write_checkpoint
     from voiceagent_b200.engine.engine import AsrEngine
     from voiceagent_b200.engine.request import SamplingParams
     from voiceagent_b200.profiling import TRANSFERS
-    from voiceagent_b200.workload import config3_clips, lognormal_durations
+    from voiceagent_b200.replicas import pin_host_cores, share_of
 
     dist = Dist()
     rank, world, local = dist.rank, dist.world, dist.local
+    cores = pin_host_cores(local, int(os.environ.get("LOCAL_WORLD_SIZE", world)))
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
 
@@ -364,24 +409,25 @@ def run_ours(args) -> None:
                        num_kvcache_blocks=1024, decode_steps=args.decode_steps)
     sampling = SamplingParams(max_new_tokens=args.decode_tokens, ignore_eos=True)
 
-    clips = config3_clips(args.clips, seed=rank)
-    durations = lognormal_durations(args.clips, seed=rank)
-    n_steps_total = max(1, args.clips // args.clips_per_step)
-    slices = [list(range(i * args.clips_per_step, (i + 1) * args.clips_per_step))
-              for i in range(n_steps_total)]
+    # One job for all ranks; the host router hands this rank its share.
+    job = make_job(args, world)
+    mine = share_of(job.durations, dist)
+    slices = step_slices(len(mine), args.clips_per_step)
+    # config 4 is a fixed job: the timed region is this rank's whole share, once
+    steps = len(slices) if args.workload == "config4" else args.steps
+    clips = job.waveforms(mine)
 
     def step_slice(i):
         return slices[i % len(slices)]
 
     # Mel features on the host once (for the HBM-resident run), then moved to the GPU.
-    from voiceagent_b200.audio.frontend import AudioFrontend
-
     host_feats = build_features(clips, AudioFrontend(str(ckpt)), torch)
     dev_feats = []
     for f in host_feats:
         g = type(f)(mel=f.mel.to(device=device, dtype=torch.bfloat16), mel_frames=f.mel_frames,
                     num_audio_tokens=f.num_audio_tokens, audio_seconds=f.audio_seconds)
         dev_feats.append(g)
+    del host_feats
     torch.cuda.synchronize()
 
     def run_features(i):
@@ -410,7 +456,7 @@ def run_ours(args) -> None:
         xfer0 = dict(TRANSFERS)
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record(stream)
-        outs = [fn(i) for i in range(args.steps)]
+        outs = [fn(i) for i in range(steps)]
         e.record(stream)
         torch.cuda.synchronize()
         if profile_range:
@@ -423,19 +469,20 @@ def run_ours(args) -> None:
                 {k: TRANSFERS[k] - xfer0[k] for k in TRANSFERS})
 
     ms, audio, toks, launches, _ = timed(run_features, profile_range=True)
-    assert toks == sum(len(step_slice(i)) for i in range(args.steps)) * args.decode_tokens
+    assert toks == sum(len(step_slice(i)) for i in range(steps)) * args.decode_tokens
     ms_max = dist.max(ms)
     audio_all = dist.sum(audio)
     value = audio_all / (ms_max / 1000.0)
+    requests_all = int(dist.sum(sum(len(step_slice(i)) for i in range(steps))))
 
     e2e = None
     if not args.no_e2e:
         ms_e, audio_e, _, _, xfer = timed(run_waveforms)
         ms_e_max = dist.max(ms_e)
         e2e = {"value": dist.sum(audio_e) / (ms_e_max / 1000.0), "unit": UNIT,
-               "h2d_bytes_per_step": int(xfer["h2d"] / args.steps),
-               "d2h_bytes_per_step": int(xfer["d2h"] / args.steps),
-               "ms_per_step": ms_e_max / args.steps,
+               "h2d_bytes_per_step": int(xfer["h2d"] / steps),
+               "d2h_bytes_per_step": int(xfer["d2h"] / steps),
+               "ms_per_step": ms_e_max / steps,
                "note": "AsrEngine.transcribe from host float32 waveforms: waveform copies "
                        "(one pinned copy per encode batch), GPU log-mel, token read-back "
                        "inside the timing"}
@@ -448,32 +495,48 @@ def run_ours(args) -> None:
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        threads = max(1, min(os.cpu_count() or 1, 32))
+        threads = max(1, min(len(cores) or os.cpu_count() or 1, 32))
         res = cpu_oracle_rate(clips[:args.cpu_sample_clips], args.preset, args.decode_tokens,
                               threads)
         cpu = {"value": res["value"], "unit": UNIT, "cores": threads, "kind": "port",
-               "sample": f"first {args.cpu_sample_clips} clips of the config-3 workload "
+               "sample": f"first {args.cpu_sample_clips} clips of the {args.workload} job "
                          f"({res['audio_s']:.1f} s of audio), {args.decode_tokens} greedy tokens "
                          "each, fp32 CPU restatement of the upstream thinker (oracle/model.py), "
                          "mel frontend included"}
 
+    if engine.model_runner.graph_runner is not None:
+        engine.model_runner.graph_runner.release()
+
+    ref = None
+    if world == 1 and not args.no_reference_engine:
+        del engine, dev_feats
+        torch.cuda.empty_cache()
+        ref = reference_engine_child(args)
+        if "value" in ref:
+            ref = {"value": ref["value"], "unit": UNIT, "ms_per_step": ref["ms_per_step"],
+                   "steps": ref["steps"], "output_tokens": ref["config"]["output_tokens"],
+                   "ratio_e2e": (e2e["value"] / ref["value"]) if e2e else None,
+                   "ratio_value": value / ref["value"],
+                   "how": "qwen_asr_vllm.AsrEngine from baseline/_ref (unmodified; flash-attn, "
+                          "Triton store, CUDA-graph decode) on the same job, weights, settings "
+                          "and steps, in a child process on this GPU after ours; wall clock "
+                          "around its timed steps, host waveforms in"}
+
     if rank == 0:
         line = {
-            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": steps,
+            "warmup": args.warmup, "ms_per_step": ms_max / steps, "higher_is_better": True,
+            "scaling": "strong" if args.workload == "config4" else "weak",
+            "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded noise + sines; random-init weights, seed 0)",
             "config": {
-                "workload": f"{'config3' if args.preset == '0.6b' else 'config4'}: "
-                            f"Qwen3-ASR-{args.preset.upper()} bf16 random-init, "
-                            f"max_num_seqs={args.concurrency}, "
-                            f"{args.clips} clips/GPU lognormal(7 s, 0.6) in [1, 35] s, "
-                            f"{args.decode_tokens} greedy tokens, CUDA-graph decode",
+                "workload": workload_label(args, world),
                 "preset": args.preset,
                 "clips_per_step": args.clips_per_step, "concurrency": args.concurrency,
-                "audio_seconds_per_gpu": float(sum(durations[j] for i in range(args.steps)
-                                                   for j in step_slice(i))),
-                "parallelism": f"dp{world} (independent replicas)",
+                "requests_timed_all_ranks": requests_all,
+                "audio_seconds_all_ranks": audio_all,
+                "parallelism": f"dp{world} (independent replicas, host-routed by duration, "
+                               "each pinned to its own host cores)",
                 "l2": "inputs larger than L2 (the decoder's weights, 1.2 GB for 0.6B and "
                       "3.4 GB for 1.7B, stream through every decode step)",
                 "timing": "CUDA events on the engine stream, max over ranks",
@@ -494,12 +557,11 @@ def run_ours(args) -> None:
                              / peaks["hbm_gbs"]}},
             "cpu_baseline": cpu,
             "e2e": e2e,
+            "reference_engine": ref,
             "gpu_launches": launches,
             "clocks": clock_info,
         }
         print(json.dumps(line), flush=True)
-    if engine.model_runner.graph_runner is not None:
-        engine.model_runner.graph_runner.release()
     dist.close()
 
 

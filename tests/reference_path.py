@@ -5,8 +5,8 @@ in torch eager -- RMSNorm with its two bf16 roundings (layers/layernorm.py:19-36
 half-split RoPE in fp32 (layers/rotary_embedding.py:9-32), F.silu(gate) * up
 (layers/activation.py:11-14), the chunk/pad/conv/windowed-attention encoder
 (models/audio_encoder.py:130-189) -- and calls ``flash_attn_varlen_func`` exactly
-as layers/attention.py does (the library is installed; if its kernels cannot run on
-this GPU it falls back to torch SDPA and says so). Weights are read from the
+as layers/attention.py does (no other attention backend: if flash-attn cannot run,
+the tests that use this path fail). Weights are read from the
 engine's own modules, so engine and reference path see identical parameters.
 
 The decoder is run teacher-forced over a whole sequence in one causal varlen pass
@@ -23,25 +23,17 @@ ATTENTION_BACKEND = {"name": None}
 
 
 def _varlen(q, k, v, cu, max_len, scale, causal):
+    """``flash_attn_varlen_func`` exactly as layers/attention.py calls it. There is no
+    fallback: if flash-attn cannot run here the parity tests fail and say why, rather
+    than comparing against a different attention implementation."""
     try:
         from flash_attn import flash_attn_varlen_func
-
-        out = flash_attn_varlen_func(q, k, v, cu_seqlens_q=cu, cu_seqlens_k=cu, max_seqlen_q=max_len,
-                                     max_seqlen_k=max_len, softmax_scale=scale, causal=causal)
-        ATTENTION_BACKEND["name"] = "flash_attn"
-        return out
-    except Exception as exc:  # flash-attn unavailable or not built for this GPU
-        ATTENTION_BACKEND["name"] = f"sdpa ({type(exc).__name__})"
-    outs = []
-    cu_l = cu.tolist()
-    for a, b in zip(cu_l[:-1], cu_l[1:]):
-        qs, ks, vs = (t[a:b].transpose(0, 1) for t in (q, k, v))
-        if ks.shape[0] != qs.shape[0]:
-            rep = qs.shape[0] // ks.shape[0]
-            ks, vs = ks.repeat_interleave(rep, 0), vs.repeat_interleave(rep, 0)
-        o = F.scaled_dot_product_attention(qs, ks, vs, is_causal=causal, scale=scale)
-        outs.append(o.transpose(0, 1))
-    return torch.cat(outs, 0)
+    except Exception as exc:
+        raise RuntimeError(f"reference path needs flash-attn: {type(exc).__name__}: {exc}") from exc
+    out = flash_attn_varlen_func(q, k, v, cu_seqlens_q=cu, cu_seqlens_k=cu, max_seqlen_q=max_len,
+                                 max_seqlen_k=max_len, softmax_scale=scale, causal=causal)
+    ATTENTION_BACKEND["name"] = "flash_attn"
+    return out
 
 
 def _rms(x, w, eps):

@@ -14,7 +14,8 @@ import numpy as np
 import pytest
 import torch.multiprocessing as mp
 
-from voiceagent_b200.replicas import ReplicaGroup, route_by_duration, throughput
+from voiceagent_b200.replicas import (ReplicaGroup, pin_host_cores, route_by_duration,
+                                      throughput, transcribe_share)
 
 
 def _free_port() -> int:
@@ -111,3 +112,46 @@ def test_reference_arm_is_rank_zero_only(monkeypatch, capsys):
                              "decode_tokens": 2, "gpus": 2})()
     bench.run_reference_arm(args)  # rank 1 of 2: exits without work or output
     assert capsys.readouterr().out == ""
+
+
+def _shared_job_worker(rank: int, world: int, port: int, results) -> None:
+    from voiceagent_b200.workload import SAMPLE_RATE, Job
+
+    _env(rank, world, port)
+    g = ReplicaGroup("gloo", timeout_s=30)
+    try:
+        cores = pin_host_cores(rank, world)
+        job = Job("config4")  # 4096 clips + a 20-minute file in 30 s chunks
+        # stand-in transcriber: one output per request, here the sample count it got
+        done = transcribe_share(g, job, lambda waves: [len(w) for w in waves], batch=512)
+        ok = all(n == int(round(job.durations[i] * SAMPLE_RATE)) for i, n in done.items())
+        audio = float(sum(job.durations[i] for i in done))
+        results.put((rank, sorted(done), ok, g.gather(cores), g.sum(audio),
+                     float(job.durations.sum())))
+    finally:
+        g.close()
+
+
+def test_two_gloo_replicas_transcribe_a_routed_job_exactly_once():
+    """One shared job (config 4's 4136 requests) split by the host router over two gloo
+    ranks, each pinned to its own host cores: every request is transcribed exactly once,
+    each rank synthesises the right waveform for each of its requests, and the summed
+    audio is the job's."""
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    results = ctx.Queue()
+    procs = [ctx.Process(target=_shared_job_worker, args=(r, 2, port, results)) for r in range(2)]
+    for p in procs:
+        p.start()
+    out = sorted(results.get(timeout=300) for _ in range(2))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    shares = [set(o[1]) for o in out]
+    assert not shares[0] & shares[1]
+    assert sorted(shares[0] | shares[1]) == list(range(4136))
+    assert all(o[2] for o in out)
+    assert out[0][4] == pytest.approx(out[0][5])  # all audio accounted for, once
+    cores = out[0][3]
+    if len(os.sched_getaffinity(0)) >= 2:
+        assert cores[0] and cores[1] and not set(cores[0]) & set(cores[1])

@@ -1,11 +1,27 @@
-"""Three-stage scheduling with mixed prefill/decode batches.
+"""Scheduling of the engine's three stages: audio encode, prefill, decode.
 
-Semantics of the reference scheduler (engine/scheduler.py:62-309): an audio-encode
-stage packs several requests into one encoder call (backlog capped at
-``max_num_seqs``); each decoder step takes every running decode first (preempting
-the newest when blocks run out, aborting a lone request that cannot grow), then
-admits prefills under the token and sequence budgets; OOM rollbacks restore batches
-exactly and halve the caps, ``relax_limits`` doubles them back.
+The decisions are the ones qwen-asr-vllm's scheduler makes (engine/scheduler.py:62-309),
+because the slot mappings and block tables this engine must reproduce follow from them:
+
+* Encode: requests leave the encode queue in arrival order, several per encoder call,
+  while the prefill backlog has room (at most ``max_num_seqs`` encoded-but-unprefilled
+  requests, since their embeddings occupy device memory), the call stays within
+  ``max_audio_batch_size`` requests and the frame cap (the first request always fits).
+* Decode first: every running request joins the step in order if its next token has
+  a cache slot. When one does not, the most recently started running request is
+  preempted -- its blocks freed, its embeddings kept, back to the front of the prefill
+  queue -- and the check repeats; a request that is the only one running and still
+  cannot grow ends as ``aborted:out_of_kv_blocks``.
+* Then prefill, in queue order, while the step has sequence slots (the adaptive cap)
+  and token budget (``max_num_batched_tokens``, decodes count one each): a request
+  longer than the remaining budget, or whose blocks are not free now, waits at the
+  head; one needing more blocks than the whole cache ends as
+  ``aborted:kv_cache_too_small``.
+* Out of memory: the failed step is undone exactly (its requests back at the front of
+  their queues, prefill blocks freed) and its cap halves (``max(1, attempted // 2)``
+  sequences, or half the failed call's frames for the encoder); a failed step of one
+  request gives that request up. Each successful step doubles the caps back toward
+  their configured values.
 """
 
 from __future__ import annotations
@@ -21,19 +37,21 @@ from voiceagent_b200.engine.request import AsrRequest, RequestStage
 
 @dataclass
 class ModelBatch:
+    """The requests of one decoder forward pass: prefills first, then decodes."""
+
     prefill: list[AsrRequest] = field(default_factory=list)
     decode: list[AsrRequest] = field(default_factory=list)
 
     @property
     def requests(self) -> list[AsrRequest]:
-        return self.prefill + self.decode
+        return [*self.prefill, *self.decode]
 
     @property
     def num_tokens(self) -> int:
         return sum(r.num_tokens_to_compute for r in self.requests)
 
     def __bool__(self) -> bool:
-        return bool(self.prefill or self.decode)
+        return len(self.prefill) + len(self.decode) > 0
 
 
 @dataclass
@@ -49,130 +67,86 @@ class SchedulerStats:
     num_audio_ooms: int = 0
 
 
+class AdaptiveCap:
+    """A limit that drops after an out-of-memory failure and climbs back by doubling
+    after each success, never above its configured ceiling."""
+
+    def __init__(self, ceiling: int):
+        self.ceiling = ceiling
+        self.value = ceiling
+
+    def cut_to(self, value: int) -> None:
+        self.value = max(1, value)
+
+    def relax(self) -> None:
+        if self.value < self.ceiling:
+            self.value = min(self.ceiling, 2 * self.value)
+
+
 class Scheduler:
     def __init__(self, config: EngineConfig, block_manager: BlockManager):
         self.config = config
         self.block_manager = block_manager
+        # the three stage queues, oldest first
         self.waiting_encode: deque[AsrRequest] = deque()
         self.waiting_prefill: deque[AsrRequest] = deque()
         self.running: deque[AsrRequest] = deque()
-        self.aborted: list[AsrRequest] = []
-        self.tracked: dict[int, AsrRequest] = {}
+        self.aborted: list[AsrRequest] = []  # ended without finishing; drained by the engine
+        self.tracked: dict[int, AsrRequest] = {}  # every in-flight request, for cancel()
         self.stats = SchedulerStats()
-        self.model_batch_limit = config.max_num_seqs
-        self.audio_frame_limit = config.max_audio_batch_frames
+        self._seq_cap = AdaptiveCap(config.max_num_seqs)
+        self._frame_cap = AdaptiveCap(config.max_audio_batch_frames)
 
-    # -------------------------------------------------------------- queues
+    @property
+    def model_batch_limit(self) -> int:
+        return self._seq_cap.value
+
+    @property
+    def audio_frame_limit(self) -> int:
+        return self._frame_cap.value
+
+    # ------------------------------------------------------------- queue access
 
     def add(self, request: AsrRequest) -> None:
-        self.waiting_encode.append(request)
         self.tracked[request.request_id] = request
+        self.waiting_encode.append(request)
 
     def admit_prefill(self, requests: list[AsrRequest]) -> None:
+        """Encoded requests join the prefill queue."""
         self.waiting_prefill.extend(requests)
 
     def drain_aborted(self) -> list[AsrRequest]:
-        out, self.aborted = self.aborted, []
+        out = self.aborted
+        self.aborted = []
         return out
-
-    def cancel(self, request_id: int) -> bool:
-        request = self.tracked.get(request_id)
-        if request is None:
-            return False
-        for queue in (self.waiting_encode, self.waiting_prefill, self.running):
-            if request in queue:
-                queue.remove(request)
-                self._give_up(request, "cancelled")
-                return True
-        request.cancel_requested = True  # inside the batch being executed
-        return True
 
     @property
     def has_work(self) -> bool:
-        return bool(self.waiting_encode or self.waiting_prefill or self.running)
+        return self.num_in_flight > 0
 
     @property
     def num_in_flight(self) -> int:
-        return len(self.waiting_encode) + len(self.waiting_prefill) + len(self.running)
+        return sum(map(len, (self.waiting_encode, self.waiting_prefill, self.running)))
 
-    # ---------------------------------------------------------- scheduling
+    def cancel(self, request_id: int) -> bool:
+        """End a request wherever it waits (it is reported with reason "cancelled").
+        One inside the step being executed is only flagged; the step's results end it.
+        Returns whether the id was in flight."""
+        request = self.tracked.get(request_id)
+        if request is None:
+            return False
+        queue = next((q for q in (self.waiting_encode, self.waiting_prefill, self.running)
+                      if request in q), None)
+        if queue is None:
+            request.cancel_requested = True
+        else:
+            queue.remove(request)
+            self._retire(request, "cancelled")
+        return True
 
-    def schedule_audio(self) -> list[AsrRequest]:
-        capacity = self.config.max_num_seqs - len(self.waiting_prefill)
-        if capacity <= 0 or not self.waiting_encode:
-            return []
-        limit = min(capacity, self.config.max_audio_batch_size)
-        picked: list[AsrRequest] = []
-        frames = 0
-        while self.waiting_encode and len(picked) < limit:
-            request = self.waiting_encode[0]
-            n = request.features.mel_frames
-            if picked and frames + n > self.audio_frame_limit:
-                break
-            self.waiting_encode.popleft()
-            request.timings.encode_start = time.perf_counter()
-            picked.append(request)
-            frames += n
-        if picked:
-            self.stats.num_encode_batches += 1
-            self.stats.num_encoded_requests += len(picked)
-        return picked
-
-    def _preempt(self, request: AsrRequest) -> None:
-        self.block_manager.deallocate(request)
-        request.num_computed_tokens = 0
-        request.stage = RequestStage.WAITING_PREFILL
-        self.waiting_prefill.appendleft(request)
-        self.stats.num_preemptions += 1
-
-    def schedule_model(self) -> ModelBatch:
-        batch = ModelBatch()
-        while self.running:
-            request = self.running[0]
-            if self.block_manager.can_append(request):
-                batch.decode.append(self.running.popleft())
-                continue
-            if len(self.running) > 1:
-                self._preempt(self.running.pop())
-                continue
-            self.running.popleft()
-            request.finish("aborted:out_of_kv_blocks")
-            self.block_manager.deallocate(request)
-            request.audio_embeds = None
-            self.aborted.append(request)
-            break
-
-        tokens_left = self.config.max_num_batched_tokens - len(batch.decode)
-        seqs_left = self.model_batch_limit - len(batch.decode)
-        while self.waiting_prefill and seqs_left > 0:
-            request = self.waiting_prefill[0]
-            if len(request) > tokens_left:
-                break
-            if not self.block_manager.can_ever_allocate(request):
-                self.waiting_prefill.popleft()
-                request.finish("aborted:kv_cache_too_small")
-                request.audio_embeds = None
-                self.aborted.append(request)
-                continue
-            if not self.block_manager.can_allocate(request):
-                break
-            self.waiting_prefill.popleft()
-            self.block_manager.allocate(request)
-            batch.prefill.append(request)
-            tokens_left -= request.num_tokens_to_compute
-            seqs_left -= 1
-
-        if batch:
-            self.stats.num_model_steps += 1
-            if batch.prefill and batch.decode:
-                self.stats.num_mixed_steps += 1
-            self.stats.num_prefilled_tokens += sum(r.num_tokens_to_compute for r in batch.prefill)
-            self.stats.num_decoded_tokens += len(batch.decode)
-        return batch
-
-    # ------------------------------------------------------------ recovery
-
-    def _give_up(self, request: AsrRequest, reason: str) -> None:
+    def _retire(self, request: AsrRequest, reason: str) -> None:
+        """End a request that did not finish normally: free everything it holds and
+        report it through ``aborted``."""
         self.block_manager.deallocate(request)
         request.num_computed_tokens = 0
         request.audio_embeds = None
@@ -180,43 +154,158 @@ class Scheduler:
         self.tracked.pop(request.request_id, None)
         self.aborted.append(request)
 
+    def _release_finished(self, request: AsrRequest) -> None:
+        self.block_manager.deallocate(request)
+        request.audio_embeds = None
+        self.tracked.pop(request.request_id, None)
+
+    # ------------------------------------------------------------------ encode
+
+    def schedule_audio(self) -> list[AsrRequest]:
+        """The requests of the next encoder call (possibly none)."""
+        room = min(self.config.max_num_seqs - len(self.waiting_prefill),
+                   self.config.max_audio_batch_size)
+        count, frames = 0, 0
+        for request in self.waiting_encode:
+            if count >= room:
+                break
+            frames += request.features.mel_frames
+            if count > 0 and frames > self._frame_cap.value:
+                break
+            count += 1
+        if count <= 0:
+            return []
+        now = time.perf_counter()
+        picked = [self.waiting_encode.popleft() for _ in range(count)]
+        for request in picked:
+            request.timings.encode_start = now
+        self.stats.num_encode_batches += 1
+        self.stats.num_encoded_requests += count
+        return picked
+
+    # ------------------------------------------------------------------- model
+
+    def _preempt(self, request: AsrRequest) -> None:
+        """Send a running request back to prefill to free its blocks (its audio
+        embeddings stay: only the text prefill repeats)."""
+        self.block_manager.deallocate(request)
+        request.num_computed_tokens = 0
+        request.move_to(RequestStage.WAITING_PREFILL)
+        self.waiting_prefill.appendleft(request)
+        self.stats.num_preemptions += 1
+
+    def _take_decodes(self, batch: ModelBatch) -> None:
+        bm = self.block_manager
+        while self.running:
+            if bm.can_append(self.running[0]):
+                batch.decode.append(self.running.popleft())
+            elif len(self.running) > 1:
+                self._preempt(self.running.pop())  # the newest makes room for the oldest
+            else:
+                self._retire(self.running.popleft(), "aborted:out_of_kv_blocks")
+                return
+
+    def _take_prefills(self, batch: ModelBatch) -> None:
+        bm = self.block_manager
+        tokens = self.config.max_num_batched_tokens - len(batch.decode)
+        seqs = self._seq_cap.value - len(batch.decode)
+        while seqs > 0 and self.waiting_prefill:
+            head = self.waiting_prefill[0]
+            # len(head) bounds the query length (a prefix-cache hit only shortens it):
+            # checked before allocating, so blocks are never taken only to be returned
+            if len(head) > tokens:
+                return
+            if not bm.can_ever_allocate(head):
+                # no amount of waiting frees enough blocks: end it instead of stalling
+                self._retire(self.waiting_prefill.popleft(), "aborted:kv_cache_too_small")
+                continue
+            if not bm.can_allocate(head):
+                return
+            self.waiting_prefill.popleft()
+            bm.allocate(head)
+            batch.prefill.append(head)
+            tokens -= head.num_tokens_to_compute
+            seqs -= 1
+
+    def schedule_model(self) -> ModelBatch:
+        """The next decoder step: running decodes first, then prefills."""
+        batch = ModelBatch()
+        self._take_decodes(batch)
+        self._take_prefills(batch)
+        if batch:
+            s = self.stats
+            s.num_model_steps += 1
+            s.num_mixed_steps += int(bool(batch.prefill and batch.decode))
+            s.num_prefilled_tokens += sum(r.num_tokens_to_compute for r in batch.prefill)
+            s.num_decoded_tokens += len(batch.decode)
+        return batch
+
+    # ---------------------------------------------------------------- recovery
+
     def on_model_oom(self, batch: ModelBatch) -> None:
-        """Put a failed decoder batch back exactly (nothing was mutated) and halve the cap."""
+        """Undo a decoder step that ran out of memory (nothing in it was mutated: tokens
+        and block growth happen in ``postprocess``) and cut the sequence cap."""
         self.stats.num_model_ooms += 1
-        attempted = len(batch.requests)
-        for request in reversed(batch.prefill):
+        for request in reversed(batch.prefill):  # newest first: the free list's order
             self.block_manager.deallocate(request)
             request.num_computed_tokens = 0
-            self.waiting_prefill.appendleft(request)
-        for request in reversed(batch.decode):
-            self.running.appendleft(request)
-        if attempted <= 1:
-            self.model_batch_limit = 1
-            if self.running:
-                self._give_up(self.running.pop(), "aborted:out_of_memory")
-            elif self.waiting_prefill:
-                self._give_up(self.waiting_prefill.popleft(), "aborted:out_of_memory")
+        self.waiting_prefill.extendleft(reversed(batch.prefill))
+        self.running.extendleft(reversed(batch.decode))
+        attempted = len(batch.prefill) + len(batch.decode)
+        if attempted > 1:
+            self._seq_cap.cut_to(attempted // 2)
             return
-        self.model_batch_limit = max(1, attempted // 2)
+        self._seq_cap.cut_to(1)  # nothing left to shrink: give one request up
+        if self.running:
+            self._retire(self.running.pop(), "aborted:out_of_memory")
+        elif self.waiting_prefill:
+            self._retire(self.waiting_prefill.popleft(), "aborted:out_of_memory")
 
     def on_audio_oom(self, requests: list[AsrRequest]) -> None:
+        """Undo an encoder call that ran out of memory and cut the frame cap."""
         self.stats.num_audio_ooms += 1
-        frames = sum(r.features.mel_frames for r in requests)
-        for request in reversed(requests):
+        for request in requests:
             request.timings.encode_start = None
             request.audio_embeds = None
-            self.waiting_encode.appendleft(request)
-        if len(requests) <= 1:
-            self._give_up(self.waiting_encode.popleft(), "aborted:out_of_memory")
-            return
-        self.audio_frame_limit = max(1, frames // 2)
+        self.waiting_encode.extendleft(reversed(requests))
+        if len(requests) > 1:
+            self._frame_cap.cut_to(sum(r.features.mel_frames for r in requests) // 2)
+        else:  # one recording alone does not fit: no cap can help it
+            self._retire(self.waiting_encode.popleft(), "aborted:out_of_memory")
 
     def relax_limits(self) -> None:
-        if self.model_batch_limit < self.config.max_num_seqs:
-            self.model_batch_limit = min(self.config.max_num_seqs, self.model_batch_limit * 2)
-        if self.audio_frame_limit < self.config.max_audio_batch_frames:
-            self.audio_frame_limit = min(self.config.max_audio_batch_frames,
-                                         self.audio_frame_limit * 2)
+        self._seq_cap.relax()
+        self._frame_cap.relax()
+
+    # ----------------------------------------------------------------- results
+
+    def _record(self, request: AsrRequest, token_id: int) -> bool:
+        """Append one sampled token; returns whether the request ended with it."""
+        request.num_computed_tokens = len(request)
+        request.append_token(token_id)
+        if request.stage is RequestStage.WAITING_PREFILL:
+            request.mark_prefilled()
+        if request.cancel_requested:
+            request.finish("cancelled")
+            return True
+        return request.check_finished()
+
+    def postprocess(self, batch: ModelBatch, token_ids: list[int]) -> list[AsrRequest]:
+        """Apply one step's sampled tokens (one per request, batch order); the requests
+        that ended are returned, the others go back to ``running`` with room for
+        their next token."""
+        requests = batch.requests
+        if len(token_ids) != len(requests):
+            raise ValueError(f"sampler returned {len(token_ids)} tokens for {len(requests)} requests")
+        finished: list[AsrRequest] = []
+        for request, token in zip(requests, token_ids):
+            if self._record(request, token):
+                self._release_finished(request)
+                finished.append(request)
+            else:
+                self.block_manager.may_append(request)
+                self.running.append(request)
+        return finished
 
     def decode_steps_for(self, batch: ModelBatch, limit: int, max_model_len: int) -> int:
         """How many decode steps a decode-only batch can run in one call (>= 1): bounded
@@ -228,71 +317,35 @@ class Scheduler:
         admission of a waiting request by up to ``steps - 1`` steps."""
         if limit <= 1 or batch.prefill or not batch.decode:
             return 1
-        steps = limit
-        for r in batch.decode:
-            if r.cancel_requested:
-                return 1
-            steps = min(steps, r.sampling.max_new_tokens - r.num_output_tokens,
-                        max_model_len - len(r) + 1)
+        if any(r.cancel_requested for r in batch.decode):
+            return 1
+        steps = min([limit] + [min(r.sampling.max_new_tokens - r.num_output_tokens,
+                                   max_model_len - len(r) + 1) for r in batch.decode])
         if steps <= 1:
             return 1
-        need = sum(self.block_manager.blocks_ahead(r, steps) for r in batch.decode)
-        if need > self.block_manager.num_free_blocks:
+        bm = self.block_manager
+        if sum(bm.blocks_ahead(r, steps) for r in batch.decode) > bm.num_free_blocks:
             return 1
         for r in batch.decode:
-            self.block_manager.append_ahead(r, steps)
+            bm.append_ahead(r, steps)
         return steps
 
     def postprocess_steps(self, batch: ModelBatch, tokens: list[list[int]]) -> list[AsrRequest]:
         """``postprocess`` for several decode steps of a decode-only batch: tokens[k][i] is
-        request i's token of step k; a request stops at its first finishing token."""
+        request i's token of step k; a request stops at its first ending token and its
+        later tokens are dropped."""
         requests = batch.decode
         if batch.prefill or any(len(step) != len(requests) for step in tokens):
             raise ValueError("multi-step results do not match the decode batch")
         finished: list[AsrRequest] = []
         for i, request in enumerate(requests):
-            done = False
-            for step in tokens:
-                request.num_computed_tokens = len(request)
-                request.append_token(step[i])
-                if request.cancel_requested:
-                    request.finish("cancelled")
-                    done = True
-                elif request.check_finished():
-                    done = True
-                if done:
-                    break
-            if not done:
+            if any(self._record(request, step[i]) for step in tokens):
+                self._release_finished(request)
+                finished.append(request)
+            else:
                 self.block_manager.may_append(request)
                 self.running.append(request)
-                continue
-            self.block_manager.deallocate(request)
-            request.audio_embeds = None
-            self.tracked.pop(request.request_id, None)
-            finished.append(request)
         extra = len(tokens) - 1
         self.stats.num_model_steps += extra
         self.stats.num_decoded_tokens += extra * len(requests)
-        return finished
-
-    def postprocess(self, batch: ModelBatch, token_ids: list[int]) -> list[AsrRequest]:
-        requests = batch.requests
-        if len(requests) != len(token_ids):
-            raise ValueError(f"sampler returned {len(token_ids)} tokens for {len(requests)} requests")
-        finished: list[AsrRequest] = []
-        for request, token_id in zip(requests, token_ids):
-            request.num_computed_tokens = len(request)
-            request.append_token(token_id)
-            if request.stage is RequestStage.WAITING_PREFILL:
-                request.mark_prefilled()
-            if request.cancel_requested:
-                request.finish("cancelled")
-            elif not request.check_finished():
-                self.block_manager.may_append(request)
-                self.running.append(request)
-                continue
-            self.block_manager.deallocate(request)
-            request.audio_embeds = None
-            self.tracked.pop(request.request_id, None)
-            finished.append(request)
         return finished

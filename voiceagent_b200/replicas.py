@@ -35,6 +35,50 @@ def route_by_duration(durations, world: int) -> list[list[int]]:
     return [sorted(x) for x in out]
 
 
+def share_of(durations, group: "ReplicaGroup") -> list[int]:
+    """This rank's request indices of a job routed by :func:`route_by_duration` (every
+    rank computes the same routing from the same durations, so no message is needed)."""
+    return route_by_duration(durations, group.world)[group.rank]
+
+
+def transcribe_share(group: "ReplicaGroup", job, transcribe, batch: int) -> dict[int, object]:
+    """Run this rank's share of ``job`` (``job.durations``, ``job.waveforms(indices)``)
+    through ``transcribe(waveforms) -> outputs`` in slices of ``batch`` requests, waveforms
+    synthesised per slice. Returns {request index: output} for the indices routed here."""
+    mine = share_of(job.durations, group)
+    out: dict[int, object] = {}
+    for i in range(0, len(mine), batch):
+        idx = mine[i:i + batch]
+        for j, o in zip(idx, transcribe(job.waveforms(idx))):
+            out[j] = o
+    return out
+
+
+def pin_host_cores(local_rank: int, local_world: int) -> list[int]:
+    """Restrict this process to its own slice of the host cores and size torch's
+    intra-op pool to it.
+
+    Each replica's scheduler, packer calls, graph launches and frontend copies are host
+    work; with one process per GPU on the same node, unpinned processes contend for the
+    same cores. The cores this process may use are split into ``local_world`` equal,
+    disjoint slices (in id order) and rank ``local_rank`` keeps slice ``local_rank``;
+    when there are fewer cores than ranks the slices overlap instead (every rank keeps
+    at least one core). Returns the cores kept."""
+    import torch
+
+    if not hasattr(os, "sched_getaffinity"):
+        return []
+    cores = sorted(os.sched_getaffinity(0))
+    if local_world <= 1 or not cores:
+        return cores
+    per = len(cores) // local_world
+    mine = (cores[local_rank * per:(local_rank + 1) * per] if per >= 1
+            else [cores[local_rank % len(cores)]])
+    os.sched_setaffinity(0, mine)
+    torch.set_num_threads(len(mine))
+    return mine
+
+
 class ReplicaGroup:
     """Process group of the replicas (no-op for a single process).
 

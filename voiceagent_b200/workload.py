@@ -37,3 +37,56 @@ def config3_clips(count: int = 512, seed: int = 0) -> list[np.ndarray]:
     durations = lognormal_durations(count, seed)
     rng = np.random.default_rng(seed + 1)
     return [synthetic_waveform(float(d), rng) for d in durations]
+
+
+# ------------------------------------------------------------ routed (shared) jobs
+#
+# A multi-GPU job is ONE list of requests that the host router splits over the
+# replicas (voiceagent_b200.replicas.route_by_duration). Every request's waveform comes
+# from its own seeded generator, so a rank synthesises only the requests routed to it
+# and the same index always yields the same samples whatever the world size.
+
+LONG_FILE_SECONDS = 1200.0  # config 4: one 20-minute recording ...
+LONG_CHUNK_SECONDS = 30.0   # ... submitted as 40 chunks of 30 s together
+
+
+class Job:
+    """A benchmark job: request durations plus the recipe for each request's waveform.
+
+    ``kind`` "config3": ``count`` lognormal clips (median 7 s, sigma 0.6, in [1, 35] s).
+    ``kind`` "config4": 4096 such clips plus one 20-minute synthetic recording cut into
+    30 s chunks (requests 4096..4135), all submitted together.
+    """
+
+    def __init__(self, kind: str, count: int = 512, seed: int = 0):
+        if kind not in ("config3", "config4"):
+            raise ValueError(f"unknown job kind {kind!r}")
+        self.kind, self.seed = kind, seed
+        n_clips = count if kind == "config3" else 4096
+        durations = list(lognormal_durations(n_clips, seed))
+        self.n_clips = n_clips
+        if kind == "config4":
+            n_chunks = int(LONG_FILE_SECONDS // LONG_CHUNK_SECONDS)
+            durations += [LONG_CHUNK_SECONDS] * n_chunks
+        self.durations = np.asarray(durations, dtype=np.float64)
+        self._long: np.ndarray | None = None
+
+    def __len__(self) -> int:
+        return len(self.durations)
+
+    def _long_file(self) -> np.ndarray:
+        if self._long is None:
+            self._long = synthetic_waveform(LONG_FILE_SECONDS,
+                                            np.random.default_rng([self.seed, 1 << 20]))
+        return self._long
+
+    def waveform(self, index: int) -> np.ndarray:
+        if index < self.n_clips:
+            return synthetic_waveform(float(self.durations[index]),
+                                      np.random.default_rng([self.seed, index]))
+        n = int(round(LONG_CHUNK_SECONDS * SAMPLE_RATE))
+        start = (index - self.n_clips) * n
+        return self._long_file()[start:start + n].copy()
+
+    def waveforms(self, indices) -> list[np.ndarray]:
+        return [self.waveform(int(i)) for i in indices]
