@@ -106,3 +106,36 @@ def record_greedy_steps(engine) -> dict[int, list[tuple[int, float, float]]]:
 
     runner._sample = sample
     return steps
+
+
+def force_tokens(engine, forced: dict[int, list[int]]) -> dict[int, list[int]]:
+    """Teacher forcing through the engine's own sampling hook: wrap
+    ``ModelRunner._sample`` (engine/model_runner.py:337-343) so that the engine keeps
+    generating from ``forced[clip]`` instead of its own samples, while recording what it
+    sampled at each position. ``forced`` is keyed by the clip's admission order (0, 1,
+    ... across this engine's ``add_request`` calls). Returns {clip: [sampled tokens]}."""
+    admit = engine.add_request
+    clip_of: dict[int, int] = {}
+    sampled: dict[int, list[int]] = {}
+
+    def add_request(*args, **kwargs):
+        request = admit(*args, **kwargs)
+        clip_of[request.request_id] = len(clip_of)
+        return request
+
+    runner = engine.model_runner
+    inner = runner._sample
+
+    def sample(logits, requests):
+        out = inner(logits, requests)
+        fed = []
+        for request, token in zip(requests, out):
+            clip = clip_of[request.request_id]
+            mine = sampled.setdefault(clip, [])
+            mine.append(int(token))
+            fed.append(int(forced[clip][len(mine) - 1]))
+        return fed
+
+    engine.add_request = add_request
+    runner._sample = sample
+    return sampled

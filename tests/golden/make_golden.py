@@ -25,6 +25,10 @@ the TTS paged decode) on the CPU interpreter. What each fixture pins:
 * ``sampler.npz``       -- greedy ``Sampler`` (sampler.py:16-27)
 * ``model_tiny.npz``    -- upstream HF Qwen3-ASR thinker on a tiny seeded config
 * ``frontend.npz``      -- ``AudioFrontend`` log-mel features (audio/frontend.py:71-94)
+* ``ref_engine_hf.npz`` -- the upstream HF thinker in bf16 (CPU), teacher forced on the
+  reference engine's tokens in ``ref_engine_tokens.npz`` (written on a B200 by
+  ``make_ref_engine_tokens.py``; run that first): the reference's two implementations
+  of the model compared position by position, with the same weights, audio and prompts
 """
 
 from __future__ import annotations
@@ -521,12 +525,12 @@ def _import_hf_with_shims():
     return hf
 
 
-def _build_hf_thinker(hf, cfg: dict, weights):
+def _build_hf_thinker(hf, cfg: dict, weights, mrope_section=(8, 4, 4)):
     import torch
     from reference import configuration_qwen3_asr as hfc
 
     audio = hfc.Qwen3ASRAudioEncoderConfig(**cfg["audio"])
-    text = hfc.Qwen3ASRTextConfig(**cfg["text"], rope_scaling={"mrope_section": [8, 4, 4],
+    text = hfc.Qwen3ASRTextConfig(**cfg["text"], rope_scaling={"mrope_section": list(mrope_section),
                                                                "rope_type": "default"})
     thinker_cfg = hfc.Qwen3ASRThinkerConfig(audio_config=audio.to_dict(), text_config=text.to_dict(),
                                             audio_token_id=cfg["audio_token_id"],
@@ -623,6 +627,67 @@ def gen_frontend(out: Path):
                         mel_filters=fe.extractor.mel_filters.astype(np.float32))
 
 
+def gen_ref_engine_hf(out: Path):
+    """The reference's upstream HF thinker (reference/modeling_qwen3_asr.py), 0.6B, the
+    seeded bf16 checkpoint weights, bf16 on the CPU, teacher forced on the reference
+    engine's greedy tokens (``ref_engine_tokens.npz``): per clip one forward over the
+    prompt plus the engine's tokens, the argmax at every generated position. Audio comes
+    from the reference's own frontend; prompts are the pinned template ids."""
+    import tempfile
+
+    import torch
+    from qwen_asr_vllm.audio.frontend import AudioFrontend
+
+    from voiceagent_b200.checkpoint import PRESETS, TOKEN_IDS, random_state_dict, write_checkpoint
+    from voiceagent_b200.prompt import PromptBuilder
+
+    sys.path.insert(0, str(HERE))
+    from make_ref_engine_tokens import workload
+
+    ref = np.load(out / "ref_engine_tokens.npz")
+    tokens = ref["tokens"]
+    meta = json.loads(str(ref["meta"]))
+    hf = _import_hf_with_shims()
+    cfg = {"audio": dict(PRESETS["0.6b"]["audio"]),
+           "text": dict(PRESETS["0.6b"]["text"]), **TOKEN_IDS}
+    weights = random_state_dict("0.6b", seed=0)  # bf16: the checkpoint's exact values
+    weights["lm_head.weight"] = weights["model.embed_tokens.weight"]
+    cfg_text = dict(cfg["text"])
+    text_cfg = {"text": cfg_text}
+    thinker = _build_hf_thinker(hf, {**cfg, **text_cfg}, {k: v.float() for k, v in weights.items()},
+                                mrope_section=[24, 20, 20]).to(torch.bfloat16)
+    ckpt = write_checkpoint(Path(tempfile.mkdtemp()) / "ckpt", "0.6b", weights=False)
+    frontend = AudioFrontend(str(ckpt))
+    builder = PromptBuilder()
+    clips, n_tokens = workload()
+    preds = np.full_like(tokens, -1)
+    torch.set_num_threads(os.cpu_count() or 1)
+    for i, (clip, n) in enumerate(zip(clips, n_tokens)):
+        feats = frontend(clip, 16000)
+        prompt = builder.build(feats.num_audio_tokens, language="English").token_ids
+        assert len(prompt) == meta["prompt_tokens"][i], (len(prompt), meta["prompt_tokens"][i])
+        ids = torch.tensor([prompt + [int(t) for t in tokens[i, :n - 1]]])
+        mel = feats.mel.to(torch.bfloat16)
+        with torch.no_grad():
+            logits = thinker(input_ids=ids, input_features=mel.unsqueeze(0),
+                             feature_attention_mask=torch.ones(1, mel.shape[1], dtype=torch.long),
+                             attention_mask=torch.ones_like(ids), use_cache=False,
+                             cache_position=torch.arange(ids.shape[1])).logits[0]
+        preds[i, :n] = logits[len(prompt) - 1:].float().argmax(-1).numpy()
+        print(f"clip {i}: {(preds[i, :n] == tokens[i, :n]).mean():.4f}", flush=True)
+    valid = tokens >= 0
+    agreement = float((preds == tokens)[valid].mean())
+    np.savez_compressed(out / "ref_engine_hf.npz", hf_forced_tokens=preds,
+                        agreement=np.asarray(agreement),
+                        meta=np.array(json.dumps({
+                            "generator": "tests/golden/make_golden.py --only ref_engine_hf",
+                            "model": "reference/modeling_qwen3_asr.py thinker, bf16, CPU, eager "
+                                     "attention, torch " + torch.__version__,
+                            "teacher_forced_on": "ref_engine_tokens.npz tokens",
+                            "agreement_with_reference_engine": agreement})))
+    print("HF bf16 vs reference engine, teacher forced:", agreement)
+
+
 GENERATORS = {
     "audio_pack": gen_audio_pack,
     "decoder_pack": gen_decoder_pack,
@@ -636,6 +701,7 @@ GENERATORS = {
     "sampler": gen_sampler,
     "model_tiny": gen_model_tiny,
     "frontend": gen_frontend,
+    "ref_engine_hf": gen_ref_engine_hf,
 }
 
 

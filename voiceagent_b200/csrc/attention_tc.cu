@@ -52,7 +52,17 @@ constexpr int kPfQBytes = 128 * 128 * 2;       // 32 KiB: 2 d-halves x [128 rows
 constexpr int kPfKVBytes = kPfBN * 128 * 2;    // 16 KiB: 2 d-halves x [64 rows x 128 B]
 constexpr int kPfPBytes = 128 * kPfBN * 2;     // 16 KiB: [128 rows x 128 B]
 constexpr int kPfStages = 2;
-constexpr int kPfSmem = 1024 /*align slack*/ + kPfQBytes + 2 * kPfStages * kPfKVBytes + kPfPBytes + 256;
+// P of tile j is written over K of tile j (same stage, same 16 KiB): S = Q K^T has
+// completed when the softmax reads S, and the stage is refilled only after P V of tile j.
+// Without a separate P buffer the CTA needs ~97 KB, so two CTAs share an SM.
+static_assert(kPfPBytes == kPfKVBytes, "P reuses its tile's K buffer");
+constexpr int kPfSmem = 1024 /*align slack*/ + kPfQBytes + 2 * kPfStages * kPfKVBytes + 256;
+// Online softmax with lazy rescaling (the conditional rescale of FlashAttention-4): the
+// running maximum a row exponentiates against only moves when a tile's maximum exceeds it
+// by more than kPfRescaleLog2 (base 2), so P stays below 2^8 and O in TMEM is rescaled
+// (a TMEM round trip of 128 columns) on few tiles instead of most. The final O / l uses
+// the same maximum for both, so the result is the softmax whichever maximum was used.
+constexpr float kPfRescaleLog2 = 8.f;
 
 struct PrefillArgs {
   const int32_t *cu_seqlens_q;
@@ -69,7 +79,7 @@ struct PrefillArgs {
   int32_t *error_flag;
 };
 
-__global__ void __launch_bounds__(kTcThreads, 1)
+__global__ void __launch_bounds__(kTcThreads, 2)
     paged_prefill_kernel(const __grid_constant__ CUtensorMap tm_q,
                          const __grid_constant__ CUtensorMap tm_k,
                          const __grid_constant__ CUtensorMap tm_v, const PrefillArgs a) {
@@ -79,16 +89,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint8_t *sQ = smem;
   uint8_t *sK = sQ + kPfQBytes;                  // [stage] 16 KiB each
   uint8_t *sV = sK + kPfStages * kPfKVBytes;     // [stage] 16 KiB each
-  uint8_t *sP = sV + kPfStages * kPfKVBytes;
-  uint64_t *bars = reinterpret_cast<uint64_t *>(sP + kPfPBytes);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(sV + kPfStages * kPfKVBytes);
   uint64_t *q_full = bars + 0;
   uint64_t *kv_full = bars + 1;   // [2]
   uint64_t *kv_empty = bars + 3;  // [2]
   uint64_t *s_full = bars + 5;    // [2]
   uint64_t *s_free = bars + 7;    // [2]
   uint64_t *p_full = bars + 9;
-  uint64_t *o_done = bars + 10;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 11);
+  uint64_t *o_done = bars + 10;   // one phase per P V tile
+  uint64_t *o_last = bars + 11;   // the last P V tile (single phase)
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 12);
   __shared__ int abort_flag;
   __shared__ int s_tile_info[4];
 
@@ -147,6 +157,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
     mbar_init(p_full, 128);
     mbar_init(o_done, 1);
+    mbar_init(o_last, 1);
     fence_barrier_init();
   }
   if (warp == 5) {
@@ -196,19 +207,20 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (lane == 0) {
       constexpr uint32_t idesc_s = idesc_bf16_f32(128, kPfBN, false, false);
       constexpr uint32_t idesc_o = idesc_bf16_f32(128, 128, false, true);
-      const uint32_t q_base = smem_addr(sQ), k_base = smem_addr(sK), v_base = smem_addr(sV),
-                     p_base = smem_addr(sP);
+      const uint32_t q_base = smem_addr(sQ), k_base = smem_addr(sK), v_base = smem_addr(sV);
       bool ok = mbar_wait(q_full, 0, a.error_flag, &abort_flag);
       auto issue_pv = [&](int jj) {
         const uint32_t vb = v_base + (jj & 1) * kPfKVBytes;
+        const uint32_t pb = k_base + (jj & 1) * kPfKVBytes;  // P(jj) over K(jj)
 #pragma unroll
         for (int k = 0; k < kPfBN / 16; ++k) {
-          const uint64_t ad = smem_desc_sw128(p_base + k * 32, 16, 1024);
+          const uint64_t ad = smem_desc_sw128(pb + k * 32, 16, 1024);
           const uint64_t bd = smem_desc_sw128(vb + k * 2048, 8192, 1024);
           umma_f16_ss(tmem + 128, ad, bd, idesc_o, (jj > 0 || k > 0) ? 1u : 0u);
         }
         umma_commit(&kv_empty[jj & 1]);
         umma_commit(o_done);
+        if (jj == n_tiles - 1) umma_commit(o_last);
       };
       for (int j = 0; ok && j < n_tiles; ++j) {
         const int st = j & 1;
@@ -262,7 +274,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         s[c] = (key0 + c <= p_row) ? s[c] * a.scale_log2 : -INFINITY;
         mx = fmaxf(mx, s[c]);
       }
-      const float m_new = fmaxf(m, mx);
+      // Tile 0 sets the maximum (key 0 is visible to every row: finite). Later tiles
+      // move it only past the threshold; O then needs its rescale, after P V of the
+      // previous tile. At tile j that P V is the only one that can be outstanding (S of
+      // tile j was issued after P V of tile j - 2), so the parity wait is exact.
+      const bool move = j == 0 || mx > m + kPfRescaleLog2;
+      const float m_new = move ? fmaxf(m, mx) : m;
       const float alpha = exp2f(m - m_new);  // m = -inf on the first tile -> 0
       float sum = 0.f;
 #pragma unroll
@@ -272,28 +289,26 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
       l = l * alpha + sum;
       m = m_new;
-      if (j > 0) {
+      if (j > 0 && __any_sync(0xffffffffu, move)) {
         if (!mbar_wait(o_done, (j - 1) & 1, a.error_flag, &abort_flag)) { ok = false; break; }
         tc_fence_after();
-        if (__any_sync(0xffffffffu, alpha < 1.f)) {
 #pragma unroll
-          for (int cc = 0; cc < 4; ++cc) {
-            float o[32];
-            tmem_ld32(lane_base + 128 + cc * 32, o);
-            tmem_wait_ld();
+        for (int cc = 0; cc < 4; ++cc) {
+          float o[32];
+          tmem_ld32(lane_base + 128 + cc * 32, o);
+          tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] *= alpha;
-            tmem_st32(lane_base + 128 + cc * 32, o);
-          }
-          tmem_wait_st();
+          for (int i = 0; i < 32; ++i) o[i] *= alpha;
+          tmem_st32(lane_base + 128 + cc * 32, o);
         }
+        tmem_wait_st();
       }
-      store_p_row64(sP, r, s);
+      store_p_row64(sK + (j & 1) * kPfKVBytes, r, s);  // P(j) over K(j)
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(p_full);
     }
-    if (ok && mbar_wait(o_done, (n_tiles - 1) & 1, a.error_flag, &abort_flag)) {
+    if (ok && mbar_wait(o_last, 0, a.error_flag, &abort_flag)) {
       tc_fence_after();
       const float inv = 1.f / l;
       __nv_bfloat16 *dst = a.out + static_cast<int64_t>(q0 + t) * a.out_stride + head * 128;
@@ -327,21 +342,42 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
 // =============================================================================
 // Windowed bidirectional attention, head_dim 64, segments of at most 128 tokens.
-// CTA = (segment, head). S = Q K^T (128x128, K=64), softmax over the whole row
+// Work item = (segment, head): S = Q K^T (128x128, K=64), softmax over the whole row
 // (no online rescaling needed), O = P V (128x64, K=128).
+//
+// Persistent pipeline: the grid is at most two CTAs per SM, and CTA c takes items c,
+// c + grid, ... (item = segment * heads + head). TMEM (S in columns 0-127, O in 128-191)
+// and the barriers are set up once per CTA. Shared memory holds two (Q, K, V) buffers:
+// the producer loads item i + 1 into one while item i computes from the other, the MMA
+// warp issues S of item i + 1 as soon as the softmax has read S of item i out of TMEM,
+// and P of item i (two 64-key K-major halves) is written over Q and K of its buffer once
+// S is done (the buffer is refilled only after P V of item i).
 // =============================================================================
 
-constexpr int kWinTile = 16384;  // [128 rows x 128 B]
-constexpr int kWinSmem = 1024 + 3 * kWinTile + 2 * kWinTile + 128;
+constexpr int kWinTile = 16384;                   // [128 rows x 128 B]
+constexpr int kWinBuf = 3 * kWinTile;             // Q | K | V of one item
+constexpr int kWinSmem = 1024 + 2 * kWinBuf + 256;
 
 struct WindowArgs {
   const int32_t *cu_seqlens;
   int num_segments;
+  int num_heads;
   float scale_log2;
   __nv_bfloat16 *out;
   int64_t out_stride;
   int32_t *error_flag;
 };
+
+// Rows and head of item `item`; false for an empty or over-long segment (skipped by every
+// role alike, so all roles see the same sequence of items).
+__device__ __forceinline__ bool window_item(const WindowArgs &a, int item, int &row0, int &len,
+                                            int &head) {
+  const int seg = item / a.num_heads;
+  head = item - seg * a.num_heads;
+  row0 = a.cu_seqlens[seg];
+  len = a.cu_seqlens[seg + 1] - row0;
+  return len > 0 && len <= 128;
+}
 
 __global__ void __launch_bounds__(kTcThreads, 2)
     varlen_window_kernel(const __grid_constant__ CUtensorMap tm_q,
@@ -350,32 +386,40 @@ __global__ void __launch_bounds__(kTcThreads, 2)
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                               ~uintptr_t(1023));
-  uint8_t *sQ = smem, *sK = smem + kWinTile, *sV = smem + 2 * kWinTile, *sP = smem + 3 * kWinTile;
-  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + 5 * kWinTile);
-  uint64_t *ld_full = bars, *s_full = bars + 1, *p_full = bars + 2, *o_full = bars + 3;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 4);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + 2 * kWinBuf);
+  uint64_t *ld_full = bars;       // [2] item's Q, K, V landed in buffer b
+  uint64_t *ld_empty = bars + 2;  // [2] buffer b free (P V of its item done)
+  uint64_t *s_full = bars + 4;    // S in TMEM
+  uint64_t *s_free = bars + 5;    // S read out by the softmax (128 arrivals)
+  uint64_t *p_full = bars + 6;    // P written (128 arrivals)
+  uint64_t *o_full = bars + 7;    // O in TMEM
+  uint64_t *o_free = bars + 8;    // O read out (128 arrivals)
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 9);
   __shared__ int abort_flag;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int seg = blockIdx.x, h = blockIdx.y;
-  const int row0 = a.cu_seqlens[seg];
-  const int len = a.cu_seqlens[seg + 1] - row0;
-  if (len <= 0) return;
-  if (len > 128) {
-    if (tid == 0) raise_flag(a.error_flag, B200ASR_DEVERR_LENGTH);
-    return;
-  }
+  const int items = a.num_segments * a.num_heads;
   if (tid == 0) {
     abort_flag = 0;
-    mbar_init(ld_full, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&ld_full[b], 1);
+      mbar_init(&ld_empty[b], 1);
+    }
     mbar_init(s_full, 1);
+    mbar_init(s_free, 128);
     mbar_init(p_full, 128);
     mbar_init(o_full, 1);
+    mbar_init(o_free, 128);
     fence_barrier_init();
   }
   if (warp == 5) {
     tmem_alloc(tmem_slot, 256);
     tmem_relinquish();
+  }
+  if (warp == 4 && lane == 0) {
+    prefetch_tmap(&tm_q);
+    prefetch_tmap(&tm_k);
+    prefetch_tmap(&tm_v);
   }
   tc_fence_before();
   __syncthreads();
@@ -383,44 +427,84 @@ __global__ void __launch_bounds__(kTcThreads, 2)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 4) {
+    // ------------------------------------------------------------ producer
     if (lane == 0) {
-      mbar_arrive_expect_tx(ld_full, 3 * kWinTile);
-      tma_load_3d(sQ, &tm_q, 0, h, row0, ld_full);
-      tma_load_3d(sK, &tm_k, 0, h, row0, ld_full);
-      tma_load_3d(sV, &tm_v, 0, h, row0, ld_full);
+      uint32_t it = 0;
+      for (int item = blockIdx.x; item < items; item += gridDim.x) {
+        int row0, len, head;
+        if (!window_item(a, item, row0, len, head)) {
+          if (len > 128) raise_flag(a.error_flag, B200ASR_DEVERR_LENGTH);
+          continue;
+        }
+        const int b = it & 1;
+        if (!mbar_wait(&ld_empty[b], ((it >> 1) & 1) ^ 1, a.error_flag, &abort_flag)) break;
+        uint8_t *buf = smem + b * kWinBuf;
+        mbar_arrive_expect_tx(&ld_full[b], kWinBuf);
+        tma_load_3d(buf, &tm_q, 0, head, row0, &ld_full[b]);
+        tma_load_3d(buf + kWinTile, &tm_k, 0, head, row0, &ld_full[b]);
+        tma_load_3d(buf + 2 * kWinTile, &tm_v, 0, head, row0, &ld_full[b]);
+        ++it;
+      }
     }
   } else if (warp == 5) {
+    // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc_s = idesc_bf16_f32(128, 128, false, false);
       constexpr uint32_t idesc_o = idesc_bf16_f32(128, 64, false, true);
-      const uint32_t qb = smem_addr(sQ), kb = smem_addr(sK), vb = smem_addr(sV), pb = smem_addr(sP);
-      if (mbar_wait(ld_full, 0, a.error_flag, &abort_flag)) {
+      const uint32_t base = smem_addr(smem);
+      // S of item `it` (buffer it & 1) into TMEM columns 0-127
+      auto issue_s = [&](uint32_t it) -> bool {
+        const uint32_t b = it & 1;
+        if (!mbar_wait(&ld_full[b], (it >> 1) & 1, a.error_flag, &abort_flag)) return false;
+        if (it > 0 && !mbar_wait(s_free, (it - 1) & 1, a.error_flag, &abort_flag)) return false;
         tc_fence_after();
+        const uint32_t qb = base + b * kWinBuf, kb = qb + kWinTile;
 #pragma unroll
         for (int k = 0; k < 4; ++k)
           umma_f16_ss(tmem, smem_desc_sw128(qb + k * 32, 16, 1024),
                       smem_desc_sw128(kb + k * 32, 16, 1024), idesc_s, k > 0 ? 1u : 0u);
         umma_commit(s_full);
-        if (mbar_wait(p_full, 0, a.error_flag, &abort_flag)) {
-          tc_fence_after();
+        return true;
+      };
+      uint32_t n = 0;  // valid items of this CTA
+      for (int item = blockIdx.x; item < items; item += gridDim.x) {
+        int row0, len, head;
+        n += window_item(a, item, row0, len, head) ? 1u : 0u;
+      }
+      bool ok = n == 0 || issue_s(0);
+      for (uint32_t it = 0; ok && it < n; ++it) {
+        if (it + 1 < n && !issue_s(it + 1)) break;  // overlaps the softmax of item `it`
+        if (!mbar_wait(p_full, it & 1, a.error_flag, &abort_flag)) break;
+        if (it > 0 && !mbar_wait(o_free, (it - 1) & 1, a.error_flag, &abort_flag)) break;
+        tc_fence_after();
+        const uint32_t pb = base + (it & 1) * kWinBuf;  // P over Q | K
+        const uint32_t vb = pb + 2 * kWinTile;
 #pragma unroll
-          for (int k = 0; k < 8; ++k)
-            umma_f16_ss(tmem + 128,
-                        smem_desc_sw128(pb + (k >> 2) * kWinTile + (k & 3) * 32, 16, 1024),
-                        smem_desc_sw128(vb + k * 2048, kWinTile, 1024), idesc_o, k > 0 ? 1u : 0u);
-          umma_commit(o_full);
-        }
+        for (int k = 0; k < 8; ++k)
+          umma_f16_ss(tmem + 128,
+                      smem_desc_sw128(pb + (k >> 2) * kWinTile + (k & 3) * 32, 16, 1024),
+                      smem_desc_sw128(vb + k * 2048, kWinTile, 1024), idesc_o, k > 0 ? 1u : 0u);
+        umma_commit(o_full);
+        umma_commit(&ld_empty[it & 1]);
       }
     }
   } else {
+    // ------------------------------------------------------------ softmax + epilogue
     const int r = tid;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
-    if (mbar_wait(s_full, 0, a.error_flag, &abort_flag)) {
+    uint32_t it = 0;
+    for (int item = blockIdx.x; item < items; item += gridDim.x) {
+      int row0, len, head;
+      if (!window_item(a, item, row0, len, head)) continue;
+      uint8_t *buf = smem + (it & 1) * kWinBuf;
+      if (!mbar_wait(s_full, it & 1, a.error_flag, &abort_flag)) break;
       tc_fence_after();
       float s[128];
 #pragma unroll
       for (int cc = 0; cc < 4; ++cc) tmem_ld32(lane_base + cc * 32, s + cc * 32);
       tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(s_free);  // the MMA warp may now compute S of the next item
       float mx = -INFINITY;
 #pragma unroll
       for (int c = 0; c < 128; ++c) {
@@ -433,33 +517,33 @@ __global__ void __launch_bounds__(kTcThreads, 2)
         s[c] = exp2f(s[c] - mx);
         sum += s[c];
       }
-      store_p_row64(sP, r, s);
-      store_p_row64(sP + kWinTile, r, s + 64);
+      store_p_row64(buf, r, s);
+      store_p_row64(buf + kWinTile, r, s + 64);
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(p_full);
-      if (mbar_wait(o_full, 0, a.error_flag, &abort_flag)) {
-        tc_fence_after();
+      if (!mbar_wait(o_full, it & 1, a.error_flag, &abort_flag)) break;
+      tc_fence_after();
+      float o[64];
+      tmem_ld32(lane_base + 128, o);
+      tmem_ld32(lane_base + 160, o + 32);
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(o_free);
+      if (r < len) {
         const float inv = 1.f / sum;
-        __nv_bfloat16 *dst = a.out + static_cast<int64_t>(row0 + r) * a.out_stride + h * 64;
+        __nv_bfloat16 *dst = a.out + static_cast<int64_t>(row0 + r) * a.out_stride + head * 64;
 #pragma unroll
-        for (int cc = 0; cc < 2; ++cc) {
-          float o[32];
-          tmem_ld32(lane_base + 128 + cc * 32, o);
-          tmem_wait_ld();
-          if (r < len) {
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              uint4 v;
-              v.x = pack2(o[8 * i + 0] * inv, o[8 * i + 1] * inv);
-              v.y = pack2(o[8 * i + 2] * inv, o[8 * i + 3] * inv);
-              v.z = pack2(o[8 * i + 4] * inv, o[8 * i + 5] * inv);
-              v.w = pack2(o[8 * i + 6] * inv, o[8 * i + 7] * inv);
-              *reinterpret_cast<uint4 *>(dst + cc * 32 + i * 8) = v;
-            }
-          }
+        for (int i = 0; i < 8; ++i) {
+          uint4 v;
+          v.x = pack2(o[8 * i + 0] * inv, o[8 * i + 1] * inv);
+          v.y = pack2(o[8 * i + 2] * inv, o[8 * i + 3] * inv);
+          v.z = pack2(o[8 * i + 4] * inv, o[8 * i + 5] * inv);
+          v.w = pack2(o[8 * i + 6] * inv, o[8 * i + 7] * inv);
+          *reinterpret_cast<uint4 *>(dst + i * 8) = v;
         }
       }
+      ++it;
     }
   }
   tc_fence_before();
@@ -554,7 +638,8 @@ extern "C" int b200asr_varlen_attention(const void *q, int64_t q_row_stride, con
                    q_row_stride % 8 == 0 && k_row_stride % 8 == 0 && v_row_stride % 8 == 0 &&
                    out_row_stride % 8 == 0,
                "varlen_attention: tensors and row strides must be 16-byte aligned");
-  B200_REQUIRE(num_segments <= 0x7fffffff && num_heads <= 65535, "varlen_attention: grid too large");
+  B200_REQUIRE(static_cast<int64_t>(num_segments) * num_heads <= 0x7fffffff,
+               "varlen_attention: too many (segment, head) items");
   CUtensorMap tq, tk, tv;
   if (!make_tmap_3d_bf16(&tq, q, 64, num_heads, total_tokens, 128, q_row_stride * 2, 64, 1, 128) ||
       !make_tmap_3d_bf16(&tk, k, 64, num_heads, total_tokens, 128, k_row_stride * 2, 64, 1, 128) ||
@@ -570,11 +655,13 @@ extern "C" int b200asr_varlen_attention(const void *q, int64_t q_row_stride, con
   WindowArgs a{};
   a.cu_seqlens = cu_seqlens;
   a.num_segments = num_segments;
+  a.num_heads = num_heads;
   a.scale_log2 = scale * kTcLog2e;
   a.out = static_cast<__nv_bfloat16 *>(out);
   a.out_stride = out_row_stride;
   a.error_flag = error_flag;
-  dim3 grid(num_segments, num_heads);
+  const int64_t items = static_cast<int64_t>(num_segments) * num_heads;
+  const int grid = static_cast<int>(std::min<int64_t>(items, 2 * num_sms()));
   varlen_window_kernel<<<grid, kTcThreads, kWinSmem, stream>>>(tq, tk, tv, a);
   B200_CUDA_LAUNCH_CHECK("varlen_attention");
   return B200ASR_OK;

@@ -39,6 +39,7 @@ constexpr int kDecStage = 16;
 constexpr int kDecStages = 3;
 constexpr int kDecMaxBatch = 1024;
 constexpr size_t kDecHeaderBytes = 4096;  // per-sequence merge counters (int32 x 1024)
+constexpr int kDecBtCache = 1024;  // block-table entries kept in shared memory (B * bt_stride)
 constexpr float kLog2e = 1.4426950408889634f;
 
 template <int HKV, int G>
@@ -53,8 +54,9 @@ struct Dec {
   static constexpr uint32_t TX_KV = 2 * KV_BYTES;
   static constexpr uint32_t TX_Q = H * kDecD * 2;
   static constexpr size_t SMEM = 1024 + static_cast<size_t>(kDecStages) * STAGE_BYTES +
-                                 4 * (kDecMaxBatch + 1) * 4 + 2 * kDecStages * 8 +
-                                 kDecStages * 32 + 64;
+                                 4 * (kDecMaxBatch + 1) * 4 + kDecBtCache * 4 +
+                                 2 * kDecStages * 8 + kDecStages * 32 + 64;
+  static_assert(SMEM <= 232448, "dynamic shared memory above the 227 KB per-CTA limit");
   static_assert(G >= 1 && G <= 8, "group size");
   static_assert(HKV <= 8, "a stage box holds at most 8 KV heads");
 };
@@ -265,8 +267,9 @@ __global__ void __launch_bounds__(Dec<HKV, G>::THREADS, 1)
   int *s_sp = s_cuk + kDecMaxBatch + 1;      // [B + 1] first stage of each sequence
   int *s_parts = s_sp + kDecMaxBatch + 1;    // [B + 1] first partial slot of each sequence
   int *s_first = s_parts + kDecMaxBatch + 1;  // [B] first CTA of each sequence
+  int *s_bt = s_first + kDecMaxBatch + 1;     // [B * bt_stride] block tables, when they fit
   uint64_t *full = reinterpret_cast<uint64_t *>(
-      (reinterpret_cast<uintptr_t>(s_first + kDecMaxBatch + 1) + 7) & ~uintptr_t(7));
+      (reinterpret_cast<uintptr_t>(s_bt + kDecBtCache) + 7) & ~uintptr_t(7));
   uint64_t *empty = full + kDecStages;
   StageInfo *info = reinterpret_cast<StageInfo *>(empty + kDecStages);
   __shared__ int abort_flag;
@@ -294,7 +297,26 @@ __global__ void __launch_bounds__(Dec<HKV, G>::THREADS, 1)
   // launches that finished before the step's decoder kernels (the packer, earlier
   // steps): with programmatic dependent launch they are read, and the first ring of
   // stages requested, before the wait on the kernel that wrote q and the newest K/V.
-  for (int i = tid; i <= B; i += blockDim.x) s_cuk[i] = a.cu_seqlens_k[i];
+  // Lengths and (when B * bt_stride entries fit) the block tables are loaded in the same
+  // round trip -- every thread issues its loads before storing any -- so the first TMA
+  // request waits for one global-memory latency instead of two.
+  const int n_bt = B * a.bt_stride;
+  const bool bt_cached = n_bt <= kDecBtCache;
+  for (int base = 0; base <= B || (bt_cached && base < n_bt); base += 4 * blockDim.x) {
+    int cu_v[4], bt_v[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int i = base + k * blockDim.x + tid;
+      cu_v[k] = i <= B ? a.cu_seqlens_k[i] : 0;
+      bt_v[k] = bt_cached && i < n_bt ? a.block_tables[i] : 0;
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int i = base + k * blockDim.x + tid;
+      if (i <= B) s_cuk[i] = cu_v[k];
+      if (bt_cached && i < n_bt) s_bt[i] = bt_v[k];
+    }
+  }
   __syncthreads();
 
   if (warp == HKV) {
@@ -365,7 +387,8 @@ __global__ void __launch_bounds__(Dec<HKV, G>::THREADS, 1)
           if (col >= a.bt_stride) {  // context longer than its block-table row
             raise_flag(a.error_flag, B200ASR_DEVERR_LENGTH);
           } else {
-            blk = a.block_tables[static_cast<int64_t>(b) * a.bt_stride + col];
+            const int64_t at = static_cast<int64_t>(b) * a.bt_stride + col;
+            blk = bt_cached ? s_bt[at] : a.block_tables[at];
             if (blk < 0 || blk >= a.num_blocks) {
               raise_flag(a.error_flag, B200ASR_DEVERR_BLOCK);
               blk = 0;
@@ -640,32 +663,38 @@ int num_sms() {
 // =============================================================================
 constexpr int kShortTok = 64;
 constexpr int kShortStages = 3;
-constexpr int kShortWarps = 4;
+constexpr int kShortWarps = 4;    // consumer warps of one group: 16 tokens of a stage each
 constexpr int kShortMaxCtx = 512;  // the host picks this kernel for max_seqlen_k <= 512
-
+// Two consumer groups where two CTAs still fit an SM (G <= 2: scratch of 8 warps x G rows).
 template <int G>
+constexpr int short_groups() { return G <= 2 ? 2 : 1; }
+
+// GR consumer groups of four warps: group g takes the stages j of a unit with j % GR == g,
+// so GR stages of one unit are processed at once; every group keeps its own softmax state
+// and the groups' states are combined at the unit's end. Each of the first GR stages of a
+// unit carries the unit's query rows (one copy per group).
+template <int G, int GR>
 struct Short {
   static constexpr int HALF = kShortTok * 128;  // 64 tokens x 64 dims x 2 B = 8 KiB
   static constexpr int KV_BYTES = 2 * HALF;     // one head's K (or V) stage: 16 KiB
   static constexpr int Q_BYTES = ((G * kDecD * 2 + 1023) / 1024) * 1024;
   static constexpr int STAGE_BYTES = 2 * KV_BYTES + Q_BYTES;
-  static constexpr int CONSUMERS = kShortWarps * 32;
+  static constexpr int WARPS = kShortWarps * GR;  // consumer warps
+  static constexpr int CONSUMERS = WARPS * 32;
   static constexpr int THREADS = CONSUMERS + 32;
-  static constexpr int SCRATCH_BYTES = kShortWarps * G * (kDecD + 2) * 4;
+  static constexpr int SCRATCH_BYTES = WARPS * G * (kDecD + 2) * 4;
   static constexpr size_t SMEM = 1024 + static_cast<size_t>(kShortStages) * STAGE_BYTES +
-                                 SCRATCH_BYTES + 2 * kShortStages * 8 + kShortStages * 16 + 64;
+                                 SCRATCH_BYTES + 2 * kShortStages * 8 + 64;
+  static_assert(GR == 1 || GR == 2, "one or two consumer groups");
+  static_assert(2 * (SMEM + 1024) <= 233472, "two CTAs per SM");
 };
 
-struct ShortStage {
-  int b, h, ntok, flags;  // flags 1: first stage of the unit (q attached), 2: last
-};
-
-template <int G>
-__global__ void __launch_bounds__(Short<G>::THREADS, 2)
+template <int G, int GR>
+__global__ void __launch_bounds__(Short<G, GR>::THREADS, 2)
     paged_decode_short_kernel(const __grid_constant__ CUtensorMap tm_k,
                               const __grid_constant__ CUtensorMap tm_v, const DecodeArgs a,
                               int hkv) {
-  using C = Short<G>;
+  using C = Short<G, GR>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                               ~uintptr_t(1023));
@@ -673,7 +702,6 @@ __global__ void __launch_bounds__(Short<G>::THREADS, 2)
   float *scratch = reinterpret_cast<float *>(smem + kShortStages * C::STAGE_BYTES);
   uint64_t *full = reinterpret_cast<uint64_t *>(reinterpret_cast<uint8_t *>(scratch) + C::SCRATCH_BYTES);
   uint64_t *empty = full + kShortStages;
-  ShortStage *info = reinterpret_cast<ShortStage *>(empty + kShortStages);
   __shared__ int abort_flag;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -683,17 +711,17 @@ __global__ void __launch_bounds__(Short<G>::THREADS, 2)
     abort_flag = 0;
     for (int s = 0; s < kShortStages; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kShortWarps);
+      mbar_init(&empty[s], kShortWarps);  // one group consumes each stage
     }
     fence_barrier_init();
   }
-  if (warp == kShortWarps && lane == 0) {
+  if (warp == C::WARPS && lane == 0) {
     prefetch_tmap(&tm_k);
     prefetch_tmap(&tm_v);
   }
   __syncthreads();
 
-  if (warp == kShortWarps) {
+  if (warp == C::WARPS) {
     // ------------------------------------------------------------------ producer
     // With programmatic dependent launch this CTA may start while the kernel before it
     // (the step's K/V store and q) still runs. The batch metadata and every cached row
@@ -718,12 +746,20 @@ __global__ void __launch_bounds__(Short<G>::THREADS, 2)
       const bool first_unit = u == static_cast<int>(blockIdx.x);
       if (!first_unit) wait_prev();
       const int b = u / hkv, h = u - (u / hkv) * hkv;
-      const int len = a.cu_seqlens_k[b + 1] - a.cu_seqlens_k[b];
+      // Lane i's block-table entry for stage i is read together with the length (the
+      // column is in the row whatever the length; it is used only if stage i exists),
+      // so the first TMA request waits for one global-memory latency, not two.
+      const int col0 = lane * kShortTok / a.block_size;
+      const int64_t row = static_cast<int64_t>(b) * a.bt_stride;
+      const int c_lo = a.cu_seqlens_k[b], c_hi = a.cu_seqlens_k[b + 1];
+      const int blk0 = col0 < a.bt_stride ? a.block_tables[row + col0] : 0;
+      const int len = c_hi - c_lo;
       if (len <= 0) continue;  // zero rows: written by CTA 0's consumers
       const int nst = (len + kShortTok - 1) / kShortTok;
+      const __nv_bfloat16 *q_src = a.q + b * a.q_stride + h * G * kDecD;
       // stages [0, early) go out before the wait (a fresh ring: no acquire blocks)
       const int early = waited ? 0 : min(nst - 1, kShortStages);
-      int q_stage = -1;  // ring slot whose barrier also counts q, when stage 0 went early
+      int q_slots[GR], n_q = 0;  // early stages whose barrier also counts q (sent after the wait)
       for (int wb = 0; wb < nst; wb += 32) {
         // lane i: cache slot of stage wb + i (block-table reads in flight together)
         const int s = wb + lane;
@@ -735,7 +771,7 @@ __global__ void __launch_bounds__(Short<G>::THREADS, 2)
           if (col >= a.bt_stride) {
             raise_flag(a.error_flag, B200ASR_DEVERR_LENGTH);
           } else {
-            blk = a.block_tables[static_cast<int64_t>(b) * a.bt_stride + col];
+            blk = wb == 0 ? blk0 : a.block_tables[row + col];
             if (blk < 0 || blk >= a.num_blocks) {
               raise_flag(a.error_flag, B200ASR_DEVERR_BLOCK);
               blk = 0;
@@ -754,53 +790,47 @@ __global__ void __launch_bounds__(Short<G>::THREADS, 2)
         for (int i = 0; i < nw; ++i) {
           const int j = wb + i;
           const int slot = __shfl_sync(0xffffffffu, d_slot, i);
-          const int n = min(kShortTok, len - j * kShortTok);
-          const int fl = (j == 0 ? 1 : 0) | (j == nst - 1 ? 2 : 0);
+          const bool with_q = j < GR;  // the first stage of each group carries q
           if (j >= early) wait_prev();
           int st;
           if (!acquire(st)) {
             wait_prev();
             return;
           }
-          if (lane == 0) {
-            info[st] = ShortStage{b, h, n, fl};
-            mbar_arrive_expect_tx(&full[st], 2 * C::KV_BYTES + ((fl & 1) ? G * kDecD * 2 : 0));
-          }
+          if (lane == 0)
+            mbar_arrive_expect_tx(&full[st], 2 * C::KV_BYTES + (with_q ? G * kDecD * 2 : 0));
           __syncwarp();
           uint8_t *stage = stages + st * C::STAGE_BYTES;
           if (lane < 2) tma_load_4d(stage + lane * C::KV_BYTES, lane ? &tm_v : &tm_k, 0, slot, 0, h, &full[st]);
-          if (fl & 1) {
+          if (with_q) {
             if (j < early) {
-              q_stage = st;
+              q_slots[n_q++] = st;
             } else if (lane == 2) {
-              bulk_g2s(stage + 2 * C::KV_BYTES, a.q + b * a.q_stride + h * G * kDecD,
-                       G * kDecD * 2, &full[st]);
+              bulk_g2s(stage + 2 * C::KV_BYTES, q_src, G * kDecD * 2, &full[st]);
             }
           }
           ++it_stage;
-          if (j == early - 1) {  // the early stages are out: wait, then q
+          if (j == early - 1) {  // the early stages are out: wait, then their q copies
             wait_prev();
-            if (q_stage >= 0 && lane == 2)
-              bulk_g2s(stages + q_stage * C::STAGE_BYTES + 2 * C::KV_BYTES,
-                       a.q + b * a.q_stride + h * G * kDecD, G * kDecD * 2, &full[q_stage]);
+            if (lane == 2)
+              for (int k = 0; k < n_q; ++k)
+                bulk_g2s(stages + q_slots[k] * C::STAGE_BYTES + 2 * C::KV_BYTES, q_src,
+                         G * kDecD * 2, &full[q_slots[k]]);
           }
         }
       }
     }
     wait_prev();
-    int st;  // terminal stage
-    if (!acquire(st)) return;
-    if (lane == 0) {
-      info[st] = ShortStage{-1, 0, 0, 0};
-      mbar_arrive(&full[st]);
-    }
     return;
   }
 
   // -------------------------------------------------------------------- consumers
+  // Every consumer warp walks the CTA's units and their stages in the producer's order
+  // (stage number = ring position), taking the stages of its group.
   pdl_wait();  // the output and the zero rows are written after the previous kernel
-  const int w = warp;               // token slice [16w, 16w + 16) of every stage
-  const int row = lane >> 2;        // MMA row = query head within the group (valid if < G)
+  const int w = warp % kShortWarps;  // token slice [16w, 16w + 16) of the group's stages
+  const int grp = warp / kShortWarps;
+  const int row = lane >> 2;         // MMA row = query head within the group (valid if < G)
   const int quad = lane & 3;
   const bool row_valid = row < G;
   const uint32_t stage_base = smem_addr(stages);
@@ -808,7 +838,7 @@ __global__ void __launch_bounds__(Short<G>::THREADS, 2)
   constexpr int H = G;  // query rows of a unit
 
   if (blockIdx.x == 0) {  // rows with no keys: zeros
-    for (int b = w; b < B; b += kShortWarps) {
+    for (int b = warp; b < B; b += C::WARPS) {
       if (a.cu_seqlens_k[b + 1] - a.cu_seqlens_k[b] <= 0) {
         for (int i = lane; i < hkv * G * kDecD / 8; i += 32)
           reinterpret_cast<uint4 *>(a.out + b * a.out_stride)[i] = make_uint4(0, 0, 0, 0);
@@ -824,103 +854,110 @@ __global__ void __launch_bounds__(Short<G>::THREADS, 2)
   // (valid when < G), and O^T for dims 16 mt + g (+ 8) of the same queries.
   uint32_t qa[8][2];  // Q as the B operand: Q[g][16 kk + 2c ..], Q[g][16 kk + 8 + 2c ..]
   float o[8][4];
-  float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
-  for (uint32_t it_stage = 0;; ++it_stage) {
-    const int st = it_stage % kShortStages;
-    const uint32_t ph = (it_stage / kShortStages) & 1;
-    if (!mbar_wait(&full[st], ph, a.error_flag, &abort_flag)) return;
-    const ShortStage si = info[st];
-    if (si.b < 0) break;
-    const int ntok = min(16, max(0, si.ntok - 16 * w));  // this warp's tokens in the stage
-    const uint32_t k_tile = stage_base + st * C::STAGE_BYTES + w * 16 * 128;
-    const uint32_t v_tile = k_tile + C::KV_BYTES;
+  float m_run[2], l_run[2];
+  bool live = true;  // false once a wait timed out: skip work, keep taking part in barriers
+  uint32_t it_stage = 0;
+  for (int u = blockIdx.x; u < units; u += gridDim.x) {
+    const int b = u / hkv, h = u - (u / hkv) * hkv;
+    const int len = a.cu_seqlens_k[b + 1] - a.cu_seqlens_k[b];
+    if (len <= 0) continue;
+    const int nst = (len + kShortTok - 1) / kShortTok;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+    m_run[0] = m_run[1] = -INFINITY;
+    l_run[0] = l_run[1] = 0.f;
+    for (int js = 0; js < nst; ++js, ++it_stage) {
+      if (js % GR != grp) continue;
+      const int st = it_stage % kShortStages;
+      const uint32_t ph = (it_stage / kShortStages) & 1;
+      if (live && !mbar_wait(&full[st], ph, a.error_flag, &abort_flag)) live = false;
+      if (!live) continue;
+      const int ntok = min(16, max(0, min(kShortTok, len - js * kShortTok) - 16 * w));
+      const uint32_t k_tile = stage_base + st * C::STAGE_BYTES + w * 16 * 128;
+      const uint32_t v_tile = k_tile + C::KV_BYTES;
 
-    if (si.flags & 1) {  // first stage of a unit: fresh state + the unit's query rows
+      if (js < GR) {  // this group's first stage of the unit: the unit's query rows
+        const uint8_t *qs = stages + st * C::STAGE_BYTES + 2 * C::KV_BYTES + (row_valid ? row : 0) * kDecD * 2;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
-      m_run[0] = m_run[1] = -INFINITY;
-      l_run[0] = l_run[1] = 0.f;
-      const uint8_t *qs = stages + st * C::STAGE_BYTES + 2 * C::KV_BYTES + (row_valid ? row : 0) * kDecD * 2;
-#pragma unroll
-      for (int kk = 0; kk < 8; ++kk) {
-        const uint32_t lo = *reinterpret_cast<const uint32_t *>(qs + (kk * 16 + quad * 2) * 2);
-        const uint32_t hi = *reinterpret_cast<const uint32_t *>(qs + (kk * 16 + 8 + quad * 2) * 2);
-        qa[kk][0] = row_valid ? lo : 0u;
-        qa[kk][1] = row_valid ? hi : 0u;
-      }
-    }
-    if (ntok > 0) {
-      if (ntok < 16) {  // clear V rows past the end so 0 * stale bytes stays 0
-        uint8_t *vt = stages + st * C::STAGE_BYTES + C::KV_BYTES + w * 16 * 128;
-        for (int i = lane; i < (16 - ntok) * 16; i += 32) {
-          const int r = ntok + i / 16, ch = i % 16;
-          *reinterpret_cast<uint4 *>(vt + (ch >> 3) * C::HALF + swz(r, ch & 7)) = make_uint4(0, 0, 0, 0);
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t lo = *reinterpret_cast<const uint32_t *>(qs + (kk * 16 + quad * 2) * 2);
+          const uint32_t hi = *reinterpret_cast<const uint32_t *>(qs + (kk * 16 + 8 + quad * 2) * 2);
+          qa[kk][0] = row_valid ? lo : 0u;
+          qa[kk][1] = row_valid ? hi : 0u;
         }
-        __syncwarp();
       }
-      // S^T[16 tokens][8 queries] = K (A, 16 x 16 per step) x Q^T (B): even / odd steps
-      // accumulate separately
-      float sa[4] = {0.f, 0.f, 0.f, 0.f}, sb[4] = {0.f, 0.f, 0.f, 0.f};
-      const int kt = (lm_mat & 1) * 8 + lm_row;  // ldmatrix row: token
+      if (ntok > 0) {
+        if (ntok < 16) {  // clear V rows past the end so 0 * stale bytes stays 0
+          uint8_t *vt = stages + st * C::STAGE_BYTES + C::KV_BYTES + w * 16 * 128;
+          for (int i = lane; i < (16 - ntok) * 16; i += 32) {
+            const int r = ntok + i / 16, ch = i % 16;
+            *reinterpret_cast<uint4 *>(vt + (ch >> 3) * C::HALF + swz(r, ch & 7)) = make_uint4(0, 0, 0, 0);
+          }
+          __syncwarp();
+        }
+        // S^T[16 tokens][8 queries] = K (A, 16 x 16 per step) x Q^T (B): even / odd steps
+        // accumulate separately
+        float sa[4] = {0.f, 0.f, 0.f, 0.f}, sb[4] = {0.f, 0.f, 0.f, 0.f};
+        const int kt = (lm_mat & 1) * 8 + lm_row;  // ldmatrix row: token
 #pragma unroll
-      for (int kk = 0; kk < 8; ++kk) {
-        const int chunk = 2 * kk + (lm_mat >> 1);
-        uint32_t a0, a1, a2, a3;
-        ldsm_x4(k_tile + (chunk >> 3) * C::HALF + swz(kt, chunk & 7), a0, a1, a2, a3);
-        mma16816_nv((kk & 1) ? sb : sa, a0, a1, a2, a3, qa[kk][0], qa[kk][1]);
-      }
-      // lane: tokens t0 = g, t1 = g + 8; queries 2c + e
-      float sv[2][2];  // [token][e]
-      const int t0 = row, t1 = row + 8;
+        for (int kk = 0; kk < 8; ++kk) {
+          const int chunk = 2 * kk + (lm_mat >> 1);
+          uint32_t a0, a1, a2, a3;
+          ldsm_x4(k_tile + (chunk >> 3) * C::HALF + swz(kt, chunk & 7), a0, a1, a2, a3);
+          mma16816_nv((kk & 1) ? sb : sa, a0, a1, a2, a3, qa[kk][0], qa[kk][1]);
+        }
+        // lane: tokens t0 = g, t1 = g + 8; queries 2c + e
+        float sv[2][2];  // [token][e]
+        const int t0 = row, t1 = row + 8;
 #pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        sv[0][e] = t0 < ntok ? (sa[e] + sb[e]) * a.scale_log2 : -INFINITY;
-        sv[1][e] = t1 < ntok ? (sa[2 + e] + sb[2 + e]) * a.scale_log2 : -INFINITY;
-      }
-      float alpha[2], pr[2][2];
+        for (int e = 0; e < 2; ++e) {
+          sv[0][e] = t0 < ntok ? (sa[e] + sb[e]) * a.scale_log2 : -INFINITY;
+          sv[1][e] = t1 < ntok ? (sa[2 + e] + sb[2 + e]) * a.scale_log2 : -INFINITY;
+        }
+        float alpha[2], pr[2][2];
 #pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        float mx = fmaxf(sv[0][e], sv[1][e]);  // over the 16 tokens: lanes of equal c
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-        const float m_new = fmaxf(m_run[e], mx);  // token 0 of the slice is valid: finite
-        alpha[e] = exp2f(m_run[e] - m_new);
-        pr[0][e] = exp2f(sv[0][e] - m_new);
-        pr[1][e] = exp2f(sv[1][e] - m_new);
-        float sum = pr[0][e] + pr[1][e];
-        sum += __shfl_xor_sync(0xffffffffu, sum, 4);
-        sum += __shfl_xor_sync(0xffffffffu, sum, 8);
-        sum += __shfl_xor_sync(0xffffffffu, sum, 16);
-        l_run[e] = l_run[e] * alpha[e] + sum;
-        m_run[e] = m_new;
-      }
+        for (int e = 0; e < 2; ++e) {
+          float mx = fmaxf(sv[0][e], sv[1][e]);  // over the 16 tokens: lanes of equal c
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+          const float m_new = fmaxf(m_run[e], mx);  // token 0 of the slice is valid: finite
+          alpha[e] = exp2f(m_run[e] - m_new);
+          pr[0][e] = exp2f(sv[0][e] - m_new);
+          pr[1][e] = exp2f(sv[1][e] - m_new);
+          float sum = pr[0][e] + pr[1][e];
+          sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+          sum += __shfl_xor_sync(0xffffffffu, sum, 8);
+          sum += __shfl_xor_sync(0xffffffffu, sum, 16);
+          l_run[e] = l_run[e] * alpha[e] + sum;
+          m_run[e] = m_new;
+        }
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        o[j][0] *= alpha[0];
-        o[j][1] *= alpha[1];
-        o[j][2] *= alpha[0];
-        o[j][3] *= alpha[1];
-      }
-      // P^T (tokens x queries) as two 8x8 blocks in accumulator layout -> transposed into
-      // the B fragments of O^T += V^T P^T (k = token, n = query)
-      const uint32_t pb0 = movmatrix_t(pack2(pr[0][0], pr[0][1]));  // tokens 0-7
-      const uint32_t pb1 = movmatrix_t(pack2(pr[1][0], pr[1][1]));  // tokens 8-15
-      const int vt_row = (lm_mat >> 1) * 8 + lm_row;  // ldmatrix row: token
+        for (int j = 0; j < 8; ++j) {
+          o[j][0] *= alpha[0];
+          o[j][1] *= alpha[1];
+          o[j][2] *= alpha[0];
+          o[j][3] *= alpha[1];
+        }
+        // P^T (tokens x queries) as two 8x8 blocks in accumulator layout -> transposed into
+        // the B fragments of O^T += V^T P^T (k = token, n = query)
+        const uint32_t pb0 = movmatrix_t(pack2(pr[0][0], pr[0][1]));  // tokens 0-7
+        const uint32_t pb1 = movmatrix_t(pack2(pr[1][0], pr[1][1]));  // tokens 8-15
+        const int vt_row = (lm_mat >> 1) * 8 + lm_row;  // ldmatrix row: token
 #pragma unroll
-      for (int mt = 0; mt < 8; ++mt) {
-        const int chunk = 2 * mt + (lm_mat & 1);
-        uint32_t a0, a1, a2, a3;
-        ldsm_x4_t(v_tile + (chunk >> 3) * C::HALF + swz(vt_row, chunk & 7), a0, a1, a2, a3);
-        mma16816_nv(o[mt], a0, a1, a2, a3, pb0, pb1);
+        for (int mt = 0; mt < 8; ++mt) {
+          const int chunk = 2 * mt + (lm_mat & 1);
+          uint32_t a0, a1, a2, a3;
+          ldsm_x4_t(v_tile + (chunk >> 3) * C::HALF + swz(vt_row, chunk & 7), a0, a1, a2, a3);
+          mma16816_nv(o[mt], a0, a1, a2, a3, pb0, pb1);
+        }
       }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[st]);
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[st]);
-    if (!(si.flags & 2)) continue;
 
-    // ----------------------------------------------- unit end: combine the 4 warps
-    float *sm = scratch + w * H * (kDecD + 2);  // [H][2] (m, l) then [H][128] o
+    // ----------------------------------------- unit end: combine every warp's state
+    float *sm = scratch + warp * H * (kDecD + 2);  // [H][2] (m, l) then [H][128] o
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
       const int q = 2 * quad + e;
@@ -936,14 +973,14 @@ __global__ void __launch_bounds__(Short<G>::THREADS, 2)
       }
     }
     consumer_sync(C::CONSUMERS);
-    for (int idx = threadIdx.x; idx < H * kDecD / 2; idx += C::CONSUMERS) {
+    for (int idx = threadIdx.x; live && idx < H * kDecD / 2; idx += C::CONSUMERS) {
       const int g = idx / (kDecD / 2), d = (idx % (kDecD / 2)) * 2;
       float mm = -INFINITY;
 #pragma unroll
-      for (int v = 0; v < kShortWarps; ++v) mm = fmaxf(mm, scratch[v * H * (kDecD + 2) + g * 2]);
+      for (int v = 0; v < C::WARPS; ++v) mm = fmaxf(mm, scratch[v * H * (kDecD + 2) + g * 2]);
       float l = 0.f, o0 = 0.f, o1 = 0.f;
 #pragma unroll
-      for (int v = 0; v < kShortWarps; ++v) {
+      for (int v = 0; v < C::WARPS; ++v) {
         const float *sv = scratch + v * H * (kDecD + 2);
         const float wgt = exp2f(sv[g * 2] - mm);  // 0 for a warp that saw no token
         l += sv[g * 2 + 1] * wgt;
@@ -951,20 +988,20 @@ __global__ void __launch_bounds__(Short<G>::THREADS, 2)
         o1 += sv[2 * H + g * kDecD + d + 1] * wgt;
       }
       const float inv = 1.f / l;
-      *reinterpret_cast<uint32_t *>(a.out + si.b * a.out_stride + (si.h * G + g) * kDecD + d) =
+      *reinterpret_cast<uint32_t *>(a.out + b * a.out_stride + (h * G + g) * kDecD + d) =
           pack2(o0 * inv, o1 * inv);
     }
     consumer_sync(C::CONSUMERS);  // scratch is reused by the next unit
   }
 }
 
-template <int G>
+template <int G, int GR>
 int launch_decode_short(const DecodeArgs &a, int hkv, const void *k_cache, const void *v_cache,
                         int64_t num_slots, cudaStream_t stream) {
-  using C = Short<G>;
+  using C = Short<G, GR>;
   static bool configured = false;
   if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(paged_decode_short_kernel<G>,
+    cudaError_t e = cudaFuncSetAttribute(paged_decode_short_kernel<G, GR>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(C::SMEM));
     if (e != cudaSuccess) {
@@ -985,7 +1022,7 @@ int launch_decode_short(const DecodeArgs &a, int hkv, const void *k_cache, const
     return B200ASR_ERR_CUDA;
   const int units = a.batch * hkv;
   const int grid = std::min(units, 2 * num_sms());
-  B200_LAUNCH_CHECK_ERR(launch_kernel(paged_decode_short_kernel<G>, dim3(grid), dim3(C::THREADS),
+  B200_LAUNCH_CHECK_ERR(launch_kernel(paged_decode_short_kernel<G, GR>, dim3(grid), dim3(C::THREADS),
                                       C::SMEM, stream, true, 1, tk, tv, a, hkv),
                         "paged_decode (short contexts)");
   return B200ASR_OK;
@@ -1092,9 +1129,9 @@ extern "C" int b200asr_paged_decode(const void *q, int64_t q_row_stride, const v
   if (max_seqlen_k <= kShortMaxCtx && block_size % kShortTok == 0 &&
       num_heads % num_kv_heads == 0 && num_kv_heads <= 8) {
     const int g = num_heads / num_kv_heads;
-    if (g == 1) return launch_decode_short<1>(a, num_kv_heads, k_cache, v_cache, slots, stream);
-    if (g == 2) return launch_decode_short<2>(a, num_kv_heads, k_cache, v_cache, slots, stream);
-    if (g == 4) return launch_decode_short<4>(a, num_kv_heads, k_cache, v_cache, slots, stream);
+    if (g == 1) return launch_decode_short<1, short_groups<1>()>(a, num_kv_heads, k_cache, v_cache, slots, stream);
+    if (g == 2) return launch_decode_short<2, short_groups<2>()>(a, num_kv_heads, k_cache, v_cache, slots, stream);
+    if (g == 4) return launch_decode_short<4, short_groups<4>()>(a, num_kv_heads, k_cache, v_cache, slots, stream);
   }
   if (num_kv_heads == 8 && num_heads == 16) return launch_decode<8, 2>(a, k_cache, v_cache, slots, stream);
   if (num_kv_heads == 8 && num_heads == 8) return launch_decode<8, 1>(a, k_cache, v_cache, slots, stream);

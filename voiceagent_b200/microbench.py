@@ -302,6 +302,50 @@ def window_config2() -> dict:
                  timing=f"graph over {sets} rotating input sets of {per_set / 1e6:.0f} MB")
 
 
+def encoder_conv(chunks: int = 512) -> list[dict]:
+    """The audio encoder's convolutional front (models/audio_encoder.py:145-175) as the
+    engine runs it today: three Conv2d(3x3, stride 2, pad 1) + GELU on cuDNN in
+    channels-last bf16 (0.6B dims: 1 -> 480 -> 480 -> 480 channels over 128 mel x 100
+    frames per chunk), then conv_out (7680 -> 896) on cuBLAS; one line per stage."""
+    import torch.nn.functional as F
+
+    dev = torch.device("cuda")
+    c, d = 480, 896
+    torch.manual_seed(0)
+    convs = [torch.nn.Conv2d(1 if i == 0 else c, c, 3, 2, padding=1).to(dev, torch.bfloat16)
+             .to(memory_format=torch.channels_last) for i in range(3)]
+    out_w = (torch.randn(d, c * 16, device=dev) * 0.02).bfloat16()
+    x0 = torch.randn(chunks, 1, 128, 100, device=dev).bfloat16().contiguous(
+        memory_format=torch.channels_last)
+    acts = [x0]
+    with torch.inference_mode():
+        for conv in convs:
+            acts.append(F.gelu(conv(acts[-1])))
+    lines = []
+    shapes = [(64, 50), (32, 25), (16, 13)]
+    for i, conv in enumerate(convs):
+        cin = 1 if i == 0 else c
+        ho, wo = shapes[i]
+        flops = 2 * chunks * ho * wo * c * cin * 9
+        nbytes = acts[i].numel() * 2 + acts[i + 1].numel() * 2 + conv.weight.numel() * 2
+
+        def op(conv=conv, x=acts[i], y=acts[i + 1]):
+            return lambda: y.copy_(F.gelu(conv(x)))
+
+        with torch.inference_mode():
+            us = graph_time_us([op() for _ in range(8)])
+        lines.append(_line("conv2d+gelu (cuDNN)", f"encoder conv{i + 1}: {chunks} chunks, {cin}->{c} "
+                           f"ch, out {ho}x{wo}", us, nbytes, flops=flops, bound="tensor"))
+    flat = acts[3].permute(0, 3, 1, 2).reshape(chunks * 13, c * 16)
+    y = torch.empty(chunks * 13, d, device=dev, dtype=torch.bfloat16)
+    with torch.inference_mode():
+        us = graph_time_us([lambda: torch.matmul(flat, out_w.T, out=y) for _ in range(8)])
+    lines.append(_line("conv_out (cuBLAS)", f"{chunks} chunks x 13 tokens, 7680 -> 896", us,
+                       flat.numel() * 2 + out_w.numel() * 2 + y.numel() * 2,
+                       flops=2 * chunks * 13 * c * 16 * d, bound="tensor"))
+    return lines
+
+
 # --------------------------------------------------------------- store / pack
 
 
@@ -519,6 +563,7 @@ BENCHES = {
     "step_profile": lambda: [decode_graph_step(True, iters=8, profile_one=True)],
     "prefill": lambda: [prefill_config2()],
     "window": lambda: [window_config2()],
+    "encoder_conv": lambda: encoder_conv(),
     "store": lambda: [store_rows(32), store_rows(8192)],
     "rope": lambda: [qk_norm_rope_rows(32), qk_norm_rope_rows(4096)],
     "pack": lambda: [pack_decoder_batch()],
