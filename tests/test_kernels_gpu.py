@@ -407,6 +407,50 @@ def test_paged_decode_peaked_scores(kx, max_len):
     assert_attn_close(out, ref, f"decode peaked scores max_seqlen_k={max_len}")
 
 
+@pytest.mark.parametrize("batch", [64, 160])
+@pytest.mark.parametrize("pdl", [False, True])
+def test_paged_decode_short_several_units_per_cta(kx, batch, pdl):
+    """The short-context kernel when a CTA takes several (sequence, KV head) units
+    (B x 8 units over at most 2 CTAs per SM: the decode graph's 64-row bucket and more)
+    and contexts of up to eight 64-token stages, so each of its two consumer groups waits
+    on ring slots the other group's stages occupied: eager, and as a PDL chain of graph
+    launches back to back. Results against the oracle; the device error word stays zero
+    (no bounded wait may time out)."""
+    rng = np.random.default_rng(batch + pdl)
+    lens = rng.integers(1, 512, size=batch)
+    lens[:4] = [511, 449, 193, 1]
+    q, kc, vc, tables, cu_k = _decode_case(rng, lens, nblocks=int(sum((lens + 255) // 256)))
+    qd, kcd, vcd = bf16(q), bf16(kc), bf16(vc)
+    cu, tb = dev(cu_k, torch.int32), dev(tables, torch.int32)
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    ws = torch.zeros(1 << 20, dtype=torch.float32, device="cuda")
+    out = torch.zeros_like(qd)
+    kx.set_pdl(pdl)
+    try:
+        def run():
+            kx.paged_decode(qd, kcd, vcd, cu, tb, max_seqlen_k=512, scale=128 ** -0.5, out=out,
+                            workspace=ws, error_flag=err)
+
+        run()
+        torch.cuda.synchronize()
+        assert err.item() == 0
+        ref = K.paged_attention(q, kc, vc, np.arange(batch + 1), cu_k, tables, 128 ** -0.5)
+        assert_attn_close(out, ref, f"short kernel, {batch} sequences, pdl={pdl}")
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for _ in range(8):
+                run()
+        out.zero_()
+        for _ in range(4):
+            graph.replay()
+        torch.cuda.synchronize()
+        del graph
+    finally:
+        kx.set_pdl(False)
+    assert err.item() == 0
+    assert_attn_close(out, ref, f"short kernel graph chain, {batch} sequences, pdl={pdl}")
+
+
 @pytest.mark.parametrize("max_len", [512, 4096])
 def test_paged_decode_newest_row_written_just_before_with_pdl(kx, max_len):
     """Both decode kernels request stages before their PDL wait, except those holding a

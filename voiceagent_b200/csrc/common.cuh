@@ -204,6 +204,18 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int32_
   }
 }
 
+// After a timed-out wait: give the copies this CTA already issued on `bar` (phase
+// `parity`) up to kDrainLimitNs to land before the CTA exits, so no copy writes into the
+// shared memory of a CTA that is later placed on the same SM. No abort check: the CTA
+// has already given up; this only bounds its exit.
+constexpr uint64_t kDrainLimitNs = 200000000ull;  // 0.2 s
+__device__ __forceinline__ void mbar_drain(uint64_t *bar, uint32_t parity) {
+  const uint64_t start = globaltimer_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (globaltimer_ns() - start > kDrainLimitNs) return;
+  }
+}
+
 // ------------------------------------------------------------------------- TMA
 
 // 1-D bulk copy global -> shared, completion counted on `bar` (bytes % 16 == 0,

@@ -93,6 +93,23 @@ __device__ __forceinline__ void consumer_sync(int threads) {
   asm volatile("bar.sync 1, %0;" ::"r"(threads) : "memory");
 }
 
+// Spin until the shared word *seq equals `want` (bounded like mbar_wait: false and the
+// timeout bit raised after kWaitLimitNs, or at once when the CTA already aborted).
+__device__ __forceinline__ bool slot_wait(volatile int *seq, int want, int32_t *err,
+                                          volatile int *abort) {
+  if (*seq == want) return true;
+  const uint64_t start = globaltimer_ns();
+  while (*seq != want) {
+    if (*abort) return false;
+    if (globaltimer_ns() - start > kWaitLimitNs) {
+      *abort = 1;
+      raise_flag(err, B200ASR_DEVERR_TIMEOUT);
+      return false;
+    }
+  }
+  return true;
+}
+
 // Largest b in [0, n) with v[b] <= x (v non-decreasing, v[0] <= x).
 __device__ __forceinline__ int upper_index(const int *v, int n, int x) {
   int lo = 0, hi = n - 1;
@@ -275,6 +292,7 @@ __global__ void __launch_bounds__(Dec<HKV, G>::THREADS, 1)
   __shared__ int abort_flag;
   __shared__ int s_pending[2];  // sequences this CTA merges after its last stage
   __shared__ int s_npending;
+  __shared__ int slot_last[kDecStages];  // stage number last issued into each ring slot
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int B = a.batch;
@@ -286,6 +304,7 @@ __global__ void __launch_bounds__(Dec<HKV, G>::THREADS, 1)
     for (int s = 0; s < kDecStages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], HKV);
+      slot_last[s] = -1;
     }
     fence_barrier_init();
   }
@@ -347,7 +366,15 @@ __global__ void __launch_bounds__(Dec<HKV, G>::THREADS, 1)
       const uint32_t ph = (it_stage / kDecStages) & 1;
       int ok = 1;
       if (lane == 0) ok = mbar_wait(&empty[st], ph ^ 1, a.error_flag, &abort_flag);
+      if (ok && lane == 0) slot_last[st] = static_cast<int>(it_stage);
       return __shfl_sync(0xffffffffu, ok, 0) != 0;
+    };
+    // After an abort, wait (bounded) for the copies of every slot's last stage to land
+    // before the CTA exits.
+    auto drain = [&]() {
+      if (lane != 0 || !abort_flag) return;
+      for (int s = 0; s < kDecStages; ++s)
+        if (slot_last[s] >= 0) mbar_drain(&full[s], (slot_last[s] / kDecStages) & 1);
     };
     // Before the wait: stages up to the first one holding a sequence's newest token, at
     // most one ring (no acquire blocks). Their q copies are issued after the wait, on the
@@ -408,6 +435,7 @@ __global__ void __launch_bounds__(Dec<HKV, G>::THREADS, 1)
           int st;
           if (!acquire(st)) {
             wait_prev();
+            drain();
             return;
           }
           if (lane == 0) {
@@ -434,7 +462,10 @@ __global__ void __launch_bounds__(Dec<HKV, G>::THREADS, 1)
     }
     wait_prev();
     int st;  // terminal stage: tells the consumers to stop
-    if (!acquire(st)) return;
+    if (!acquire(st)) {
+      drain();
+      return;
+    }
     if (lane == 0) {
       info[st] = StageInfo{-1, 0, 0};
       mbar_arrive(&full[st]);
@@ -684,7 +715,7 @@ struct Short {
   static constexpr int THREADS = CONSUMERS + 32;
   static constexpr int SCRATCH_BYTES = WARPS * G * (kDecD + 2) * 4;
   static constexpr size_t SMEM = 1024 + static_cast<size_t>(kShortStages) * STAGE_BYTES +
-                                 SCRATCH_BYTES + 2 * kShortStages * 8 + 64;
+                                 SCRATCH_BYTES + 2 * kShortStages * 8 + kShortStages * 4 + 64;
   static_assert(GR == 1 || GR == 2, "one or two consumer groups");
   static_assert(2 * (SMEM + 1024) <= 233472, "two CTAs per SM");
 };
@@ -702,6 +733,13 @@ __global__ void __launch_bounds__(Short<G, GR>::THREADS, 2)
   float *scratch = reinterpret_cast<float *>(smem + kShortStages * C::STAGE_BYTES);
   uint64_t *full = reinterpret_cast<uint64_t *>(reinterpret_cast<uint8_t *>(scratch) + C::SCRATCH_BYTES);
   uint64_t *empty = full + kShortStages;
+  // slot_seq[s]: number of the stage the producer last placed in ring slot s (-1: none).
+  // With two groups, a group may reach its wait for stage q while the other group's stage
+  // q - 3 still occupies the slot, possibly not yet landed: a parity wait would then match
+  // the slot's older completed phase and pass early. A consumer therefore first waits
+  // until slot_seq shows its own stage -- the producer writes it only after acquiring the
+  // slot, i.e. after stage q - 3 was consumed -- and only then waits on the parity.
+  volatile int *slot_seq = reinterpret_cast<volatile int *>(empty + kShortStages);
   __shared__ int abort_flag;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -712,6 +750,7 @@ __global__ void __launch_bounds__(Short<G, GR>::THREADS, 2)
     for (int s = 0; s < kShortStages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kShortWarps);  // one group consumes each stage
+      slot_seq[s] = -1;
     }
     fence_barrier_init();
   }
@@ -741,6 +780,12 @@ __global__ void __launch_bounds__(Short<G, GR>::THREADS, 2)
       int ok = 1;
       if (lane == 0) ok = mbar_wait(&empty[st], ph ^ 1, a.error_flag, &abort_flag);
       return __shfl_sync(0xffffffffu, ok, 0) != 0;
+    };
+    // After an abort, wait (bounded) for the copies of every slot's last stage to land.
+    auto drain = [&]() {
+      if (lane != 0 || !abort_flag) return;
+      for (int s = 0; s < kShortStages; ++s)
+        if (slot_seq[s] >= 0) mbar_drain(&full[s], (slot_seq[s] / kShortStages) & 1);
     };
     for (int u = blockIdx.x; u < units; u += gridDim.x) {
       const bool first_unit = u == static_cast<int>(blockIdx.x);
@@ -795,10 +840,13 @@ __global__ void __launch_bounds__(Short<G, GR>::THREADS, 2)
           int st;
           if (!acquire(st)) {
             wait_prev();
+            drain();
             return;
           }
-          if (lane == 0)
+          if (lane == 0) {
+            slot_seq[st] = static_cast<int>(it_stage);  // the slot's previous stage is consumed
             mbar_arrive_expect_tx(&full[st], 2 * C::KV_BYTES + (with_q ? G * kDecD * 2 : 0));
+          }
           __syncwarp();
           uint8_t *stage = stages + st * C::STAGE_BYTES;
           if (lane < 2) tma_load_4d(stage + lane * C::KV_BYTES, lane ? &tm_v : &tm_k, 0, slot, 0, h, &full[st]);
@@ -821,6 +869,7 @@ __global__ void __launch_bounds__(Short<G, GR>::THREADS, 2)
       }
     }
     wait_prev();
+    drain();
     return;
   }
 
@@ -870,6 +919,8 @@ __global__ void __launch_bounds__(Short<G, GR>::THREADS, 2)
       if (js % GR != grp) continue;
       const int st = it_stage % kShortStages;
       const uint32_t ph = (it_stage / kShortStages) & 1;
+      if (live && !slot_wait(&slot_seq[st], static_cast<int>(it_stage), a.error_flag, &abort_flag))
+        live = false;
       if (live && !mbar_wait(&full[st], ph, a.error_flag, &abort_flag)) live = false;
       if (!live) continue;
       const int ntok = min(16, max(0, min(kShortTok, len - js * kShortTok) - 16 * w));
@@ -993,6 +1044,10 @@ __global__ void __launch_bounds__(Short<G, GR>::THREADS, 2)
     }
     consumer_sync(C::CONSUMERS);  // scratch is reused by the next unit
   }
+  // A consumer that gave up leaves stages unconsumed: let their copies land before exit.
+  if (threadIdx.x == 0 && abort_flag)
+    for (int s = 0; s < kShortStages; ++s)
+      if (slot_seq[s] >= 0) mbar_drain(&full[s], (slot_seq[s] / kShortStages) & 1);
 }
 
 template <int G, int GR>

@@ -117,13 +117,19 @@ class ModelRunner:
         runner.capture()
         self.graph_runner = runner
 
+    # bits of the device error word (include/b200asr.h; 16 = a bounded wait gave up)
+    DEVICE_ERRORS = {1: "KV slot outside the cache", 2: "block id outside the pool",
+                     4: "position outside the RoPE table", 8: "length beyond its table or buffer",
+                     16: "a kernel's bounded wait timed out"}
+
     def check_device_errors(self) -> None:
-        """Raise if a kernel flagged an out-of-range index since the last check."""
+        """Raise if a kernel flagged an out-of-range index or a timed-out wait since the
+        last check."""
         flag = int(self.error_flag.item())
         if flag:
             self.error_flag.zero_()
-            raise RuntimeError(f"b200asr kernel index check failed (flags 0x{flag:x}): slot, block "
-                               "or position outside the cache / RoPE table")
+            what = "; ".join(v for k, v in self.DEVICE_ERRORS.items() if flag & k)
+            raise RuntimeError(f"b200asr device check failed (flags 0x{flag:x}): {what}")
 
     # ------------------------------------------------------------------- step
 
