@@ -413,6 +413,31 @@ B200ASR_API int b200asr_log_mel(const float *waveform, const int64_t *cu_samples
                     void *workspace, size_t workspace_bytes, void *out, int64_t out_stride,
                     const int32_t *out_col, int32_t *error_flag, b200asr_stream_t stream);
 
+/* --------------------------------------------------------------- encoder front ----
+ * Conv2d(kernel 3, stride 2, padding 1) + bias + GELU (erf form), the audio tower's
+ * downsampler convolutions: conv2d1 / conv2d2 / conv2d3 each followed by F.gelu in
+ * AudioEncoder (models/audio_encoder.py:145-175), which the reference runs as cuDNN
+ * convolutions plus separate bias and GELU kernels.
+ * x: channels-last bf16 [n][h][w][c_in] (for c_in = 1 simply [n][h][w]). Output
+ * ho = (h - 1) / 2 + 1, wo = (w - 1) / 2 + 1; y[i * y_stride_n + oy * y_stride_y +
+ * ox * y_stride_x + c] bf16 (channels contiguous, any pixel order -- e.g. [n][ox][oy][c]
+ * for the conv_out projection that follows). Rounding as the reference: bf16
+ * convolution output, bias added and rounded, GELU rounded.
+ * packed_weight: b200asr_conv_weight_bytes(c_out, c_in) bytes written by
+ * b200asr_conv_pack_weight from the module's [c_out][c_in][3][3] bf16 weight (once, at
+ * load time). c_in = 1 runs a direct stencil on CUDA cores; c_in > 1 (a multiple of 8)
+ * an implicit GEMM on tcgen05 with c_out a multiple of 32. error_flag records a
+ * timed-out wait (B200ASR_DEVERR_TIMEOUT 16).                                        */
+B200ASR_API size_t b200asr_conv_weight_bytes(int32_t c_out, int32_t c_in);
+B200ASR_API int b200asr_conv_pack_weight(const void *weight, int32_t c_out, int32_t c_in,
+                                         void *packed, b200asr_stream_t stream);
+B200ASR_API int b200asr_conv3x3s2_gelu(const void *x, int32_t n, int32_t h, int32_t w,
+                                       int32_t c_in, const void *packed_weight,
+                                       const void *bias, int32_t c_out, void *y,
+                                       int64_t y_stride_n, int64_t y_stride_y,
+                                       int64_t y_stride_x, int32_t *error_flag,
+                                       b200asr_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -188,6 +188,18 @@ class OracleThinker:
 
     # audio -----------------------------------------------------------------
 
+    def conv_front(self, chunks: torch.Tensor) -> torch.Tensor:
+        """Chunks (n, bins, frames) -> conv_out output (n, tokens, d_model): three
+        Conv2d(3, stride 2, pad 1) + GELU and the (channel, frequency)-flattened conv_out
+        projection, modeling_qwen3_asr.py:700-710, in fp32."""
+        w = self.w
+        x = chunks.unsqueeze(1)
+        for n in ("conv2d1", "conv2d2", "conv2d3"):
+            x = F.gelu(F.conv2d(x, w[f"audio_tower.{n}.weight"], w[f"audio_tower.{n}.bias"],
+                                stride=2, padding=1))
+        b, c, f, t = x.shape
+        return x.permute(0, 3, 1, 2).reshape(b, t, c * f) @ w["audio_tower.conv_out.weight"].T
+
     def encode_audio(self, mel: torch.Tensor) -> torch.Tensor:
         """One request's mel (bins, frames) -> (audio tokens, output_dim).
 
@@ -204,12 +216,8 @@ class OracleThinker:
         for i, n in enumerate(lens):
             chunks[i, :, :n] = mel[:, s : s + n]
             s += n
-        x = chunks.unsqueeze(1)
-        for n in ("conv2d1", "conv2d2", "conv2d3"):
-            x = F.gelu(F.conv2d(x, w[f"audio_tower.{n}.weight"], w[f"audio_tower.{n}.bias"],
-                                stride=2, padding=1))
-        b, c, f, t = x.shape
-        x = x.permute(0, 3, 1, 2).reshape(b, t, c * f) @ w["audio_tower.conv_out.weight"].T
+        x = self.conv_front(chunks)
+        t = x.shape[1]
         x = x + self.pos[:t].unsqueeze(0)
         valid = [(((n - 1) // 2 + 1 - 1) // 2 + 1 - 1) // 2 + 1 for n in lens]
         h = torch.cat([x[i, :v] for i, v in enumerate(valid)], dim=0)

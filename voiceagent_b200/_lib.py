@@ -78,6 +78,10 @@ SIGNATURES: dict[str, tuple] = {
                                             P, c_int64, c_int64, c_int32, c_int32, c_float,
                                             P, c_size_t, P, P]),
     "b200asr_greedy_argmax": (c_int32, [P, c_int64, c_int32, c_int32, P, P]),
+    "b200asr_conv_weight_bytes": (c_size_t, [c_int32, c_int32]),
+    "b200asr_conv_pack_weight": (c_int32, [P, c_int32, c_int32, P, P]),
+    "b200asr_conv3x3s2_gelu": (c_int32, [P, c_int32, c_int32, c_int32, c_int32, P, P, c_int32,
+                                         P, c_int64, c_int64, c_int64, P, P]),
 }
 
 

@@ -121,9 +121,6 @@ class AsrEngine:
             load_tensors(model, random_state_dict(preset, seed).items(), prefixed=False)
         else:
             raise ValueError(f"unknown weights source {weights!r}")
-        for module in model.modules():  # the encoder's convolutions run channels-last
-            if isinstance(module, torch.nn.Conv2d):
-                module.to(memory_format=torch.channels_last)
         return model.eval()
 
     def _limit_frontend_threads(self) -> None:

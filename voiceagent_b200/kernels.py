@@ -551,6 +551,49 @@ def linear_small_norm_qk_rope(state: NormState, norm_weight, eps: float, weight,
     return q_out
 
 
+# ----------------------------------------------------------------- encoder front
+
+
+def conv_pack_weight(weight: torch.Tensor) -> torch.Tensor:
+    """A Conv2d(3x3) weight [C_out, C_in, 3, 3] bf16 repacked for
+    :func:`conv3x3s2_gelu` (call once, at load time)."""
+    _cuda(weight)
+    c_out, c_in = weight.shape[:2]
+    _need(weight.dtype == BF16 and tuple(weight.shape[2:]) == (3, 3), "bf16 [C_out, C_in, 3, 3]")
+    weight = weight.contiguous()
+    packed = torch.empty(lib.b200asr_conv_weight_bytes(c_out, c_in) // 2, dtype=BF16,
+                         device=weight.device)
+    _count()
+    check(lib.b200asr_conv_pack_weight(_p(weight), c_out, c_in, _p(packed), _stream()),
+          "conv_pack_weight")
+    return packed
+
+
+def conv3x3s2_gelu(x: torch.Tensor, packed_weight: torch.Tensor, bias: torch.Tensor, *,
+                   c_out: int, out: torch.Tensor | None = None, out_order: str = "nyxc",
+                   error_flag=None) -> torch.Tensor:
+    """GELU(Conv2d(x, kernel 3, stride 2, padding 1) + bias) on channels-last bf16
+    x [N, H, W, C_in] (models/audio_encoder.py:145-175). The output is [N, Ho, Wo, C_out]
+    (``out_order`` "nyxc") or [N, Wo, Ho, C_out] ("nxyc": per chunk, time-major rows of
+    (frequency, channel) -- the layout conv_out reads)."""
+    _cuda(x, packed_weight, bias, out)
+    n, h, w, c_in = x.shape
+    _need(x.dtype == BF16 and x.is_contiguous(), "conv3x3s2_gelu: contiguous bf16 channels-last x")
+    _need(bias.dtype == BF16 and bias.numel() == c_out, "conv3x3s2_gelu: bf16 bias [C_out]")
+    ho, wo = (h - 1) // 2 + 1, (w - 1) // 2 + 1
+    shape = (n, ho, wo, c_out) if out_order == "nyxc" else (n, wo, ho, c_out)
+    if out is None:
+        out = torch.empty(shape, dtype=BF16, device=x.device)
+    _need(tuple(out.shape) == shape and out.is_contiguous(), "conv3x3s2_gelu: output shape")
+    sn = ho * wo * c_out
+    sy, sx = (wo * c_out, c_out) if out_order == "nyxc" else (c_out, ho * c_out)
+    _count()
+    check(lib.b200asr_conv3x3s2_gelu(_p(x), n, h, w, c_in, _p(packed_weight), _p(bias), c_out,
+                                     _p(out), sn, sy, sx, _p(error_flag), _stream()),
+          "conv3x3s2_gelu")
+    return out
+
+
 def set_pdl(enable: bool) -> None:
     """Programmatic dependent launch for the decode-path kernels (process-wide)."""
     lib.b200asr_set_pdl(1 if enable else 0)

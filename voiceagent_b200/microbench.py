@@ -336,6 +336,26 @@ def encoder_conv(chunks: int = 512) -> list[dict]:
             us = graph_time_us([op() for _ in range(8)])
         lines.append(_line("conv2d+gelu (cuDNN)", f"encoder conv{i + 1}: {chunks} chunks, {cin}->{c} "
                            f"ch, out {ho}x{wo}", us, nbytes, flops=flops, bound="tensor"))
+    # this library's kernels on the same inputs (csrc/conv.cu)
+    packed = [kx.conv_pack_weight(conv.weight.detach().contiguous()) for conv in convs]
+    x = [x0.view(chunks, 128, 100, 1)]
+    for i, conv in enumerate(convs):
+        x.append(kx.conv3x3s2_gelu(x[i], packed[i], conv.bias.detach(), c_out=c))
+    for i, conv in enumerate(convs):
+        cin = 1 if i == 0 else c
+        ho, wo = shapes[i]
+        flops = 2 * chunks * ho * wo * c * cin * 9
+        nbytes = x[i].numel() * 2 + x[i + 1].numel() * 2 + conv.weight.numel() * 2
+
+        def op(i=i, conv=conv):
+            return lambda: kx.conv3x3s2_gelu(x[i], packed[i], conv.bias.detach(), c_out=c,
+                                             out=x[i + 1])
+
+        us = graph_time_us([op() for _ in range(8)])
+        kind = "direct stencil" if i == 0 else "tcgen05 implicit GEMM"
+        lines.append(_line(f"conv3x3s2_gelu ({kind})", f"encoder conv{i + 1}: {chunks} chunks, "
+                           f"{cin}->{c} ch, out {ho}x{wo}, bias + GELU fused", us, nbytes,
+                           flops=flops, bound="hbm" if i == 0 else "tensor"))
     flat = acts[3].permute(0, 3, 1, 2).reshape(chunks * 13, c * 16)
     y = torch.empty(chunks * 13, d, device=dev, dtype=torch.bfloat16)
     with torch.inference_mode():

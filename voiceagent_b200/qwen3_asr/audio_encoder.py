@@ -6,12 +6,13 @@ Differences from the reference, all numerically neutral: the chunk padding is th
 valid-token gather uses host-known indices instead of a boolean mask (no device
 sync), and window attention is the tcgen05 ``varlen_attention`` kernel.
 
-The convolutional downsampler runs on groups of a few fixed sizes (8, 16, 32 or 64
-chunks, the last group zero-padded) in channels-last layout. Every encode batch has a
-different chunk count, and cuDNN builds an execution plan per new input shape -- tens
-of milliseconds of host time that dwarfed the few milliseconds of GPU work; with fixed
-group shapes the plans are built once. Chunks are independent through the convolutions
-(padding only ever adds whole zero chunks), so the grouping does not change results.
+The convolutional downsampler runs on this library's kernels (csrc/conv.cu): conv2d1
+(one input channel) as a direct stencil, conv2d2 and conv2d3 as tcgen05 implicit GEMMs,
+each with its bias and GELU fused and the reference's roundings, on channels-last
+activations over all chunks of the batch at once. conv2d3 writes its pixels in the
+order conv_out reads them (per chunk, time-major rows of (frequency, channel)), so
+conv_out multiplies by its weight with the columns permuted to match -- no transpose
+copy. The modules keep the checkpoint's parameters; ``prepare_kernels`` repacks them.
 """
 
 from __future__ import annotations
@@ -97,49 +98,48 @@ class AudioEncoder(nn.Module):
         self.proj1 = nn.Linear(config.d_model, config.d_model)
         self.proj2 = nn.Linear(config.d_model, config.output_dim)
 
-    CONV_GROUPS = (8, 16, 32, 64)  # chunk counts of the conv launches (shape-stable)
-
-    @classmethod
-    def conv_rows(cls, num_chunks: int) -> int:
-        """Rows to allocate for ``num_chunks`` chunks: whole fixed-size groups."""
-        g = cls.conv_group(num_chunks)
-        return -(-num_chunks // g) * g
-
-    @classmethod
-    def conv_group(cls, num_chunks: int) -> int:
-        return next((g for g in cls.CONV_GROUPS if g >= num_chunks), cls.CONV_GROUPS[-1])
+    @torch.inference_mode()
+    def prepare_kernels(self) -> None:
+        """Repack the convolution weights for csrc/conv.cu and permute conv_out's columns
+        from the reference's (channel, frequency) order to the (frequency, channel) order
+        conv2d3 writes. Call after the weights are loaded."""
+        self._conv_packed = [kx.conv_pack_weight(c.weight.detach().contiguous())
+                             for c in (self.conv2d1, self.conv2d2, self.conv2d3)]
+        w = self.conv_out.weight.detach()
+        c = self.config.downsample_hidden_size
+        freq = w.shape[1] // c
+        self._conv_out_fc = w.view(w.shape[0], c, freq).transpose(1, 2).reshape(w.shape[0], -1) \
+            .contiguous()
 
     def _downsample(self, padded: torch.Tensor, num_chunks: int) -> torch.Tensor:
-        g = self.conv_group(num_chunks)
-        outs = []
-        for part in padded.split(g, dim=0):
-            h = F.gelu(self.conv2d1(part.contiguous(memory_format=torch.channels_last)))
-            h = F.gelu(self.conv2d2(h))
-            outs.append(F.gelu(self.conv2d3(h)))
-        x = torch.cat(outs, dim=0) if len(outs) > 1 else outs[0]
-        x = x[:num_chunks]
-        n, c, f, t = x.shape
-        return self.conv_out(x.permute(0, 3, 1, 2).reshape(n, t, c * f))
+        """[chunks, mel bins, frames] -> conv_out embeddings [chunks, tokens, d_model]."""
+        if getattr(self, "_conv_packed", None) is None:
+            self.prepare_kernels()
+        c = self.config.downsample_hidden_size
+        convs = (self.conv2d1, self.conv2d2, self.conv2d3)
+        x = padded.unsqueeze(-1)  # channels-last with one channel
+        for i, (conv, packed) in enumerate(zip(convs, self._conv_packed)):
+            x = kx.conv3x3s2_gelu(x, packed, conv.bias.detach(), c_out=c,
+                                  out_order="nxyc" if i == 2 else "nyxc")
+        n, t, f, _ = x.shape
+        return x.view(n, t, f * c) @ self._conv_out_fc.T
 
     @torch.inference_mode()
     def warm_up(self) -> None:
-        """Build the cuDNN plans of every conv group shape once, at engine start."""
+        """Repack the convolution weights and run the front once, at engine start."""
+        self.prepare_kernels()
         p = next(self.parameters())
-        for g in self.CONV_GROUPS:
-            self._downsample(torch.zeros(g, 1, self.config.num_mel_bins, self.chunk_frames,
-                                         dtype=p.dtype, device=p.device), g)
+        self._downsample(torch.zeros(1, self.config.num_mel_bins, self.chunk_frames,
+                                     dtype=p.dtype, device=p.device), 1)
 
     @torch.inference_mode()
     def forward(self, batch: PackedAudioBatch) -> torch.Tensor:
         """Encode a packed batch into (total audio tokens, output_dim)."""
-        rows = self.conv_rows(batch.num_chunks)
-        padded = torch.empty(rows, self.config.num_mel_bins, self.chunk_frames,
+        padded = torch.empty(batch.num_chunks, self.config.num_mel_bins, self.chunk_frames,
                              dtype=batch.mel.dtype, device=batch.mel.device)
-        if rows > batch.num_chunks:
-            padded[batch.num_chunks:].zero_()
         kx.audio_chunk_pad(batch.mel, batch.chunk_start, batch.chunk_lengths, batch.num_chunks,
                            self.chunk_frames, padded)
-        embed = self._downsample(padded.unsqueeze(1), batch.num_chunks)
+        embed = self._downsample(padded, batch.num_chunks)
         embed = embed + self.positional_embedding[: embed.shape[1]].unsqueeze(0).to(embed.dtype)
         flat = embed.reshape(-1, embed.shape[-1])
         t = batch.token_index.numel()
