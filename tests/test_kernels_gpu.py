@@ -583,6 +583,46 @@ def test_paged_prefill_config2_lengths(kx):
     assert_attn_close(out, ref, "prefill config2")
 
 
+def _poison_unused(kc, vc, tables, k_lens, block=256):
+    """NaN in every cache slot that no sequence holds: never-written pages and the tails of
+    the sequences' last pages (what a freshly allocated cache may contain). flash-attn's
+    paged kernels never let those slots reach an output; neither may ours."""
+    used = np.zeros(kc.shape[:2], bool)
+    for i, n in enumerate(k_lens):
+        for b in range((int(n) + block - 1) // block):
+            used[tables[i, b], : min(block, int(n) - b * block)] = True
+    kc, vc = kc.copy(), vc.copy()
+    kc[~used] = np.nan
+    vc[~used] = np.nan
+    return kc, vc
+
+
+@pytest.mark.parametrize("q_lens,k_lens", [
+    ([76, 1, 300, 1, 40], [76, 257, 300, 1000, 552]),
+    ([63, 130, 1], [63, 130, 1]),
+])
+def test_paged_prefill_ignores_unwritten_cache_slots(kx, q_lens, k_lens):
+    rng = np.random.default_rng(sum(k_lens) + 5)
+    q, kc, vc, tables, cu_q, cu_k = _prefill_case(rng, q_lens, k_lens)
+    ref = K.paged_attention(q, kc, vc, cu_q, cu_k, tables, 128 ** -0.5)
+    kc, vc = _poison_unused(kc, vc, tables, k_lens)
+    out = _run_prefill(kx, q, kc, vc, tables, cu_q, cu_k)
+    assert torch.isfinite(out).all()
+    assert_attn_close(out, ref, f"prefill over a NaN-filled cache {q_lens}/{k_lens}")
+
+
+@pytest.mark.parametrize("max_len", [512, 4096])
+def test_paged_decode_ignores_unwritten_cache_slots(kx, max_len):
+    rng = np.random.default_rng(31)
+    lens = [1, 17, 64, 65, 200, 256, 300, 511]
+    q, kc, vc, tables, cu_k = _decode_case(rng, lens, nblocks=64)
+    ref = K.paged_attention(q, kc, vc, np.arange(len(lens) + 1), cu_k, tables, 128 ** -0.5)
+    kc, vc = _poison_unused(kc, vc, tables, lens)
+    out = _run_decode(kx, q, kc, vc, tables, cu_k, max_len)
+    assert torch.isfinite(out).all()
+    assert_attn_close(out, ref, f"decode over a NaN-filled cache max_seqlen_k={max_len}")
+
+
 def _window_case(rng, token_lens, heads=14, d=64):
     cu = np.asarray(K.build_window_boundaries(token_lens, 104), np.int32)
     t = int(cu[-1])
@@ -604,6 +644,29 @@ def test_varlen_window_attention_matches_oracle(kx, token_lens):
     ref = K.varlen_attention(qkv[:, 0], qkv[:, 1], qkv[:, 2], cu, 64 ** -0.5)
     assert_attn_close(out, ref, f"window {token_lens}")
     assert err.item() == 0
+
+
+def test_varlen_window_segments_stay_independent(kx):
+    """A segment's 128-row tile reaches into the next segments: NaN in one segment's K
+    and V must not leak into the segment before it (the reference's varlen kernel keeps
+    segments apart)."""
+    rng = np.random.default_rng(12)
+    token_lens = [46, 26, 95, 30]
+    qkv, cu = _window_case(rng, token_lens)
+    ref = K.varlen_attention(qkv[:, 0], qkv[:, 1], qkv[:, 2], cu, 64 ** -0.5)
+    poisoned = qkv.copy()
+    bad = slice(int(cu[1]), int(cu[2]))  # segment 1
+    poisoned[bad, 1:] = np.nan
+    d = bf16(poisoned.reshape(poisoned.shape[0], -1))
+    q = d[:, : 14 * 64].view(-1, 14, 64)
+    k = d[:, 14 * 64 : 28 * 64].view(-1, 14, 64)
+    v = d[:, 28 * 64 :].view(-1, 14, 64)
+    out = kx.varlen_attention(q, k, v, dev(cu, torch.int32), int(np.diff(cu).max()), 64 ** -0.5)
+    keep = np.ones(qkv.shape[0], bool)
+    keep[bad] = False
+    got = out[torch.from_numpy(keep).cuda()]
+    assert torch.isfinite(got).all()
+    assert_attn_close(got, ref[keep], "window segments next to a NaN segment")
 
 
 # ------------------------------------------------------------------ mel frontend

@@ -304,6 +304,17 @@ __global__ void __launch_bounds__(kTcThreads, 2)
         tmem_wait_st();
       }
       store_p_row64(sK + (j & 1) * kPfKVBytes, r, s);  // P(j) over K(j)
+      // Keys from n_kv on get P = 0 in every row, but their V rows hold whatever the
+      // cache pages hold past the sequence (never-written memory may be NaN or Inf, and
+      // 0 * NaN poisons the row sums): clear those V rows of the last tile. Thread r owns
+      // key t of d-half r >> 6.
+      if (j == n_tiles - 1 && key0 + t >= n_kv) {
+        fence_proxy_async_smem();  // after the tile's TMA bytes, before these stores
+        uint4 *row = reinterpret_cast<uint4 *>(sV + (j & 1) * kPfKVBytes + (r >> 6) * 8192 +
+                                               (t >> 3) * 1024 + (t & 7) * 128);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) row[c] = make_uint4(0u, 0u, 0u, 0u);
+      }
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(p_full);
@@ -519,6 +530,15 @@ __global__ void __launch_bounds__(kTcThreads, 2)
       }
       store_p_row64(buf, r, s);
       store_p_row64(buf + kWinTile, r, s + 64);
+      // Keys from len on belong to other segments (or lie past the tensor): P = 0 there,
+      // and their V rows are cleared so that a NaN or Inf outside the segment stays out
+      // of it. Thread r owns key r.
+      if (r >= len) {
+        fence_proxy_async_smem();  // after the item's TMA bytes, before these stores
+        uint4 *row = reinterpret_cast<uint4 *>(buf + 2 * kWinTile + (r >> 3) * 1024 + (r & 7) * 128);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) row[c] = make_uint4(0u, 0u, 0u, 0u);
+      }
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(p_full);
