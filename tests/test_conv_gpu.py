@@ -52,6 +52,11 @@ def _close(got, want, pre, conv, what):
     (5, 13, 11, 1, 32),       # the tiny test preset, odd sizes
     (4, 7, 6, 32, 32),
     (1, 9, 9, 64, 128),
+    # more tiles than SMs: each persistent CTA walks several tiles and reuses both
+    # accumulators (channel tiles of 240, 128 and 32)
+    (64, 64, 50, 480, 480),
+    (96, 32, 25, 64, 256),
+    (600, 16, 16, 32, 32),
 ])
 def test_conv_matches_reference_rounding(n, h, w, cin, cout):
     from voiceagent_b200 import kernels as kx

@@ -14,16 +14,17 @@
 //  * conv1 (C_in = 1): a direct stencil on CUDA cores -- 9 multiply-adds per output, far
 //    too few for a tensor-core GEMM; each thread owns 8 output channels (their 72
 //    weights in registers) of one pixel and writes them as one 16-byte store.
-//  * conv2, conv3 (C_in = C_out = 480 for Qwen3-ASR): implicit GEMM on tcgen05. Output
-//    pixels of all chunks are flattened into one row space; a CTA owns 256 of them (two
-//    128-row accumulators in TMEM) and NT output channels. K runs over 9 taps x C_in in
-//    64-channel blocks. The A operand (the 3x3 / stride-2 gather of the input) is built
+//  * conv2, conv3 (C_in = C_out = 480 for Qwen3-ASR): implicit GEMM on tcgen05, one
+//    persistent CTA per SM. Output pixels of all chunks are flattened into one row space
+//    and cut into tiles of 128 pixels x NT output channels; K runs over C_in in 64-channel
+//    blocks x the 9 taps. The A operand (the 3x3 / stride-2 gather of the input) is built
 //    by four warps with 16-byte cp.async copies, eight lanes per 128-byte input row --
 //    zero-filled where the tap falls into the padding or past C_in -- straight into the
 //    128-byte-swizzled K-major layout; each thread's copies arrive on the stage's full
 //    barrier when they land (cp.async.mbarrier.arrive), so the gather never stalls on
 //    its own copies. The weights arrive by TMA from a [C_out][9][C_pad] repacking; one
-//    thread issues the MMAs; the same four warps then run the bias + GELU epilogue.
+//    thread issues the MMAs into one of two TMEM accumulators while four epilogue warps
+//    run bias + GELU on the other (the previous tile).
 #include "common.cuh"
 
 namespace b200asr {
@@ -99,22 +100,24 @@ __global__ void __launch_bounds__(256) conv1_gelu_kernel(const Conv1Args a) {
 
 // ------------------------------------------------- conv2/conv3: tcgen05 implicit GEMM
 
-constexpr int kCvBK = 64;        // input channels per K block (one 128-byte swizzle row)
-constexpr int kCvRows = 128;     // rows (pixels) per accumulator = MMA M
-constexpr int kCvSub = 2;        // accumulators per CTA: 256 pixels
-constexpr int kCvStages = 3;
-constexpr int kCvThreads = 192;  // warps 0-3 A + epilogue, warp 4 weights (TMA), warp 5 MMA
+constexpr int kCvBK = 64;         // input channels per K block (one 128-byte swizzle row)
+constexpr int kCvRows = 128;      // pixels per tile = MMA M = TMEM lanes
+constexpr int kCvThreads = 320;   // warps 0-3 A gather, 4-7 epilogue, 8 weights (TMA), 9 MMA
+constexpr int kCvSmemBudget = 200 * 1024;
 
 template <int NT>
 struct Cv {
-  static constexpr int A_BYTES = kCvSub * kCvRows * 128;  // 32 KiB
-  static constexpr int B_BYTES = NT * 128;                // NT rows x 64 channels
+  static constexpr int A_BYTES = kCvRows * 128;  // 16 KiB: 128 pixels x 64 channels
+  static constexpr int B_BYTES = NT * 128;       // NT output channels x 64 channels
   static constexpr int STAGE = A_BYTES + B_BYTES;
+  static constexpr int STAGES = kCvSmemBudget / STAGE < 8 ? kCvSmemBudget / STAGE : 8;
   static constexpr int ACC_STRIDE = NT <= 128 ? 128 : 256;  // TMEM columns per accumulator
-  static constexpr uint32_t TMEM_COLS = kCvSub * ACC_STRIDE;
-  static constexpr size_t SMEM = 1024 + static_cast<size_t>(kCvStages) * STAGE + 256;
+  static constexpr uint32_t TMEM_COLS = 2 * ACC_STRIDE;      // two accumulators
+  static constexpr size_t SMEM = 1024 + static_cast<size_t>(STAGES) * STAGE + 256;
   static_assert(NT % 16 == 0 && NT >= 16 && NT <= 256, "MMA N");
   static_assert(STAGE % 1024 == 0, "stages keep the 1024-byte swizzle alignment");
+  static_assert(STAGES >= 3, "pipeline depth");
+  static_assert(2 * STAGES * 8 + 2 * 2 * 8 + 4 <= 256, "barriers fit their slot");
 };
 
 struct ConvArgs {
@@ -131,7 +134,6 @@ __device__ __forceinline__ void cp_async16_zfill(uint32_t saddr, const void *gpt
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(saddr), "l"(gptr), "r"(bytes)
                : "memory");
 }
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 // Arrive on `bar` once all of this thread's earlier cp.async copies have landed; the
 // arrival is part of the barrier's initial count (.noinc).
 __device__ __forceinline__ void cp_async_mbar_arrive_noinc(uint64_t *bar) {
@@ -184,41 +186,51 @@ __device__ __forceinline__ void conv_store(const float *acc, const __nv_bfloat16
   }
 }
 
+// Persistent: one CTA per SM walks tiles t = blockIdx.x, + gridDim.x, ...; tile t is
+// pixel tile t / ntiles (128 pixels) x output-channel tile t % ntiles (NT channels), so
+// the channel tiles of one pixel tile run side by side and share the gathered input in
+// L2. K runs channel-block-major (64 channels, then the 9 taps), which keeps the input
+// rows of the SM-wide working set (~70 KB per tile) in L2 across the taps. Two TMEM
+// accumulators: the epilogue warps drain tile i while the MMA warp accumulates tile i + 1.
 template <int NT>
 __global__ void __launch_bounds__(kCvThreads, 1)
     conv_gemm_gelu_kernel(const __grid_constant__ CUtensorMap tm_w, const ConvArgs a) {
   using C = Cv<NT>;
+  constexpr int S = C::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                               ~uintptr_t(1023));
-  uint64_t *full = reinterpret_cast<uint64_t *>(smem + kCvStages * C::STAGE);
-  uint64_t *empty = full + kCvStages;
-  uint64_t *acc_full = empty + kCvStages;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_full + 1);
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + S * C::STAGE);
+  uint64_t *empty = full + S;
+  uint64_t *acc_full = empty + S;   // [2] accumulator b holds a finished tile
+  uint64_t *acc_empty = acc_full + 2;  // [2] accumulator b drained by the epilogue
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + 2);
   __shared__ int abort_flag;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int kblocks = 9 * a.cblocks;
-  // the output-channel tiles of one pixel tile are neighbours in the grid, so they run
-  // together and share the gathered input through L2
   const int ntiles = a.co / NT;
-  const int64_t p0 = static_cast<int64_t>(blockIdx.x / ntiles) * (kCvSub * kCvRows);
-  const int n0 = static_cast<int>(blockIdx.x % ntiles) * NT;
+  const int64_t ptiles = (a.pixels + kCvRows - 1) / kCvRows;
+  const int64_t tiles = ptiles * ntiles;
+  const int64_t per_image = static_cast<int64_t>(a.ho) * a.wo;
 
   if (tid == 0) {
     abort_flag = 0;
-    for (int s = 0; s < kCvStages; ++s) {
-      mbar_init(&full[s], kCvRows + 1);  // 128 A-producer threads + the weights' TMA
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], kCvRows + 1);  // 128 gather threads + the weights' TMA
       mbar_init(&empty[s], 1);
     }
-    mbar_init(acc_full, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], kCvRows);
+    }
     fence_barrier_init();
   }
-  if (warp == 5) {
+  if (warp == 9) {
     tmem_alloc(tmem_slot, C::TMEM_COLS);
     tmem_relinquish();
   }
-  if (warp == 4 && lane == 0) prefetch_tmap(&tm_w);
+  if (warp == 8 && lane == 0) prefetch_tmap(&tm_w);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -226,138 +238,154 @@ __global__ void __launch_bounds__(kCvThreads, 1)
 
   if (warp < 4) {
     // -------------------------------------------------------- A operand (im2col gather)
-    // Eight lanes per 128-byte row (lane & 7 = 16-byte chunk), four rows per warp
-    // instruction: each copy instruction covers four whole lines of the input. Thread
-    // (warp, lane) gathers rows warp * 32 + (lane >> 3) + 4 i, i < 8, of each accumulator.
+    // Eight lanes per 128-byte input row (lane & 7 = 16-byte chunk), four rows per warp
+    // instruction, so each copy instruction covers four whole lines. Thread (warp, lane)
+    // gathers tile rows warp * 32 + (lane >> 3) + 4 i, i < 8; its copies arrive on the
+    // stage's full barrier when they land, so it never waits for its own copies.
     const int chunk = lane & 7;
-    const int64_t per_image = static_cast<int64_t>(a.ho) * a.wo;
-    int pix[kCvSub][8], iy0[kCvSub][8], ix0[kCvSub][8];
-#pragma unroll
-    for (int s = 0; s < kCvSub; ++s)
+    uint32_t g = 0;  // K blocks issued so far (stage ring position)
+    bool ok = true;
+    for (int64_t t = blockIdx.x; ok && t < tiles; t += gridDim.x) {
+      const int64_t p0 = (t / ntiles) * kCvRows;
+      int pix[8], iy0[8], ix0[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        const int64_t p = p0 + s * kCvRows + warp * 32 + (lane >> 3) + 4 * i;
+        const int64_t p = p0 + warp * 32 + (lane >> 3) + 4 * i;
         if (p < a.pixels) {
           const int im = static_cast<int>(p / per_image);
           const int rem = static_cast<int>(p - im * per_image);
           const int oy = rem / a.wo;
-          pix[s][i] = im * a.h * a.w;
-          iy0[s][i] = 2 * oy - 1;
-          ix0[s][i] = 2 * (rem - oy * a.wo) - 1;
+          pix[i] = im * a.h * a.w;
+          iy0[i] = 2 * oy - 1;
+          ix0[i] = 2 * (rem - oy * a.wo) - 1;
         } else {  // past the last pixel: every tap reads as padding
-          pix[s][i] = 0;
-          iy0[s][i] = -(1 << 20);
-          ix0[s][i] = 0;
+          pix[i] = 0;
+          iy0[i] = -(1 << 20);
+          ix0[i] = 0;
         }
       }
-    int kb = 0;
-    for (; kb < kblocks; ++kb) {
-      const int st = kb % kCvStages;
-      if (!mbar_wait(&empty[st], ((kb / kCvStages) & 1) ^ 1, a.error_flag, &abort_flag)) break;
-      const int tap = kb / a.cblocks, c0 = (kb - tap * a.cblocks) * kCvBK;
-      const int ky = tap / 3, kx = tap - ky * 3;
-      const bool have_c = c0 + 8 * chunk < a.ci;
-      const __nv_bfloat16 *xc = a.x + c0 + 8 * chunk;
-      const uint32_t stage_a = smem_addr(smem + st * C::STAGE);
+      for (int cb = 0; cb < a.cblocks; ++cb) {
+        const int c0 = cb * kCvBK;
+        const bool have_c = c0 + 8 * chunk < a.ci;
+        const __nv_bfloat16 *xc = a.x + c0 + 8 * chunk;
+        for (int tap = 0; tap < 9; ++tap, ++g) {
+          const int st = static_cast<int>(g % S);
+          if (!mbar_wait(&empty[st], ((g / S) & 1) ^ 1, a.error_flag, &abort_flag)) {
+            ok = false;
+            break;
+          }
+          const int ky = tap / 3, kx = tap - ky * 3;
+          const uint32_t stage_a = smem_addr(smem + st * C::STAGE);
 #pragma unroll
-      for (int s = 0; s < kCvSub; ++s)
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int r = warp * 32 + (lane >> 3) + 4 * i;
-          const int iy = iy0[s][i] + ky, ix = ix0[s][i] + kx;
-          const bool in = have_c && static_cast<unsigned>(iy) < static_cast<unsigned>(a.h) &&
-                          static_cast<unsigned>(ix) < static_cast<unsigned>(a.w);
-          const __nv_bfloat16 *src =
-              in ? xc + static_cast<int64_t>(pix[s][i] + iy * a.w + ix) * a.ci : a.x;
-          cp_async16_zfill(stage_a + s * (kCvRows * 128) + (r >> 3) * 1024 + (r & 7) * 128 +
-                               ((chunk ^ (r & 7)) << 4),
-                           src, in ? 16u : 0u);
+          for (int i = 0; i < 8; ++i) {
+            const int r = warp * 32 + (lane >> 3) + 4 * i;
+            const int iy = iy0[i] + ky, ix = ix0[i] + kx;
+            const bool in = have_c && static_cast<unsigned>(iy) < static_cast<unsigned>(a.h) &&
+                            static_cast<unsigned>(ix) < static_cast<unsigned>(a.w);
+            const __nv_bfloat16 *src =
+                in ? xc + static_cast<int64_t>(pix[i] + iy * a.w + ix) * a.ci : a.x;
+            cp_async16_zfill(stage_a + (r >> 3) * 1024 + (r & 7) * 128 + ((chunk ^ (r & 7)) << 4),
+                             src, in ? 16u : 0u);
+          }
+          cp_async_mbar_arrive_noinc(&full[st]);
         }
-      // full[st] counts this thread once its copies have landed; the thread moves on
-      cp_async_mbar_arrive_noinc(&full[st]);
+        if (!ok) break;
+      }
     }
     cp_async_wait<0>();  // nothing of this thread's is in flight past this point
-    if (kb == kblocks) {
-      // ------------------------------------------------------------ bias + GELU epilogue
-      // TMEM lane = accumulator row: thread tid stores row tid of each accumulator.
-      if (mbar_wait(acc_full, 0, a.error_flag, &abort_flag)) {
-        tc_fence_after();
-        const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
-#pragma unroll
-        for (int s = 0; s < kCvSub; ++s) {
-          const int64_t p = p0 + s * kCvRows + tid;
-          const bool live = p < a.pixels;
-          const int64_t pp = live ? p : 0;
-          const int im = static_cast<int>(pp / per_image);
-          const int rem = static_cast<int>(pp - im * per_image);
-          const int oy = rem / a.wo, ox = rem - oy * a.wo;
-          __nv_bfloat16 *dst = a.y + im * a.sn + oy * a.sy + ox * a.sx + n0;
-          const uint32_t acc_base = lane_base + s * C::ACC_STRIDE;
-#pragma unroll
-          for (int col = 0; col + 32 <= NT; col += 32) {
-            float v[32];
-            tmem_ld32(acc_base + col, v);
-            tmem_wait_ld();
-            if (live) conv_store<32>(v, a.bias + n0 + col, dst + col);
-          }
-          if (NT % 32) {
-            float v[16];
-            tmem_ld16(acc_base + (NT - 16), v);
-            tmem_wait_ld();
-            if (live) conv_store<16>(v, a.bias + n0 + NT - 16, dst + NT - 16);
-          }
-        }
+  } else if (warp < 8) {
+    // ------------------------------------------------------------ bias + GELU epilogue
+    // Warp w reads TMEM lanes 32 (w - 4) .. + 31: thread = tile row (pixel).
+    const int r = (warp - 4) * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>((warp - 4) * 32) << 16;
+    uint32_t i = 0;
+    for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x, ++i) {
+      const int b = static_cast<int>(i & 1);
+      if (!mbar_wait(&acc_full[b], (i >> 1) & 1, a.error_flag, &abort_flag)) break;
+      tc_fence_after();
+      const int64_t p = (t / ntiles) * kCvRows + r;
+      const int n0 = static_cast<int>(t % ntiles) * NT;
+      const bool live = p < a.pixels;
+      const int64_t pp = live ? p : 0;
+      const int im = static_cast<int>(pp / per_image);
+      const int rem = static_cast<int>(pp - im * per_image);
+      const int oy = rem / a.wo, ox = rem - oy * a.wo;
+      __nv_bfloat16 *dst = a.y + im * a.sn + oy * a.sy + ox * a.sx + n0;
+      const uint32_t acc = tmem + lane_off + b * C::ACC_STRIDE;
+#pragma unroll 1
+      for (int col = 0; col + 32 <= NT; col += 32) {
+        float v[32];
+        tmem_ld32(acc + col, v);
+        tmem_wait_ld();
+        if (live) conv_store<32>(v, a.bias + n0 + col, dst + col);
       }
+      if (NT % 32) {
+        float v[16];
+        tmem_ld16(acc + (NT - 16), v);
+        tmem_wait_ld();
+        if (live) conv_store<16>(v, a.bias + n0 + NT - 16, dst + NT - 16);
+      }
+      tc_fence_before();
+      mbar_arrive(&acc_empty[b]);
     }
-  } else if (warp == 4) {
+  } else if (warp == 8) {
     // ------------------------------------------------------------ weights (TMA)
     if (lane == 0) {
-      int last = -1;
-      for (int kb = 0; kb < kblocks; ++kb) {
-        const int st = kb % kCvStages;
-        if (!mbar_wait(&empty[st], ((kb / kCvStages) & 1) ^ 1, a.error_flag, &abort_flag)) break;
-        const int tap = kb / a.cblocks, c0 = (kb - tap * a.cblocks) * kCvBK;
-        mbar_arrive_expect_tx(&full[st], C::B_BYTES);
-        tma_load_2d(smem + st * C::STAGE + C::A_BYTES, &tm_w, tap * a.cblocks * kCvBK + c0, n0,
-                    &full[st]);
-        last = kb;
+      uint32_t g = 0;
+      bool ok = true;
+      for (int64_t t = blockIdx.x; ok && t < tiles; t += gridDim.x) {
+        const int n0 = static_cast<int>(t % ntiles) * NT;
+        for (int kb = 0; kb < kblocks; ++kb, ++g) {
+          const int st = static_cast<int>(g % S);
+          if (!mbar_wait(&empty[st], ((g / S) & 1) ^ 1, a.error_flag, &abort_flag)) {
+            ok = false;
+            break;
+          }
+          const int cb = kb / 9, tap = kb - cb * 9;
+          mbar_arrive_expect_tx(&full[st], C::B_BYTES);
+          tma_load_2d(smem + st * C::STAGE + C::A_BYTES, &tm_w, tap * a.cblocks * kCvBK + cb * kCvBK,
+                      n0, &full[st]);
+        }
       }
       // after an abort: let the weight tiles already requested land before the CTA exits
-      if (abort_flag)
-        for (int k = max(0, last - kCvStages + 1); k <= last; ++k)
-          mbar_drain(&full[k % kCvStages], (k / kCvStages) & 1);
+      if (!ok)
+        for (uint32_t k = g > static_cast<uint32_t>(S) ? g - S : 0; k < g; ++k)
+          mbar_drain(&full[k % S], (k / S) & 1);
     }
   } else {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       const uint32_t idesc = idesc_bf16_f32(kCvRows, NT, false, false);
       const uint32_t base = smem_addr(smem);
+      uint32_t g = 0, i = 0;
       bool ok = true;
-      for (int kb = 0; kb < kblocks; ++kb) {
-        const int st = kb % kCvStages;
-        if (!mbar_wait(&full[st], (kb / kCvStages) & 1, a.error_flag, &abort_flag)) {
-          ok = false;
-          break;
-        }
+      for (int64_t t = blockIdx.x; ok && t < tiles; t += gridDim.x, ++i) {
+        const int b = static_cast<int>(i & 1);
+        if (!mbar_wait(&acc_empty[b], ((i >> 1) & 1) ^ 1, a.error_flag, &abort_flag)) break;
         tc_fence_after();
-        fence_proxy_async_smem();  // the A bytes came from cp.async (generic proxy)
-        const uint32_t sa = base + st * C::STAGE, sb = sa + C::A_BYTES;
-#pragma unroll
-        for (int s = 0; s < kCvSub; ++s)
+        const uint32_t d = tmem + b * C::ACC_STRIDE;
+        for (int kb = 0; kb < kblocks; ++kb, ++g) {
+          const int st = static_cast<int>(g % S);
+          if (!mbar_wait(&full[st], (g / S) & 1, a.error_flag, &abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          fence_proxy_async_smem();  // the A bytes came from cp.async (generic proxy)
+          const uint32_t sa = base + st * C::STAGE, sb = sa + C::A_BYTES;
 #pragma unroll
           for (int k = 0; k < kCvBK / 16; ++k)
-            umma_f16_ss(tmem + s * C::ACC_STRIDE,
-                        smem_desc_sw128(sa + s * (kCvRows * 128) + k * 32, 16, 1024),
-                        smem_desc_sw128(sb + k * 32, 16, 1024), idesc,
-                        (kb > 0 || k > 0) ? 1u : 0u);
-        umma_commit(&empty[st]);
+            umma_f16_ss(d, smem_desc_sw128(sa + k * 32, 16, 1024),
+                        smem_desc_sw128(sb + k * 32, 16, 1024), idesc, (kb > 0 || k > 0) ? 1u : 0u);
+          umma_commit(&empty[st]);
+        }
+        if (ok) umma_commit(&acc_full[b]);
       }
-      if (ok) umma_commit(acc_full);
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 9) {
     tc_fence_after();
     tmem_dealloc(tmem, C::TMEM_COLS);
   }
@@ -397,8 +425,8 @@ int launch_conv_gemm(const ConvArgs &a, const void *packed, int co, int cpad, cu
   const uint64_t strides[1] = {static_cast<uint64_t>(9) * cpad * 2};
   const uint32_t box[2] = {kCvBK, NT};
   if (!make_tmap_bf16(&tw, packed, 2, dims, strides, box)) return B200ASR_ERR_CUDA;
-  const int64_t ctas = (a.pixels + kCvSub * kCvRows - 1) / (kCvSub * kCvRows);
-  dim3 grid(static_cast<unsigned>(ctas * (co / NT)));
+  const int64_t tiles = (a.pixels + kCvRows - 1) / kCvRows * (co / NT);
+  const int grid = static_cast<int>(std::min<int64_t>(tiles, num_sms()));
   conv_gemm_gelu_kernel<NT><<<grid, kCvThreads, C::SMEM, stream>>>(tw, a);
   B200_CUDA_LAUNCH_CHECK("conv3x3s2_gelu");
   return B200ASR_OK;

@@ -303,10 +303,11 @@ def window_config2() -> dict:
 
 
 def encoder_conv(chunks: int = 512) -> list[dict]:
-    """The audio encoder's convolutional front (models/audio_encoder.py:145-175) as the
-    engine runs it today: three Conv2d(3x3, stride 2, pad 1) + GELU on cuDNN in
-    channels-last bf16 (0.6B dims: 1 -> 480 -> 480 -> 480 channels over 128 mel x 100
-    frames per chunk), then conv_out (7680 -> 896) on cuBLAS; one line per stage."""
+    """The audio encoder's convolutional front (models/audio_encoder.py:145-175), 0.6B
+    dims (1 -> 480 -> 480 -> 480 channels over 128 mel x 100 frames per chunk): three
+    Conv2d(3x3, stride 2, pad 1) + GELU on cuDNN in channels-last bf16 (the comparison),
+    then this library's conv3x3s2_gelu kernels on the same inputs, then conv_out
+    (7680 -> 896) on cuBLAS; one line per stage."""
     import torch.nn.functional as F
 
     dev = torch.device("cuda")
