@@ -43,8 +43,17 @@ __device__ __forceinline__ void store_p_row64(uint8_t *tile, int r, const float 
 
 // =============================================================================
 // Paged causal GQA prefill, head_dim 128, query heads = 2 x KV heads.
-// CTA = (64 query tokens of one sequence) x (one KV head g): M rows 0-63 are query
+// Work item = (64 query tokens of one sequence) x (one KV head g): M rows 0-63 are query
 // head 2g, rows 64-127 query head 2g+1, tokens t = row & 63.
+//
+// Persistent: the grid is at most two CTAs per SM and CTA c takes items c, c + grid, ...
+// (item = query tile * KV heads + g, query tiles numbered sequence by sequence). TMEM
+// (S in two 64-column buffers, O in 128 columns) and the barriers are set up once per
+// CTA. Only the producer warp locates an item (a warp scan over the query lengths, the
+// lengths and the block ids of its KV tiles): it runs ahead, and hands the item's
+// parameters to the MMA and softmax warps through a two-slot shared-memory ring. The
+// next item's Q and first K/V tiles load while the current item's last P V and epilogue
+// run; its first P V waits until the epilogue has read O.
 // =============================================================================
 
 constexpr int kPfBN = 64;                      // keys per KV tile
@@ -56,7 +65,7 @@ constexpr int kPfStages = 2;
 // completed when the softmax reads S, and the stage is refilled only after P V of tile j.
 // Without a separate P buffer the CTA needs ~97 KB, so two CTAs share an SM.
 static_assert(kPfPBytes == kPfKVBytes, "P reuses its tile's K buffer");
-constexpr int kPfSmem = 1024 /*align slack*/ + kPfQBytes + 2 * kPfStages * kPfKVBytes + 256;
+constexpr int kPfSmem = 1024 /*align slack*/ + kPfQBytes + 2 * kPfStages * kPfKVBytes + 512;
 // Online softmax with lazy rescaling (the conditional rescale of FlashAttention-4): the
 // running maximum a row exponentiates against only moves when a tile's maximum exceeds it
 // by more than kPfRescaleLog2 (base 2), so P stays below 2^8 and O in TMEM is rescaled
@@ -73,10 +82,16 @@ struct PrefillArgs {
   int num_blocks;
   int block_size;
   int num_kv_heads;
+  int items;  // upper bound of (query tile, KV head) items
   float scale_log2;
   __nv_bfloat16 *out;
   int64_t out_stride;
   int32_t *error_flag;
+};
+
+// An item's parameters as the producer publishes them (one ring slot).
+struct PfItem {
+  int q0, nq, p_first, n_kv, n_tiles, g;  // n_tiles < 0: no more items
 };
 
 __global__ void __launch_bounds__(kTcThreads, 2)
@@ -90,74 +105,40 @@ __global__ void __launch_bounds__(kTcThreads, 2)
   uint8_t *sK = sQ + kPfQBytes;                  // [stage] 16 KiB each
   uint8_t *sV = sK + kPfStages * kPfKVBytes;     // [stage] 16 KiB each
   uint64_t *bars = reinterpret_cast<uint64_t *>(sV + kPfStages * kPfKVBytes);
-  uint64_t *q_full = bars + 0;
-  uint64_t *kv_full = bars + 1;   // [2]
-  uint64_t *kv_empty = bars + 3;  // [2]
-  uint64_t *s_full = bars + 5;    // [2]
-  uint64_t *s_free = bars + 7;    // [2]
-  uint64_t *p_full = bars + 9;
-  uint64_t *o_done = bars + 10;   // one phase per P V tile
-  uint64_t *o_last = bars + 11;   // the last P V tile (single phase)
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 12);
+  uint64_t *q_full = bars + 0;     // Q of the item landed (one phase per item)
+  uint64_t *q_empty = bars + 1;    // the item's last S = Q K^T done: Q may be refilled
+  uint64_t *kv_full = bars + 2;    // [2] per KV tile (global tile count)
+  uint64_t *kv_empty = bars + 4;   // [2]
+  uint64_t *s_full = bars + 6;     // [2]
+  uint64_t *s_free = bars + 8;     // [2] (128 arrivals)
+  uint64_t *p_full = bars + 10;    // [2] (128 arrivals)
+  uint64_t *o_done = bars + 12;    // one phase per P V tile
+  uint64_t *o_last = bars + 13;    // one phase per item: its last P V
+  uint64_t *o_free = bars + 14;    // one phase per item: O read by the epilogue (128)
+  uint64_t *meta_full = bars + 15;   // [2] ring slot written
+  uint64_t *meta_empty = bars + 17;  // [2] ring slot read by the MMA thread and the softmax
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 19);
+  PfItem *ring = reinterpret_cast<PfItem *>(bars + 20);  // [2]
   __shared__ int abort_flag;
-  __shared__ int s_tile_info[4];
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int g = blockIdx.y;
-
-  // ---- locate (sequence, query tile) of this CTA
-  if (warp == 0) {
-    int carry = 0, found = -1, found_tile = 0;
-    for (int b0 = 0; b0 < a.batch && found < 0; b0 += 32) {
-      const int b = b0 + lane;
-      int n = 0;
-      if (b < a.batch) n = (a.cu_seqlens_q[b + 1] - a.cu_seqlens_q[b] + 63) / 64;
-      int incl = n;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += y;
-      }
-      const int excl = carry + incl - n;
-      const bool mine = b < a.batch && (int)blockIdx.x >= excl && (int)blockIdx.x < excl + n;
-      const unsigned ball = __ballot_sync(0xffffffffu, mine);
-      if (ball) {
-        const int src = __ffs(ball) - 1;
-        found = b0 + src;
-        found_tile = static_cast<int>(blockIdx.x) - __shfl_sync(0xffffffffu, excl, src);
-      }
-      carry += __shfl_sync(0xffffffffu, incl, 31);
-    }
-    if (lane == 0) {
-      s_tile_info[0] = found;
-      s_tile_info[1] = found_tile;
-    }
-  }
-  __syncthreads();
-  const int b = s_tile_info[0];
-  if (b < 0) return;  // grid upper bound overshoot: no work, nothing allocated
-  const int qtile = s_tile_info[1];
-  const int q_len = a.cu_seqlens_q[b + 1] - a.cu_seqlens_q[b];
-  const int k_len = a.cu_seqlens_k[b + 1] - a.cu_seqlens_k[b];
-  const int q0 = a.cu_seqlens_q[b] + qtile * 64;
-  const int nq = min(64, q_len - qtile * 64);
-  const int offset = k_len - q_len;                 // bottom-right alignment
-  const int p_first = offset + qtile * 64;          // absolute position of token 0
-  const int n_kv = min(k_len, p_first + nq);        // keys any row of this tile may see
-  const int n_tiles = n_kv > 0 ? (n_kv + kPfBN - 1) / kPfBN : 0;
 
   if (tid == 0) {
     abort_flag = 0;
     mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
     for (int s = 0; s < 2; ++s) {
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
       mbar_init(&s_full[s], 1);
       mbar_init(&s_free[s], 128);
+      mbar_init(&p_full[s], 128);
+      mbar_init(&meta_full[s], 1);
+      mbar_init(&meta_empty[s], 129);
     }
-    mbar_init(p_full, 128);
     mbar_init(o_done, 1);
     mbar_init(o_last, 1);
+    mbar_init(o_free, 128);
     fence_barrier_init();
   }
   if (warp == 5) {
@@ -174,33 +155,136 @@ __global__ void __launch_bounds__(kTcThreads, 2)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (n_tiles == 0 || offset < 0) {
-    if (tid == 0 && offset < 0) raise_flag(a.error_flag, B200ASR_DEVERR_LENGTH);
-  } else if (warp == 4) {
-    // ------------------------------------------------------------ producer
-    if (lane == 0) {
-      mbar_arrive_expect_tx(q_full, kPfQBytes);
-      for (int hh = 0; hh < 2; ++hh)
-        for (int dh = 0; dh < 2; ++dh)
-          tma_load_3d(sQ + dh * 16384 + hh * 8192, &tm_q, dh * 64, 2 * g + hh, q0, q_full);
-      for (int j = 0; j < n_tiles; ++j) {
-        const int st = j & 1;
-        if (!mbar_wait(&kv_empty[st], ((j >> 1) & 1) ^ 1, a.error_flag, &abort_flag)) break;
-        const int key0 = j * kPfBN;
-        int block = a.block_tables[static_cast<int64_t>(b) * a.bt_stride + key0 / a.block_size];
-        if (block < 0 || block >= a.num_blocks) {
-          raise_flag(a.error_flag, B200ASR_DEVERR_BLOCK);
-          block = 0;
+  if (warp == 4) {
+    // ------------------------------------------------------------ producer (whole warp)
+    // Query tiles are located by a warp scan over the sequences' tile counts; the items
+    // of this CTA come in increasing order, so the scan resumes where it stopped.
+    int scan_b0 = 0, scan_carry = 0;
+    auto locate = [&](int t, int &b, int &qtile) -> bool {
+      while (scan_b0 < a.batch) {
+        const int bb = scan_b0 + lane;
+        int n = 0;
+        if (bb < a.batch) n = (a.cu_seqlens_q[bb + 1] - a.cu_seqlens_q[bb] + 63) / 64;
+        int incl = n;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int y = __shfl_up_sync(0xffffffffu, incl, o);
+          if (lane >= o) incl += y;
         }
-        const int slot = block * a.block_size + (key0 % a.block_size);
-        mbar_arrive_expect_tx(&kv_full[st], 2 * kPfKVBytes);
-        uint8_t *k_dst = sK + st * kPfKVBytes;
-        uint8_t *v_dst = sV + st * kPfKVBytes;
-        for (int dh = 0; dh < 2; ++dh) {
-          tma_load_3d(k_dst + dh * 8192, &tm_k, dh * 64, g, slot, &kv_full[st]);
-          tma_load_3d(v_dst + dh * 8192, &tm_v, dh * 64, g, slot, &kv_full[st]);
+        const int total = __shfl_sync(0xffffffffu, incl, 31);
+        if (t < scan_carry + total) {
+          const int excl = scan_carry + incl - n;
+          const unsigned ball = __ballot_sync(0xffffffffu, bb < a.batch && t >= excl && t < excl + n);
+          const int src = __ffs(ball) - 1;
+          b = scan_b0 + src;
+          qtile = t - __shfl_sync(0xffffffffu, excl, src);
+          return true;
+        }
+        scan_carry += total;
+        scan_b0 += 32;
+      }
+      return false;
+    };
+    uint32_t it = 0, jg = 0;  // items published, KV tiles issued
+    bool ok = true;
+    // publish ring slot it & 1 (after its previous readers are done)
+    auto publish = [&](const PfItem &item) -> bool {
+      const int slot = it & 1;
+      int good = 1;
+      if (lane == 0) {
+        good = it < 2 || mbar_wait(&meta_empty[slot], ((it >> 1) & 1) ^ 1, a.error_flag, &abort_flag);
+        if (good) {
+          volatile PfItem *r = ring + slot;
+          r->q0 = item.q0;
+          r->nq = item.nq;
+          r->p_first = item.p_first;
+          r->n_kv = item.n_kv;
+          r->n_tiles = item.n_tiles;
+          r->g = item.g;
+          mbar_arrive(&meta_full[slot]);
         }
       }
+      return __shfl_sync(0xffffffffu, good, 0) != 0;
+    };
+    for (int i = blockIdx.x; ok && i < a.items; i += gridDim.x) {
+      const int t = i / a.num_kv_heads, g = i - t * a.num_kv_heads;
+      int b, qtile;
+      if (!locate(t, b, qtile)) break;  // past the last query tile
+      const int q_len = a.cu_seqlens_q[b + 1] - a.cu_seqlens_q[b];
+      const int k_len = a.cu_seqlens_k[b + 1] - a.cu_seqlens_k[b];
+      PfItem item;
+      item.q0 = a.cu_seqlens_q[b] + qtile * 64;
+      item.nq = min(64, q_len - qtile * 64);
+      const int offset = k_len - q_len;  // bottom-right alignment
+      item.p_first = offset + qtile * 64;
+      item.n_kv = min(k_len, item.p_first + item.nq);
+      item.n_tiles = item.n_kv > 0 ? (item.n_kv + kPfBN - 1) / kPfBN : 0;
+      item.g = g;
+      if (offset < 0) {
+        if (lane == 0) raise_flag(a.error_flag, B200ASR_DEVERR_LENGTH);
+        continue;
+      }
+      if (item.n_tiles == 0) continue;
+      if (!publish(item)) {
+        ok = false;
+        break;
+      }
+      // Q: after the previous item's last S = Q K^T
+      if (lane == 0) {
+        if (it > 0 && !mbar_wait(q_empty, (it - 1) & 1, a.error_flag, &abort_flag)) ok = false;
+        if (ok) {
+          mbar_arrive_expect_tx(q_full, kPfQBytes);
+          for (int hh = 0; hh < 2; ++hh)
+            for (int dh = 0; dh < 2; ++dh)
+              tma_load_3d(sQ + dh * 16384 + hh * 8192, &tm_q, dh * 64, 2 * g + hh, item.q0, q_full);
+        }
+      }
+      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+      ++it;
+      // K/V tiles: lane l reads the cache slot of tile w0 + l (reads in flight together)
+      const int64_t bt_row = static_cast<int64_t>(b) * a.bt_stride;
+      for (int w0 = 0; ok && w0 < item.n_tiles; w0 += 32) {
+        int slot = 0;
+        if (w0 + lane < item.n_tiles) {
+          const int key0 = (w0 + lane) * kPfBN;
+          int block = a.block_tables[bt_row + key0 / a.block_size];
+          if (block < 0 || block >= a.num_blocks) {
+            raise_flag(a.error_flag, B200ASR_DEVERR_BLOCK);
+            block = 0;
+          }
+          slot = block * a.block_size + (key0 % a.block_size);
+        }
+        const int nw = min(32, item.n_tiles - w0);
+        for (int l = 0; l < nw; ++l, ++jg) {
+          const int sl = __shfl_sync(0xffffffffu, slot, l);
+          if (lane == 0) {
+            const int st = jg & 1;
+            if (!mbar_wait(&kv_empty[st], ((jg >> 1) & 1) ^ 1, a.error_flag, &abort_flag)) {
+              ok = false;
+            } else {
+              mbar_arrive_expect_tx(&kv_full[st], 2 * kPfKVBytes);
+              uint8_t *k_dst = sK + st * kPfKVBytes;
+              uint8_t *v_dst = sV + st * kPfKVBytes;
+              for (int dh = 0; dh < 2; ++dh) {
+                tma_load_3d(k_dst + dh * 8192, &tm_k, dh * 64, g, sl, &kv_full[st]);
+                tma_load_3d(v_dst + dh * 8192, &tm_v, dh * 64, g, sl, &kv_full[st]);
+              }
+            }
+          }
+          ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+          if (!ok) break;
+        }
+      }
+    }
+    if (ok) {  // end marker
+      PfItem end{};
+      end.n_tiles = -1;
+      publish(end);
+    }
+    // after an abort: let the copies already requested land before the CTA exits
+    if (lane == 0 && abort_flag) {
+      if (it > 0) mbar_drain(q_full, (it - 1) & 1);
+      for (uint32_t k = jg > 2 ? jg - 2 : 0; k < jg; ++k) mbar_drain(&kv_full[k & 1], (k >> 1) & 1);
     }
   } else if (warp == 5) {
     // ------------------------------------------------------------ MMA issuer
@@ -208,137 +292,174 @@ __global__ void __launch_bounds__(kTcThreads, 2)
       constexpr uint32_t idesc_s = idesc_bf16_f32(128, kPfBN, false, false);
       constexpr uint32_t idesc_o = idesc_bf16_f32(128, 128, false, true);
       const uint32_t q_base = smem_addr(sQ), k_base = smem_addr(sK), v_base = smem_addr(sV);
-      bool ok = mbar_wait(q_full, 0, a.error_flag, &abort_flag);
-      auto issue_pv = [&](int jj) {
+      // P V of global tile jj, tile j of the item (j == 0 overwrites O)
+      auto issue_pv = [&](uint32_t jj, int j, bool last) {
         const uint32_t vb = v_base + (jj & 1) * kPfKVBytes;
         const uint32_t pb = k_base + (jj & 1) * kPfKVBytes;  // P(jj) over K(jj)
 #pragma unroll
         for (int k = 0; k < kPfBN / 16; ++k) {
           const uint64_t ad = smem_desc_sw128(pb + k * 32, 16, 1024);
           const uint64_t bd = smem_desc_sw128(vb + k * 2048, 8192, 1024);
-          umma_f16_ss(tmem + 128, ad, bd, idesc_o, (jj > 0 || k > 0) ? 1u : 0u);
+          umma_f16_ss(tmem + 128, ad, bd, idesc_o, (j > 0 || k > 0) ? 1u : 0u);
         }
         umma_commit(&kv_empty[jj & 1]);
         umma_commit(o_done);
-        if (jj == n_tiles - 1) umma_commit(o_last);
+        if (last) umma_commit(o_last);
       };
-      for (int j = 0; ok && j < n_tiles; ++j) {
-        const int st = j & 1;
-        if (!mbar_wait(&kv_full[st], (j >> 1) & 1, a.error_flag, &abort_flag)) break;
-        if (j >= 2 && !mbar_wait(&s_free[j & 1], ((j - 2) >> 1) & 1, a.error_flag, &abort_flag))
-          break;
-        tc_fence_after();
-        const uint32_t kb = k_base + st * kPfKVBytes;
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const uint32_t off = (k >> 2) * 16384 + (k & 3) * 32;
-          const uint32_t koff = (k >> 2) * 8192 + (k & 3) * 32;
-          const uint64_t ad = smem_desc_sw128(q_base + off, 16, 1024);
-          const uint64_t bd = smem_desc_sw128(kb + koff, 16, 1024);
-          umma_f16_ss(tmem + (j & 1) * kPfBN, ad, bd, idesc_s, k > 0 ? 1u : 0u);
-        }
-        umma_commit(&s_full[j & 1]);
-        if (j >= 1) {
-          if (!mbar_wait(p_full, (j - 1) & 1, a.error_flag, &abort_flag)) break;
+      uint32_t jg = 0;
+      bool ok = true;
+      for (uint32_t it = 0; ok; ++it) {
+        const int slot = it & 1;
+        if (!mbar_wait(&meta_full[slot], (it >> 1) & 1, a.error_flag, &abort_flag)) break;
+        const int n_tiles = ring[slot].n_tiles;
+        tc_fence_before();
+        mbar_arrive(&meta_empty[slot]);
+        if (n_tiles < 0) break;
+        if (!mbar_wait(q_full, it & 1, a.error_flag, &abort_flag)) break;
+        // the item's first P V overwrites O: the previous item's epilogue must have read it
+        bool o_ready = it == 0;
+        auto wait_o = [&]() -> bool {
+          if (!o_ready) o_ready = mbar_wait(o_free, (it - 1) & 1, a.error_flag, &abort_flag);
+          return o_ready;
+        };
+        for (int j = 0; j < n_tiles; ++j, ++jg) {
+          const int st = jg & 1;
+          if (!mbar_wait(&kv_full[st], (jg >> 1) & 1, a.error_flag, &abort_flag)) { ok = false; break; }
+          if (jg >= 2 && !mbar_wait(&s_free[st], ((jg - 2) >> 1) & 1, a.error_flag, &abort_flag)) {
+            ok = false;
+            break;
+          }
           tc_fence_after();
-          issue_pv(j - 1);
+          const uint32_t kb = k_base + st * kPfKVBytes;
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const uint32_t off = (k >> 2) * 16384 + (k & 3) * 32;
+            const uint32_t koff = (k >> 2) * 8192 + (k & 3) * 32;
+            const uint64_t ad = smem_desc_sw128(q_base + off, 16, 1024);
+            const uint64_t bd = smem_desc_sw128(kb + koff, 16, 1024);
+            umma_f16_ss(tmem + st * kPfBN, ad, bd, idesc_s, k > 0 ? 1u : 0u);
+          }
+          umma_commit(&s_full[st]);
+          if (j == n_tiles - 1) umma_commit(q_empty);  // Q of this item no longer read
+          if (j >= 1) {
+            const uint32_t jp = jg - 1;
+            if (!mbar_wait(&p_full[jp & 1], (jp >> 1) & 1, a.error_flag, &abort_flag) ||
+                (j == 1 && !wait_o())) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_pv(jp, j - 1, false);
+          }
         }
-      }
-      if (!abort_flag && mbar_wait(p_full, (n_tiles - 1) & 1, a.error_flag, &abort_flag)) {
+        if (!ok) break;
+        const uint32_t jl = jg - 1;
+        if (!mbar_wait(&p_full[jl & 1], (jl >> 1) & 1, a.error_flag, &abort_flag) || !wait_o()) break;
         tc_fence_after();
-        issue_pv(n_tiles - 1);
+        issue_pv(jl, n_tiles - 1, true);
       }
     }
   } else {
     // ------------------------------------------------------------ softmax (warps 0-3)
     const int r = tid;                   // accumulator row == TMEM lane
     const int t = r & 63;
-    const int head = 2 * g + (r >> 6);
-    const int p_row = p_first + t;       // last key this row may attend
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
-    float m = -INFINITY, l = 0.f;
-    bool ok = true;
-    for (int j = 0; j < n_tiles; ++j) {
-      if (!mbar_wait(&s_full[j & 1], (j >> 1) & 1, a.error_flag, &abort_flag)) { ok = false; break; }
+    uint32_t jg = 0;
+    for (uint32_t it = 0;; ++it) {
+      const int slot = it & 1;
+      if (!mbar_wait(&meta_full[slot], (it >> 1) & 1, a.error_flag, &abort_flag)) break;
+      const PfItem item = *const_cast<const PfItem *>(ring + slot);
+      tc_fence_before();
+      mbar_arrive(&meta_empty[slot]);
+      if (item.n_tiles < 0) break;
+      const int head = 2 * item.g + (r >> 6);
+      const int p_row = item.p_first + t;  // last key this row may attend
+      float m = -INFINITY, l = 0.f;
+      bool ok = true;
+      for (int j = 0; j < item.n_tiles; ++j, ++jg) {
+        const int st = jg & 1;
+        if (!mbar_wait(&s_full[st], (jg >> 1) & 1, a.error_flag, &abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        float s[kPfBN];
+        tmem_ld32(lane_base + st * kPfBN, s);
+        tmem_ld32(lane_base + st * kPfBN + 32, s + 32);
+        tmem_wait_ld();
+        tc_fence_before();
+        mbar_arrive(&s_free[st]);
+        const int key0 = j * kPfBN;
+        float mx = -INFINITY;
+#pragma unroll
+        for (int c = 0; c < kPfBN; ++c) {
+          s[c] = (key0 + c <= p_row) ? s[c] * a.scale_log2 : -INFINITY;
+          mx = fmaxf(mx, s[c]);
+        }
+        // Tile 0 sets the maximum (key 0 is visible to every row: finite). Later tiles
+        // move it only past the threshold; O then needs its rescale, after P V of the
+        // previous tile. At tile j that P V is the only one that can be outstanding (S of
+        // tile j was issued after P V of tile j - 2), so the parity wait is exact.
+        const bool move = j == 0 || mx > m + kPfRescaleLog2;
+        const float m_new = move ? fmaxf(m, mx) : m;
+        const float alpha = exp2f(m - m_new);  // m = -inf on the first tile -> 0
+        float sum = 0.f;
+#pragma unroll
+        for (int c = 0; c < kPfBN; ++c) {
+          s[c] = exp2f(s[c] - m_new);
+          sum += s[c];
+        }
+        l = l * alpha + sum;
+        m = m_new;
+        if (j > 0 && __any_sync(0xffffffffu, move)) {
+          if (!mbar_wait(o_done, (jg - 1) & 1, a.error_flag, &abort_flag)) { ok = false; break; }
+          tc_fence_after();
+#pragma unroll
+          for (int cc = 0; cc < 4; ++cc) {
+            float o[32];
+            tmem_ld32(lane_base + 128 + cc * 32, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] *= alpha;
+            tmem_st32(lane_base + 128 + cc * 32, o);
+          }
+          tmem_wait_st();
+        }
+        store_p_row64(sK + st * kPfKVBytes, r, s);  // P(j) over K(j)
+        // Keys from n_kv on get P = 0 in every row, but their V rows hold whatever the
+        // cache pages hold past the sequence (never-written memory may be NaN or Inf, and
+        // 0 * NaN poisons the row sums): clear those V rows of the last tile. Thread r owns
+        // key t of d-half r >> 6.
+        if (j == item.n_tiles - 1 && key0 + t >= item.n_kv) {
+          fence_proxy_async_smem();  // after the tile's TMA bytes, before these stores
+          uint4 *row = reinterpret_cast<uint4 *>(sV + st * kPfKVBytes + (r >> 6) * 8192 +
+                                                 (t >> 3) * 1024 + (t & 7) * 128);
+#pragma unroll
+          for (int c = 0; c < 8; ++c) row[c] = make_uint4(0u, 0u, 0u, 0u);
+        }
+        fence_proxy_async_smem();
+        tc_fence_before();
+        mbar_arrive(&p_full[st]);
+      }
+      if (!ok || !mbar_wait(o_last, it & 1, a.error_flag, &abort_flag)) break;
       tc_fence_after();
-      float s[kPfBN];
-      tmem_ld32(lane_base + (j & 1) * kPfBN, s);
-      tmem_ld32(lane_base + (j & 1) * kPfBN + 32, s + 32);
+      float o[4][32];
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) tmem_ld32(lane_base + 128 + cc * 32, o[cc]);
       tmem_wait_ld();
       tc_fence_before();
-      mbar_arrive(&s_free[j & 1]);
-      const int key0 = j * kPfBN;
-      float mx = -INFINITY;
+      mbar_arrive(o_free);  // the next item's first P V may overwrite O
+      if (t < item.nq) {
+        const float inv = 1.f / l;
+        __nv_bfloat16 *dst = a.out + static_cast<int64_t>(item.q0 + t) * a.out_stride + head * 128;
 #pragma unroll
-      for (int c = 0; c < kPfBN; ++c) {
-        s[c] = (key0 + c <= p_row) ? s[c] * a.scale_log2 : -INFINITY;
-        mx = fmaxf(mx, s[c]);
-      }
-      // Tile 0 sets the maximum (key 0 is visible to every row: finite). Later tiles
-      // move it only past the threshold; O then needs its rescale, after P V of the
-      // previous tile. At tile j that P V is the only one that can be outstanding (S of
-      // tile j was issued after P V of tile j - 2), so the parity wait is exact.
-      const bool move = j == 0 || mx > m + kPfRescaleLog2;
-      const float m_new = move ? fmaxf(m, mx) : m;
-      const float alpha = exp2f(m - m_new);  // m = -inf on the first tile -> 0
-      float sum = 0.f;
-#pragma unroll
-      for (int c = 0; c < kPfBN; ++c) {
-        s[c] = exp2f(s[c] - m_new);
-        sum += s[c];
-      }
-      l = l * alpha + sum;
-      m = m_new;
-      if (j > 0 && __any_sync(0xffffffffu, move)) {
-        if (!mbar_wait(o_done, (j - 1) & 1, a.error_flag, &abort_flag)) { ok = false; break; }
-        tc_fence_after();
-#pragma unroll
-        for (int cc = 0; cc < 4; ++cc) {
-          float o[32];
-          tmem_ld32(lane_base + 128 + cc * 32, o);
-          tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] *= alpha;
-          tmem_st32(lane_base + 128 + cc * 32, o);
-        }
-        tmem_wait_st();
-      }
-      store_p_row64(sK + (j & 1) * kPfKVBytes, r, s);  // P(j) over K(j)
-      // Keys from n_kv on get P = 0 in every row, but their V rows hold whatever the
-      // cache pages hold past the sequence (never-written memory may be NaN or Inf, and
-      // 0 * NaN poisons the row sums): clear those V rows of the last tile. Thread r owns
-      // key t of d-half r >> 6.
-      if (j == n_tiles - 1 && key0 + t >= n_kv) {
-        fence_proxy_async_smem();  // after the tile's TMA bytes, before these stores
-        uint4 *row = reinterpret_cast<uint4 *>(sV + (j & 1) * kPfKVBytes + (r >> 6) * 8192 +
-                                               (t >> 3) * 1024 + (t & 7) * 128);
-#pragma unroll
-        for (int c = 0; c < 8; ++c) row[c] = make_uint4(0u, 0u, 0u, 0u);
-      }
-      fence_proxy_async_smem();
-      tc_fence_before();
-      mbar_arrive(p_full);
-    }
-    if (ok && mbar_wait(o_last, 0, a.error_flag, &abort_flag)) {
-      tc_fence_after();
-      const float inv = 1.f / l;
-      __nv_bfloat16 *dst = a.out + static_cast<int64_t>(q0 + t) * a.out_stride + head * 128;
-#pragma unroll
-      for (int cc = 0; cc < 4; ++cc) {
-        float o[32];
-        tmem_ld32(lane_base + 128 + cc * 32, o);
-        tmem_wait_ld();
-        if (t < nq) {
+        for (int cc = 0; cc < 4; ++cc)
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
             uint4 v;
-            v.x = pack2(o[8 * i + 0] * inv, o[8 * i + 1] * inv);
-            v.y = pack2(o[8 * i + 2] * inv, o[8 * i + 3] * inv);
-            v.z = pack2(o[8 * i + 4] * inv, o[8 * i + 5] * inv);
-            v.w = pack2(o[8 * i + 6] * inv, o[8 * i + 7] * inv);
+            v.x = pack2(o[cc][8 * i + 0] * inv, o[cc][8 * i + 1] * inv);
+            v.y = pack2(o[cc][8 * i + 2] * inv, o[cc][8 * i + 3] * inv);
+            v.z = pack2(o[cc][8 * i + 4] * inv, o[cc][8 * i + 5] * inv);
+            v.w = pack2(o[cc][8 * i + 6] * inv, o[cc][8 * i + 7] * inv);
             *reinterpret_cast<uint4 *>(dst + cc * 32 + i * 8) = v;
           }
-        }
       }
     }
   }
@@ -406,6 +527,9 @@ __global__ void __launch_bounds__(kTcThreads, 2)
   uint64_t *o_full = bars + 7;    // O in TMEM
   uint64_t *o_free = bars + 8;    // O read out (128 arrivals)
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 9);
+  // meta[b] = {row0, len, head} of the item in buffer b, written by the producer before
+  // the item's loads (published by ld_full[b]); len < 0 marks the end of the CTA's items.
+  volatile int *meta = reinterpret_cast<volatile int *>(bars + 10);
   __shared__ int abort_flag;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -439,8 +563,11 @@ __global__ void __launch_bounds__(kTcThreads, 2)
 
   if (warp == 4) {
     // ------------------------------------------------------------ producer
+    // The only role that reads the segment bounds from global memory: it runs ahead of
+    // the others (loads of item i + 1 overlap item i), so those reads leave the chain.
     if (lane == 0) {
       uint32_t it = 0;
+      bool ok = true;
       for (int item = blockIdx.x; item < items; item += gridDim.x) {
         int row0, len, head;
         if (!window_item(a, item, row0, len, head)) {
@@ -448,13 +575,26 @@ __global__ void __launch_bounds__(kTcThreads, 2)
           continue;
         }
         const int b = it & 1;
-        if (!mbar_wait(&ld_empty[b], ((it >> 1) & 1) ^ 1, a.error_flag, &abort_flag)) break;
+        if (!mbar_wait(&ld_empty[b], ((it >> 1) & 1) ^ 1, a.error_flag, &abort_flag)) {
+          ok = false;
+          break;
+        }
+        meta[4 * b] = row0;
+        meta[4 * b + 1] = len;
+        meta[4 * b + 2] = head;
         uint8_t *buf = smem + b * kWinBuf;
         mbar_arrive_expect_tx(&ld_full[b], kWinBuf);
         tma_load_3d(buf, &tm_q, 0, head, row0, &ld_full[b]);
         tma_load_3d(buf + kWinTile, &tm_k, 0, head, row0, &ld_full[b]);
         tma_load_3d(buf + 2 * kWinTile, &tm_v, 0, head, row0, &ld_full[b]);
         ++it;
+      }
+      // end marker through the same pipeline: the next buffer's phase completes with no
+      // bytes and len = -1
+      const int b = it & 1;
+      if (ok && mbar_wait(&ld_empty[b], ((it >> 1) & 1) ^ 1, a.error_flag, &abort_flag)) {
+        meta[4 * b + 1] = -1;
+        mbar_arrive(&ld_full[b]);
       }
     }
   } else if (warp == 5) {
@@ -463,11 +603,13 @@ __global__ void __launch_bounds__(kTcThreads, 2)
       constexpr uint32_t idesc_s = idesc_bf16_f32(128, 128, false, false);
       constexpr uint32_t idesc_o = idesc_bf16_f32(128, 64, false, true);
       const uint32_t base = smem_addr(smem);
-      // S of item `it` (buffer it & 1) into TMEM columns 0-127
-      auto issue_s = [&](uint32_t it) -> bool {
+      // S of item `it` (buffer it & 1) into TMEM columns 0-127; 0 at the end marker,
+      // -1 on a timed-out wait
+      auto issue_s = [&](uint32_t it) -> int {
         const uint32_t b = it & 1;
-        if (!mbar_wait(&ld_full[b], (it >> 1) & 1, a.error_flag, &abort_flag)) return false;
-        if (it > 0 && !mbar_wait(s_free, (it - 1) & 1, a.error_flag, &abort_flag)) return false;
+        if (!mbar_wait(&ld_full[b], (it >> 1) & 1, a.error_flag, &abort_flag)) return -1;
+        if (meta[4 * b + 1] < 0) return 0;
+        if (it > 0 && !mbar_wait(s_free, (it - 1) & 1, a.error_flag, &abort_flag)) return -1;
         tc_fence_after();
         const uint32_t qb = base + b * kWinBuf, kb = qb + kWinTile;
 #pragma unroll
@@ -475,16 +617,12 @@ __global__ void __launch_bounds__(kTcThreads, 2)
           umma_f16_ss(tmem, smem_desc_sw128(qb + k * 32, 16, 1024),
                       smem_desc_sw128(kb + k * 32, 16, 1024), idesc_s, k > 0 ? 1u : 0u);
         umma_commit(s_full);
-        return true;
+        return 1;
       };
-      uint32_t n = 0;  // valid items of this CTA
-      for (int item = blockIdx.x; item < items; item += gridDim.x) {
-        int row0, len, head;
-        n += window_item(a, item, row0, len, head) ? 1u : 0u;
-      }
-      bool ok = n == 0 || issue_s(0);
-      for (uint32_t it = 0; ok && it < n; ++it) {
-        if (it + 1 < n && !issue_s(it + 1)) break;  // overlaps the softmax of item `it`
+      int have = issue_s(0);
+      for (uint32_t it = 0; have > 0; ++it) {
+        have = issue_s(it + 1);  // overlaps the softmax of item `it`
+        if (have < 0) break;
         if (!mbar_wait(p_full, it & 1, a.error_flag, &abort_flag)) break;
         if (it > 0 && !mbar_wait(o_free, (it - 1) & 1, a.error_flag, &abort_flag)) break;
         tc_fence_after();
@@ -503,11 +641,15 @@ __global__ void __launch_bounds__(kTcThreads, 2)
     // ------------------------------------------------------------ softmax + epilogue
     const int r = tid;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
-    uint32_t it = 0;
-    for (int item = blockIdx.x; item < items; item += gridDim.x) {
-      int row0, len, head;
-      if (!window_item(a, item, row0, len, head)) continue;
-      uint8_t *buf = smem + (it & 1) * kWinBuf;
+    for (uint32_t it = 0;; ++it) {
+      const int b = it & 1;
+      // the item's bounds, published with its loads (the buffer cannot be refilled
+      // before this item's P V, so the phase waited for is this item's)
+      if (!mbar_wait(&ld_full[b], (it >> 1) & 1, a.error_flag, &abort_flag)) break;
+      const int len = meta[4 * b + 1];
+      if (len < 0) break;
+      const int row0 = meta[4 * b], head = meta[4 * b + 2];
+      uint8_t *buf = smem + b * kWinBuf;
       if (!mbar_wait(s_full, it & 1, a.error_flag, &abort_flag)) break;
       tc_fence_after();
       float s[128];
@@ -563,7 +705,6 @@ __global__ void __launch_bounds__(kTcThreads, 2)
           *reinterpret_cast<uint4 *>(dst + i * 8) = v;
         }
       }
-      ++it;
     }
   }
   tc_fence_before();
@@ -635,8 +776,10 @@ extern "C" int b200asr_paged_prefill(const void *q, int64_t q_row_stride, const 
   a.out_stride = out_row_stride;
   a.error_flag = error_flag;
   (void)max_seqlen_q;
-  const int tiles = total_q / 64 + batch;  // >= sum over rows of ceil(q_len / 64)
-  dim3 grid(tiles, num_kv_heads);
+  const int64_t tiles = static_cast<int64_t>(total_q) / 64 + batch;  // >= sum of ceil(q_len / 64)
+  B200_REQUIRE(tiles * num_kv_heads < (int64_t{1} << 31), "paged_prefill: too many query tiles");
+  a.items = static_cast<int>(tiles * num_kv_heads);
+  const int grid = static_cast<int>(std::min<int64_t>(a.items, 2 * num_sms()));
   paged_prefill_kernel<<<grid, kTcThreads, kPfSmem, stream>>>(tq, tk, tv, a);
   B200_CUDA_LAUNCH_CHECK("paged_prefill");
   return B200ASR_OK;
