@@ -478,12 +478,14 @@ __global__ void __launch_bounds__(kTcThreads, 2)
 // (no online rescaling needed), O = P V (128x64, K=128).
 //
 // Persistent pipeline: the grid is at most two CTAs per SM, and CTA c takes items c,
-// c + grid, ... (item = segment * heads + head). TMEM (S in columns 0-127, O in 128-191)
-// and the barriers are set up once per CTA. Shared memory holds two (Q, K, V) buffers:
-// the producer loads item i + 1 into one while item i computes from the other, the MMA
-// warp issues S of item i + 1 as soon as the softmax has read S of item i out of TMEM,
-// and P of item i (two 64-key K-major halves) is written over Q and K of its buffer once
-// S is done (the buffer is refilled only after P V of item i).
+// c + grid, ... (item = segment * heads + head). TMEM (S in columns 0-127, O of items
+// i & 1 in 128-191 / 192-255) and the barriers are set up once per CTA. Shared memory
+// holds two (Q, K, V) buffers: the producer loads item i + 1 into one while item i
+// computes from the other, the MMA warp issues S of item i + 1 as soon as the softmax has
+// read S of item i out of TMEM, and P of item i (two 64-key K-major halves) is written
+// over Q and K of its buffer once S is done (the buffer is refilled only after P V of
+// item i). The softmax warps write item i's output after item i + 1's softmax, so P V
+// of item i runs under that softmax instead of stalling the warps.
 // =============================================================================
 
 constexpr int kWinTile = 16384;                   // [128 rows x 128 B]
@@ -523,13 +525,13 @@ __global__ void __launch_bounds__(kTcThreads, 2)
   uint64_t *ld_empty = bars + 2;  // [2] buffer b free (P V of its item done)
   uint64_t *s_full = bars + 4;    // S in TMEM
   uint64_t *s_free = bars + 5;    // S read out by the softmax (128 arrivals)
-  uint64_t *p_full = bars + 6;    // P written (128 arrivals)
-  uint64_t *o_full = bars + 7;    // O in TMEM
-  uint64_t *o_free = bars + 8;    // O read out (128 arrivals)
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 9);
+  uint64_t *p_full = bars + 6;    // [2] P of item i written (128 arrivals), by i & 1
+  uint64_t *o_full = bars + 8;    // [2] O of item i in TMEM
+  uint64_t *o_free = bars + 10;   // [2] O of item i read out (128 arrivals)
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 12);
   // meta[b] = {row0, len, head} of the item in buffer b, written by the producer before
   // the item's loads (published by ld_full[b]); len < 0 marks the end of the CTA's items.
-  volatile int *meta = reinterpret_cast<volatile int *>(bars + 10);
+  volatile int *meta = reinterpret_cast<volatile int *>(bars + 13);
   __shared__ int abort_flag;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -542,9 +544,11 @@ __global__ void __launch_bounds__(kTcThreads, 2)
     }
     mbar_init(s_full, 1);
     mbar_init(s_free, 128);
-    mbar_init(p_full, 128);
-    mbar_init(o_full, 1);
-    mbar_init(o_free, 128);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&p_full[b], 128);
+      mbar_init(&o_full[b], 1);
+      mbar_init(&o_free[b], 128);
+    }
     fence_barrier_init();
   }
   if (warp == 5) {
@@ -623,17 +627,19 @@ __global__ void __launch_bounds__(kTcThreads, 2)
       for (uint32_t it = 0; have > 0; ++it) {
         have = issue_s(it + 1);  // overlaps the softmax of item `it`
         if (have < 0) break;
-        if (!mbar_wait(p_full, it & 1, a.error_flag, &abort_flag)) break;
-        if (it > 0 && !mbar_wait(o_free, (it - 1) & 1, a.error_flag, &abort_flag)) break;
+        const int ob = it & 1;
+        if (!mbar_wait(&p_full[ob], (it >> 1) & 1, a.error_flag, &abort_flag)) break;
+        // O buffer ob last held item it - 2: its output must have been read
+        if (it >= 2 && !mbar_wait(&o_free[ob], ((it - 2) >> 1) & 1, a.error_flag, &abort_flag)) break;
         tc_fence_after();
         const uint32_t pb = base + (it & 1) * kWinBuf;  // P over Q | K
         const uint32_t vb = pb + 2 * kWinTile;
 #pragma unroll
         for (int k = 0; k < 8; ++k)
-          umma_f16_ss(tmem + 128,
+          umma_f16_ss(tmem + 128 + 64 * ob,
                       smem_desc_sw128(pb + (k >> 2) * kWinTile + (k & 3) * 32, 16, 1024),
                       smem_desc_sw128(vb + k * 2048, kWinTile, 1024), idesc_o, k > 0 ? 1u : 0u);
-        umma_commit(o_full);
+        umma_commit(&o_full[ob]);
         umma_commit(&ld_empty[it & 1]);
       }
     }
@@ -641,13 +647,46 @@ __global__ void __launch_bounds__(kTcThreads, 2)
     // ------------------------------------------------------------ softmax + epilogue
     const int r = tid;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
-    for (uint32_t it = 0;; ++it) {
+    // the previous item, whose output is written after this item's softmax
+    int p_row0 = 0, p_len = 0, p_head = 0;
+    float p_sum = 1.f;
+    auto epilogue = [&](uint32_t pi) -> bool {
+      const int ob = pi & 1;
+      if (!mbar_wait(&o_full[ob], (pi >> 1) & 1, a.error_flag, &abort_flag)) return false;
+      tc_fence_after();
+      float o[64];
+      tmem_ld32(lane_base + 128 + 64 * ob, o);
+      tmem_ld32(lane_base + 160 + 64 * ob, o + 32);
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(&o_free[ob]);
+      if (r < p_len) {
+        const float inv = 1.f / p_sum;
+        __nv_bfloat16 *dst = a.out + static_cast<int64_t>(p_row0 + r) * a.out_stride + p_head * 64;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          uint4 v;
+          v.x = pack2(o[8 * i + 0] * inv, o[8 * i + 1] * inv);
+          v.y = pack2(o[8 * i + 2] * inv, o[8 * i + 3] * inv);
+          v.z = pack2(o[8 * i + 4] * inv, o[8 * i + 5] * inv);
+          v.w = pack2(o[8 * i + 6] * inv, o[8 * i + 7] * inv);
+          *reinterpret_cast<uint4 *>(dst + i * 8) = v;
+        }
+      }
+      return true;
+    };
+    bool ended = false;
+    uint32_t it = 0;
+    for (;; ++it) {
       const int b = it & 1;
       // the item's bounds, published with its loads (the buffer cannot be refilled
       // before this item's P V, so the phase waited for is this item's)
       if (!mbar_wait(&ld_full[b], (it >> 1) & 1, a.error_flag, &abort_flag)) break;
       const int len = meta[4 * b + 1];
-      if (len < 0) break;
+      if (len < 0) {
+        ended = true;
+        break;
+      }
       const int row0 = meta[4 * b], head = meta[4 * b + 2];
       uint8_t *buf = smem + b * kWinBuf;
       if (!mbar_wait(s_full, it & 1, a.error_flag, &abort_flag)) break;
@@ -683,29 +722,14 @@ __global__ void __launch_bounds__(kTcThreads, 2)
       }
       fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(p_full);
-      if (!mbar_wait(o_full, it & 1, a.error_flag, &abort_flag)) break;
-      tc_fence_after();
-      float o[64];
-      tmem_ld32(lane_base + 128, o);
-      tmem_ld32(lane_base + 160, o + 32);
-      tmem_wait_ld();
-      tc_fence_before();
-      mbar_arrive(o_free);
-      if (r < len) {
-        const float inv = 1.f / sum;
-        __nv_bfloat16 *dst = a.out + static_cast<int64_t>(row0 + r) * a.out_stride + head * 64;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          uint4 v;
-          v.x = pack2(o[8 * i + 0] * inv, o[8 * i + 1] * inv);
-          v.y = pack2(o[8 * i + 2] * inv, o[8 * i + 3] * inv);
-          v.z = pack2(o[8 * i + 4] * inv, o[8 * i + 5] * inv);
-          v.w = pack2(o[8 * i + 6] * inv, o[8 * i + 7] * inv);
-          *reinterpret_cast<uint4 *>(dst + i * 8) = v;
-        }
-      }
+      mbar_arrive(&p_full[b]);
+      if (it > 0 && !epilogue(it - 1)) break;
+      p_row0 = row0;
+      p_len = len;
+      p_head = head;
+      p_sum = sum;
     }
+    if (ended && it > 0) epilogue(it - 1);
   }
   tc_fence_before();
   __syncthreads();
