@@ -193,8 +193,10 @@ class AsrEngine:
         if encode_batch:
             started = time.perf_counter()
             try:
+                # No host sync: the embeddings stay on the device and everything that
+                # reads them runs later on the same stream, so the host goes on to
+                # schedule and launch the next work while the encoder still runs.
                 self.audio_runner.encode(encode_batch)
-                torch.cuda.synchronize()
             except OutOfMemoryError:
                 logger.warning("audio encode ran out of memory on %d requests; rolling back",
                                len(encode_batch))
