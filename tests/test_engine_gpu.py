@@ -187,6 +187,23 @@ def test_long_context_crosses_blocks(tiny_dir, clips):
     _assert_agrees(_agreement_with_reference(engine, long_clip, [out]), "long clip")
 
 
+def test_wide_mlp_takes_the_fused_step(tmp_path, clips):
+    """A decoder with a wide MLP (4608; the 1.7B one is 6144) runs the fused decode step
+    -- 72 gate_up tiles, down_proj streaming a long K past its ring -- and agrees with
+    the reference path; graph and eager decode give the same tokens."""
+    from voiceagent_b200.checkpoint import PRESETS, write_checkpoint
+
+    tiny = PRESETS["tiny"]
+    wide = {"audio": {**tiny["audio"], "output_dim": 512},
+            "text": {**tiny["text"], "hidden_size": 512, "intermediate_size": 4608}}
+    engine = _engine(str(write_checkpoint(tmp_path / "wide", wide, weights=False)))
+    assert engine.model.model.fused_step_ok(4)
+    outs = _run(engine, clips[:4])
+    _assert_agrees(_agreement_with_reference(engine, clips[:4], outs), "wide MLP, fused step")
+    eager = _run(_engine(str(tmp_path / "wide"), enforce_eager=True), clips[:4])
+    assert [o.output_token_ids for o in outs] == [o.output_token_ids for o in eager]
+
+
 def test_config0_full_size_against_reference_and_oracle(tmp_path):
     """Config 0 workload on the 0.6B architecture (random init, seed 0)."""
     from oracle import model as M

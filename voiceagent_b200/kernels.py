@@ -463,8 +463,13 @@ class NormState:
 def fused_decode_ok(m: int, hidden: int, intermediate: int, num_heads: int, num_kv_heads: int,
                     head_dim: int) -> bool:
     """Whether the fused decode-step projections take a batch of ``m`` rows."""
+    # The RMSNorm prologue needs a CTA's whole K slice (the hidden size / the split) in its
+    # 4-stage ring. Up to hidden 1024 a 4-way split does that; at 2048 (1.7B) it takes an
+    # 8-way split -- 768 gate_up CTAs, 2.6 waves -- and the fused 1.7B step measured
+    # 3487 us against 2286 us for the unfused kernels at 64 rows, so wider models take the
+    # unfused path. The MLP width only sets gate_up's tile count and down_proj's K.
     return (1 <= m <= LINEAR_SMALL_MAX_ROWS and head_dim == 128 and hidden % 512 == 0
-            and hidden <= 4096 and intermediate % 64 == 0 and intermediate <= 4096
+            and hidden <= 1024 and intermediate % 64 == 0 and intermediate <= 16384
             and (num_heads * head_dim) % 64 == 0 and num_heads % num_kv_heads == 0)
 
 

@@ -519,25 +519,27 @@ class _DecodeRow:
 
 
 def decode_graph_step(fused: bool, iters: int = 64, l2_prefetch: bool = False,
-                      profile_one: bool = False) -> dict:
-    """One whole decode step of Qwen3-ASR-0.6B (random init) as the engine replays it:
-    the bucket-32 CUDA graph (28 layers of projections, norms, RoPE + KV store, paged
-    attention, lm_head, argmax, descriptor advance) over 32 rows of contexts U[80, 250],
-    with the decoder's projections fused (five launches per layer) or not (eight)."""
+                      profile_one: bool = False, preset: str = "0.6b", rows_n: int = 32) -> dict:
+    """One whole decode step of Qwen3-ASR (random init) as the engine replays it: the
+    bucket CUDA graph (28 layers of projections, norms, RoPE + KV store, paged attention,
+    lm_head, argmax, descriptor advance) over `rows_n` rows of contexts U[80, 250], with
+    the decoder's projections fused (five launches per layer) or not (eight). Defaults:
+    the 0.6B model at 32 rows (benchmark configuration 3); preset "1.7b" with 64 rows is
+    configuration 4's step."""
     import tempfile
 
     from voiceagent_b200.checkpoint import write_checkpoint
     from voiceagent_b200.engine.engine import AsrEngine
 
-    path = write_checkpoint(Path(tempfile.mkdtemp()) / "c06", "0.6b", weights=False)
-    eng = AsrEngine(str(path), weights="random", seed=0, max_num_seqs=32, max_model_len=1024,
-                    num_kvcache_blocks=96, fused_decode=fused, l2_prefetch=l2_prefetch)
+    path = write_checkpoint(Path(tempfile.mkdtemp()) / "ckpt", preset, weights=False)
+    eng = AsrEngine(str(path), weights="random", seed=0, max_num_seqs=rows_n, max_model_len=1024,
+                    num_kvcache_blocks=3 * rows_n, fused_decode=fused, l2_prefetch=l2_prefetch)
     gr = eng.model_runner.graph_runner
     rng = np.random.default_rng(3)
-    lens = rng.integers(80, 251, size=32)
+    lens = rng.integers(80, 251, size=rows_n)
     rows = [_DecodeRow(int(n), [3 * i, 3 * i + 1, 3 * i + 2]) for i, n in enumerate(lens)]
     gr.run(rows, 1)  # uploads the descriptor; each replay then advances it on the device
-    graph = gr.graphs[(32, True)]
+    graph = gr.graphs[(rows_n, True)]
     for _ in range(3):
         graph.replay()
     torch.cuda.synchronize()
@@ -558,17 +560,18 @@ def decode_graph_step(fused: bool, iters: int = 64, l2_prefetch: bool = False,
     per_layer = (t.hidden_size * (t.num_attention_heads + 2 * t.num_key_value_heads) * hd
                  + t.num_attention_heads * hd * t.hidden_size + 3 * t.hidden_size * t.intermediate_size) * 2
     weights = t.num_hidden_layers * per_layer + t.vocab_size * t.hidden_size * 2
-    ctx = int(lens.sum()) + 32 * (3 + iters // 2)  # mean context over the timed replays
+    ctx = int(lens.sum()) + rows_n * (3 + iters // 2)  # mean context over the timed replays
     kv = ctx * t.num_hidden_layers * t.num_key_value_heads * hd * 2 * 2
-    launches = gr.kernels_per_replay[(32, True)]
+    launches = gr.kernels_per_replay[(rows_n, True)]
     del eng, gr, graph
     torch.cuda.empty_cache()
     what = ("fused projections" + (", next-layer L2 prefetch" if l2_prefetch else "")) if fused \
         else "unfused projections"
-    return _line("decode_step_graph", f"0.6B decode step, 32 rows ctx~U[80,250], {what}",
+    return _line("decode_step_graph",
+                 f"{preset.upper()} decode step, {rows_n} rows ctx~U[80,250], {what}",
                  us, weights + kv,
                  bound="hbm (weights + KV, latency-bound)", launches_per_step=launches,
-                 timing=f"{iters} replays of the bucket-32 graph back to back")
+                 timing=f"{iters} replays of the bucket-{rows_n} graph back to back")
 
 
 BENCHES = {
@@ -580,6 +583,7 @@ BENCHES = {
                        label="config3 decode-step shape B=32 ctx~U[80,250], stream-K kernel")],
     "step": lambda: [decode_graph_step(True), decode_graph_step(True, l2_prefetch=True),
                      decode_graph_step(False)],
+    "step_1p7b": lambda: [decode_graph_step(True, preset="1.7b", rows_n=64)],
     # one fused decode step bracketed for a profiler: its launch list is the step's kernels
     "step_profile": lambda: [decode_graph_step(True, iters=8, profile_one=True)],
     "prefill": lambda: [prefill_config2()],
