@@ -50,13 +50,18 @@ constexpr int kLnStages = 4;
 constexpr int kLnThreads = 128;
 constexpr int kLnMaxSplit = 16;
 
-template <int MP>
+// Ring depth: 4 stages, except for 64 rows fed by TMA, where 3 stages (~106 KB) let two
+// CTAs share an SM (4 stages, ~130 KB, fit only one). The RMSNorm prologue keeps 4: it
+// needs a CTA's whole K slice in the ring.
+template <int MP, bool NORM_IN = false>
 struct Ln {
+  static constexpr int STAGES = (MP == 64 && !NORM_IN) ? 3 : kLnStages;
   static constexpr int W_BYTES = kLnRows * kLnBK * 2;  // 16 KiB
   static constexpr int X_BYTES = MP * kLnBK * 2;       // 4 or 8 KiB
   static constexpr int STAGE = W_BYTES + X_BYTES;
   static constexpr int RED_BYTES = MP * kLnRows * 4;   // [MP][128] fp32 partial
-  static constexpr size_t SMEM = 1024 + static_cast<size_t>(kLnStages) * STAGE + RED_BYTES + 256;
+  static constexpr size_t SMEM = 1024 + static_cast<size_t>(STAGES) * STAGE + RED_BYTES + 256;
+  static_assert(STAGES * STAGE >= MP * kLnRows * 4, "the ring holds the column-major partial");
   static constexpr uint32_t TMEM_COLS = MP;            // 32 or 64 (power of two >= 32)
   static_assert(MP == 32 || MP == 64, "MMA N");
 };
@@ -217,7 +222,7 @@ template <int MP>
 __device__ __forceinline__ void norm_in_fill(uint8_t *stages, const LinearArgs &a,
                                              const LinearFuse &f, int k0,
                                              const uint4 (&wv)[kLnStages][2]) {
-  using C = Ln<MP>;
+  using C = Ln<MP, true>;  // the RMSNorm prologue
   const int tid = threadIdx.x;
 #pragma unroll
   for (int rr = 0; rr < MP / 32; ++rr) {
@@ -381,15 +386,15 @@ __global__ void __launch_bounds__(kLnThreads)
     linear_small_kernel(const __grid_constant__ CUtensorMap tm_w,
                         const __grid_constant__ CUtensorMap tm_x, const LinearArgs a,
                         const __grid_constant__ LinearFuse f) {
-  using C = Ln<MP>;
+  using C = Ln<MP, NORM_IN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                               ~uintptr_t(1023));
   uint8_t *stages = smem;
-  float *red = reinterpret_cast<float *>(smem + kLnStages * C::STAGE);
-  uint64_t *full = reinterpret_cast<uint64_t *>(smem + kLnStages * C::STAGE + C::RED_BYTES);
-  uint64_t *empty = full + kLnStages;
-  uint64_t *done = empty + kLnStages;
+  float *red = reinterpret_cast<float *>(smem + C::STAGES * C::STAGE);
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + C::STAGES * C::STAGE + C::RED_BYTES);
+  uint64_t *empty = full + C::STAGES;
+  uint64_t *done = empty + C::STAGES;
   uint64_t *recv_bar = done + 1;  // completes when every peer's columns have arrived
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(recv_bar + 1);
   __shared__ int abort_flag;
@@ -413,7 +418,7 @@ __global__ void __launch_bounds__(kLnThreads)
 
   if (tid == 0) {
     abort_flag = 0;
-    for (int s = 0; s < kLnStages; ++s) {
+    for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
@@ -442,7 +447,7 @@ __global__ void __launch_bounds__(kLnThreads)
     // The weights are static: the first ring's worth is requested before waiting for
     // the kernel that produces x (programmatic dependent launch). With the RMSNorm
     // prologue the whole K slice fits the ring (the host guarantees steps <= stages).
-    const int first = a.steps < kLnStages ? a.steps : kLnStages;
+    const int first = a.steps < C::STAGES ? a.steps : C::STAGES;
     for (int s = 0; s < first; ++s) {
       uint8_t *w = stages + s * C::STAGE;
       const int kc = k0 + s * kLnBK;
@@ -465,7 +470,7 @@ __global__ void __launch_bounds__(kLnThreads)
     for (int i = 0; i < 2; ++i)
       if (f.pf_range[i] != nullptr) prefetch_range_share(f.pf_range[i], f.pf_range_bytes[i], lane);
   if (NORM_IN) {
-    uint4 wv[kLnStages][2];
+    uint4 wv[kLnStages][2];  // NORM_IN: C::STAGES == kLnStages
     norm_in_weights(wv, a, f, k0);
     pdl_wait();  // h and the tile sums come from the previous kernel
     __syncwarp();
@@ -473,13 +478,13 @@ __global__ void __launch_bounds__(kLnThreads)
     fence_proxy_async_smem();  // generic-proxy stores -> visible to the tensor core
     __syncthreads();
   } else if (warp == 0 && lane == 0) {
-    const int first = a.steps < kLnStages ? a.steps : kLnStages;
+    const int first = a.steps < C::STAGES ? a.steps : C::STAGES;
     pdl_wait();
     for (int s = 0; s < first; ++s)
       tma_load_2d(stages + s * C::STAGE + C::W_BYTES, &tm_x, k0 + s * kLnBK, 0, &full[s]);
     for (int s = first; s < a.steps; ++s) {
-      const int st = s % kLnStages;
-      if (!mbar_wait(&empty[st], ((s / kLnStages) - 1) & 1, a.error_flag, &abort_flag)) break;
+      const int st = s % C::STAGES;
+      if (!mbar_wait(&empty[st], ((s / C::STAGES) - 1) & 1, a.error_flag, &abort_flag)) break;
       uint8_t *w = stages + st * C::STAGE;
       const int kc = k0 + s * kLnBK;
       mbar_arrive_expect_tx(&full[st], C::STAGE);
@@ -492,8 +497,8 @@ __global__ void __launch_bounds__(kLnThreads)
     constexpr uint32_t idesc = idesc_bf16_f32(kLnRows, MP, false, false);
     bool ok = true;
     for (int s = 0; s < a.steps && ok; ++s) {
-      const int st = s % kLnStages;
-      ok = mbar_wait(&full[st], (s / kLnStages) & 1, a.error_flag, &abort_flag);
+      const int st = s % C::STAGES;
+      ok = mbar_wait(&full[st], (s / C::STAGES) & 1, a.error_flag, &abort_flag);
       if (!ok) break;
       tc_fence_after();
       const uint32_t wb = smem_addr(stages + st * C::STAGE), xb = wb + C::W_BYTES;
@@ -714,7 +719,7 @@ template <int MP, bool NORM_IN, int EPI>
 int launch_linear(const void *x, int64_t x_stride, int m, int k, const void *w, int n,
                   const LinearArgs &proto, const LinearFuse &fuse, int tiles,
                   cudaStream_t stream) {
-  using C = Ln<MP>;
+  using C = Ln<MP, NORM_IN>;
   auto kfn = linear_small_kernel<MP, NORM_IN, EPI>;
   static bool configured = false;
   if (!configured) {
