@@ -584,6 +584,8 @@ BENCHES = {
     "step": lambda: [decode_graph_step(True), decode_graph_step(True, l2_prefetch=True),
                      decode_graph_step(False)],
     "step_1p7b": lambda: [decode_graph_step(True, preset="1.7b", rows_n=64)],
+    "step_1p7b_profile": lambda: [decode_graph_step(True, iters=8, profile_one=True, preset="1.7b",
+                                                    rows_n=64)],
     # one fused decode step bracketed for a profiler: its launch list is the step's kernels
     "step_profile": lambda: [decode_graph_step(True, iters=8, profile_one=True)],
     "prefill": lambda: [prefill_config2()],
