@@ -83,12 +83,13 @@ def _sets(per_set_bytes: int) -> int:
 
 def decode_config1(iters: int = 64, sets: int = 4, lo: int = 64, hi: int = 1024,
                    label: str = "config1 B=32 ctx~U[64,1024] Hq16/Hkv8 d128",
-                   max_seqlen_k: int = 4096, pdl: bool = False) -> dict:
+                   max_seqlen_k: int = 4096, pdl: bool = False, batch: int = 32) -> dict:
     """Paged decode, config 1: B = 32, ctx ~ U[lo, hi] (64-1024), 4096-block pool (2 GiB per
-    K/V), block tables = slices of a random permutation; ``sets`` disjoint table sets rotate."""
+    K/V), block tables = slices of a random permutation; ``sets`` disjoint table sets rotate.
+    ``batch`` = 64 gives the decode-step shape of configuration 4."""
     dev = torch.device("cuda")
     rng = np.random.default_rng(0)
-    b, h, hkv, d, nb = 32, 16, 8, 128, 4096
+    b, h, hkv, d, nb = batch, 16, 8, 128, 4096
     lens = rng.integers(lo, hi + 1, size=b)
     need = int(sum((lens + 255) // 256))
     gen = torch.Generator(device=dev).manual_seed(0)
@@ -584,6 +585,11 @@ BENCHES = {
     "step": lambda: [decode_graph_step(True), decode_graph_step(True, l2_prefetch=True),
                      decode_graph_step(False)],
     "step_1p7b": lambda: [decode_graph_step(True, preset="1.7b", rows_n=64)],
+    "decode_step_64": lambda: [
+        decode_config1(lo=80, hi=250, sets=8, max_seqlen_k=512, batch=64,
+                       label="config4 decode-step shape B=64 ctx~U[80,250], short-context kernel"),
+        decode_config1(lo=80, hi=250, sets=8, max_seqlen_k=4096, batch=64,
+                       label="config4 decode-step shape B=64 ctx~U[80,250], stream-K kernel")],
     "step_1p7b_profile": lambda: [decode_graph_step(True, iters=8, profile_one=True, preset="1.7b",
                                                     rows_n=64)],
     # one fused decode step bracketed for a profiler: its launch list is the step's kernels
