@@ -387,6 +387,17 @@ B200ASR_API int b200asr_linear_small_norm_qk_rope(
     void *q_out, int64_t q_out_row_stride, void *k_cache, void *v_cache,
     const int32_t *slot_mapping, int64_t num_slots, const b200asr_l2_prefetch *prefetch,
     int32_t *error_flag, b200asr_stream_t stream);
+/* linear_small_qk_rope: the same qkv_proj + q/k norm + RoPE + KV store on an already
+ * normalised bf16 x [m, k] (row stride in elements) -- the unfused decode step's qkv_proj
+ * (models/qwen3.py:43-48 after the layer's input norm) for models whose hidden size is
+ * too large for the RMSNorm prologue; any k that is a multiple of 64.                 */
+B200ASR_API int b200asr_linear_small_qk_rope(
+    const void *x, int64_t x_row_stride, int32_t m, int32_t k, const void *w, int32_t num_heads,
+    int32_t num_kv_heads, int32_t head_dim, const void *q_norm_weight, const void *k_norm_weight,
+    float qk_eps, const int64_t *positions, const float *cos_sin_cache, int32_t max_position,
+    void *q_out, int64_t q_out_row_stride, void *k_cache, void *v_cache,
+    const int32_t *slot_mapping, int64_t num_slots, int32_t *error_flag,
+    b200asr_stream_t stream);
 B200ASR_API int b200asr_rms_stats(const void *x, void *residual, int32_t rows, int32_t hidden,
                       float *h_out, float *ss_out, b200asr_stream_t stream);
 B200ASR_API int b200asr_norm_apply(const float *h, const float *ss, const void *weight, float eps,

@@ -856,6 +856,45 @@ def test_linear_small_norm_matches_unfused(kx, m, silu, hidden, inner):
         assert err <= 2e-2 * unfused.float().abs().max().item() and same >= 0.97, (err, same)
 
 
+@pytest.mark.parametrize("m", [1, 33, 64])
+@pytest.mark.parametrize("hidden", [1024, 2048])  # 0.6B, 1.7B
+def test_linear_small_qk_rope_matches_unfused(kx, m, hidden):
+    """qkv_proj on a normalised x + q/k norm + RoPE + KV store in one kernel: q, K and V
+    bit-exact against linear_small followed by qk_norm_rope_store (same K split, same
+    per-head arithmetic); slot -1 rows leave the cache untouched."""
+    from voiceagent_b200.layers.norm import rope_table
+
+    g = torch.Generator(device="cuda").manual_seed(11 + m + hidden)
+    hq, hkv, d = 16, 8, 128
+    base = torch.randn(m, hidden + 64, device="cuda", generator=g).bfloat16()
+    x = base[:, :hidden]  # a strided view
+    w = (torch.randn((hq + 2 * hkv) * d, hidden, device="cuda", generator=g) * 0.03).bfloat16()
+    qw = (1 + 0.1 * torch.randn(d, device="cuda", generator=g)).bfloat16()
+    kw = (1 + 0.1 * torch.randn(d, device="cuda", generator=g)).bfloat16()
+    positions = torch.randint(0, 4096, (m,), device="cuda", generator=g)
+    nslots = 4 * 256
+    slots = torch.randperm(nslots, device="cuda", generator=g)[:m].int()
+    slots[::5] = -1
+    table = rope_table(d, 4096, 1e6, "cuda")
+    outs = []
+    for fused in (True, False):
+        kc = torch.full((4, 256, hkv, d), 7.0, device="cuda").bfloat16()
+        vc = kc.clone()
+        q = torch.empty(m, hq, d, device="cuda", dtype=torch.bfloat16)
+        heads = dict(num_heads=hq, num_kv_heads=hkv, head_dim=d, q_weight=qw, k_weight=kw,
+                     cos_sin_cache=table, q_out=q, k_cache=kc, v_cache=vc, slot_mapping=slots)
+        if fused:
+            kx.linear_small_qk_rope(x, w, positions, qk_eps=1e-6, **heads)
+        else:
+            kx.qk_norm_rope_store(kx.linear_small(x, w), positions, eps=1e-6, **heads)
+        outs.append((q, kc, vc))
+    for a, b in zip(*outs):
+        assert torch.equal(a, b)
+    untouched = torch.ones(nslots, dtype=torch.bool, device="cuda")
+    untouched[slots[slots >= 0].long()] = False
+    assert bool((outs[0][1].view(nslots, -1)[untouched] == 7.0).all())
+
+
 @pytest.mark.parametrize("m", [1, 32, 64])
 @pytest.mark.parametrize("hidden", [1024, 2048])  # 0.6B, 1.7B
 def test_linear_small_norm_qk_rope_matches_unfused(kx, m, hidden):

@@ -52,6 +52,9 @@ SIGNATURES: dict[str, tuple] = {
                                                     c_int32, P, c_int32, c_int32, c_int32, P, P,
                                                     c_float, P, P, c_int32, P, c_int64, P, P, P,
                                                     c_int64, P, P, P]),
+    "b200asr_linear_small_qk_rope": (c_int32, [P, c_int64, c_int32, c_int32, P, c_int32, c_int32,
+                                               c_int32, P, P, c_float, P, P, c_int32, P, c_int64,
+                                               P, P, P, c_int64, P, P]),
     "b200asr_rms_stats": (c_int32, [P, P, c_int32, c_int32, P, P, P]),
     "b200asr_norm_apply": (c_int32, [P, P, P, c_float, c_int32, c_int32, P, P]),
     "b200asr_log_mel_workspace_size": (c_size_t, [c_int32, c_int32]),

@@ -1019,6 +1019,49 @@ extern "C" int b200asr_linear_small_norm_qk_rope(
                                            static_cast<cudaStream_t>(stream));
 }
 
+extern "C" int b200asr_linear_small_qk_rope(
+    const void *x, int64_t x_row_stride, int32_t m, int32_t k, const void *w, int32_t num_heads,
+    int32_t num_kv_heads, int32_t head_dim, const void *q_norm_weight, const void *k_norm_weight,
+    float qk_eps, const int64_t *positions, const float *cos_sin_cache, int32_t max_position,
+    void *q_out, int64_t q_out_row_stride, void *k_cache, void *v_cache,
+    const int32_t *slot_mapping, int64_t num_slots, int32_t *error_flag,
+    b200asr_stream_t stream) {
+  B200_REQUIRE(m >= 0 && m <= 64, "linear_small_qk_rope: %d rows (at most 64)", m);
+  if (m == 0) return B200ASR_OK;
+  B200_REQUIRE(head_dim == kLnRows, "linear_small_qk_rope: head_dim %d (needs %d)", head_dim,
+               kLnRows);
+  B200_REQUIRE(num_heads > 0 && num_kv_heads > 0 && num_heads % num_kv_heads == 0,
+               "linear_small_qk_rope: bad head counts %d / %d", num_heads, num_kv_heads);
+  B200_REQUIRE(k > 0 && k % kLnBK == 0, "linear_small_qk_rope: K %d must be a multiple of %d", k,
+               kLnBK);
+  B200_REQUIRE(x && aligned16(x) && x_row_stride >= k && x_row_stride % 8 == 0 && w &&
+                   aligned16(w) && q_norm_weight && k_norm_weight && positions && cos_sin_cache &&
+                   q_out && aligned16(q_out) && q_out_row_stride >= num_heads * head_dim &&
+                   q_out_row_stride % 4 == 0 && k_cache && v_cache && aligned16(k_cache) &&
+                   aligned16(v_cache) && max_position > 0,
+               "linear_small_qk_rope: null or misaligned tensor");
+  LinearFuse f = {};
+  const int n = (num_heads + 2 * num_kv_heads) * head_dim;
+  const int tiles = n / kLnRows;
+  f.num_heads = num_heads;
+  f.num_kv_heads = num_kv_heads;
+  f.q_w = static_cast<const __nv_bfloat16 *>(q_norm_weight);
+  f.k_w = static_cast<const __nv_bfloat16 *>(k_norm_weight);
+  f.qk_eps = qk_eps;
+  f.positions = positions;
+  f.cos_sin = cos_sin_cache;
+  f.max_position = max_position;
+  f.q_out = static_cast<__nv_bfloat16 *>(q_out);
+  f.q_out_stride = q_out_row_stride;
+  f.k_cache = static_cast<__nv_bfloat16 *>(k_cache);
+  f.v_cache = static_cast<__nv_bfloat16 *>(v_cache);
+  f.slot_mapping = slot_mapping;
+  f.num_slots = num_slots;
+  const LinearArgs a = make_args(m, linear_split(tiles, k / kLnBK), 0, nullptr, 0, error_flag);
+  return dispatch_linear<false, kEpiQkRope>(x, x_row_stride, m, k, w, n, a, f, tiles,
+                                            static_cast<cudaStream_t>(stream));
+}
+
 extern "C" int b200asr_rms_stats(const void *x, void *residual, int32_t rows, int32_t hidden,
                                  float *h_out, float *ss_out, b200asr_stream_t stream) {
   B200_REQUIRE(rows >= 0 && rows <= 64, "rms_stats: %d rows (at most 64)", rows);

@@ -556,6 +556,30 @@ def linear_small_norm_qk_rope(state: NormState, norm_weight, eps: float, weight,
     return q_out
 
 
+def linear_small_qk_rope(x, weight, positions, *, num_heads: int, num_kv_heads: int,
+                         head_dim: int, q_weight, k_weight, qk_eps: float, cos_sin_cache, q_out,
+                         k_cache, v_cache, slot_mapping, error_flag=None) -> torch.Tensor:
+    """qkv_proj of an already normalised x, then q/k RMSNorm + RoPE and the K/V cache
+    store per head: :func:`linear_small` followed by :func:`qk_norm_rope_store` in one
+    kernel."""
+    _cuda(x, weight, positions, q_weight, k_weight, cos_sin_cache, q_out, k_cache, v_cache,
+          slot_mapping)
+    _need(x.dtype == BF16 and x.dim() == 2 and x.stride(1) == 1, "x bf16 [m, k], unit column stride")
+    _need(positions.dtype == torch.int64 and slot_mapping.dtype == torch.int32,
+          "positions int64, slot_mapping int32")
+    _need(cos_sin_cache.dtype == torch.float32 and cos_sin_cache.is_contiguous(), "fp32 rope table")
+    _need(weight.dtype == BF16 and weight.is_contiguous() and weight.shape[1] == x.shape[1],
+          "qkv weight [n, k] bf16")
+    num_slots = k_cache.numel() // (num_kv_heads * head_dim)
+    _count()
+    check(lib.b200asr_linear_small_qk_rope(
+        _p(x), x.stride(0), x.shape[0], x.shape[1], _p(weight), num_heads, num_kv_heads, head_dim,
+        _p(q_weight), _p(k_weight), float(qk_eps), _p(positions), _p(cos_sin_cache),
+        cos_sin_cache.shape[0], _p(q_out), q_out.stride(0), _p(k_cache), _p(v_cache),
+        _p(slot_mapping), num_slots, _p(error_flag), _stream()), "linear_small_qk_rope")
+    return q_out
+
+
 # ----------------------------------------------------------------- encoder front
 
 

@@ -48,15 +48,23 @@ class Qwen3Attention(nn.Module):
 
     def forward(self, positions: torch.Tensor, hidden_states: torch.Tensor) -> torch.Tensor:
         ctx = get_attention_context()
-        qkv = project(hidden_states, self.qkv_proj)
-        t = qkv.shape[0]
-        q = torch.empty(t, self.num_heads, self.head_dim, dtype=qkv.dtype, device=qkv.device)
-        # q/k RMSNorm + RoPE; K and V go straight into the paged cache.
-        kx.qk_norm_rope_store(
-            qkv, positions, num_heads=self.num_heads, num_kv_heads=self.num_kv_heads,
-            head_dim=self.head_dim, q_weight=self.q_norm.weight, k_weight=self.k_norm.weight,
-            eps=self.eps, cos_sin_cache=self.rope.table, q_out=q, k_cache=self.attn.k_cache,
-            v_cache=self.attn.v_cache, slot_mapping=ctx.slot_mapping, error_flag=ctx.error_flag)
+        t = hidden_states.shape[0]
+        q = torch.empty(t, self.num_heads, self.head_dim, dtype=hidden_states.dtype,
+                        device=hidden_states.device)
+        # q/k RMSNorm + RoPE; K and V go straight into the paged cache. Decode-size batches
+        # do it in the projection's epilogue (one kernel), larger ones after cuBLAS.
+        heads = dict(num_heads=self.num_heads, num_kv_heads=self.num_kv_heads,
+                     head_dim=self.head_dim, q_weight=self.q_norm.weight,
+                     k_weight=self.k_norm.weight, cos_sin_cache=self.rope.table, q_out=q,
+                     k_cache=self.attn.k_cache, v_cache=self.attn.v_cache,
+                     slot_mapping=ctx.slot_mapping, error_flag=ctx.error_flag)
+        if (self.qkv_proj.bias is None and self.head_dim == 128
+                and kx.linear_small_ok(hidden_states, self.qkv_proj.weight)):
+            kx.linear_small_qk_rope(hidden_states, self.qkv_proj.weight, positions,
+                                    qk_eps=self.eps, **heads)
+        else:
+            qkv = project(hidden_states, self.qkv_proj)
+            kx.qk_norm_rope_store(qkv, positions, eps=self.eps, **heads)
         attn_out = self.attn(q)
         return project(attn_out.view(t, self.q_size), self.o_proj)
 
