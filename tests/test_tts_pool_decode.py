@@ -413,3 +413,51 @@ def test_matches_reference_triton_kernel_live():
     torch.cuda.synchronize()
     assert torch.equal(k1, k2) and torch.equal(v1, v2)
     _assert_close(mine.float().cpu().numpy(), theirs.float().cpu().numpy(), "vs reference Triton")
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("hq,hkv", [(16, 8), (8, 8), (16, 4), (4, 2)])
+def test_stream_k_path_matches_chunked_kernel(hq, hkv):
+    """The talker's case (bf16, head_dim 128, 16-position pages, heads contiguous) runs on
+    the stream-K decode kernel; tokens_per_cta != 0 keeps the chunked CUDA-core kernel.
+    Both against the oracle and each other on the awkward rows: one fully masked, one whose
+    current token lies past max_seq_len (stored, not attended), one page outside the pool,
+    long rows split over several CTAs -- with the same pool writes and error bits."""
+    from voiceagent_b200 import kernels as kx
+
+    rng = np.random.default_rng(hq * 31 + hkv)
+    lens = [3, 500, 1900, 64, 16, 1301]
+    c = _random_case(rng, batch=len(lens), hq=hq, hkv=hkv, d=128, ps=16, lens=lens,
+                     dtype=torch.bfloat16)
+    max_len = 1500  # row 2 (1900) is cut off: its current token is stored, not attended
+    valid = rng.random((len(lens), 1400)) > 0.1
+    valid[0, :] = False  # row 0: nothing attended -> zeros
+    table = c["table"].copy()
+    table[5, 3] = 10**6  # a page outside the pool: skipped, BLOCK raised
+    outs, pools, flags = [], [], []
+    for tpc in (0, 64):
+        t = {k: torch.from_numpy(c[k]).bfloat16().cuda() for k in ("q", "kp", "vp", "nk", "nv")}
+        qs = t["q"].transpose(1, 2).contiguous().transpose(1, 2)
+        out = torch.empty_like(qs)
+        flag = torch.zeros(1, dtype=torch.int32, device="cuda")
+        kx.pool_paged_decode(qs, t["kp"], t["vp"], _dev(table), _dev(c["lens"]),
+                             max_seq_len=max_len, scale=128 ** -0.5, out=out,
+                             key_valid_mask=_dev(valid), new_key=t["nk"], new_value=t["nv"],
+                             tokens_per_cta=tpc, error_flag=flag)
+        outs.append(out.float().cpu().numpy())
+        pools.append((t["kp"].float().cpu().numpy(), t["vp"].float().cpu().numpy()))
+        flags.append(int(flag.item()))
+    kw, vw = c["kp"].copy(), c["vp"].copy()
+    attend = np.ones((len(lens), max(lens)), bool)
+    attend[:, :1400] = valid
+    p_bad = 3 * 16
+    attend[5, p_bad:p_bad + 16] = False
+    want = K.pool_paged_attention(c["q"], kw, vw, table, c["lens"], 128 ** -0.5,
+                                  key_valid_mask=attend, new_key=c["nk"], new_value=c["nv"],
+                                  kernel_seq_len=max_len)
+    for got, what in zip(outs, ("stream-K", "chunked")):
+        assert not np.abs(got[0]).any(), what
+        _assert_close(got, want, what)
+    np.testing.assert_array_equal(pools[0][0], pools[1][0])
+    np.testing.assert_array_equal(pools[0][1], pools[1][1])
+    assert flags[0] == flags[1] == (2 | 8)  # BLOCK (the bad page) | LENGTH (row 2)

@@ -372,6 +372,36 @@ bool make_tmap_bf16(CUtensorMap *map, const void *base, int rank, const uint64_t
                     const uint64_t *strides_bytes, const uint32_t *box);
 EncodeTiledFn encode_tiled_fn();  // defined in capi.cu
 
+// The TTS pool decode's bf16 / head_dim 128 / 16-token-page case on the stream-K decode
+// kernel (paged_decode.cu). *taken is false (and nothing is launched) when the call does
+// not fit it; b200asr_pool_paged_decode then runs its own kernel.
+struct PoolStreamK {
+  int batch, num_heads, num_kv_heads, head_dim;
+  const void *query;
+  int64_t q_stride_b, q_stride_h;
+  void *key_pool, *value_pool;
+  int num_pages, page_size;
+  int64_t kv_stride_p, kv_stride_h, kv_stride_s;
+  const int64_t *page_table;
+  int64_t table_stride;
+  int table_width;
+  const int64_t *seq_lens;
+  const uint8_t *valid;
+  int64_t valid_stride;
+  int valid_len;
+  const void *new_key, *new_value;
+  int64_t new_stride_b, new_stride_h;
+  void *out;
+  int64_t out_stride_b, out_stride_h;
+  int max_seq_len;
+  float scale;
+  void *workspace;
+  size_t workspace_bytes, workspace_head;  // head: bytes of counters the pool kernel keeps
+  int32_t *error_flag;
+  void *stream;
+};
+int pool_decode_stream_k(const PoolStreamK &p, bool *taken);
+
 // 3-D bf16 tensor map: dims {d0 (contiguous), d1, d2}, strides in bytes for d1, d2,
 // box {b0, b1, b2}, 128-byte swizzle. Returns false (error set) on failure.
 bool make_tmap_3d_bf16(CUtensorMap *map, const void *base, uint64_t d0, uint64_t d1,

@@ -79,14 +79,34 @@ struct DecodeArgs {
   int parts_cap;
   int32_t *error_flag;
   int early;  // launched with programmatic dependent launch: request stages before the wait
+  // Page-pool layout (the TTS talker's [pages, kv_heads, 16, 128] pool; POOL kernels only):
+  // lengths, page table and key-valid mask as b200asr_pool_paged_decode takes them, and
+  // the current token's K/V, stored at position seq_len - 1 before its stage is loaded.
+  const int64_t *seq_lens;
+  int max_seq_len;
+  const int64_t *page_table;
+  int64_t table_stride;
+  int table_width;
+  const uint8_t *valid;
+  int64_t valid_stride;
+  int valid_len;
+  const __nv_bfloat16 *nk, *nv;
+  int64_t n_sb, n_sh;
+  __nv_bfloat16 *kp, *vp;
+  int64_t sp, sh, ss;  // pool element strides: page, head, position
 };
 
 // What the producer tells the consumers about a stage (written before the stage's
 // mbarrier arrive, read after the matching wait).
 struct StageInfo {
   int b;      // sequence, or -1 for the terminal stage
-  int ntok;   // valid tokens (1..16)
+  int ntok;   // tokens of the sequence in the stage (1..16)
   int flags;  // 1: first stage of a segment (q attached), 2: last stage, 4: whole sequence
+  int vbits;  // POOL: bit t set when token t is attended (in range, page valid, mask set)
+  // POOL, the row's last stage with a current token: the stage row that holds it (-1:
+  // none, or not attended) and its element offset in the pools (-1: page unusable)
+  int new_row;
+  int64_t new_off;
 };
 
 __device__ __forceinline__ void consumer_sync(int threads) {
@@ -193,6 +213,18 @@ __device__ __forceinline__ void tma_load_4d(void *dst, const CUtensorMap *map, i
       : "memory");
 }
 
+// 5-D tiled tensor load (no multicast) into shared memory.
+__device__ __forceinline__ void tma_load_5d(void *dst, const CUtensorMap *map, int32_t c0,
+                                            int32_t c1, int32_t c2, int32_t c3, int32_t c4,
+                                            uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4),
+      "r"(smem_addr(bar))
+      : "memory");
+}
+
 // The same box, into L2 only (no shared memory, no barrier).
 __device__ __forceinline__ void tma_prefetch_4d(const CUtensorMap *map, int32_t c0, int32_t c1,
                                                 int32_t c2, int32_t c3) {
@@ -209,7 +241,7 @@ __device__ __forceinline__ void tma_prefetch_4d(const CUtensorMap *map, int32_t 
 // cp.async.cg (L2, never a stale L1 line: other SMs wrote them), so a chunk costs one L2
 // round trip. Lane l owns dims 4l..4l+3 of every head; the online rescale carries
 // across chunks, so any number of partials merges.
-template <class C>
+template <class C, bool POOL>
 __device__ __forceinline__ void merge_staged(const DecodeArgs &a, uint8_t *buf, int first,
                                              int n_parts, int b, int w, int lane, int tid) {
   constexpr int H = C::H;
@@ -242,7 +274,9 @@ __device__ __forceinline__ void merge_staged(const DecodeArgs &a, uint8_t *buf, 
       float cm = -INFINITY;
       for (int i = lane; i < n; i += 32) cm = fmaxf(cm, sml[i * H + hh].x);
       const float mn = fmaxf(m[g], warp_max(cm));
-      const float sc = exp2f(m[g] - mn);
+      // POOL: a partial with every key masked has m = -inf (and l = 0, O = 0)
+      const float mu = POOL && mn == -INFINITY ? 0.f : mn;
+      const float sc = exp2f(m[g] - mu);
       l[g] *= sc;
       acc[g][0] *= sc;
       acc[g][1] *= sc;
@@ -250,7 +284,7 @@ __device__ __forceinline__ void merge_staged(const DecodeArgs &a, uint8_t *buf, 
       acc[g][3] *= sc;
       for (int i = 0; i < n; ++i) {
         const float2 st = sml[i * H + hh];
-        const float wgt = exp2f(st.x - mn);
+        const float wgt = exp2f(st.x - mu);
         const float4 v = so[(i * H + hh) * (kDecD / 4) + lane];
         l[g] += st.y * wgt;
         acc[g][0] += v.x * wgt;
@@ -264,14 +298,14 @@ __device__ __forceinline__ void merge_staged(const DecodeArgs &a, uint8_t *buf, 
   }
 #pragma unroll
   for (int g = 0; g < G; ++g) {
-    const float inv = 1.f / l[g];
+    const float inv = POOL && l[g] == 0.f ? 0.f : 1.f / l[g];  // no attended key: zeros
     __nv_bfloat16 *dst = a.out + b * a.out_stride + (w * G + g) * kDecD + lane * 4;
     *reinterpret_cast<uint2 *>(dst) = make_uint2(pack2(acc[g][0] * inv, acc[g][1] * inv),
                                                  pack2(acc[g][2] * inv, acc[g][3] * inv));
   }
 }
 
-template <int HKV, int G>
+template <int HKV, int G, bool POOL = false>
 __global__ void __launch_bounds__(Dec<HKV, G>::THREADS, 1)
     paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
                         const __grid_constant__ CUtensorMap tm_v, const DecodeArgs a) {
@@ -319,9 +353,36 @@ __global__ void __launch_bounds__(Dec<HKV, G>::THREADS, 1)
   // Lengths and (when B * bt_stride entries fit) the block tables are loaded in the same
   // round trip -- every thread issues its loads before storing any -- so the first TMA
   // request waits for one global-memory latency instead of two.
-  const int n_bt = B * a.bt_stride;
-  const bool bt_cached = n_bt <= kDecBtCache;
-  for (int base = 0; base <= B || (bt_cached && base < n_bt); base += 4 * blockDim.x) {
+  const int n_bt = POOL ? 0 : B * a.bt_stride;
+  const bool bt_cached = !POOL && n_bt <= kDecBtCache;
+  if constexpr (POOL) {
+    // Row b attends positions < min(seq_lens[b], max_seq_len); s_cuk becomes the
+    // exclusive prefix of those lengths (warp 0 scans after the loads).
+    for (int i = tid; i < B; i += blockDim.x) {
+      const int64_t sq = a.seq_lens[i];
+      s_cuk[i + 1] = sq <= 0 ? 0 : static_cast<int>(sq < a.max_seq_len ? sq : a.max_seq_len);
+      if (blockIdx.x == 0 && (sq <= 0 || sq > a.max_seq_len))
+        raise_flag(a.error_flag, B200ASR_DEVERR_LENGTH);
+    }
+    __syncthreads();
+    if (warp == 0) {
+      int carry = 0;
+      for (int b0 = 0; b0 < B; b0 += 32) {
+        const int b = b0 + lane;
+        const int v = b < B ? s_cuk[b + 1] : 0;
+        int incl = v;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int y = __shfl_up_sync(0xffffffffu, incl, o);
+          if (lane >= o) incl += y;
+        }
+        if (b < B) s_cuk[b + 1] = carry + incl;
+        carry += __shfl_sync(0xffffffffu, incl, 31);
+      }
+      if (lane == 0) s_cuk[0] = 0;
+    }
+  }
+  for (int base = 0; !POOL && (base <= B || (bt_cached && base < n_bt)); base += 4 * blockDim.x) {
     int cu_v[4], bt_v[4];
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
@@ -400,7 +461,8 @@ __global__ void __launch_bounds__(Dec<HKV, G>::THREADS, 1)
         // Lane i describes stage wb + i: sequence, token count, flags and cache slot
         // (the block-table reads of 32 stages are in flight together).
         const int j = wb + lane;
-        int d_b = 0, d_n = 0, d_fl = 0, d_slot = 0, d_end = 0;
+        int d_b = 0, d_n = 0, d_fl = 0, d_slot = 0, d_end = 0, d_vb = 0, d_nrow = -1;
+        int64_t d_noff = -1;
         if (j < j1) {
           const int b = upper_index(s_sp, B + 1, j);  // s_sp[b] <= j < s_sp[b + 1]
           const int len = s_cuk[b + 1] - s_cuk[b];
@@ -409,21 +471,64 @@ __global__ void __launch_bounds__(Dec<HKV, G>::THREADS, 1)
           d_end = t0 + d_n == len;  // holds the sequence's newest token
           const bool first = t0 == 0 || j == j0, last = t0 + d_n == len || j == j1 - 1;
           const bool whole = s_sp[b] >= j0 && s_sp[b + 1] <= j1;
-          const int col = t0 / a.block_size;
-          int blk = 0;
-          if (col >= a.bt_stride) {  // context longer than its block-table row
-            raise_flag(a.error_flag, B200ASR_DEVERR_LENGTH);
-          } else {
-            const int64_t at = static_cast<int64_t>(b) * a.bt_stride + col;
-            blk = bt_cached ? s_bt[at] : a.block_tables[at];
-            if (blk < 0 || blk >= a.num_blocks) {
-              raise_flag(a.error_flag, B200ASR_DEVERR_BLOCK);
-              blk = 0;
-            }
-          }
           d_b = b;
           d_fl = (first ? 1 : 0) | (last ? 2 : 0) | (whole ? 4 : 0);
-          d_slot = blk * a.block_size + t0 % a.block_size;
+          if constexpr (POOL) {
+            // one stage = one 16-token page; an unusable page is loaded from page 0 with
+            // none of its tokens attended
+            const int col = t0 / kDecStage;
+            int64_t page = -1;
+            if (col < a.table_width) page = a.page_table[static_cast<int64_t>(b) * a.table_stride + col];
+            const bool page_ok = page >= 0 && page < a.num_blocks;
+            if (!page_ok) raise_flag(a.error_flag, B200ASR_DEVERR_BLOCK);
+            d_slot = page_ok ? static_cast<int>(page) : 0;
+            int bits = 0;
+            if (page_ok) {
+              const uint8_t *vrow = a.valid + static_cast<int64_t>(b) * a.valid_stride;
+#pragma unroll
+              for (int t = 0; t < kDecStage; ++t) {
+                const int pos = t0 + t;
+                const bool on = t < d_n && (a.valid == nullptr || pos >= a.valid_len || vrow[pos] != 0);
+                bits |= on ? (1 << t) : 0;
+              }
+            }
+            // the current token (position seq_len - 1): its pool slot, and its row here
+            // when this stage holds it and it is attended (the consumers copy it in)
+            if (d_end && a.nk != nullptr) {
+              const int64_t pos = a.seq_lens[b] - 1;
+              const int64_t pcol = pos / kDecStage;
+              int64_t npage = -1;
+              if (pos >= 0 && pcol < a.table_width)
+                npage = a.page_table[static_cast<int64_t>(b) * a.table_stride + pcol];
+              if (npage >= 0 && npage < a.num_blocks) {
+                d_noff = npage * a.sp + (pos - pcol * kDecStage) * a.ss;
+              } else if (pos >= 0) {
+                raise_flag(a.error_flag, B200ASR_DEVERR_BLOCK);
+              }
+              const int64_t r = pos - t0;
+              if (r >= 0 && r < d_n &&
+                  (a.valid == nullptr || pos >= a.valid_len ||
+                   a.valid[static_cast<int64_t>(b) * a.valid_stride + pos] != 0)) {
+                d_nrow = static_cast<int>(r);
+                bits |= 1 << d_nrow;  // attended from new_key / new_value even on a bad page
+              }
+            }
+            d_vb = bits;
+          } else {
+            const int col = t0 / a.block_size;
+            int blk = 0;
+            if (col >= a.bt_stride) {  // context longer than its block-table row
+              raise_flag(a.error_flag, B200ASR_DEVERR_LENGTH);
+            } else {
+              const int64_t at = static_cast<int64_t>(b) * a.bt_stride + col;
+              blk = bt_cached ? s_bt[at] : a.block_tables[at];
+              if (blk < 0 || blk >= a.num_blocks) {
+                raise_flag(a.error_flag, B200ASR_DEVERR_BLOCK);
+                blk = 0;
+              }
+            }
+            d_slot = blk * a.block_size + t0 % a.block_size;
+          }
         }
         const int nw = min(32, j1 - wb);
         for (int i = 0; i < nw; ++i) {
@@ -431,7 +536,11 @@ __global__ void __launch_bounds__(Dec<HKV, G>::THREADS, 1)
           const int n = __shfl_sync(0xffffffffu, d_n, i);
           const int fl = __shfl_sync(0xffffffffu, d_fl, i);
           const int slot = __shfl_sync(0xffffffffu, d_slot, i);
-          if (__shfl_sync(0xffffffffu, d_end, i) || n_early == kDecStages) wait_prev();
+          const int vb = __shfl_sync(0xffffffffu, d_vb, i);
+          const int nrow = __shfl_sync(0xffffffffu, d_nrow, i);
+          const int64_t noff = __shfl_sync(0xffffffffu, d_noff, i);
+          const int end = __shfl_sync(0xffffffffu, d_end, i);
+          if (end || n_early == kDecStages) wait_prev();
           int st;
           if (!acquire(st)) {
             wait_prev();
@@ -439,13 +548,17 @@ __global__ void __launch_bounds__(Dec<HKV, G>::THREADS, 1)
             return;
           }
           if (lane == 0) {
-            info[st] = StageInfo{b, n, fl};
+            info[st] = StageInfo{b, n, fl, vb, nrow, noff};
             mbar_arrive_expect_tx(&full[st], C::TX_KV + ((fl & 1) ? C::TX_Q : 0));
           }
           __syncwarp();
           uint8_t *stage = stages + st * C::STAGE_BYTES;
           // One box per operand: 16 tokens x every KV head x both 64-dim halves (32 KiB).
-          if (lane < 2) tma_load_4d(stage + lane * C::KV_BYTES, lane ? &tm_v : &tm_k, 0, slot, 0, 0, &full[st]);
+          if constexpr (POOL) {
+            if (lane < 2) tma_load_5d(stage + lane * C::KV_BYTES, lane ? &tm_v : &tm_k, 0, 0, 0, 0, slot, &full[st]);
+          } else {
+            if (lane < 2) tma_load_4d(stage + lane * C::KV_BYTES, lane ? &tm_v : &tm_k, 0, slot, 0, 0, &full[st]);
+          }
           if (fl & 1) {
             if (!waited) {
               dq_st[n_dq] = st;
@@ -467,7 +580,7 @@ __global__ void __launch_bounds__(Dec<HKV, G>::THREADS, 1)
       return;
     }
     if (lane == 0) {
-      info[st] = StageInfo{-1, 0, 0};
+      info[st] = StageInfo{-1, 0, 0, 0, -1, -1};
       mbar_arrive(&full[st]);
     }
     return;
@@ -550,11 +663,29 @@ __global__ void __launch_bounds__(Dec<HKV, G>::THREADS, 1)
         qa[kk][1] = row_valid ? hi : 0u;
       }
     }
-    if (ntok < kDecStage) {  // clear V rows past the end so 0 * stale bytes stays 0
+    const int vbits = POOL ? si.vbits : (1 << ntok) - 1;
+    if constexpr (POOL) {
+      // The current token of the row: this warp's KV head row of new_key / new_value goes
+      // into the stage (when attended here) and into the pools (when its page is usable).
+      if (si.new_row >= 0 || si.new_off >= 0) {
+        const int c = lane & 15, is_v = lane >> 4;
+        const uint4 val = *reinterpret_cast<const uint4 *>((is_v ? a.nv : a.nk) + si.b * a.n_sb +
+                                                           w * a.n_sh + c * 8);
+        if (si.new_row >= 0) {
+          uint8_t *tile = stages + st * C::STAGE_BYTES + is_v * C::KV_BYTES + w * C::HEAD_TILE;
+          *reinterpret_cast<uint4 *>(tile + (c >> 3) * 2048 + swz(si.new_row, c & 7)) = val;
+        }
+        if (si.new_off >= 0)
+          *reinterpret_cast<uint4 *>((is_v ? a.vp : a.kp) + si.new_off + w * a.sh + c * 8) = val;
+        __syncwarp();
+      }
+    }
+    if (vbits != (1 << kDecStage) - 1) {  // clear V rows not attended: 0 * stale bytes stays 0
       uint8_t *vt = stages + st * C::STAGE_BYTES + C::KV_BYTES + w * C::HEAD_TILE;
-      for (int i = lane; i < (kDecStage - ntok) * 16; i += 32) {
-        const int r = ntok + i / 16, ch = i % 16;
-        *reinterpret_cast<uint4 *>(vt + (ch >> 3) * 2048 + swz(r, ch & 7)) = make_uint4(0, 0, 0, 0);
+      for (int i = lane; i < kDecStage * 16; i += 32) {
+        const int r = i / 16, ch = i % 16;
+        if (!((vbits >> r) & 1))
+          *reinterpret_cast<uint4 *>(vt + (ch >> 3) * 2048 + swz(r, ch & 7)) = make_uint4(0, 0, 0, 0);
       }
       __syncwarp();
     }
@@ -580,19 +711,21 @@ __global__ void __launch_bounds__(Dec<HKV, G>::THREADS, 1)
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         const int t = nt * 8 + quad * 2 + e;
-        s[nt][e] = t < ntok ? s[nt][e] * a.scale_log2 : -INFINITY;
+        s[nt][e] = ((vbits >> t) & 1) ? s[nt][e] * a.scale_log2 : -INFINITY;
         mx = fmaxf(mx, s[nt][e]);
       }
     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-    const float m_new = fmaxf(m_run, mx);  // token 0 of every stage is valid: finite
-    const float alpha = exp2f(m_run - m_new);
+    const float m_new = fmaxf(m_run, mx);  // ASR: token 0 of every stage is valid: finite
+    // POOL: every key so far masked leaves m = -inf: exponentiate against 0 (all zeros)
+    const float m_use = POOL && m_new == -INFINITY ? 0.f : m_new;
+    const float alpha = exp2f(m_run - m_use);
     float p[2][2], sum = 0.f;
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
-        p[nt][e] = exp2f(s[nt][e] - m_new);
+        p[nt][e] = exp2f(s[nt][e] - m_use);
         sum += p[nt][e];
       }
     sum += __shfl_xor_sync(0xffffffffu, sum, 1);
@@ -625,7 +758,7 @@ __global__ void __launch_bounds__(Dec<HKV, G>::THREADS, 1)
     const int h = w * G + row;
     if (si.flags & 4) {
       if (row_valid) {
-        const float inv = 1.f / l_run;
+        const float inv = POOL && l_run == 0.f ? 0.f : 1.f / l_run;  // no attended key: zeros
         __nv_bfloat16 *dst = a.out + b * a.out_stride + h * kDecD + quad * 2;
 #pragma unroll
         for (int j = 0; j < 16; ++j)
@@ -664,7 +797,7 @@ __global__ void __launch_bounds__(Dec<HKV, G>::THREADS, 1)
   consumer_sync(C::CONSUMERS);  // all stages consumed: the stage buffers are free
   for (int k = 0; k < s_npending; ++k) {
     const int b = s_pending[k];
-    merge_staged<C>(a, stages, s_parts[b], s_parts[b + 1] - s_parts[b], b, w, lane, tid);
+    merge_staged<C, POOL>(a, stages, s_parts[b], s_parts[b + 1] - s_parts[b], b, w, lane, tid);
   }
 }
 
@@ -1120,6 +1253,97 @@ int launch_decode(const DecodeArgs &a, const void *k_cache, const void *v_cache,
 
 // Partials: every sequence contributes at most one per CTA boundary it straddles plus one.
 size_t decode_parts_cap(int batch) { return static_cast<size_t>(batch) + kDecMaxGrid; }
+
+template <int HKV, int G>
+int launch_decode_pool(const DecodeArgs &a, const CUtensorMap &tk, const CUtensorMap &tv,
+                       cudaStream_t stream) {
+  using C = Dec<HKV, G>;
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(paged_decode_kernel<HKV, G, true>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(C::SMEM));
+    if (e != cudaSuccess) {
+      set_error("pool_paged_decode: cannot reserve %zu bytes of shared memory: %s", C::SMEM,
+                cudaGetErrorString(e));
+      return B200ASR_ERR_CUDA;
+    }
+    configured = true;
+  }
+  const int grid = std::min(num_sms(), kDecMaxGrid);
+  B200_LAUNCH_CHECK_ERR(launch_kernel(paged_decode_kernel<HKV, G, true>, dim3(grid),
+                                      dim3(C::THREADS), C::SMEM, stream, false, 1, tk, tv, a),
+                        "pool_paged_decode (stream-K)");
+  return B200ASR_OK;
+}
+
+int pool_decode_stream_k(const PoolStreamK &p, bool *taken) {
+  *taken = false;
+  const int hq = p.num_heads, hkv = p.num_kv_heads;
+  const bool heads = (hkv == 8 && (hq == 16 || hq == 8)) || (hkv == 4 && (hq == 16 || hq == 8)) ||
+                     (hkv == 2 && hq == 4);
+  if (!heads || p.head_dim != kDecD || p.page_size != kDecStage || p.batch > kDecMaxBatch ||
+      p.q_stride_h != kDecD || p.out_stride_h != kDecD || p.q_stride_b % 8 != 0 ||
+      p.out_stride_b % 4 != 0 || p.kv_stride_s % 8 != 0 || p.kv_stride_h % 8 != 0 ||
+      p.kv_stride_p % 8 != 0 || p.kv_stride_s < kDecD || p.num_pages <= 0)
+    return B200ASR_OK;
+  const size_t parts = decode_parts_cap(p.batch);
+  const size_t base = (p.workspace_head + 255) / 256 * 256 > kDecHeaderBytes
+                          ? (p.workspace_head + 255) / 256 * 256 : kDecHeaderBytes;
+  if (p.workspace_bytes < base + parts * hq * (kDecD + 2) * sizeof(float)) return B200ASR_OK;
+  // Pool [pages][heads][16][128] bf16 as {64 dims, 16 positions, 2 halves, heads, pages}: a
+  // box {64, 16, 2, HKV, 1} lands as [head][half][token][64 dims], the stage layout the
+  // stream-K consumers read.
+  CUtensorMap tk, tv;
+  const uint64_t dims[5] = {64, kDecStage, 2, static_cast<uint64_t>(hkv),
+                            static_cast<uint64_t>(p.num_pages)};
+  const uint64_t strides[4] = {static_cast<uint64_t>(p.kv_stride_s) * 2, 128,
+                               static_cast<uint64_t>(p.kv_stride_h) * 2,
+                               static_cast<uint64_t>(p.kv_stride_p) * 2};
+  const uint32_t box[5] = {64, kDecStage, 2, static_cast<uint32_t>(hkv), 1};
+  if (!make_tmap_bf16(&tk, p.key_pool, 5, dims, strides, box) ||
+      !make_tmap_bf16(&tv, p.value_pool, 5, dims, strides, box))
+    return B200ASR_ERR_CUDA;
+  DecodeArgs a{};
+  a.q = static_cast<const __nv_bfloat16 *>(p.query);
+  a.q_stride = p.q_stride_b;
+  a.num_blocks = p.num_pages;
+  a.block_size = kDecStage;
+  a.batch = p.batch;
+  a.scale_log2 = p.scale * kLog2e;
+  a.out = static_cast<__nv_bfloat16 *>(p.out);
+  a.out_stride = p.out_stride_b;
+  a.parts_cap = static_cast<int>(parts);
+  a.counters = static_cast<int *>(p.workspace);  // zero at rest, like the pool kernel's
+  a.ws_ml = reinterpret_cast<float *>(static_cast<uint8_t *>(p.workspace) + base);
+  a.ws_o = a.ws_ml + parts * hq * 2;
+  a.error_flag = p.error_flag;
+  a.early = 0;
+  a.seq_lens = p.seq_lens;
+  a.max_seq_len = p.max_seq_len;
+  a.page_table = p.page_table;
+  a.table_stride = p.table_stride;
+  a.table_width = p.table_width;
+  a.valid = p.valid;
+  a.valid_stride = p.valid_stride;
+  a.valid_len = p.valid ? p.valid_len : 0;
+  a.nk = static_cast<const __nv_bfloat16 *>(p.new_key);
+  a.nv = static_cast<const __nv_bfloat16 *>(p.new_value);
+  a.n_sb = p.new_stride_b;
+  a.n_sh = p.new_stride_h;
+  a.kp = static_cast<__nv_bfloat16 *>(p.key_pool);
+  a.vp = static_cast<__nv_bfloat16 *>(p.value_pool);
+  a.sp = p.kv_stride_p;
+  a.sh = p.kv_stride_h;
+  a.ss = p.kv_stride_s;
+  *taken = true;
+  const cudaStream_t st = static_cast<cudaStream_t>(p.stream);
+  if (hkv == 8 && hq == 16) return launch_decode_pool<8, 2>(a, tk, tv, st);
+  if (hkv == 8 && hq == 8) return launch_decode_pool<8, 1>(a, tk, tv, st);
+  if (hkv == 4 && hq == 16) return launch_decode_pool<4, 4>(a, tk, tv, st);
+  if (hkv == 4 && hq == 8) return launch_decode_pool<4, 2>(a, tk, tv, st);
+  return launch_decode_pool<2, 2>(a, tk, tv, st);
+}
 
 }  // namespace b200asr
 

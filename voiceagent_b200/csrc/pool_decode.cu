@@ -545,6 +545,50 @@ extern "C" int b200asr_pool_paged_decode(
     set_error("pool_paged_decode: workspace %zu bytes < %zu needed", workspace_bytes, need);
     return B200ASR_ERR_WORKSPACE;
   }
+  // The talker's case -- bf16, head_dim 128, 16-position pages, heads contiguous in query
+  // and out -- runs on the stream-K decode kernel (every CTA the same share of the batch's
+  // pages, one TMA box per K / V page); tokens_per_cta != 0 asks for this kernel instead.
+  if (dtype == B200ASR_DTYPE_BF16 && tokens_per_cta == 0) {
+    PoolStreamK p{};
+    p.batch = batch;
+    p.num_heads = num_heads;
+    p.num_kv_heads = num_kv_heads;
+    p.head_dim = head_dim;
+    p.query = query;
+    p.q_stride_b = q_stride_b;
+    p.q_stride_h = q_stride_h;
+    p.key_pool = key_pool;
+    p.value_pool = value_pool;
+    p.num_pages = num_pages;
+    p.page_size = page_size;
+    p.kv_stride_p = kv_stride_p;
+    p.kv_stride_h = kv_stride_h;
+    p.kv_stride_s = kv_stride_s;
+    p.page_table = page_table;
+    p.table_stride = table_stride;
+    p.table_width = table_width;
+    p.seq_lens = seq_lens;
+    p.valid = key_valid_mask;
+    p.valid_stride = valid_stride;
+    p.valid_len = valid_len;
+    p.new_key = new_key;
+    p.new_value = new_value;
+    p.new_stride_b = new_stride_b;
+    p.new_stride_h = new_stride_h;
+    p.out = out;
+    p.out_stride_b = out_stride_b;
+    p.out_stride_h = out_stride_h;
+    p.max_seq_len = max_seq_len;
+    p.scale = scale;
+    p.workspace = workspace;
+    p.workspace_bytes = workspace_bytes;
+    p.workspace_head = header_bytes(static_cast<int64_t>(batch) * num_heads);
+    p.error_flag = error_flag;
+    p.stream = stream;
+    bool taken = false;
+    const int rc = pool_decode_stream_k(p, &taken);
+    if (taken || rc != B200ASR_OK) return rc;
+  }
 
   PoolArgs a{};
   a.q = query;
