@@ -132,6 +132,55 @@ def decode_config1(iters: int = 64, sets: int = 4, lo: int = 64, hi: int = 1024,
                                               if pdl else ""))
 
 
+def tts_pool_decode_variants(iters: int = 64) -> list[dict]:
+    """The talker's pool decode (the same geometry as ``tts_pool_decode``) through the
+    public wrapper with and without its optional inputs -- the key-valid mask and the
+    current token's K/V -- and on the chunked CUDA-core kernel (``tokens_per_cta``), to
+    show what each part of the call costs."""
+    dev = torch.device("cuda")
+    rng = np.random.default_rng(0)
+    b, h, hkv, d, page = 32, 16, 8, 128, 16
+    pages = (1 << 21) // page
+    lens = rng.integers(64, 1025, size=b)
+    need = (lens + page - 1) // page
+    gen = torch.Generator(device=dev).manual_seed(0)
+    kp = (torch.randn(pages, hkv, page, d, device=dev, generator=gen) / d ** 0.5).bfloat16()
+    vp = kp.clone()
+    q = (torch.randn(b, h, 1, d, device=dev, generator=gen) / d ** 0.5).bfloat16()
+    nk = (torch.randn(b, hkv, 1, d, device=dev, generator=gen) / d ** 0.5).bfloat16()
+    nv = nk.clone()
+    perm = rng.permutation(pages)
+    tables = []
+    for k in range(4):
+        t = np.full((b, 64), -1, np.int64)
+        c = k * int(need.sum())
+        for i, n in enumerate(need):
+            t[i, :n] = perm[c:c + n]
+            c += int(n)
+        tables.append(torch.from_numpy(t).to(dev))
+    seq = torch.from_numpy(lens.astype(np.int64)).to(dev)
+    valid = torch.ones(b, 1024, dtype=torch.bool, device=dev)
+    out = torch.empty_like(q)
+    ws = kx.pool_decode_workspace(b, h, d, 1024, dev)
+    algo = int(lens.sum()) * hkv * d * 2 * 2 + 2 * b * h * d * 2
+    lines = []
+    for name, kw in (("mask + current token", dict(key_valid_mask=valid, new_key=nk, new_value=nv)),
+                     ("current token only", dict(new_key=nk, new_value=nv)),
+                     ("mask only", dict(key_valid_mask=valid)),
+                     ("neither", {}),
+                     ("mask + current token, chunked kernel (tokens_per_cta 256)",
+                      dict(key_valid_mask=valid, new_key=nk, new_value=nv, tokens_per_cta=256))):
+        ops = [lambda i=i, kw=kw: kx.pool_paged_decode(q, kp, vp, tables[i % 4], seq,
+                                                        max_seq_len=1024, scale=d ** -0.5,
+                                                        out=out, workspace=ws, **kw)
+               for i in range(iters)]
+        lines.append(_line("pool_paged_decode", f"talker B=32 ctx~U[64,1024], {name}",
+                           graph_time_us(ops), algo, timing=f"graph of {iters} launches"))
+    del kp, vp
+    torch.cuda.empty_cache()
+    return lines
+
+
 def _reference_tts_module():
     """The reference's TTS paged attention module from its installed copy (baseline/_ref),
     or None when it or Triton is unavailable."""
@@ -604,6 +653,7 @@ BENCHES = {
     "argmax": lambda: [argmax_rows(32)],
     "log_mel": lambda: [log_mel_config3()],
     "tts_decode": lambda: tts_pool_decode(),
+    "tts_decode_variants": lambda: tts_pool_decode_variants(),
     # a 256 MB pool and four launches: the size for an ncu capture of one launch
     "tts_decode_profile": lambda: tts_pool_decode(iters=4, sets=1, pool_tokens=131072,
                                                   reference=False),
