@@ -409,3 +409,36 @@ def test_multi_step_postprocess_equals_single_steps(config):
     single, multi = run(False), run(True)
     assert single == multi
     assert multi[1] == [2]  # the EOS request finished; its third token was discarded
+
+
+def test_batched_record_equals_per_token_record(config):
+    """Scheduler._record_run (one append per request and call) leaves every request as
+    the per-token _record loop does: tokens kept, computed count, stage, finish reason;
+    over stop tokens at every position, caps reached before, at and after the stop,
+    ignore_eos and cancels."""
+    scheduler = Scheduler(config(), BlockManager(64, BS))
+    rng = np.random.default_rng(11)
+    stop = 151645
+    for case in range(2000):
+        steps = int(rng.integers(1, 5))
+        run = tuple(int(t) for t in rng.integers(100, 200, size=steps))
+        if rng.random() < 0.6:
+            run = tuple(stop if rng.random() < 0.3 else t for t in run)
+        made = []
+        for _ in range(2):
+            r = make_request(40, max_new_tokens=int(rng.integers(1, 8)))
+            r.stage = RequestStage.RUNNING_DECODE
+            made.append(r)
+        outputs = int(rng.integers(0, 9))
+        ignore, cancel = rng.random() < 0.2, rng.random() < 0.05
+        for r in made:
+            r.token_ids += [150] * outputs
+            r.num_computed_tokens = len(r) - 1
+            r.sampling.max_new_tokens = made[0].sampling.max_new_tokens
+            r.sampling.ignore_eos, r.cancel_requested = ignore, cancel
+        per_token = any(scheduler._record(made[0], t) for t in run)
+        batched = scheduler._record_run(made[1], run)
+        want, got = made
+        assert (per_token, want.token_ids, want.num_computed_tokens, want.stage, want.finish_reason) \
+            == (batched, got.token_ids, got.num_computed_tokens, got.stage, got.finish_reason), \
+            (case, run, outputs, want.sampling)

@@ -151,13 +151,11 @@ class GpuMelFrontend:
         hv = host.numpy()
         hv[:meta_i64.nbytes] = meta_i64.view(np.uint8)
         hv[meta_i64.nbytes:meta_i64.nbytes + meta_i32.nbytes] = meta_i32.view(np.uint8)
-        # the samples: torch's copy runs on the intra-op threads (a 32-clip batch is ~14 MB;
-        # a single-threaded numpy copy cost ~2.5 ms of host time per batch)
+        # the samples: one torch.cat on the intra-op threads (a 32-clip batch is ~14 MB; a
+        # single-threaded numpy copy cost ~2.5 ms of host time per batch, one torch copy
+        # per clip ~2 ms)
         wave_host = host[wave_at:].view(torch.float32)
-        off = 0
-        for f in features:
-            wave_host[off:off + f.waveform.size].copy_(torch.from_numpy(f.waveform))
-            off += f.waveform.size
+        torch.cat([torch.from_numpy(f.waveform) for f in features], out=wave_host)
         dev = host.to(self.device, non_blocking=True)
         cu_samples = dev[:meta_i64.nbytes].view(torch.int64)
         i32 = dev[meta_i64.nbytes:meta_i64.nbytes + meta_i32.nbytes].view(torch.int32)

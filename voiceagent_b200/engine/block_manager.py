@@ -118,7 +118,7 @@ class BlockManager:
         """Cover the position the next decode step writes (len - 1). Equivalent to the
         reference's ``len % block_size == 1`` test, and a no-op when the block was
         already taken ahead (multi-step decode)."""
-        if len(request.block_table) < request.num_blocks:
+        if len(request.block_table) * self.block_size < len(request.token_ids):  # < num_blocks
             request.block_table.append(self._take_any().block_id)
 
     def blocks_ahead(self, request: AsrRequest, steps: int) -> int:

@@ -21,6 +21,7 @@ short one when every context, including the steps it adds, fits.
 
 from __future__ import annotations
 
+import itertools
 import logging
 
 import torch
@@ -149,18 +150,20 @@ class GraphRunner:
         if not 1 <= steps <= self.max_steps:
             raise ValueError(f"steps must be in [1, {self.max_steps}], got {steps}")
         m, h = self.max_batch, self._host_np
-        cursor = 4 * m
-        for i, r in enumerate(requests):
-            table = r.block_table
-            h[i] = len(r)
-            h[m + i] = r.token_ids[-1]
-            h[2 * m + i] = cursor - 4 * m
-            h[3 * m + i] = len(table)
-            h[cursor:cursor + len(table)] = table
-            cursor += len(table)
+        # one slice store per descriptor field (numpy converts each list in C)
+        lengths = [len(r.token_ids) for r in requests]
+        tables = [r.block_table for r in requests]
+        table_lens = [len(t) for t in tables]
+        flat = list(itertools.chain.from_iterable(tables))
+        h[0:n] = lengths
+        h[m:m + n] = [r.token_ids[-1] for r in requests]
+        h[2 * m:2 * m + n] = list(itertools.accumulate(table_lens, initial=0))[:n]
+        h[3 * m:3 * m + n] = table_lens
+        cursor = 4 * m + len(flat)
+        h[4 * m:cursor] = flat
         self._fill_padding(n)
         self.desc[:cursor].copy_(self.host_desc[:cursor], non_blocking=True)
-        key = (bucket, self.uses_short_graph(max(len(r) for r in requests), steps))
+        key = (bucket, self.uses_short_graph(max(lengths), steps))
         for k in range(steps):
             self.graphs[key].replay()
             self.host_tokens[k, :n].copy_(self.token_ids[:n], non_blocking=True)

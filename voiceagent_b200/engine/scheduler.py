@@ -196,6 +196,13 @@ class Scheduler:
 
     def _take_decodes(self, batch: ModelBatch) -> None:
         bm = self.block_manager
+        # can_append asks for at most one free block and taking a request changes no
+        # free count: with one free (or no request opening a block) all of them join
+        if self.running and (bm.num_free_blocks > 0 or all(
+                len(r.token_ids) % bm.block_size != 1 for r in self.running)):
+            batch.decode.extend(self.running)
+            self.running.clear()
+            return
         while self.running:
             if bm.can_append(self.running[0]):
                 batch.decode.append(self.running.popleft())
@@ -290,6 +297,36 @@ class Scheduler:
             return True
         return request.check_finished()
 
+    def _record_run(self, request: AsrRequest, run) -> bool:
+        """``_record`` of each token of ``run`` in turn, stopping at the first that ends
+        the request (the rest are dropped). A decoding request that no cancel has
+        reached takes them in one append: the first ending token is the first stop
+        token (unless ignored) or the one that reaches the output cap, whichever
+        comes first -- a stop token at the cap ends it as "stop", as
+        ``check_finished`` rules."""
+        if request.cancel_requested or request.stage is not RequestStage.RUNNING_DECODE:
+            return any(self._record(request, token) for token in run)
+        ids = request.token_ids
+        sampling = request.sampling
+        end = sampling.max_new_tokens - (len(ids) - request.num_prompt_tokens) - 1
+        end = max(end, 0)  # index of the token that reaches the cap
+        reason = "length"
+        if not sampling.ignore_eos:
+            stops = request.stop_token_ids
+            for k, token in enumerate(run):
+                if token in stops:
+                    if k <= end:
+                        end, reason = k, "stop"
+                    break
+        if end >= len(run):
+            ids.extend(run)
+            request.num_computed_tokens = len(ids) - 1
+            return False
+        ids.extend(run[:end + 1])
+        request.num_computed_tokens = len(ids) - 1
+        request.finish(reason)
+        return True
+
     def postprocess(self, batch: ModelBatch, token_ids: list[int]) -> list[AsrRequest]:
         """Apply one step's sampled tokens (one per request, batch order); the requests
         that ended are returned, the others go back to ``running`` with room for
@@ -299,7 +336,7 @@ class Scheduler:
             raise ValueError(f"sampler returned {len(token_ids)} tokens for {len(requests)} requests")
         finished: list[AsrRequest] = []
         for request, token in zip(requests, token_ids):
-            if self._record(request, token):
+            if self._record_run(request, (token,)):
                 self._release_finished(request)
                 finished.append(request)
             else:
@@ -317,16 +354,26 @@ class Scheduler:
         admission of a waiting request by up to ``steps - 1`` steps."""
         if limit <= 1 or batch.prefill or not batch.decode:
             return 1
-        if any(r.cancel_requested for r in batch.decode):
-            return 1
-        steps = min([limit] + [min(r.sampling.max_new_tokens - r.num_output_tokens,
-                                   max_model_len - len(r) + 1) for r in batch.decode])
+        steps = limit
+        lengths = []
+        for r in batch.decode:
+            if r.cancel_requested:
+                return 1
+            n = len(r.token_ids)
+            lengths.append(n)
+            steps = min(steps, r.sampling.max_new_tokens - (n - r.num_prompt_tokens),
+                        max_model_len - n + 1)
         if steps <= 1:
             return 1
         bm = self.block_manager
-        if sum(bm.blocks_ahead(r, steps) for r in batch.decode) > bm.num_free_blocks:
+        bs = bm.block_size
+        # BlockManager.blocks_ahead of every request, without re-measuring them
+        ahead = [(r, -(-(n + steps - 1) // bs) - len(r.block_table))
+                 for r, n in zip(batch.decode, lengths)]
+        ahead = [(r, k) for r, k in ahead if k > 0]
+        if sum(k for _, k in ahead) > bm.num_free_blocks:
             return 1
-        for r in batch.decode:
+        for r, _ in ahead:
             bm.append_ahead(r, steps)
         return steps
 
@@ -338,12 +385,13 @@ class Scheduler:
         if batch.prefill or any(len(step) != len(requests) for step in tokens):
             raise ValueError("multi-step results do not match the decode batch")
         finished: list[AsrRequest] = []
-        for i, request in enumerate(requests):
-            if any(self._record(request, step[i]) for step in tokens):
+        may_append = self.block_manager.may_append
+        for request, run in zip(requests, zip(*tokens)):
+            if self._record_run(request, run):
                 self._release_finished(request)
                 finished.append(request)
             else:
-                self.block_manager.may_append(request)
+                may_append(request)
                 self.running.append(request)
         extra = len(tokens) - 1
         self.stats.num_model_steps += extra
