@@ -134,6 +134,23 @@ def test_gpu_frontend_matches_host_frontend(tiny_dir, clips):
     assert same / total >= 0.99, same / total
 
 
+def test_waveforms_staged_during_decode_give_the_same_tokens(tiny_dir, clips):
+    """Clips waiting to be encoded are copied into pinned memory while decoder calls run
+    (ModelRunner.host_work); with more clips than sequence slots some are, and the tokens
+    equal those of an engine that stages every batch at its encoder call."""
+    many = clips * 3
+    staging = _engine(tiny_dir, max_num_seqs=2, max_audio_batch_size=2)
+    calls = []
+    stage = staging.audio_runner.renderer.stage
+    staging.audio_runner.renderer.stage = lambda f: calls.append(stage(f)) or calls[-1]
+    got = _run(staging, many)
+    assert sum(calls) > 0  # some clips crossed from their own pinned buffers
+    plain = _engine(tiny_dir, max_num_seqs=2, max_audio_batch_size=2)
+    plain.model_runner.host_work = None
+    want = _run(plain, many)
+    assert [o.output_token_ids for o in got] == [o.output_token_ids for o in want]
+
+
 def test_pdl_launches_do_not_change_tokens(tiny_dir, clips):
     """Programmatic dependent launch only overlaps prologues: tokens are identical."""
     from voiceagent_b200 import kernels as kx

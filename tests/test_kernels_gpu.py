@@ -739,6 +739,27 @@ def test_log_mel_matches_oracle_on_mixed_lengths(gpu_frontend):
     assert torch.isnan(out[:, ~covered.cuda()].float()).all()  # nothing written outside
 
 
+@pytest.mark.parametrize("staged", [(0, 1, 2, 3, 4), (1, 3), (0, 4), (2,)])
+def test_log_mel_of_clips_staged_ahead_is_identical(gpu_frontend, staged):
+    """Clips copied into pinned memory ahead of their batch (GpuMelFrontend.stage, as the
+    engine does while a decoder call runs) render exactly as clips staged with the batch,
+    for every pattern of staged / not staged runs; the staged buffers are released."""
+    from voiceagent_b200.workload import synthetic_waveform
+
+    rng = np.random.default_rng(9)
+    clips = [synthetic_waveform(s, rng) for s in (1.7, 3.05, 0.4, 7.3, 2.0)]
+    want, frames = _render(gpu_frontend, clips)
+    feats = [gpu_frontend(c) for c in clips]
+    for i in staged:
+        assert gpu_frontend.stage(feats[i]) and not gpu_frontend.stage(feats[i])
+    columns = list(np.concatenate([[0], np.cumsum(frames)])[:-1])
+    got = torch.full_like(want, float("nan"))
+    gpu_frontend.render(feats, got, [int(c) for c in columns])
+    torch.cuda.synchronize()
+    assert torch.equal(got, want)
+    assert all(f.staged is None for f in feats)
+
+
 def test_log_mel_rejects_short_clips(gpu_frontend):
     with pytest.raises(ValueError):
         gpu_frontend(np.zeros(200, np.float32))

@@ -8,13 +8,15 @@ depends on what it was batched with.
 ``GpuMelFrontend`` defers the work: a request keeps its waveform (its frame and
 token counts are closed-form in the sample count) until its encode batch, where the
 batch's clips cross to the GPU in one pinned copy and ``b200asr_log_mel`` writes the
-bf16 features straight into the encoder's packed input.
+bf16 features straight into the encoder's packed input. A clip can be staged into
+pinned memory earlier (``GpuMelFrontend.stage``, which the engine calls while the GPU
+runs a decoder step); its encode batch then copies it to the device directly.
 """
 
 from __future__ import annotations
 
 import os
-from dataclasses import dataclass
+from dataclasses import dataclass, field
 
 import numpy as np
 import torch
@@ -31,6 +33,9 @@ class AudioFeatures:
     num_audio_tokens: int
     audio_seconds: float
     waveform: np.ndarray | None = None  # 16 kHz float32 samples awaiting the GPU frontend
+    # the samples copied into pinned host memory ahead of the encode batch
+    # (GpuMelFrontend.stage), so that batch crosses to the GPU without a host copy
+    staged: torch.Tensor | None = field(default=None, repr=False, compare=False)
 
 
 class AudioFrontend:
@@ -128,6 +133,17 @@ class GpuMelFrontend:
         return AudioFeatures(mel=None, mel_frames=frames, num_audio_tokens=num_audio_tokens(frames),
                              audio_seconds=audio.size / TARGET_SAMPLE_RATE, waveform=audio)
 
+    def stage(self, features: AudioFeatures) -> bool:
+        """Copy a deferred clip's samples into pinned host memory now, ahead of its encode
+        batch. Returns whether it copied (False: not deferred, already staged, or no GPU)."""
+        if (self.device.type != "cuda" or features.waveform is None or features.mel is not None
+                or features.staged is not None):
+            return False
+        staged = torch.empty(features.waveform.size, dtype=torch.float32, pin_memory=True)
+        staged.copy_(torch.from_numpy(features.waveform))
+        features.staged = staged
+        return True
+
     def render(self, features: list[AudioFeatures], out: torch.Tensor, columns: list[int],
                error_flag: torch.Tensor | None = None) -> int:
         """Write the log-mel of every deferred clip into ``out[:, columns[i]:...]``
@@ -153,10 +169,30 @@ class GpuMelFrontend:
         hv[meta_i64.nbytes:meta_i64.nbytes + meta_i32.nbytes] = meta_i32.view(np.uint8)
         # the samples: one torch.cat on the intra-op threads (a 32-clip batch is ~14 MB; a
         # single-threaded numpy copy cost ~2.5 ms of host time per batch, one torch copy
-        # per clip ~2 ms)
+        # per clip ~2 ms), unless clips were staged ahead: those copy from their own
+        # pinned buffers, the others through this one
         wave_host = host[wave_at:].view(torch.float32)
-        torch.cat([torch.from_numpy(f.waveform) for f in features], out=wave_host)
-        dev = host.to(self.device, non_blocking=True)
+        if all(f.staged is None for f in features):
+            torch.cat([torch.from_numpy(f.waveform) for f in features], out=wave_host)
+            dev = host.to(self.device, non_blocking=True)
+        else:
+            dev = torch.empty_like(host, device=self.device)
+            dev[:wave_at].copy_(host[:wave_at], non_blocking=True)
+            wave_dev = dev[wave_at:].view(torch.float32)
+            starts = meta_i64.tolist()
+            run = None  # [first, end) of clips not staged, copied as one range
+            for i, f in enumerate(features + [None]):
+                if f is not None and f.staged is None:
+                    lo, hi = starts[i], starts[i + 1]
+                    wave_host[lo:hi].copy_(torch.from_numpy(f.waveform))
+                    run = (run[0] if run else lo, hi)
+                    continue
+                if run:
+                    wave_dev[run[0]:run[1]].copy_(wave_host[run[0]:run[1]], non_blocking=True)
+                    run = None
+                if f is not None:
+                    wave_dev[starts[i]:starts[i + 1]].copy_(f.staged, non_blocking=True)
+                    f.staged = None  # the copy holds the pinned block until it has run
         cu_samples = dev[:meta_i64.nbytes].view(torch.int64)
         i32 = dev[meta_i64.nbytes:meta_i64.nbytes + meta_i32.nbytes].view(torch.int32)
         frame_start, out_col = i32[:b + 1], i32[b + 1:]

@@ -9,6 +9,7 @@ on the b200asr sm_100a kernels and decode steps replay whole-step CUDA graphs.
 
 from __future__ import annotations
 
+import itertools
 import logging
 import time
 from dataclasses import dataclass, field
@@ -91,6 +92,7 @@ class AsrEngine:
         self.model.audio_tower.warm_up()
         if isinstance(self.frontend, GpuMelFrontend):
             self.audio_runner.renderer = self.frontend
+            self.model_runner.host_work = self._stage_upcoming_audio
         self.block_manager = BlockManager(num_blocks, self.config.kvcache_block_size,
                                           self.config.enable_prefix_cache)
         self.scheduler = Scheduler(self.config, self.block_manager)
@@ -185,6 +187,15 @@ class AsrEngine:
                          num_audio_tokens=request.layout.audio_length, num_output_tokens=len(ids),
                          finish_reason=request.finish_reason, timings=request.timings,
                          output_token_ids=list(ids))
+
+    def _stage_upcoming_audio(self) -> None:
+        """While a decoder call runs on the GPU: copy the waveforms of the requests at the
+        head of the encode queue (the next encoder call's, at most one call's worth) into
+        pinned memory, so that call's host-to-device copy needs no host copy first."""
+        stage = self.audio_runner.renderer.stage
+        for request in itertools.islice(self.scheduler.waiting_encode,
+                                        self.config.max_audio_batch_size):
+            stage(request.features)
 
     # -------------------------------------------------------------- loop
 

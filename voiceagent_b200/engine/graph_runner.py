@@ -139,10 +139,11 @@ class GraphRunner:
         return None
 
     @torch.inference_mode()
-    def run(self, requests, steps: int = 1) -> list[int] | list[list[int]]:
+    def run(self, requests, steps: int = 1, host_work=None) -> list[int] | list[list[int]]:
         """Replay ``steps`` decode steps for ``requests`` (their block tables must already
         cover every position those steps write). Returns the sampled ids of the one step,
-        or one list per step when ``steps > 1``."""
+        or one list per step when ``steps > 1``. ``host_work`` (a callable) runs after the
+        replays are queued, while the GPU executes them."""
         n = len(requests)
         bucket = self.bucket_for(n)
         if bucket is None:
@@ -170,6 +171,8 @@ class GraphRunner:
         kx.LAUNCHES["count"] += steps * self.kernels_per_replay[key]
         TRANSFERS["h2d"] += 4 * cursor
         TRANSFERS["d2h"] += 8 * n * steps
+        if host_work is not None:
+            host_work()
         torch.cuda.current_stream().synchronize()
         if steps == 1:
             return self.host_tokens[0, :n].tolist()

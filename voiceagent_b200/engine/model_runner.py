@@ -63,6 +63,9 @@ class ModelRunner:
         self.kv_cache: torch.Tensor | None = None
         self.num_blocks = 0
         self.graph_runner: GraphRunner | None = None
+        # host work to overlap with the GPU: called once a decoder call is queued, before
+        # the host waits for its tokens (the engine stages upcoming clips' waveforms)
+        self.host_work = None
         self.timer = NULL_TIMER
         self.error_flag = torch.zeros(1, dtype=torch.int32, device=self.device)
         max_tables = config.max_num_seqs * (-(-config.max_model_len // self.block_size))
@@ -226,13 +229,13 @@ class ModelRunner:
         if not self.can_use_graph(batch) or batch.prefill:
             raise ValueError("multi-step decode needs a graph-eligible decode-only batch")
         with self.timer.phase("llm_decode"):
-            return self.graph_runner.run(batch.decode, steps)
+            return self.graph_runner.run(batch.decode, steps, host_work=self.host_work)
 
     @torch.inference_mode()
     def run(self, batch: ModelBatch) -> list[int]:
         with self.timer.phase(self._phase_name(batch)):
             if self.can_use_graph(batch):
-                return self.graph_runner.run(batch.decode)
+                return self.graph_runner.run(batch.decode, host_work=self.host_work)
             logits = self._forward_eager(batch)
             return self._sample(logits, batch.requests)
 
@@ -265,6 +268,8 @@ class ModelRunner:
             n, dtype=torch.int64, pin_memory=True)
         host.copy_(ids, non_blocking=True)
         TRANSFERS["d2h"] += 8 * n
+        if self.host_work is not None:
+            self.host_work()
         torch.cuda.current_stream().synchronize()
         return host.tolist()
 
