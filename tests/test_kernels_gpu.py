@@ -202,6 +202,34 @@ def test_audio_chunk_pad_matches_oracle(kx):
                                   K.chunk_and_pad(mel, meta["chunk_lengths"]))
 
 
+@pytest.mark.parametrize("frames,d", [([350, 7, 100, 201], 896), ([1, 99, 100, 101, 3000], 64)])
+def test_audio_gather_pos_matches_reference_mask_select(kx, frames, d):
+    """Positional add + valid-token gather of the conv front against the reference's
+    eager form (models/audio_encoder.py:169-173: ``embed + pos.to(bf16)``, rounded once,
+    then ``embed[positions < chunk_valid_lens]``), bit for bit; padding rows are zero."""
+    rng = np.random.default_rng(len(frames))
+    meta = K.pack_audio_metadata(frames)
+    valid = np.asarray(meta["chunk_valid_lens"])
+    chunks, per = len(valid), 13
+    embed = K.bf16_round(rng.standard_normal((chunks, per, d)).astype(np.float32))
+    pos = K.bf16_round(rng.standard_normal((per, d)).astype(np.float32))
+    mask = np.arange(per)[None, :] < valid[:, None]
+    want = K.bf16_round((embed + pos[None]).astype(np.float32))[mask]
+    index = np.flatnonzero(mask.ravel()).astype(np.int64)
+    rows = len(index) + 11
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    got = kx.audio_gather_pos(bf16(embed), bf16(pos), dev(index), rows, error_flag=err)
+    assert err.item() == 0
+    np.testing.assert_array_equal(got[:len(index)].float().cpu().numpy(), want)
+    assert not got[len(index):].float().abs().sum().item()
+    # an index past the conv output is flagged and its row zeroed, the others kept
+    bad = index.copy()
+    bad[1] = chunks * per
+    got = kx.audio_gather_pos(bf16(embed), bf16(pos), dev(bad), len(bad), error_flag=err)
+    assert err.item() == 8 and not got[1].float().abs().sum().item()
+    np.testing.assert_array_equal(got[2:].float().cpu().numpy(), want[2:])
+
+
 # -------------------------------------------------------------------- KV store
 
 

@@ -35,6 +35,8 @@ SIGNATURES: dict[str, tuple] = {
     "b200asr_pack_audio": (c_int32, [P, c_int32, c_int32, c_int32, c_int32, c_int32,
                                      P, P, P, P, P, P, P, P]),
     "b200asr_audio_chunk_pad": (c_int32, [P, c_int32, c_int32, P, P, c_int32, c_int32, P, P]),
+    "b200asr_audio_gather_pos": (c_int32, [P, c_int64, P, c_int32, P, c_int32, c_int32, c_int32,
+                                             P, P, P]),
     "b200asr_store_kvcache": (c_int32, [P, c_int64, P, c_int64, P, P, P, c_int32, c_int32,
                                         c_int32, c_int64, P, P]),
     "b200asr_qk_norm_rope_store": (c_int32, [P, c_int64, P, c_int32, c_int32, c_int32, c_int32,

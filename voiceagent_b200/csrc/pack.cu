@@ -5,6 +5,8 @@
 // pack_audio          <- pack_audio_batch metadata      (audio/batcher.py:101-141,
 //                                                        audio/tokens.py:30-52)
 // audio_chunk_pad     <- AudioEncoder._chunk_and_pad    (models/audio_encoder.py:130-143)
+// audio_gather_pos    <- AudioEncoder.forward "conv.gather" (models/audio_encoder.py:169-173):
+//                        positional add + valid-token selection of the conv output
 //
 // The host uploads one compact per-request descriptor (a few int32 per request plus
 // the concatenated block tables and query tokens); everything per token is derived
@@ -252,6 +254,48 @@ __global__ void audio_chunk_pad_kernel(const __nv_bfloat16 *__restrict__ mel, in
   }
 }
 
+// Valid-token gather of the conv front with the positional add, one warp per output row
+// (16-byte accesses): row i < tokens is embed[src] + pos[src % tokens_per_chunk] with
+// src = token_index[i], added in fp32 and rounded once to bf16 (torch's bf16 + bf16);
+// rows [tokens, rows_out) are zero (the bucketed padding the encoder layers run over).
+// An index outside embed's rows raises B200ASR_DEVERR_LENGTH and its row is zeroed.
+__global__ void audio_gather_pos_kernel(const __nv_bfloat16 *__restrict__ embed,
+                                        int64_t embed_rows, const __nv_bfloat16 *__restrict__ pos,
+                                        int tokens_per_chunk,
+                                        const int64_t *__restrict__ token_index, int tokens,
+                                        int rows_out, int d, __nv_bfloat16 *__restrict__ out,
+                                        int32_t *error_flag) {
+  const int row = static_cast<int>((blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows_out) return;
+  uint4 *dst = reinterpret_cast<uint4 *>(out + static_cast<int64_t>(row) * d);
+  const int n8 = d >> 3;
+  int64_t src = -1;
+  if (row < tokens) {
+    src = token_index[row];
+    if (src < 0 || src >= embed_rows) {
+      if (lane == 0) raise_flag(error_flag, B200ASR_DEVERR_LENGTH);
+      src = -1;
+    }
+  }
+  if (src < 0) {
+    for (int i = lane; i < n8; i += 32) dst[i] = make_uint4(0, 0, 0, 0);
+    return;
+  }
+  const uint4 *e = reinterpret_cast<const uint4 *>(embed + src * d);
+  const uint4 *p = reinterpret_cast<const uint4 *>(pos + (src % tokens_per_chunk) * d);
+  for (int i = lane; i < n8; i += 32) {
+    const uint4 a = e[i], b = p[i];
+    const uint32_t av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+    uint32_t y[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      y[k] = pack2(__uint_as_float(av[k] << 16) + __uint_as_float(bv[k] << 16),
+                   __uint_as_float(av[k] & 0xffff0000u) + __uint_as_float(bv[k] & 0xffff0000u));
+    dst[i] = make_uint4(y[0], y[1], y[2], y[3]);
+  }
+}
+
 // Advances a decode-bucket descriptor by one generated token on the device: for every
 // real row (non-empty block table) the length grows by one and the last token becomes
 // the one just sampled. Lets consecutive decode-graph replays run without a host round
@@ -367,5 +411,26 @@ extern "C" int b200asr_audio_chunk_pad(const void *mel, int32_t bins, int32_t to
       static_cast<const __nv_bfloat16 *>(mel), bins, total_frames, chunk_start, chunk_lengths,
       num_chunks, chunk_frames, static_cast<__nv_bfloat16 *>(padded));
   B200_CUDA_LAUNCH_CHECK("audio_chunk_pad");
+  return B200ASR_OK;
+}
+
+extern "C" int b200asr_audio_gather_pos(const void *embed, int64_t embed_rows, const void *pos,
+                                        int32_t tokens_per_chunk, const int64_t *token_index,
+                                        int32_t tokens, int32_t rows_out, int32_t d, void *out,
+                                        int32_t *error_flag, b200asr_stream_t stream) {
+  B200_REQUIRE(embed_rows >= 0 && tokens_per_chunk >= 1 && tokens >= 0 && rows_out >= tokens &&
+                   d >= 8 && d % 8 == 0,
+               "audio_gather_pos: bad sizes (tokens %d, rows_out %d, d %d)", tokens, rows_out, d);
+  if (rows_out == 0) return B200ASR_OK;
+  B200_REQUIRE(out && (tokens == 0 || (embed && pos && token_index)),
+               "audio_gather_pos: null pointer");
+  B200_REQUIRE(aligned16(out) && (tokens == 0 || (aligned16(embed) && aligned16(pos))),
+               "audio_gather_pos: rows must be 16-byte aligned");
+  const int64_t threads = static_cast<int64_t>(rows_out) * 32;
+  audio_gather_pos_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, stream>>>(
+      static_cast<const __nv_bfloat16 *>(embed), embed_rows,
+      static_cast<const __nv_bfloat16 *>(pos), tokens_per_chunk, token_index, tokens, rows_out, d,
+      static_cast<__nv_bfloat16 *>(out), error_flag);
+  B200_CUDA_LAUNCH_CHECK("audio_gather_pos");
   return B200ASR_OK;
 }

@@ -119,6 +119,30 @@ def audio_chunk_pad(mel, chunk_start, chunk_lengths, num_chunks: int, chunk_fram
     return out
 
 
+def audio_gather_pos(embed, pos, token_index, rows_out: int, error_flag=None) -> torch.Tensor:
+    """Positional add + valid-token selection of the conv front ("conv.gather" in
+    AudioEncoder.forward, models/audio_encoder.py:169-173): embed bf16 [chunks, P, d],
+    pos bf16 [P, d] -> [rows_out, d] whose first token_index.numel() rows are
+    embed[i] + pos[i % P] for i in token_index (flat rows) and the rest zero."""
+    _cuda(embed, pos, token_index)
+    _need(embed.dtype == BF16 and pos.dtype == BF16 and embed.is_contiguous() and pos.is_contiguous(),
+          "audio_gather_pos: contiguous bf16 embed and pos")
+    _need(token_index.dtype == torch.int64 and token_index.is_contiguous(),
+          "audio_gather_pos: int64 token_index")
+    d = embed.shape[-1]
+    per_chunk = pos.shape[0]
+    _need(embed.dim() == 3 and embed.shape[1] == per_chunk and pos.shape[1] == d,
+          "audio_gather_pos: embed [chunks, P, d] and pos [P, d]")
+    tokens = token_index.numel()
+    _need(rows_out >= tokens, "audio_gather_pos: rows_out below the token count")
+    out = torch.empty(rows_out, d, dtype=BF16, device=embed.device)
+    _count()
+    check(lib.b200asr_audio_gather_pos(_p(embed), embed.shape[0] * per_chunk, _p(pos), per_chunk,
+                                       _p(token_index), tokens, rows_out, d, _p(out),
+                                       _p(error_flag), _stream()), "audio_gather_pos")
+    return out
+
+
 # -------------------------------------------------------------------- KV store
 
 

@@ -3,8 +3,9 @@
 Differences from the reference, all numerically neutral: the chunk padding is the
 ``audio_chunk_pad`` kernel instead of a Python loop, q/k/v are one fused projection
 (``qkv_proj`` = [q | k | v] rows, loaded from the checkpoint's three tensors), the
-valid-token gather uses host-known indices instead of a boolean mask (no device
-sync), and window attention is the tcgen05 ``varlen_attention`` kernel.
+positional add and the valid-token gather are one ``audio_gather_pos`` kernel over
+host-known indices instead of a boolean mask (no device sync), and window attention is
+the tcgen05 ``varlen_attention`` kernel.
 
 The convolutional downsampler runs on this library's kernels (csrc/conv.cu): conv2d1
 (one input channel) as a direct stencil, conv2d2 and conv2d3 as tcgen05 implicit GEMMs,
@@ -140,13 +141,12 @@ class AudioEncoder(nn.Module):
         kx.audio_chunk_pad(batch.mel, batch.chunk_start, batch.chunk_lengths, batch.num_chunks,
                            self.chunk_frames, padded)
         embed = self._downsample(padded, batch.num_chunks)
-        embed = embed + self.positional_embedding[: embed.shape[1]].unsqueeze(0).to(embed.dtype)
-        flat = embed.reshape(-1, embed.shape[-1])
         t = batch.token_index.numel()
-        # bucketed row count (shape-stable GEMMs); rows t.. are zeros that attention never
-        # reads (cu_seqlens covers the first t) and that are dropped at the end
-        hidden = flat.new_zeros(padded_rows(t), flat.shape[-1])
-        torch.index_select(flat, 0, batch.token_index, out=hidden[:t])
+        # positional add + valid-token gather in one kernel, into a bucketed row count
+        # (shape-stable GEMMs); rows t.. are zeros that attention never reads (cu_seqlens
+        # covers the first t) and that are dropped at the end
+        pos = self.positional_embedding[: embed.shape[1]].to(embed.dtype).contiguous()
+        hidden = kx.audio_gather_pos(embed, pos, batch.token_index, padded_rows(t))
         for layer in self.layers:
             hidden = layer(hidden, batch.cu_seqlens, batch.max_seqlen)
         hidden = self.ln_post(hidden[:t])
