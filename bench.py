@@ -440,6 +440,9 @@ def run_ours(args) -> None:
 
     for i in range(args.warmup):
         run_features(i)
+    if not args.no_e2e:  # the waveform path too (pinned staging buffers, log-mel batches)
+        for i in range(args.warmup):
+            run_waveforms(i)
     torch.cuda.synchronize()
 
     clocks = ClockSampler(list(range(world)) if rank == 0 else [local])

@@ -442,3 +442,35 @@ def test_batched_record_equals_per_token_record(config):
         assert (per_token, want.token_ids, want.num_computed_tokens, want.stage, want.finish_reason) \
             == (batched, got.token_ids, got.num_computed_tokens, got.stage, got.finish_reason), \
             (case, run, outputs, want.sampling)
+
+
+def test_waveform_staging_during_decode_respects_queue_order_cap_and_budget():
+    """AsrEngine._stage_upcoming_audio (run while a decoder call executes) stages the
+    head of the encode queue in order, at most one encoder call's worth, skips clips
+    already staged, and stops after the first clip past its time budget."""
+    from collections import deque
+    from types import SimpleNamespace
+
+    from voiceagent_b200.engine.engine import AsrEngine
+
+    staged = []
+
+    def stage(features):
+        if features in staged:
+            return False
+        staged.append(features)
+        return True
+
+    queue = deque(SimpleNamespace(features=f"clip{i}") for i in range(10))
+    fake = SimpleNamespace(scheduler=SimpleNamespace(waiting_encode=queue),
+                           config=SimpleNamespace(max_audio_batch_size=4),
+                           audio_runner=SimpleNamespace(renderer=SimpleNamespace(stage=stage)))
+    AsrEngine._stage_upcoming_audio(fake, 0.0)  # no budget: one clip per call
+    assert staged == ["clip0"]
+    AsrEngine._stage_upcoming_audio(fake, 0.0)
+    assert staged == ["clip0", "clip1"]
+    AsrEngine._stage_upcoming_audio(fake, 10.0)  # the rest of the next encoder call
+    assert staged == ["clip0", "clip1", "clip2", "clip3"]
+    queue.popleft()
+    AsrEngine._stage_upcoming_audio(fake, 10.0)
+    assert staged[-1] == "clip4" and len(staged) == 5

@@ -188,14 +188,17 @@ class AsrEngine:
                          finish_reason=request.finish_reason, timings=request.timings,
                          output_token_ids=list(ids))
 
-    def _stage_upcoming_audio(self) -> None:
+    def _stage_upcoming_audio(self, budget_seconds: float) -> None:
         """While a decoder call runs on the GPU: copy the waveforms of the requests at the
         head of the encode queue (the next encoder call's, at most one call's worth) into
-        pinned memory, so that call's host-to-device copy needs no host copy first."""
+        pinned memory, so that call's host-to-device copy needs no host copy first. Stops
+        once ``budget_seconds`` of host time are spent (the rest waits for the next call)."""
+        deadline = time.perf_counter() + budget_seconds
         stage = self.audio_runner.renderer.stage
         for request in itertools.islice(self.scheduler.waiting_encode,
                                         self.config.max_audio_batch_size):
-            stage(request.features)
+            if stage(request.features) and time.perf_counter() >= deadline:
+                return
 
     # -------------------------------------------------------------- loop
 

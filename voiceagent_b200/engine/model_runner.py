@@ -16,7 +16,7 @@ import torch
 from voiceagent_b200 import kernels as kx
 from voiceagent_b200.shapes import padded_rows
 from voiceagent_b200.config import EngineConfig
-from voiceagent_b200.engine.graph_runner import GraphRunner
+from voiceagent_b200.engine.graph_runner import HOST_WORK_SECONDS_PER_STEP, GraphRunner
 from voiceagent_b200.engine.request import AsrRequest
 from voiceagent_b200.engine.scheduler import ModelBatch
 from voiceagent_b200.layers.attention import PagedAttention
@@ -63,8 +63,9 @@ class ModelRunner:
         self.kv_cache: torch.Tensor | None = None
         self.num_blocks = 0
         self.graph_runner: GraphRunner | None = None
-        # host work to overlap with the GPU: called once a decoder call is queued, before
-        # the host waits for its tokens (the engine stages upcoming clips' waveforms)
+        # host work to overlap with the GPU: called with a time budget (seconds) once a
+        # decoder call is queued, before the host waits for its tokens (the engine stages
+        # upcoming clips' waveforms)
         self.host_work = None
         self.timer = NULL_TIMER
         self.error_flag = torch.zeros(1, dtype=torch.int32, device=self.device)
@@ -269,7 +270,7 @@ class ModelRunner:
         host.copy_(ids, non_blocking=True)
         TRANSFERS["d2h"] += 8 * n
         if self.host_work is not None:
-            self.host_work()
+            self.host_work(HOST_WORK_SECONDS_PER_STEP)
         torch.cuda.current_stream().synchronize()
         return host.tolist()
 
