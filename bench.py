@@ -486,9 +486,10 @@ def run_ours(args) -> None:
                "h2d_bytes_per_step": int(xfer["h2d"] / steps),
                "d2h_bytes_per_step": int(xfer["d2h"] / steps),
                "ms_per_step": ms_e_max / steps,
-               "note": "AsrEngine.transcribe from host float32 waveforms: waveform copies "
-                       "(one pinned copy per encode batch), GPU log-mel, token read-back "
-                       "inside the timing"}
+               "note": "AsrEngine.transcribe from host float32 waveforms: pinned staging "
+                       "and host-to-device copies of the waveforms (per clip when staged "
+                       "during decoder calls, else one per encode batch), GPU log-mel and "
+                       "token read-back inside the timing; W untimed waveform steps first"}
     clock_info = clocks.stop() if rank == 0 else None
 
     roof = decode_roofline(torch, device)
