@@ -169,3 +169,18 @@ def test_linear_small_validates_on_the_host(lib):
     assert lib.b200asr_linear_small(dummy, 1024, 8, 1024, dummy, 6000, 3000, dummy, 3000, None,
                                     None) == 1 and "SiLU" in _err(lib)
     assert lib.b200asr_linear_small(None, 0, 0, 1024, None, 128, 0, None, 0, None, None) == 0
+
+
+def test_audio_gather_pos_validates_on_the_host(lib):
+    dummy = ctypes.c_void_p(256)
+    # d must be a multiple of 8, rows_out cover the tokens, rows 16-byte aligned
+    assert lib.b200asr_audio_gather_pos(dummy, 26, dummy, 13, dummy, 20, 24, 892, dummy,
+                                        None, None) == 1 and "bad sizes" in _err(lib)
+    assert lib.b200asr_audio_gather_pos(dummy, 26, dummy, 13, dummy, 20, 19, 896, dummy, None,
+                                        None) == 1
+    assert lib.b200asr_audio_gather_pos(ctypes.c_void_p(258), 26, dummy, 13, dummy, 20, 24, 896,
+                                        dummy, None, None) == 1 and "aligned" in _err(lib)
+    assert lib.b200asr_audio_gather_pos(dummy, 26, None, 13, dummy, 20, 24, 896, dummy, None,
+                                        None) == 1 and "null" in _err(lib)
+    assert lib.b200asr_audio_gather_pos(None, 0, None, 13, None, 0, 0, 896, None, None,
+                                        None) == 0  # nothing to write: no launch
