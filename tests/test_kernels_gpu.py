@@ -842,6 +842,28 @@ def test_linear_small_lm_head_width(kx):
     assert ok and exact >= 0.98, exact
 
 
+@pytest.mark.parametrize("m,k,tiles", [(32, 1024, 1187), (1, 1024, 297), (17, 2048, 700),
+                                       (64, 2048, 1187), (40, 1024, 333)])
+def test_linear_small_persistent_stream_equals_one_cta_per_tile(kx, m, k, tiles):
+    """Projections with more 128-row tiles than two waves of CTAs (the lm_head) run on the
+    persistent streaming kernel; its output is bit-identical to the one-CTA-per-tile
+    kernel's, which even slices of 120-256 tiles still take (no K split at that many
+    tiles, so the same summation order), and close to fp32."""
+    g = torch.Generator(device="cuda").manual_seed(m + k + tiles)
+    x = torch.randn(m, k, device="cuda", generator=g).bfloat16()
+    w = (torch.randn(tiles * 128, k, device="cuda", generator=g) * 0.03).bfloat16()
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    y = kx.linear_small(x, w, error_flag=err)
+    cuts = np.linspace(0, tiles, -(-tiles // 256) + 1).round().astype(int) * 128
+    assert all(120 * 128 <= b - a <= 256 * 128 for a, b in zip(cuts[:-1], cuts[1:]))
+    parts = [kx.linear_small(x, w[a:b], error_flag=err) for a, b in zip(cuts[:-1], cuts[1:])]
+    torch.cuda.synchronize()
+    assert err.item() == 0
+    assert torch.equal(y, torch.cat(parts, dim=1))
+    ok, exact = _close_to(y, x.float() @ w.float().T)
+    assert ok and exact >= 0.98, exact
+
+
 def _within_one_ulp(got, ref, exact_frac=0.99):
     """bf16 tensors that differ only by fp32 summation order upstream."""
     g, r = got.float(), ref.float()

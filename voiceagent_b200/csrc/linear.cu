@@ -640,6 +640,201 @@ __global__ void __launch_bounds__(kLnThreads)
   }
 }
 
+// -----------------------------------------------------------------------------
+// Persistent streaming projection for plain outputs with more 128-row tiles than two
+// waves of CTAs (the lm_head: 151936 vocabulary rows = 1187 tiles). linear_small gives
+// each tile a CTA, so such a launch runs in ~4 waves and every CTA pays its own set-up,
+// first TMA round trip and epilogue. Here at most two CTAs per SM walk the tiles
+// (t = blockIdx.x, + gridDim.x, ...) through one continuous TMA ring: warp 4 streams the
+// weight and activation stages of tile after tile, warp 5 issues the MMAs into one of two
+// TMEM accumulators, and warps 0-3 write a tile out of the other while the next tile
+// accumulates. The MMA sequence of a tile is linear_small's with one K split (same
+// stages, same order), so the outputs are identical.
+// -----------------------------------------------------------------------------
+constexpr int kLsThreads = 192;  // warps 0-3 epilogue, 4 producer, 5 TMEM + MMA
+constexpr int kLsStages = 4;
+
+template <int MP>
+struct Ls {
+  static constexpr int W_BYTES = kLnRows * kLnBK * 2;
+  static constexpr int X_BYTES = MP * kLnBK * 2;
+  static constexpr int STAGE = W_BYTES + X_BYTES;
+  static constexpr size_t SMEM = 1024 + static_cast<size_t>(kLsStages) * STAGE + 256;
+  static constexpr uint32_t TMEM_COLS = 2 * MP;  // two accumulators
+};
+
+template <int MP>
+__global__ void __launch_bounds__(kLsThreads, 2)
+    linear_stream_kernel(const __grid_constant__ CUtensorMap tm_w,
+                         const __grid_constant__ CUtensorMap tm_x, int m, int k_steps, int tiles,
+                         __nv_bfloat16 *__restrict__ y, int64_t y_stride, int32_t *error_flag) {
+  using C = Ls<MP>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *stages = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                                ~uintptr_t(1023));
+  uint64_t *full = reinterpret_cast<uint64_t *>(stages + kLsStages * C::STAGE);
+  uint64_t *empty = full + kLsStages;
+  uint64_t *acc_full = empty + kLsStages;   // [2] the tile's MMAs are done
+  uint64_t *acc_empty = acc_full + 2;       // [2] the epilogue has read the accumulator
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + 2);
+  __shared__ int abort_flag;
+  __shared__ int slot_last[kLsStages];      // ring position last issued into each slot
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  pdl_trigger();
+  if (tid == 0) {
+    abort_flag = 0;
+    for (int s = 0; s < kLsStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+      slot_last[s] = -1;
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 128);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 5) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 4) {
+    // ------------------------------------------------------------------ producer
+    if (lane == 0) {
+      prefetch_tmap(&tm_w);
+      prefetch_tmap(&tm_x);
+      // The weights are static: the first ring's worth (of the first tile) is requested
+      // before waiting for the kernel that produces x; those stages' x follow the wait.
+      const int first = k_steps < kLsStages ? k_steps : kLsStages;
+      const int t0 = blockIdx.x;
+      for (int s = 0; s < first; ++s) {
+        uint8_t *w = stages + s * C::STAGE;
+        mbar_arrive_expect_tx(&full[s], C::STAGE);
+        tma_load_2d(w, &tm_w, s * kLnBK, t0 * kLnRows, &full[s]);
+        tma_load_2d(w + C::W_BYTES / 2, &tm_w, s * kLnBK, t0 * kLnRows + 64, &full[s]);
+        slot_last[s] = s;
+      }
+      pdl_wait();
+      for (int s = 0; s < first; ++s)
+        tma_load_2d(stages + s * C::STAGE + C::W_BYTES, &tm_x, s * kLnBK, 0, &full[s]);
+      uint32_t it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+        for (int s = 0; s < k_steps; ++s, ++it) {
+          if (t == static_cast<int>(blockIdx.x) && s < first) continue;  // issued above
+          const int st = static_cast<int>(it % kLsStages);
+          ok = mbar_wait(&empty[st], ((it / kLsStages) - 1) & 1, error_flag, &abort_flag);
+          if (!ok) break;
+          uint8_t *w = stages + st * C::STAGE;
+          mbar_arrive_expect_tx(&full[st], C::STAGE);
+          tma_load_2d(w, &tm_w, s * kLnBK, t * kLnRows, &full[st]);
+          tma_load_2d(w + C::W_BYTES / 2, &tm_w, s * kLnBK, t * kLnRows + 64, &full[st]);
+          tma_load_2d(w + C::W_BYTES, &tm_x, s * kLnBK, 0, &full[st]);
+          slot_last[st] = static_cast<int>(it);
+        }
+      }
+      if (abort_flag)  // let the copies already issued land before the CTA exits
+        for (int s = 0; s < kLsStages; ++s)
+          if (slot_last[s] >= 0) mbar_drain(&full[s], (slot_last[s] / kLsStages) & 1);
+    }
+  } else if (warp == 5) {
+    // ---------------------------------------------------------------------- MMA
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(kLnRows, MP, false, false);
+      uint32_t it = 0;
+      int j = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++j) {
+        const int acc = j & 1;
+        ok = mbar_wait(&acc_empty[acc], ((j >> 1) & 1) ^ 1, error_flag, &abort_flag);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t d = tmem + acc * MP;
+        for (int s = 0; s < k_steps; ++s, ++it) {
+          const int st = static_cast<int>(it % kLsStages);
+          ok = mbar_wait(&full[st], (it / kLsStages) & 1, error_flag, &abort_flag);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t wb = smem_addr(stages + st * C::STAGE), xb = wb + C::W_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < kLnBK / 16; ++kk)
+            umma_f16_ss(d, smem_desc_sw128(wb + kk * 32, 16, 1024),
+                        smem_desc_sw128(xb + kk * 32, 16, 1024), idesc, (s > 0 || kk > 0) ? 1u : 0u);
+          umma_commit(&empty[st]);
+        }
+        if (ok) umma_commit(&acc_full[acc]);
+      }
+    }
+  } else {
+    // ----------------------------------------------------------------- epilogue
+    // Thread = TMEM lane = weight row (warp * 32 + lane) of the tile; column c of the
+    // accumulator is activation row c. Each column's 32 lanes store 64 contiguous bytes.
+    pdl_wait();  // outputs are written after the kernel before this one
+    const int row = warp * 32 + lane;
+    int j = 0;
+    for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++j) {
+      const int acc = j & 1;
+      if (!mbar_wait(&acc_full[acc], (j >> 1) & 1, error_flag, &abort_flag)) break;
+      tc_fence_after();
+      float v[MP];
+      const uint32_t base = tmem + acc * MP + (static_cast<uint32_t>(warp * 32) << 16);
+#pragma unroll
+      for (int cc = 0; cc < MP / 32; ++cc) tmem_ld32(base + cc * 32, v + cc * 32);
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(&acc_empty[acc]);
+      __nv_bfloat16 *dst = y + static_cast<int64_t>(t) * kLnRows + row;
+#pragma unroll
+      for (int c = 0; c < MP; ++c)
+        if (c < m) dst[c * y_stride] = __float2bfloat16_rn(v[c]);
+    }
+  }
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+template <int MP>
+int launch_linear_stream(const void *x, int64_t x_stride, int m, int k, const void *w, int n,
+                         void *y, int64_t y_stride, int32_t *error_flag, cudaStream_t stream) {
+  using C = Ls<MP>;
+  auto kfn = linear_stream_kernel<MP>;
+  static bool configured = false;
+  if (!configured) {
+    const cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               static_cast<int>(C::SMEM));
+    if (e != cudaSuccess) {
+      set_error("linear_small (stream): kernel configuration failed: %s", cudaGetErrorString(e));
+      return B200ASR_ERR_CUDA;
+    }
+    configured = true;
+  }
+  CUtensorMap tw, tx;
+  const uint64_t wdims[2] = {static_cast<uint64_t>(k), static_cast<uint64_t>(n)};
+  const uint64_t wstr[1] = {static_cast<uint64_t>(k) * 2};
+  const uint32_t wbox[2] = {kLnBK, 64};
+  if (!make_tmap_bf16(&tw, w, 2, wdims, wstr, wbox)) return B200ASR_ERR_CUDA;
+  const uint64_t xdims[2] = {static_cast<uint64_t>(k), static_cast<uint64_t>(m)};
+  const uint64_t xstr[1] = {static_cast<uint64_t>(x_stride) * 2};
+  const uint32_t xbox[2] = {kLnBK, MP};
+  if (!make_tmap_bf16(&tx, x, 2, xdims, xstr, xbox)) return B200ASR_ERR_CUDA;
+  const int tiles = n / kLnRows;
+  const int grid = std::min(tiles, 2 * num_sms());
+  B200_LAUNCH_CHECK_ERR(launch_kernel(kfn, dim3(grid), dim3(kLsThreads), C::SMEM, stream, true,
+                                      1, tw, tx, m, k / kLnBK, tiles,
+                                      static_cast<__nv_bfloat16 *>(y), y_stride, error_flag),
+                        "linear_small (stream)");
+  return B200ASR_OK;
+}
+
 // Rows of x (+ residual, updated in place) as the residual-add epilogue would leave them:
 // h (fp32) and per-128-column partial sums of squares, for a following RMSNorm prologue
 // or norm_apply. One warp per (row, 128 columns).
@@ -907,6 +1102,12 @@ extern "C" int b200asr_linear_small(const void *x, int64_t x_row_stride, int32_t
                                  error_flag);
   const LinearFuse f = {};
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // More tiles than two waves of CTAs, no K split: the persistent streaming kernel.
+  if (!silu_inner && a.k_split == 1 && tiles > 2 * num_sms())
+    return m <= 32 ? launch_linear_stream<32>(x, x_row_stride, m, k, w, n, y, y_row_stride,
+                                              error_flag, st)
+                   : launch_linear_stream<64>(x, x_row_stride, m, k, w, n, y, y_row_stride,
+                                              error_flag, st);
   return silu_inner ? dispatch_linear<false, kEpiSilu>(x, x_row_stride, m, k, w, n, a, f, tiles, st)
                     : dispatch_linear<false, kEpiPlain>(x, x_row_stride, m, k, w, n, a, f, tiles, st);
 }

@@ -522,6 +522,22 @@ def linear_decode(m: int = 32) -> list[dict]:
     return lines
 
 
+def lm_head(rows: int = 32, hidden: int = 1024, vocab: int = 151936) -> dict:
+    """The decode step's lm_head projection alone: ``rows`` activation rows against the
+    [vocab, hidden] bf16 weight (311 MB for the 0.6B model, 622 MB for the 1.7B: above L2,
+    so each launch streams it from HBM), on the persistent streaming kernel."""
+    dev = torch.device("cuda")
+    gen = torch.Generator(device=dev).manual_seed(0)
+    x = torch.randn(rows, hidden, device=dev, generator=gen).bfloat16()
+    w = (torch.randn(vocab, hidden, device=dev, generator=gen) * 0.03).bfloat16()
+    out = torch.empty(rows, vocab, dtype=torch.bfloat16, device=dev)
+    us = graph_time_us([lambda: kx.linear_small(x, w, out=out)] * 16)
+    nbytes = vocab * hidden * 2 + rows * hidden * 2 + rows * vocab * 2
+    del w
+    torch.cuda.empty_cache()
+    return _line("linear_small (lm_head)", f"{rows} x {hidden} -> {vocab}", us, nbytes)
+
+
 def argmax_rows(rows: int = 32) -> dict:
     dev = torch.device("cuda")
     per = rows * 151936 * 2
@@ -631,6 +647,7 @@ BENCHES = {
                        label="config3 decode-step shape B=32 ctx~U[80,250], short-context kernel"),
         decode_config1(lo=80, hi=250, sets=16, max_seqlen_k=4096,
                        label="config3 decode-step shape B=32 ctx~U[80,250], stream-K kernel")],
+    "lm_head": lambda: [lm_head(), lm_head(rows=64, hidden=2048)],
     "step": lambda: [decode_graph_step(True), decode_graph_step(True, l2_prefetch=True),
                      decode_graph_step(False)],
     "step_1p7b": lambda: [decode_graph_step(True, preset="1.7b", rows_n=64)],
