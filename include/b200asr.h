@@ -335,7 +335,9 @@ B200ASR_API int b200asr_greedy_argmax(const void *logits, int64_t row_stride, in
  * w is [n, k] row-major (k % 64 == 0, n % 128 == 0). With silu_inner = I > 0 the
  * weight is the fused [gate; up] of 2I rows (I % 64 == 0) and
  *   y[r, j] = bf16(bf16(silu(bf16(gate))) * bf16(up)),  j < I.
- * No workspace; launches thread-block clusters (split-K reduced on chip).           */
+ * No workspace; launches thread-block clusters (split-K reduced on chip). A plain
+ * projection with more 128-row tiles than two CTAs per SM (the lm_head) runs on a
+ * persistent kernel that streams the tiles through one TMA ring; same results.       */
 B200ASR_API int b200asr_linear_small(const void *x, int64_t x_row_stride, int32_t m, int32_t k,
                          const void *w, int32_t n, int32_t silu_inner, void *y,
                          int64_t y_row_stride, int32_t *error_flag, b200asr_stream_t stream);
