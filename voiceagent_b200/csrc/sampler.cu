@@ -117,14 +117,18 @@ __global__ void __cluster_dims__(kArgmaxCluster, 1, 1) __launch_bounds__(kArgmax
     if (lane == 0) cta_best = b;
   }
   cluster.sync();
-  if (rank == 0 && threadIdx.x == 0) {
-    Best b = cta_best;
-    for (int r = 1; r < kArgmaxCluster; ++r) {
-      const Best *other = cluster.map_shared_rank(&cta_best, r);
-      const Best o = *other;
-      if (better(o.v, o.idx, b.v, b.idx)) b = o;
+  if (rank == 0 && warp == 0) {
+    // lane r < 8 reads CTA r's result (the remote reads in flight together), then a
+    // shuffle reduction; better() orders by value and index, so the order is free
+    Best b{-INFINITY, INT_MAX};
+    if (lane < kArgmaxCluster) b = *cluster.map_shared_rank(&cta_best, lane);
+#pragma unroll
+    for (int o = kArgmaxCluster / 2; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, b.v, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, b.idx, o);
+      if (better(ov, oi, b.v, b.idx)) b = {ov, oi};
     }
-    out_ids[row] = b.idx == INT_MAX ? 0 : b.idx;
+    if (lane == 0) out_ids[row] = b.idx == INT_MAX ? 0 : b.idx;
   }
   cluster.sync();  // keep every CTA's shared memory alive until the leader has read it
 }
