@@ -474,3 +474,107 @@ def test_waveform_staging_during_decode_respects_queue_order_cap_and_budget():
     queue.popleft()
     AsrEngine._stage_upcoming_audio(fake, 10.0)
     assert staged[-1] == "clip4" and len(staged) == 5
+
+
+def _reference_take_decodes(scheduler, batch):
+    """The per-request form of Scheduler._take_decodes (the reference's loop)."""
+    bm = scheduler.block_manager
+    while scheduler.running:
+        if bm.can_append(scheduler.running[0]):
+            batch.decode.append(scheduler.running.popleft())
+        elif len(scheduler.running) > 1:
+            scheduler._preempt(scheduler.running.pop())
+        else:
+            scheduler._retire(scheduler.running.popleft(), "aborted:out_of_kv_blocks")
+            return
+
+
+def _reference_decode_steps_for(scheduler, batch, limit, max_model_len):
+    """The per-request form of Scheduler.decode_steps_for."""
+    if limit <= 1 or batch.prefill or not batch.decode:
+        return 1
+    if any(r.cancel_requested for r in batch.decode):
+        return 1
+    steps = min([limit] + [min(r.sampling.max_new_tokens - r.num_output_tokens,
+                               max_model_len - len(r) + 1) for r in batch.decode])
+    if steps <= 1:
+        return 1
+    bm = scheduler.block_manager
+    if sum(bm.blocks_ahead(r, steps) for r in batch.decode) > bm.num_free_blocks:
+        return 1
+    for r in batch.decode:
+        bm.append_ahead(r, steps)
+    return steps
+
+
+def _random_decode_state(config, rng, n_blocks):
+    manager = BlockManager(n_blocks, BS, enable_prefix_cache=False)
+    scheduler = Scheduler(config(max_num_seqs=16), manager)
+    made = []
+    for _ in range(int(rng.integers(1, 7))):
+        prompt = int(rng.integers(22, 3 * BS))
+        outputs = int(rng.integers(0, 12))
+        if rng.random() < 0.6:  # land near a block boundary: lengths BS k - 2 .. BS k + 2
+            target = BS * (prompt // BS + 1) + int(rng.integers(-2, 3))
+            outputs = max(0, target - prompt)
+        r = make_request(prompt, max_new_tokens=outputs + int(rng.integers(2, 40)))
+        if manager.num_free_blocks < -(-(prompt + outputs) // BS):  # prompt + outputs' blocks
+            break
+        start_decoding(scheduler, manager, r)
+        r.token_ids += [150] * outputs  # outputs already sampled
+        manager.may_append(r)
+        made.append(r)
+    # use up free blocks so that block-opening requests meet a full cache
+    while manager.num_free_blocks > int(rng.integers(0, 3)):
+        manager._take_any()
+    return scheduler, manager, made
+
+
+def test_take_decodes_equals_the_per_request_loop(config):
+    """Scheduler._take_decodes' shortcut (every request joins when a block is free or none
+    opens one) decides exactly as the reference's request-by-request loop: same decode
+    batch, preemptions, aborts and block-manager state, over random caches near full."""
+    import copy
+
+    rng = np.random.default_rng(21)
+    for case in range(300):
+        scheduler, manager, made = _random_decode_state(config, rng, int(rng.integers(3, 12)))
+        if not made:
+            continue
+        other = copy.deepcopy((scheduler, made))
+        fast_batch, ref_batch = ModelBatch(), ModelBatch()
+        scheduler._take_decodes(fast_batch)
+        _reference_take_decodes(other[0], ref_batch)
+        ids = lambda rs: [r.request_id for r in rs]
+        assert ids(fast_batch.decode) == ids(ref_batch.decode), case
+        assert ids(scheduler.running) == ids(other[0].running), case
+        assert ids(scheduler.waiting_prefill) == ids(other[0].waiting_prefill), case
+        assert ids(scheduler.aborted) == ids(other[0].aborted), case
+        assert manager.num_free_blocks == other[0].block_manager.num_free_blocks, case
+        assert [r.block_table for r in made] == [r.block_table for r in other[1]], case
+
+
+def test_decode_steps_for_equals_the_per_request_form(config):
+    """Scheduler.decode_steps_for (lengths measured once, only block-opening requests
+    visited) returns the same step count and takes the same blocks as the per-request
+    form, over random budgets, model lengths and nearly full caches."""
+    import copy
+
+    rng = np.random.default_rng(22)
+    for case in range(300):
+        scheduler, manager, made = _random_decode_state(config, rng, int(rng.integers(4, 14)))
+        if not made:
+            continue
+        batch = scheduler.schedule_model()
+        if not batch.decode or batch.prefill:
+            continue
+        if rng.random() < 0.05:
+            batch.decode[0].cancel_requested = True
+        limit = int(rng.integers(1, 6))
+        max_len = int(rng.integers(BS, 4 * BS))
+        other_sched, other_batch = copy.deepcopy((scheduler, batch))
+        got = scheduler.decode_steps_for(batch, limit, max_len)
+        want = _reference_decode_steps_for(other_sched, other_batch, limit, max_len)
+        assert got == want, (case, got, want)
+        assert [r.block_table for r in batch.decode] == [r.block_table for r in other_batch.decode]
+        assert manager.num_free_blocks == other_sched.block_manager.num_free_blocks
