@@ -4,13 +4,13 @@
     python bench.py [--gpus N --steps K --warmup W] [--impl reference]
     torchrun --nproc-per-node N bench.py --gpus N ...   (one process per GPU)
 
-Default workload: a job of 512 synthetic 16 kHz clips per GPU,
+Default workload (benchmark configuration 3): a job of 512 synthetic 16 kHz clips per GPU,
 durations lognormal(median 7 s, sigma 0.6) clipped to 1-35 s, Qwen3-ASR-0.6B with
 seeded random-init bf16 weights, max_num_seqs = 32, exactly 64 greedy tokens per
 request (EOS ignored), CUDA-graph decode on. The job is ONE request list that the host
 router (``replicas.route_by_duration``) splits over the ranks; each rank synthesises
 only its own requests and transcribes them in steps of ``--clips-per-step`` through
-``AsrEngine.transcribe``. ``--workload config4`` runs BASELINE config 4 instead: the
+``AsrEngine.transcribe``. ``--workload config4`` runs benchmark configuration 4 instead: the
 1.7B architecture at 64 concurrent requests, 4096 clips plus one 20-minute recording
 cut into 30 s chunks, 96 greedy tokens each, the whole job split over the ranks
 (strong scaling).
@@ -82,7 +82,7 @@ def parse_args():
                    help="only the config-1 paged decode op (e.g. for an ncu capture)")
     args = p.parse_args()
     if args.workload == "config4":
-        # 1.7B at 64 concurrent requests, 96 greedy tokens per chunk
+        # benchmark configuration 4: 1.7B at 64 concurrent requests, 96 greedy tokens per chunk
         args.preset = args.preset or "1.7b"
         if args.concurrency == 32:
             args.concurrency = 64
