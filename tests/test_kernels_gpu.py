@@ -531,7 +531,7 @@ def test_paged_decode_newest_row_written_just_before_with_pdl(kx, max_len):
 
 
 def test_paged_decode_config1(kx):
-    """B=32, ctx ~ U[64, 1024], 4096-block pool, random tables."""
+    """Benchmark configuration 1: B=32, ctx ~ U[64, 1024], 4096-block pool, random tables."""
     rng = np.random.default_rng(0)
     lens = rng.integers(64, 1025, size=32)
     q, kc, vc, tables, cu_k = _decode_case(rng, lens)
@@ -601,7 +601,7 @@ def test_paged_prefill_matches_oracle(kx, q_lens, k_lens):
 
 
 def test_paged_prefill_config2_lengths(kx):
-    """BASELINE config 2 decoder part: 32 prompts of 13*s + 24 tokens, s ~ U(2, 30)."""
+    """Benchmark configuration 2, decoder part: 32 prompts of 13*s + 24 tokens, s ~ U(2, 30)."""
     rng = np.random.default_rng(2)
     secs = rng.uniform(2, 30, size=32)
     lens = [int(K.num_audio_tokens(int(100 * s))) + 24 for s in secs]
