@@ -578,3 +578,33 @@ def test_decode_steps_for_equals_the_per_request_form(config):
         assert got == want, (case, got, want)
         assert [r.block_table for r in batch.decode] == [r.block_table for r in other_batch.decode]
         assert manager.num_free_blocks == other_sched.block_manager.num_free_blocks
+
+
+def test_decode_descriptor_fill_equals_the_per_request_layout():
+    """graph_runner.fill_decode_descriptor (one slice store per field) writes the same
+    descriptor as a request-by-request fill: lengths, last ids, table offsets and lengths,
+    the concatenated tables; untouched padding slots keep their values."""
+    from types import SimpleNamespace
+
+    from voiceagent_b200.engine.graph_runner import fill_decode_descriptor
+
+    rng = np.random.default_rng(23)
+    for case in range(200):
+        m = int(rng.choice([1, 4, 8, 32, 64]))
+        n = int(rng.integers(1, m + 1))
+        reqs = [SimpleNamespace(token_ids=list(rng.integers(0, 1000, size=int(rng.integers(1, 600)))),
+                                block_table=list(rng.integers(0, 4096, size=int(rng.integers(0, 5)))))
+                for _ in range(n)]
+        got = np.full(4 * m + 5 * m, -7, np.int32)
+        want = got.copy()
+        cursor, longest = fill_decode_descriptor(got, m, reqs)
+        at = 4 * m
+        for i, r in enumerate(reqs):  # the request-by-request form
+            want[i] = len(r.token_ids)
+            want[m + i] = r.token_ids[-1]
+            want[2 * m + i] = at - 4 * m
+            want[3 * m + i] = len(r.block_table)
+            want[at:at + len(r.block_table)] = r.block_table
+            at += len(r.block_table)
+        assert cursor == at and longest == max(len(r.token_ids) for r in reqs)
+        np.testing.assert_array_equal(got, want, err_msg=str(case))

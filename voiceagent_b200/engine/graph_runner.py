@@ -40,6 +40,25 @@ DEFAULT_BUCKETS = (1, 2, 4, 8, 16, 24, 32, 48, 64)
 HOST_WORK_SECONDS_PER_STEP = 0.4e-3
 
 
+def fill_decode_descriptor(h, m: int, requests) -> tuple[int, int]:
+    """Write the rows of ``requests`` into the host descriptor ``h`` (int32, laid out as
+    lengths [m] | last token ids [m] | table offsets [m] | table lengths [m] | the
+    concatenated block tables) with one slice store per field. Returns (the number of
+    ints used, the longest length)."""
+    n = len(requests)
+    lengths = [len(r.token_ids) for r in requests]
+    tables = [r.block_table for r in requests]
+    table_lens = [len(t) for t in tables]
+    flat = list(itertools.chain.from_iterable(tables))
+    h[0:n] = lengths
+    h[m:m + n] = [r.token_ids[-1] for r in requests]
+    h[2 * m:2 * m + n] = list(itertools.accumulate(table_lens, initial=0))[:n]
+    h[3 * m:3 * m + n] = table_lens
+    cursor = 4 * m + len(flat)
+    h[4 * m:cursor] = flat
+    return cursor, max(lengths)
+
+
 class GraphRunner:
     def __init__(self, model, config: EngineConfig, error_flag: torch.Tensor | None = None,
                  buckets: tuple[int, ...] = DEFAULT_BUCKETS):
@@ -154,21 +173,10 @@ class GraphRunner:
             raise ValueError(f"no captured graph for a batch of {n}")
         if not 1 <= steps <= self.max_steps:
             raise ValueError(f"steps must be in [1, {self.max_steps}], got {steps}")
-        m, h = self.max_batch, self._host_np
-        # one slice store per descriptor field (numpy converts each list in C)
-        lengths = [len(r.token_ids) for r in requests]
-        tables = [r.block_table for r in requests]
-        table_lens = [len(t) for t in tables]
-        flat = list(itertools.chain.from_iterable(tables))
-        h[0:n] = lengths
-        h[m:m + n] = [r.token_ids[-1] for r in requests]
-        h[2 * m:2 * m + n] = list(itertools.accumulate(table_lens, initial=0))[:n]
-        h[3 * m:3 * m + n] = table_lens
-        cursor = 4 * m + len(flat)
-        h[4 * m:cursor] = flat
+        cursor, max_len = fill_decode_descriptor(self._host_np, self.max_batch, requests)
         self._fill_padding(n)
         self.desc[:cursor].copy_(self.host_desc[:cursor], non_blocking=True)
-        key = (bucket, self.uses_short_graph(max(lengths), steps))
+        key = (bucket, self.uses_short_graph(max_len, steps))
         for k in range(steps):
             self.graphs[key].replay()
             self.host_tokens[k, :n].copy_(self.token_ids[:n], non_blocking=True)
