@@ -608,3 +608,16 @@ def test_decode_descriptor_fill_equals_the_per_request_layout():
             at += len(r.block_table)
         assert cursor == at and longest == max(len(r.token_ids) for r in reqs)
         np.testing.assert_array_equal(got, want, err_msg=str(case))
+
+
+def test_encoder_positions_equal_the_oracle_table():
+    """The encoder's sinusoid position table (the pos operand of audio_gather_pos) equals
+    the oracle's restatement of SinusoidsPositionEmbedding, in fp32 and after the bf16
+    cast the encoder applies."""
+    from oracle.model import sinusoid_table as oracle_table
+    from voiceagent_b200.qwen3_asr.audio_encoder import sinusoid_table
+
+    for length, channels in ((1500, 896), (1500, 1280), (13, 64)):
+        got, want = sinusoid_table(length, channels), oracle_table(length, channels)
+        assert got.dtype == want.dtype == torch.float32
+        assert torch.equal(got, want) and torch.equal(got.bfloat16(), want.bfloat16())
