@@ -184,3 +184,22 @@ def test_audio_gather_pos_validates_on_the_host(lib):
                                         None) == 1 and "null" in _err(lib)
     assert lib.b200asr_audio_gather_pos(None, 0, None, 13, None, 0, 0, 896, None, None,
                                         None) == 0  # nothing to write: no launch
+
+
+def test_integration_stub_matches_the_bindings():
+    """Every ``_lib.<fn>.argtypes = [...]`` line of the INTEGRATION.md ctypes stub lists the
+    same argument types as the library's own binding (voiceagent_b200/_lib.py), so the stub
+    a maintainer copies calls each entry point with the header's signature."""
+    from voiceagent_b200._lib import SIGNATURES
+
+    text = (REPO / "INTEGRATION.md").read_text()
+    alias = {"P": ctypes.c_void_p, "I32": ctypes.c_int32, "I64": ctypes.c_int64,
+             "F32": ctypes.c_float, "SZ": ctypes.c_size_t}
+    found = re.findall(r"_lib\.(b200asr_[a-z0-9_]+)\.argtypes = \[([^\]]*)\]", text)
+    assert len(found) >= 25
+    for name, body in found:
+        got = [alias[t.strip()] for t in body.replace("\n", " ").split(",") if t.strip()]
+        want = SIGNATURES[name][1]
+        norm = lambda ts: [ctypes.c_void_p if t in (ctypes.c_void_p, ctypes.c_char_p) else t
+                           for t in ts]
+        assert norm(got) == norm(want), name
