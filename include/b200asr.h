@@ -136,8 +136,8 @@ B200ASR_API int b200asr_audio_chunk_pad(const void *mel, int32_t bins, int32_t t
                             int32_t num_chunks, int32_t chunk_frames, void *padded,
                             b200asr_stream_t stream);
 
-/* Replaces the "conv.gather" step of AudioEncoder.forward (models/audio_encoder.py:
- * 169-173): out[i] = bf16(embed[src] + pos[src % tokens_per_chunk]) with
+/* Replaces the "conv.gather" step of AudioEncoder.forward
+ * (models/audio_encoder.py:169-173): out[i] = bf16(embed[src] + pos[src % tokens_per_chunk]) with
  * src = token_index[i] for i < tokens (embed bf16[embed_rows, d], the conv_out rows of
  * every chunk; pos bf16[tokens_per_chunk, d]); rows [tokens, rows_out) of out are zero.
  * An index outside [0, embed_rows) raises B200ASR_DEVERR_LENGTH (its row is zeroed).  */
